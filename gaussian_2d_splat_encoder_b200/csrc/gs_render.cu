@@ -1,0 +1,1335 @@
+// gs_render.cu -- tile-binned, order-independent ("odds"/alpha) splat renderer for sm_100a.
+//
+// Replaces the reference's render path (bigwolfeman/gaussian-2d-splat-encoder,
+// gaussian_splat_encoder/render_triton.py): the octave routing + per-octave _build_tiles +
+// _gather_pairs + _render_fwd_cull_kernel + _upsample_field + composite (forward), and
+// _render_bwd_cull_kernel + index_add_ + the autograd of the upsample/composite (backward).
+//
+// Forward, one launch sequence for the whole batch and all octaves (no host sync):
+//   k_preprocess   per splat: softplus scale, octave, clamped tile rectangle, 48-byte render record
+//   k_scan_blocks  exclusive scan of per-block pair counts
+//   k_emit         (global tile id, splat id) pairs in splat order, load-balanced per block
+//   k_radix_*      stable LSD radix sort of the pairs by global tile id (2 passes for <= 16 bits)
+//   k_ranges       [begin, end) of every tile in the sorted pair list
+//   k_fields_fwd   one CTA per tile: raw sums S_log, S_w, S_wc of every group (octave) at its own
+//                  resolution; splat records staged per warp in shared memory
+//   k_composite    bilinear upsample of every present group to native resolution, sum, composite
+// Backward:
+//   k_composite_bwd  dS fields at native resolution, bg gradient
+//   k_adjoint        adjoint of the bilinear upsample -> dS fields of every coarse group
+//   k_fields_bwd     one CTA per tile, one lane per (tile, splat) pair looping over the tile's
+//                    pixels; 9 per-splat sums leave through 3 vector atomics per pair
+//   k_finalize       per-splat chain rule (rotation, scale, softplus) into the leaf gradients
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include "../../include/gsplat_b200.h"
+#include "gs_common.cuh"
+
+static thread_local char g_last_error[512] = "";
+static unsigned long long g_launches = 0;  // kernels enqueued by this library (all threads)
+
+#define GS_COUNT(n) __atomic_fetch_add(&g_launches, (unsigned long long)(n), __ATOMIC_RELAXED)
+
+// Optional CUDA-event timing of the render stages (gs_profile_enable / gs_profile_collect): events are
+// recorded on the launching stream around each stage, so the durations are device time of exactly
+// those kernels.
+#include <memory>
+#include <mutex>
+#include <vector>
+namespace {
+enum { PR_BIN = 0, PR_FIELDS_FWD = 1, PR_COMPOSITE = 2, PR_COMPOSITE_BWD = 3, PR_FIELDS_BWD = 4, PR_FINALIZE = 5,
+       PR_N = 8 };
+struct ProfEvent {
+    int region;
+    cudaEvent_t a, b;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<ProfEvent> g_prof;
+struct ProfScope {
+    bool on;
+    ProfEvent ev;
+    cudaStream_t s;
+    ProfScope(int region, cudaStream_t st) : on(g_prof_on), s(st) {
+        if (!on) return;
+        ev.region = region;
+        cudaEventCreate(&ev.a);
+        cudaEventCreate(&ev.b);
+        cudaEventRecord(ev.a, s);
+    }
+    ~ProfScope() {
+        if (!on) return;
+        cudaEventRecord(ev.b, s);
+        std::lock_guard<std::mutex> lk(g_prof_mu);
+        g_prof.push_back(ev);
+    }
+};
+}  // namespace
+
+static int set_cuda_error(cudaError_t e, const char *where) {
+    snprintf(g_last_error, sizeof(g_last_error), "%s: %s", where, cudaGetErrorString(e));
+    return GS_ERR_CUDA;
+}
+
+#define GS_CHECK_LAUNCH(where)                                   \
+    do {                                                         \
+        GS_COUNT(1);                                             \
+        cudaError_t _e = cudaGetLastError();                     \
+        if (_e != cudaSuccess) return set_cuda_error(_e, where); \
+    } while (0)
+
+// ----------------------------------------------------------------------------------------------------
+// block-wide helpers
+
+template <int NT>
+__device__ __forceinline__ int block_excl_scan(int v, int *warp_sums, int *total) {
+    constexpr int NWARP = NT / 32;
+    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int s = lane < NWARP ? warp_sums[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        if (lane < NWARP) warp_sums[lane] = s;  // inclusive
+    }
+    __syncthreads();
+    int warp_prefix = warp > 0 ? warp_sums[warp - 1] : 0;
+    if (total) *total = warp_sums[NWARP - 1];
+    int r = warp_prefix + x - v;
+    __syncthreads();
+    return r;
+}
+
+// ----------------------------------------------------------------------------------------------------
+// geometry of a splat (render_triton.py:362-377 and 925-952), fp32 with no contraction so the tile
+// rectangle is bit-identical to the reference's separate torch ops.
+
+__device__ __forceinline__ int octave_of(float sy, float sx, float rep, float bt, int maxo) {
+    float sp = __fmul_rn(fmaxf(sy, sx), rep);
+    float q = __fdiv_rn(sp, bt);
+    q = fmaxf(q, 1e-6f);
+    float o = ceilf(log2f(q));
+    o = fminf(fmaxf(o, 0.0f), (float)maxo);
+    return (int)o;
+}
+
+__device__ __forceinline__ void tile_rect(float muy, float mux, float sy, float sx, int Hg, int Wg, int T,
+                                          float cutoff, int ntx, int nty, int &x0, int &x1, int &y0, int &y1) {
+    float cx = __fmul_rn(mux, (float)Wg);
+    float cy = __fmul_rn(muy, (float)Hg);
+    float r = __fmul_rn(cutoff, fmaxf(sy, sx));
+    float rx = __fmul_rn(r, (float)Wg);
+    float ry = __fmul_rn(r, (float)Hg);
+    float fT = (float)T;
+    float a = floorf(__fdiv_rn(__fsub_rn(cx, rx), fT));
+    float b = floorf(__fdiv_rn(__fadd_rn(cx, rx), fT));
+    float c = floorf(__fdiv_rn(__fsub_rn(cy, ry), fT));
+    float d = floorf(__fdiv_rn(__fadd_rn(cy, ry), fT));
+    float mx = (float)(ntx - 1), my = (float)(nty - 1);
+    x0 = (int)fminf(fmaxf(a, 0.0f), mx);
+    x1 = (int)fminf(fmaxf(b, 0.0f), mx);
+    y0 = (int)fminf(fmaxf(c, 0.0f), my);
+    y1 = (int)fminf(fmaxf(d, 0.0f), my);
+}
+
+__device__ __forceinline__ int group_of_splat(const RenderGeom &G, int i, float sy, float sx) {
+    if (G.mode == GS_MODE_OCTAVE) return octave_of(sy, sx, G.rep, G.base_texels, G.max_oct);
+    if (G.mode == GS_MODE_MULTIRES) return (G.n_coarse > 0 && G.n_coarse < G.N && i < G.n_coarse) ? 0 : 1;
+    return 0;
+}
+
+// ----------------------------------------------------------------------------------------------------
+// forward: preprocessing
+
+// meta = {global tile id of the rectangle's top-left, width | group << 24, ntx of the group, count}
+__global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *__restrict__ mu,
+                                                    const float *__restrict__ ls, const float *__restrict__ col,
+                                                    const float *__restrict__ op, const float *__restrict__ th,
+                                                    SplatRec *__restrict__ rec, int4 *__restrict__ meta,
+                                                    int *__restrict__ counts, int *__restrict__ bsum,
+                                                    unsigned long long *__restrict__ gpairs,
+                                                    int *__restrict__ gsplats) {
+    __shared__ int wsum[8];
+    __shared__ unsigned long long s_pairs[4 * GS_MAX_GROUPS];
+    __shared__ int s_spl[4 * GS_MAX_GROUPS];
+    if (threadIdx.x < 4 * GS_MAX_GROUPS) {
+        s_pairs[threadIdx.x] = 0ull;
+        s_spl[threadIdx.x] = 0;
+    }
+    __syncthreads();
+    const int b0 = G.N > 0 ? (int)(((long long)blockIdx.x * blockDim.x) / G.N) : 0;
+    long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    int count = 0;
+    if (s < (long long)G.B * G.N) {
+        int b = (int)(s / G.N), i = (int)(s - (long long)b * G.N);
+        float2 m = reinterpret_cast<const float2 *>(mu)[s];  // (y, x)
+        float2 l = reinterpret_cast<const float2 *>(ls)[s];
+        float sy = gs_softplus_eps(l.x), sx = gs_softplus_eps(l.y);
+        float o = op[s];
+        float cth = 1.0f, sth = 0.0f;
+        if (G.has_theta) {
+            float t = th[s];
+            sincosf(t, &sth, &cth);
+        }
+        float c0 = 0.f, c1 = 0.f, c2 = 0.f;
+        if (G.C > 0) c0 = col[s * G.C + 0];
+        if (G.C > 1) c1 = col[s * G.C + 1];
+        if (G.C > 2) c2 = col[s * G.C + 2];
+        float iy = GS_K / sy, ix = GS_K / sx;
+        SplatRec r;
+        r.a = make_float4(m.x, m.y, cth * iy, sth * iy);
+        r.b = make_float4(-sth * ix, cth * ix, o, log2f(o));
+        r.c = make_float4(c0, c1, c2, o <= GS_DEAD_OP ? 1.0f : 0.0f);
+        rec[s] = r;
+        int g = group_of_splat(G, i, sy, sx);
+        int4 mt = make_int4(0, 0, 1, 0);
+        if (G.mode != GS_MODE_EXACT) {
+            GroupGeom gg = G.g[g];
+            int x0, x1, y0, y1;
+            tile_rect(m.x, m.y, sy, sx, gg.H, gg.W, G.tile, G.cutoff, gg.ntx, gg.nty, x0, x1, y0, y1);
+            int w = x1 - x0 + 1;
+            count = w * (y1 - y0 + 1);
+            mt = make_int4(b * G.tiles_per_image + gg.tile_off + y0 * gg.ntx + x0, w | (g << 24), gg.ntx, count);
+        } else {
+            mt.y = g << 24;
+        }
+        meta[s] = mt;
+        counts[s] = count;
+        if (b - b0 < 4) {
+            atomicAdd(&s_pairs[(b - b0) * GS_MAX_GROUPS + g], (unsigned long long)count);
+            atomicAdd(&s_spl[(b - b0) * GS_MAX_GROUPS + g], 1);
+        } else {
+            atomicAdd(&gpairs[b * G.ngroups + g], (unsigned long long)count);
+            atomicAdd(&gsplats[b * G.ngroups + g], 1);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < 4 * GS_MAX_GROUPS && s_spl[threadIdx.x] > 0) {
+        int bb = b0 + threadIdx.x / GS_MAX_GROUPS, gg = threadIdx.x % GS_MAX_GROUPS;
+        atomicAdd(&gpairs[bb * G.ngroups + gg], s_pairs[threadIdx.x]);
+        atomicAdd(&gsplats[bb * G.ngroups + gg], s_spl[threadIdx.x]);
+    }
+    // per-block pair total
+    int v = count;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int t = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += wsum[w];
+        bsum[blockIdx.x] = t;
+    }
+}
+
+// single-block exclusive scan of n ints in place; total -> *total (as long long)
+__global__ void __launch_bounds__(1024) k_scan_blocks(int *__restrict__ data, int n, long long *__restrict__ total) {
+    __shared__ int wsum[32];
+    int per = (n + 1023) / 1024;
+    int lo = threadIdx.x * per, hi = min(n, lo + per);
+    int s = 0;
+    for (int i = lo; i < hi; i++) s += data[i];
+    int tot;
+    int pre = block_excl_scan<1024>(s, wsum, &tot);
+    for (int i = lo; i < hi; i++) {
+        int v = data[i];
+        data[i] = pre;
+        pre += v;
+    }
+    if (threadIdx.x == 0) *total = tot;
+}
+
+// pairs in splat order: key = global tile id, value = global splat id
+__global__ void __launch_bounds__(256) k_emit(RenderGeom G, const int4 *__restrict__ meta,
+                                              const int *__restrict__ counts, const int *__restrict__ bpre,
+                                              unsigned *__restrict__ keys, int *__restrict__ vals,
+                                              int *__restrict__ status) {
+    __shared__ int wsum[8];
+    __shared__ int soff[257];
+    __shared__ int4 smeta[256];
+    long long s0 = (long long)blockIdx.x * 256;
+    long long s = s0 + threadIdx.x;
+    int c = 0;
+    int4 mt = make_int4(0, 0, 1, 0);
+    if (s < (long long)G.B * G.N) {
+        c = counts[s];
+        mt = meta[s];
+    }
+    int tot;
+    int off = block_excl_scan<256>(c, wsum, &tot);
+    soff[threadIdx.x] = off;
+    smeta[threadIdx.x] = mt;
+    if (threadIdx.x == 0) soff[256] = tot;
+    __syncthreads();
+    long long base = bpre[blockIdx.x];
+    for (int e = threadIdx.x; e < tot; e += 256) {
+        // splat k of this block with soff[k] <= e < soff[k+1]
+        int lo = 0, hi = 255;
+        while (lo < hi) {
+            int mid = (lo + hi + 1) >> 1;
+            if (soff[mid] <= e) lo = mid; else hi = mid - 1;
+        }
+        int4 m = smeta[lo];
+        int r = e - soff[lo];
+        int w = m.y & 0xffffff;
+        int q = r / w;
+        unsigned tile = (unsigned)(m.x + q * m.z + (r - q * w));
+        long long pos = base + e;
+        if (pos < G.cap) {
+            keys[pos] = tile;
+            vals[pos] = (int)(s0 + lo);
+        } else {
+            atomicOr(status, 1);
+        }
+    }
+}
+
+// ----------------------------------------------------------------------------------------------------
+// stable LSD radix sort of (key, value) pairs; n read from the device, grids sized for the capacity.
+
+#define RS_THREADS 256
+#define RS_ROUNDS 8
+#define RS_ITEMS (RS_THREADS * RS_ROUNDS)
+
+__device__ __forceinline__ long long clamp_n(const long long *n_ptr, long long cap) {
+    long long n = *n_ptr;
+    return n < cap ? n : cap;
+}
+
+__global__ void __launch_bounds__(RS_THREADS) k_radix_upsweep(const unsigned *__restrict__ keys,
+                                                              const long long *__restrict__ n_ptr, long long cap,
+                                                              int shift, int radix, int *__restrict__ hist,
+                                                              int nblk_cap) {
+    __shared__ int h[256];
+    long long n = clamp_n(n_ptr, cap);
+    long long base = (long long)blockIdx.x * RS_ITEMS;
+    if (base >= n) return;
+    for (int d = threadIdx.x; d < radix; d += RS_THREADS) h[d] = 0;
+    __syncthreads();
+    unsigned mask = (unsigned)radix - 1u;
+    for (int r = 0; r < RS_ROUNDS; r++) {
+        long long i = base + r * RS_THREADS + threadIdx.x;
+        if (i < n) atomicAdd(&h[(keys[i] >> shift) & mask], 1);
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < radix; d += RS_THREADS) hist[d * nblk_cap + blockIdx.x] = h[d];
+}
+
+// grid = radix blocks: exclusive scan of one digit's per-block counts; digit total -> dtot[d]
+__global__ void __launch_bounds__(256) k_radix_scan(int *__restrict__ hist, const long long *__restrict__ n_ptr,
+                                                    long long cap, int nblk_cap, int *__restrict__ dtot) {
+    __shared__ int wsum[8];
+    long long n = clamp_n(n_ptr, cap);
+    int nblk = (int)((n + RS_ITEMS - 1) / RS_ITEMS);
+    int *h = hist + (long long)blockIdx.x * nblk_cap;
+    int carry = 0;
+    for (int c0 = 0; c0 < nblk; c0 += 256) {
+        int i = c0 + threadIdx.x;
+        int v = i < nblk ? h[i] : 0;
+        int tot;
+        int pre = block_excl_scan<256>(v, wsum, &tot);
+        if (i < nblk) h[i] = carry + pre;
+        carry += tot;
+    }
+    if (threadIdx.x == 0) dtot[blockIdx.x] = carry;
+}
+
+__global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep(const unsigned *__restrict__ kin,
+                                                                const int *__restrict__ vin,
+                                                                unsigned *__restrict__ kout, int *__restrict__ vout,
+                                                                const long long *__restrict__ n_ptr, long long cap,
+                                                                int shift, int radix, const int *__restrict__ hist,
+                                                                int nblk_cap, const int *__restrict__ dtot) {
+    constexpr int NWARP = RS_THREADS / 32;
+    __shared__ int wsum[NWARP];
+    __shared__ int base_d[256];   // digit base + this block's scanned offset, advanced per round
+    __shared__ int wcnt[NWARP][256];
+    long long n = clamp_n(n_ptr, cap);
+    long long base = (long long)blockIdx.x * RS_ITEMS;
+    if (base >= n) return;
+    int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // digit bases: exclusive scan of digit totals (radix <= 256 = RS_THREADS)
+    int dv = tid < radix ? dtot[tid] : 0;
+    int dpre = block_excl_scan<RS_THREADS>(dv, wsum, nullptr);
+    if (tid < radix) base_d[tid] = dpre + hist[tid * nblk_cap + blockIdx.x];
+    for (int d = tid; d < 256; d += RS_THREADS)
+        for (int w = 0; w < NWARP; w++) wcnt[w][d] = 0;
+    __syncthreads();
+    unsigned mask = (unsigned)radix - 1u;
+    unsigned lt_mask = (1u << lane) - 1u;
+    for (int r = 0; r < RS_ROUNDS; r++) {
+        long long i = base + r * RS_THREADS + tid;
+        bool valid = i < n;
+        unsigned key = valid ? kin[i] : 0u;
+        int val = valid ? vin[i] : 0;
+        int d = valid ? (int)((key >> shift) & mask) : 256 + lane;  // invalid lanes: unique dummy digits
+        unsigned peers = __match_any_sync(0xffffffffu, d);
+        int wrank = __popc(peers & lt_mask);
+        bool leader = (peers & lt_mask) == 0u;
+        if (valid && leader) wcnt[warp][d] = __popc(peers);
+        __syncthreads();
+        if (tid < radix) {
+            int run = base_d[tid];
+#pragma unroll
+            for (int w = 0; w < NWARP; w++) {
+                int c = wcnt[w][tid];
+                wcnt[w][tid] = run;
+                run += c;
+            }
+            base_d[tid] = run;
+        }
+        __syncthreads();
+        if (valid) {
+            int pos = wcnt[warp][d] + wrank;
+            kout[pos] = key;
+            vout[pos] = val;
+        }
+        __syncthreads();
+        if (valid && leader) wcnt[warp][d] = 0;
+        // entries of digits this warp did not touch are already 0 except the prefix written above:
+        // reset every written prefix (all radix entries were overwritten by the scan step)
+        if (tid < radix) {
+#pragma unroll
+            for (int w = 0; w < NWARP; w++) wcnt[w][tid] = 0;
+        }
+        __syncthreads();
+    }
+}
+
+// [begin, end) of every tile present in the sorted key list (ranges zeroed beforehand)
+__global__ void __launch_bounds__(256) k_ranges(const unsigned *__restrict__ keys, const long long *__restrict__ n_ptr,
+                                                long long cap, int2 *__restrict__ ranges) {
+    long long n = clamp_n(n_ptr, cap);
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    unsigned k = keys[i];
+    if (i == 0 || keys[i - 1] != k) ranges[k].x = (int)i;
+    if (i == n - 1 || keys[i + 1] != k) ranges[k].y = (int)(i + 1);
+}
+
+// ----------------------------------------------------------------------------------------------------
+// forward: per-tile field sums (render_triton.py:423-517 with FIELDS=True)
+
+__device__ __forceinline__ int group_of_tile(const RenderGeom &G, int lt) {
+    int g = 0;
+#pragma unroll
+    for (int k = 0; k < GS_MAX_GROUPS; k++)
+        if (k < G.ngroups && lt >= G.g[k].tile_off && lt < G.g[k].tile_off + G.g[k].ntx * G.g[k].nty) g = k;
+    return g;
+}
+
+__device__ __forceinline__ void renorm(float &P, int &E) {
+    int bits = __float_as_int(P);
+    E += ((bits >> 23) & 0xff) - 126;
+    P = __int_as_float((bits & 0x807fffff) | 0x3f000000);
+}
+
+template <int TILE, int NW>
+__global__ void __launch_bounds__(NW * 32) k_fields_fwd(RenderGeom G, const SplatRec *__restrict__ rec,
+                                                        const int2 *__restrict__ ranges,
+                                                        const int *__restrict__ vals, float *__restrict__ fields) {
+    constexpr int NPIX = TILE * TILE;
+    constexpr int PPL = NPIX >= 32 ? NPIX / 32 : 1;
+    __shared__ SplatRec srec[NW][32];
+    __shared__ float red[NW][5][NPIX];
+    const int gt = blockIdx.x;
+    const int b = gt / G.tiles_per_image;
+    const int lt = gt - b * G.tiles_per_image;
+    const int g = group_of_tile(G, lt);
+    const int Hg = G.g[g].H, Wg = G.g[g].W, ntx = G.g[g].ntx;
+    const int t = lt - G.g[g].tile_off;
+    const int tx = t % ntx, ty = t / ntx;
+    int p0, p1;
+    const bool dense = G.mode == GS_MODE_EXACT;
+    if (dense) {
+        p0 = 0;
+        p1 = G.N;
+    } else {
+        int2 rg = ranges[gt];
+        p0 = rg.x;
+        p1 = rg.y;
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float py[PPL], px[PPL];
+#pragma unroll
+    for (int j = 0; j < PPL; j++) {
+        int q = lane + 32 * j;
+        int ly = q / TILE, lx = q % TILE;
+        py[j] = __fdiv_rn((float)(ty * TILE + ly) + 0.5f, (float)Hg);
+        px[j] = __fdiv_rn((float)(tx * TILE + lx) + 0.5f, (float)Wg);
+    }
+    float P[PPL], Sw[PPL], S0[PPL], S1[PPL], S2[PPL];
+    int E[PPL];
+#pragma unroll
+    for (int j = 0; j < PPL; j++) {
+        P[j] = 1.0f; E[j] = 0; Sw[j] = 0.f; S0[j] = 0.f; S1[j] = 0.f; S2[j] = 0.f;
+    }
+    const int n = p1 - p0;
+    const bool odds = G.odds != 0;
+    for (int base = warp * 32; base < n; base += NW * 32) {
+        int k = base + lane;
+        if (k < n) {
+            int sid = dense ? b * G.N + k : vals[p0 + k];
+            srec[warp][lane] = rec[sid];
+        }
+        __syncwarp();
+        const int nb = min(32, n - base);
+        for (int i = 0; i < nb; ++i) {
+            const float4 A = srec[warp][i].a, Bv = srec[warp][i].b, Cv = srec[warp][i].c;
+            const bool series = odds && Cv.w != 0.0f;
+#pragma unroll
+            for (int j = 0; j < PPL; j++) {
+                float dy = py[j] - A.x, dx = px[j] - A.y;
+                float u = fmaf(A.z, dy, A.w * dx);
+                float v = fmaf(Bv.x, dy, Bv.y * dx);
+                float arg = fmaf(-u, u, fmaf(-v, v, Bv.w));
+                float a = fminf(gs_ex2(arg), GS_ALPHA_MAX);
+                float om = 1.0f - a;
+                P[j] *= om;
+                float w;
+                if (!odds) w = a;
+                else if (series) w = a * fmaf(a, fmaf(a, fmaf(a, 1.0f, 1.0f), 1.0f), 1.0f);
+                else w = a * gs_rcp(om);
+                Sw[j] += w;
+                S0[j] = fmaf(w, Cv.x, S0[j]);
+                S1[j] = fmaf(w, Cv.y, S1[j]);
+                S2[j] = fmaf(w, Cv.z, S2[j]);
+            }
+            if ((i & 7) == 7) {
+#pragma unroll
+                for (int j = 0; j < PPL; j++) renorm(P[j], E[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < PPL; j++) renorm(P[j], E[j]);
+        __syncwarp();
+    }
+#pragma unroll
+    for (int j = 0; j < PPL; j++) {
+        int q = lane + 32 * j;
+        if (q < NPIX) {
+            red[warp][0][q] = logf(P[j]) + (float)E[j] * GS_LN2;
+            red[warp][1][q] = Sw[j];
+            red[warp][2][q] = S0[j];
+            red[warp][3][q] = S1[j];
+            red[warp][4][q] = S2[j];
+        }
+    }
+    __syncthreads();
+    float *fb = fields + (long long)b * G.fld_per_image + G.g[g].fld_off;
+    const long long plane = (long long)Hg * Wg;
+    for (int q = threadIdx.x; q < 5 * NPIX; q += NW * 32) {
+        int c = q / NPIX, pq = q - c * NPIX;
+        int yp = ty * TILE + pq / TILE, xp = tx * TILE + pq % TILE;
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; w++) s += red[w][c][pq];
+        if (yp < Hg && xp < Wg) fb[c * plane + (long long)yp * Wg + xp] = s;
+    }
+}
+
+// ----------------------------------------------------------------------------------------------------
+// bilinear upsample with torch's align_corners=False source-index rule
+
+__device__ __forceinline__ void lin_index(int d, int in_size, int out_size, int &i0, int &i1, float &l0, float &l1) {
+    float scale = __fdiv_rn((float)in_size, (float)out_size);
+    float src = __fsub_rn(__fmul_rn(scale, __fadd_rn((float)d, 0.5f)), 0.5f);
+    if (src < 0.0f) src = 0.0f;
+    int i = (int)src;
+    if (i > in_size - 1) i = in_size - 1;
+    int ip = (i < in_size - 1) ? 1 : 0;
+    float lam = fminf(fmaxf(src - (float)i, 0.0f), 1.0f);
+    i0 = i;
+    i1 = i + ip;
+    l1 = lam;
+    l0 = 1.0f - lam;
+}
+
+__device__ __forceinline__ bool group_native(const RenderGeom &G, int g) { return G.g[g].H == G.H && G.g[g].W == G.W; }
+
+// one native pixel per thread: sum the present groups' fields, composite, keep the sums for backward
+__global__ void __launch_bounds__(256) k_composite(RenderGeom G, const float *__restrict__ fields,
+                                                   const int *__restrict__ gsplats, const float *__restrict__ bg,
+                                                   float *__restrict__ out, float *__restrict__ F) {
+    const int b = blockIdx.y;
+    const long long P = (long long)G.H * G.W;
+    long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= P) return;
+    int y = (int)(p / G.W), x = (int)(p - (long long)y * G.W);
+    float S[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+    const float *fimg = fields + (long long)b * G.fld_per_image;
+#pragma unroll
+    for (int k = 0; k < GS_MAX_GROUPS; k++) {
+        if (k >= G.ngroups) break;
+        int g = G.order[k];
+        if (gsplats[b * G.ngroups + g] == 0) continue;
+        const float *f = fimg + G.g[g].fld_off;
+        int Hg = G.g[g].H, Wg = G.g[g].W;
+        long long plane = (long long)Hg * Wg;
+        if (Hg == G.H && Wg == G.W) {
+#pragma unroll
+            for (int c = 0; c < 5; c++) S[c] += f[c * plane + p];
+        } else {
+            int y0, y1, x0, x1;
+            float h0, h1, w0, w1;
+            lin_index(y, Hg, G.H, y0, y1, h0, h1);
+            lin_index(x, Wg, G.W, x0, x1, w0, w1);
+#pragma unroll
+            for (int c = 0; c < 5; c++) {
+                const float *fc = f + c * plane;
+                float v = h0 * (w0 * fc[(long long)y0 * Wg + x0] + w1 * fc[(long long)y0 * Wg + x1]) +
+                          h1 * (w0 * fc[(long long)y1 * Wg + x0] + w1 * fc[(long long)y1 * Wg + x1]);
+                S[c] += v;
+            }
+        }
+    }
+    float asum = fmaxf(S[1], 1e-8f);
+    float T = expf(S[0]);
+    float *ob = out + (long long)b * G.C * P;
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+        if (c < G.C) {
+            float fg = S[2 + c] / asum;
+            ob[c * P + p] = (1.0f - T) * fg + T * bg[b * G.C + c];
+        }
+    }
+    if (F) {
+        float *Fb = F + (long long)b * 5 * P;
+#pragma unroll
+        for (int c = 0; c < 5; c++) Fb[c * P + p] = S[c];
+    }
+}
+
+// ----------------------------------------------------------------------------------------------------
+// backward
+
+// dS at native resolution from dL/dimage (torch autograd of render_triton.py:976-979; the cull and
+// exact paths skip the clamp_min mask, render_triton.py:644-654); bg gradient sum_p g * T.
+__global__ void __launch_bounds__(256) k_composite_bwd(RenderGeom G, const float *__restrict__ F,
+                                                       const float *__restrict__ bg,
+                                                       const float *__restrict__ gout, float *__restrict__ Gn,
+                                                       float *__restrict__ gbg, int clamp_mask) {
+    __shared__ float red[3][8];
+    const int b = blockIdx.y;
+    const long long P = (long long)G.H * G.W;
+    long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    float gT[3] = {0.f, 0.f, 0.f};
+    if (p < P) {
+        const float *Fb = F + (long long)b * 5 * P;
+        float Sl = Fb[p], Sw = Fb[P + p];
+        float asum = fmaxf(Sw, 1e-8f);
+        float T = expf(Sl);
+        float dT = 0.f, dasum = 0.f, dsc[3] = {0.f, 0.f, 0.f};
+        const float *gb = gout + (long long)b * G.C * P;
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+            if (c < G.C) {
+                float gc = gb[c * P + p];
+                float fg = Fb[(2 + c) * P + p] / asum;
+                dT += gc * (bg[b * G.C + c] - fg);
+                float dfg = gc * (1.0f - T);
+                dsc[c] = dfg / asum;
+                dasum += dfg * fg;
+                gT[c] = gc * T;
+            }
+        }
+        float dsw = -dasum / asum;
+        if (clamp_mask && !(Sw >= 1e-8f)) dsw = 0.0f;
+        float *Gb = Gn + (long long)b * 5 * P;
+        Gb[p] = dT * T;
+        Gb[P + p] = dsw;
+        Gb[2 * P + p] = dsc[0];
+        Gb[3 * P + p] = dsc[1];
+        Gb[4 * P + p] = dsc[2];
+    }
+    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+        float v = gT[c];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[c][warp] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < 3 && threadIdx.x < G.C) {
+        float v = 0.f;
+        for (int w = 0; w < 8; w++) v += red[threadIdx.x][w];
+        atomicAdd(&gbg[b * 4 + threadIdx.x], v);
+    }
+}
+
+// adjoint of the bilinear upsample for every present coarse group: each texel gathers, in a fixed
+// order, the native-resolution dS values whose bilinear taps touched it (deterministic).
+__global__ void __launch_bounds__(256) k_adjoint(RenderGeom G, const int *__restrict__ gsplats,
+                                                 const float *__restrict__ Gn, float *__restrict__ gfields) {
+    const int b = blockIdx.y;
+    long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    // locate the group: texel index space = concatenation of all groups' planes
+    int g = -1;
+    long long acc = 0;
+#pragma unroll
+    for (int k = 0; k < GS_MAX_GROUPS; k++) {
+        if (k < G.ngroups && g < 0) {
+            long long np = (long long)G.g[k].H * G.g[k].W;
+            if (q < acc + np) g = k; else acc += np;
+        }
+    }
+    if (g < 0) return;
+    if (group_native(G, g) || gsplats[b * G.ngroups + g] == 0) return;
+    q -= acc;
+    const int Hg = G.g[g].H, Wg = G.g[g].W;
+    const int i = (int)(q / Wg), j = (int)(q - (long long)i * Wg);
+    const long long P = (long long)G.H * G.W;
+    const float sy = (float)G.H / (float)Hg, sx = (float)G.W / (float)Wg;
+    int ylo = max(0, (int)floorf((i - 0.5f) * sy - 0.5f) - 2), yhi = min(G.H - 1, (int)ceilf((i + 1.5f) * sy - 0.5f) + 2);
+    int xlo = max(0, (int)floorf((j - 0.5f) * sx - 0.5f) - 2), xhi = min(G.W - 1, (int)ceilf((j + 1.5f) * sx - 0.5f) + 2);
+    float acc5[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+    const float *Gb = Gn + (long long)b * 5 * P;
+    for (int y = ylo; y <= yhi; y++) {
+        int y0, y1;
+        float h0, h1;
+        lin_index(y, Hg, G.H, y0, y1, h0, h1);
+        float wy = (y0 == i ? h0 : 0.f) + (y1 == i ? h1 : 0.f);
+        if (wy == 0.f && y0 != i && y1 != i) continue;
+        for (int x = xlo; x <= xhi; x++) {
+            int x0, x1;
+            float w0, w1;
+            lin_index(x, Wg, G.W, x0, x1, w0, w1);
+            if (x0 != j && x1 != j) continue;
+            float wx = (x0 == j ? w0 : 0.f) + (x1 == j ? w1 : 0.f);
+            float w = wy * wx;
+            long long p = (long long)y * G.W + x;
+#pragma unroll
+            for (int c = 0; c < 5; c++) acc5[c] += w * Gb[c * P + p];
+        }
+    }
+    float *gf = gfields + (long long)b * G.fld_per_image + G.g[g].fld_off;
+    long long plane = (long long)Hg * Wg;
+#pragma unroll
+    for (int c = 0; c < 5; c++) gf[c * plane + q] = acc5[c];
+}
+
+// one CTA per tile; lane = one (tile, splat) pair looping over the tile's pixels
+// (render_triton.py:602-720 with FIELDS=True; the index_add_ of render_triton.py:757-761/803-807
+// becomes three 16-byte vector atomics per pair into the per-splat sums).
+template <int TILE, int NW>
+__global__ void __launch_bounds__(NW * 32) k_fields_bwd(RenderGeom G, const SplatRec *__restrict__ rec,
+                                                        const int2 *__restrict__ ranges,
+                                                        const int *__restrict__ vals, const float *__restrict__ Gn,
+                                                        const float *__restrict__ gfields,
+                                                        float *__restrict__ acc) {
+    constexpr int NPIX = TILE * TILE;
+    __shared__ float4 dsa[NPIX];
+    __shared__ float dsb[NPIX];
+    __shared__ float spy[TILE], spx[TILE];
+    const int gt = blockIdx.x;
+    const int b = gt / G.tiles_per_image;
+    const int lt = gt - b * G.tiles_per_image;
+    const int g = group_of_tile(G, lt);
+    const int Hg = G.g[g].H, Wg = G.g[g].W, ntx = G.g[g].ntx;
+    const int t = lt - G.g[g].tile_off;
+    const int tx = t % ntx, ty = t / ntx;
+    int p0, p1;
+    const bool dense = G.mode == GS_MODE_EXACT;
+    if (dense) {
+        p0 = 0;
+        p1 = G.N;
+    } else {
+        int2 rg = ranges[gt];
+        p0 = rg.x;
+        p1 = rg.y;
+    }
+    if (p1 <= p0) return;
+    const float *src;
+    long long plane = (long long)Hg * Wg;
+    if (group_native(G, g)) src = Gn + (long long)b * 5 * plane;
+    else src = gfields + (long long)b * G.fld_per_image + G.g[g].fld_off;
+    for (int q = threadIdx.x; q < NPIX; q += NW * 32) {
+        int yp = ty * TILE + q / TILE, xp = tx * TILE + q % TILE;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        float v4 = 0.f;
+        if (yp < Hg && xp < Wg) {
+            long long p = (long long)yp * Wg + xp;
+            v = make_float4(src[p], src[plane + p], src[2 * plane + p], src[3 * plane + p]);
+            v4 = src[4 * plane + p];
+        }
+        dsa[q] = v;
+        dsb[q] = v4;
+    }
+    if (threadIdx.x < TILE) {
+        spy[threadIdx.x] = __fdiv_rn((float)(ty * TILE + threadIdx.x) + 0.5f, (float)Hg);
+        spx[threadIdx.x] = __fdiv_rn((float)(tx * TILE + threadIdx.x) + 0.5f, (float)Wg);
+    }
+    __syncthreads();
+    const bool odds = G.odds != 0;
+    const int n = p1 - p0;
+    for (int k = threadIdx.x; k < ((n + 31) & ~31); k += NW * 32) {
+        if (k >= n) continue;  // whole-warp granularity: tail lanes idle
+        const int sid = dense ? b * G.N + k : vals[p0 + k];
+        const SplatRec r = rec[sid];
+        const float muy = r.a.x, mux = r.a.y, A = r.a.z, Bc = r.a.w;
+        const float Cc = r.b.x, D = r.b.y, op = r.b.z;
+        const float c0 = r.c.x, c1 = r.c.y, c2 = r.c.z;
+        float ux[TILE], vx[TILE];
+#pragma unroll
+        for (int lx = 0; lx < TILE; lx++) {
+            float dx = spx[lx] - mux;
+            ux[lx] = Bc * dx;
+            vx[lx] = D * dx;
+        }
+        float Su = 0.f, Sv = 0.f, Suu = 0.f, Svv = 0.f, Suv = 0.f, Sf = 0.f, Sc0 = 0.f, Sc1 = 0.f, Sc2 = 0.f;
+#pragma unroll
+        for (int ly = 0; ly < TILE; ly++) {
+            const float dy = spy[ly] - muy;
+            const float uy = A * dy, vy = Cc * dy;
+#pragma unroll
+            for (int lx = 0; lx < TILE; lx++) {
+                const int q = ly * TILE + lx;
+                const float4 d4 = dsa[q];
+                const float dS2 = dsb[q];
+                const float u = uy + ux[lx];
+                const float v = vy + vx[lx];
+                const float f = gs_ex2(-fmaf(u, u, v * v));
+                const float fo = op * f;
+                const float a = fminf(fo, GS_ALPHA_MAX);
+                const float om = 1.0f - a;
+                const float rr = gs_rcp(om);
+                const float col_term = fmaf(d4.z, c0, fmaf(d4.w, c1, dS2 * c2));
+                float da, cw;
+                if (odds) {
+                    da = fmaf(d4.y + col_term, rr, -d4.x) * rr;
+                    cw = a * rr;
+                } else {
+                    da = fmaf(-d4.x, rr, d4.y + col_term);
+                    cw = a;
+                }
+                Sc0 = fmaf(cw, d4.z, Sc0);
+                Sc1 = fmaf(cw, d4.w, Sc1);
+                Sc2 = fmaf(cw, dS2, Sc2);
+                const float dafo = fo < GS_ALPHA_MAX ? da : 0.0f;
+                Sf = fmaf(dafo, f, Sf);
+                const float Gm = dafo * fo;
+                const float Gu = Gm * u, Gv = Gm * v;
+                Su += Gu;
+                Sv += Gv;
+                Suu = fmaf(Gu, u, Suu);
+                Svv = fmaf(Gv, v, Svv);
+                Suv = fmaf(Gu, v, Suv);
+            }
+        }
+        float *ap = acc + (long long)sid * 12;
+        gs_red_add_v4(ap, Su, Sv, Suu, Svv);
+        gs_red_add_v4(ap + 4, Suv, Sf, Sc0, Sc1);
+        gs_red_add_v4(ap + 8, Sc2, 0.f, 0.f, 0.f);
+    }
+}
+
+// per-splat chain rule from the 9 sums (u = K*rotated_y/sigma_y, v = K*rotated_x/sigma_x,
+// Gm = dL/da * a on unclamped pairs) to the reference's leaf gradients.
+__global__ void __launch_bounds__(256) k_finalize(RenderGeom G, const float *__restrict__ ls,
+                                                  const float *__restrict__ th, const float *__restrict__ acc,
+                                                  const float *__restrict__ gbg_ws, float *__restrict__ g_mu,
+                                                  float *__restrict__ g_ls, float *__restrict__ g_col,
+                                                  float *__restrict__ g_op, float *__restrict__ g_bg,
+                                                  float *__restrict__ g_th) {
+    long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (s < (long long)G.B * G.C && g_bg) {
+        int b = (int)(s / G.C), c = (int)(s - (long long)b * G.C);
+        g_bg[s] = gbg_ws[b * 4 + c];
+    }
+    if (s >= (long long)G.B * G.N) return;
+    const float4 a0 = reinterpret_cast<const float4 *>(acc)[s * 3 + 0];
+    const float4 a1 = reinterpret_cast<const float4 *>(acc)[s * 3 + 1];
+    const float4 a2 = reinterpret_cast<const float4 *>(acc)[s * 3 + 2];
+    const float Su = a0.x, Sv = a0.y, Suu = a0.z, Svv = a0.w, Suv = a1.x, Sf = a1.y;
+    float2 l = reinterpret_cast<const float2 *>(ls)[s];
+    float sy = gs_softplus_eps(l.x), sx = gs_softplus_eps(l.y);
+    float cth = 1.0f, sth = 0.0f;
+    if (G.has_theta) sincosf(th[s], &sth, &cth);
+    const float invK = 1.0f / GS_K, invK2 = invK * invK;
+    float gsy = Suu * invK2 / sy;
+    float gsx = Svv * invK2 / sx;
+    float gmuy = (cth / sy * Su - sth / sx * Sv) * invK;
+    float gmux = (sth / sy * Su + cth / sx * Sv) * invK;
+    reinterpret_cast<float2 *>(g_mu)[s] = make_float2(gmuy, gmux);
+    reinterpret_cast<float2 *>(g_ls)[s] = make_float2(gsy * gs_softplus_grad(l.x), gsx * gs_softplus_grad(l.y));
+    g_op[s] = Sf;
+    if (G.C > 0) g_col[s * G.C + 0] = a1.z;
+    if (G.C > 1) g_col[s * G.C + 1] = a1.w;
+    if (G.C > 2) g_col[s * G.C + 2] = a2.x;
+    if (G.has_theta && g_th) g_th[s] = -(sx / sy - sy / sx) * Suv * invK2;
+}
+
+__global__ void k_activate_scale(const float *__restrict__ ls, float *__restrict__ out, long long n) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = gs_softplus_eps(ls[i]);
+}
+
+// ----------------------------------------------------------------------------------------------------
+// host side: geometry, bounds, workspace plan
+
+namespace {
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct Plan {
+    RenderGeom G;
+    int ngroups;
+    long long cap;
+    int nblk_pre, nblk_sort, passes, radix_bits;
+    size_t o_rec, o_meta, o_counts, o_bsum, o_zero, o_gpairs, o_gsplats, o_misc, o_ranges, z_len;
+    size_t o_keys_a, o_vals_a, o_keys_b, o_vals_b, o_hist, o_dtot, o_fields, o_F, fwd_bytes;
+    size_t o_G, o_gfields, o_bzero, o_acc, o_gbg, bz_len, total_bytes;
+};
+
+int validate(const gs_render_desc *d) {
+    if (!d) return GS_ERR_BAD_ARGUMENT;
+    if (d->mode < 0 || d->mode > 3) return GS_ERR_BAD_ARGUMENT;
+    if (d->B < 1 || d->N < 0 || d->C < 1 || d->C > 3 || d->H < 1 || d->W < 1) return GS_ERR_BAD_ARGUMENT;
+    if (!(d->tile == 4 || d->tile == 8 || d->tile == 16)) return GS_ERR_BAD_ARGUMENT;
+    if (d->mode == GS_MODE_OCTAVE && (d->max_octaves < 0 || d->max_octaves > GS_MAX_GROUPS - 1))
+        return GS_ERR_BAD_ARGUMENT;
+    if (d->mode == GS_MODE_EXACT && d->odds) return GS_ERR_BAD_ARGUMENT;
+    if (!(d->cutoff > 0.0f)) return GS_ERR_BAD_ARGUMENT;
+    if ((long long)d->B * d->N >= (1LL << 31)) return GS_ERR_BAD_ARGUMENT;
+    return GS_OK;
+}
+
+void make_geom(const gs_render_desc *d, RenderGeom &G) {
+    memset(&G, 0, sizeof(G));
+    G.mode = d->mode; G.B = d->B; G.N = d->N; G.C = d->C; G.H = d->H; G.W = d->W; G.tile = d->tile;
+    G.odds = d->odds; G.has_theta = d->has_theta; G.max_oct = d->max_octaves;
+    G.n_coarse = d->n_coarse; G.cutoff = d->cutoff; G.base_texels = d->base_texels;
+    G.rep = (float)std::min(d->H, d->W);
+    int T = d->tile;
+    int res[GS_MAX_GROUPS][2];
+    int ng;
+    if (d->mode == GS_MODE_OCTAVE) {
+        ng = d->max_octaves + 1;
+        for (int o = 0; o < ng; o++) {
+            res[o][0] = std::max(8, d->H >> o);
+            res[o][1] = std::max(8, d->W >> o);
+        }
+        for (int k = 0; k < ng; k++) G.order[k] = k;  // octave 0 first (render_triton.py:959-972)
+    } else if (d->mode == GS_MODE_MULTIRES) {
+        ng = 2;
+        int m = std::min(d->H, d->W) / 8;
+        int cf = std::min(d->coarse_factor, std::max(1, m));
+        res[0][0] = std::max(1, d->H / cf);
+        res[0][1] = std::max(1, d->W / cf);
+        res[1][0] = d->H;
+        res[1][1] = d->W;
+        G.order[0] = 1;  // fine + upsampled coarse (render_triton.py:914-916)
+        G.order[1] = 0;
+    } else {
+        ng = 1;
+        res[0][0] = d->H;
+        res[0][1] = d->W;
+        G.order[0] = 0;
+    }
+    G.ngroups = ng;
+    // tile numbering: coarsest group first so the deep (long) tiles are scheduled early
+    int toff = 0;
+    long long foff = 0;
+    for (int k = ng - 1; k >= 0; k--) {
+        GroupGeom &gg = G.g[k];
+        gg.H = res[k][0];
+        gg.W = res[k][1];
+        gg.ntx = (gg.W + T - 1) / T;
+        gg.nty = (gg.H + T - 1) / T;
+        gg.tile_off = toff;
+        toff += gg.ntx * gg.nty;
+    }
+    for (int k = 0; k < ng; k++) {
+        G.g[k].fld_off = (int)foff;
+        foff += 5LL * G.g[k].H * G.g[k].W;
+    }
+    G.tiles_per_image = toff;
+    G.fld_per_image = foff;
+}
+
+// per-splat upper bound on the tiles of group g (see gs_render_pair_bound)
+long long group_tile_bound(const gs_render_desc *d, const RenderGeom &G, int g) {
+    const GroupGeom &gg = G.g[g];
+    long long nt = (long long)gg.ntx * gg.nty;
+    if (d->mode != GS_MODE_OCTAVE || g == d->max_octaves) return nt;
+    // octave o < max: ceil(log2(sigma_px / base_texels)) <= o  =>  sigma <= base_texels * 2^o / min(H, W)
+    double smax = (double)d->base_texels * (double)(1LL << g) / (double)std::min(d->H, d->W);
+    smax *= 1.0 + 1e-5;
+    double r = (double)d->cutoff * smax;
+    double rx = r * gg.W, ry = r * gg.H;
+    long long sx = std::min<long long>(gg.ntx, (long long)(2.0 * rx / d->tile) + 2);
+    long long sy = std::min<long long>(gg.nty, (long long)(2.0 * ry / d->tile) + 2);
+    return std::min(nt, sx * sy);
+}
+
+long long pair_bound(const gs_render_desc *d, const RenderGeom &G) {
+    if (d->mode == GS_MODE_EXACT) return 0;
+    long long worst = 0;
+    for (int g = 0; g < G.ngroups; g++) worst = std::max(worst, group_tile_bound(d, G, g));
+    if (d->mode == GS_MODE_MULTIRES && d->n_coarse > 0 && d->n_coarse < d->N) {
+        long long b0 = group_tile_bound(d, G, 0) * d->n_coarse + group_tile_bound(d, G, 1) * (d->N - d->n_coarse);
+        return b0 * d->B;
+    }
+    return worst * (long long)d->N * d->B;
+}
+
+void make_plan(const gs_render_desc *d, Plan &pl) {
+    memset(&pl, 0, sizeof(pl));
+    make_geom(d, pl.G);
+    pl.ngroups = pl.G.ngroups;
+    long long cap = d->pair_capacity > 0 ? d->pair_capacity : pair_bound(d, pl.G);
+    if (d->mode == GS_MODE_EXACT) cap = 0;
+    pl.cap = cap;
+    pl.G.cap = cap;
+    long long BN = (long long)d->B * d->N;
+    pl.nblk_pre = (int)std::max<long long>(1, (BN + 255) / 256);
+    pl.nblk_sort = (int)std::max<long long>(1, (cap + RS_ITEMS - 1) / RS_ITEMS);
+    long long ntiles = (long long)d->B * pl.G.tiles_per_image;
+    int bits = 0;
+    while ((1LL << bits) < ntiles) bits++;
+    pl.passes = (bits + 7) / 8;
+    pl.radix_bits = pl.passes ? (bits + pl.passes - 1) / pl.passes : 0;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { size_t r = o; o = align256(o + bytes); return r; };
+    pl.o_rec = take(sizeof(SplatRec) * (size_t)std::max<long long>(BN, 1));
+    pl.o_meta = take(sizeof(int4) * (size_t)std::max<long long>(BN, 1));
+    pl.o_counts = take(sizeof(int) * (size_t)std::max<long long>(BN, 1));
+    pl.o_bsum = take(sizeof(int) * (size_t)pl.nblk_pre);
+    // zeroed block: group stats, misc (total pairs as int64 + status), tile ranges
+    pl.o_zero = o;
+    pl.o_gpairs = take(sizeof(unsigned long long) * (size_t)d->B * pl.ngroups);
+    pl.o_gsplats = take(sizeof(int) * (size_t)d->B * pl.ngroups);
+    pl.o_misc = take(64);
+    pl.o_ranges = take(sizeof(int2) * (size_t)ntiles);
+    pl.z_len = o - pl.o_zero;
+    pl.o_keys_a = take(sizeof(unsigned) * (size_t)std::max<long long>(cap, 1));
+    pl.o_vals_a = take(sizeof(int) * (size_t)std::max<long long>(cap, 1));
+    pl.o_keys_b = take(sizeof(unsigned) * (size_t)std::max<long long>(cap, 1));
+    pl.o_vals_b = take(sizeof(int) * (size_t)std::max<long long>(cap, 1));
+    pl.o_hist = take(sizeof(int) * 256 * (size_t)pl.nblk_sort);
+    pl.o_dtot = take(sizeof(int) * 256);
+    pl.o_fields = take(sizeof(float) * (size_t)d->B * pl.G.fld_per_image);
+    pl.o_F = take(sizeof(float) * 5 * (size_t)d->B * d->H * d->W);
+    pl.fwd_bytes = o;
+    pl.o_G = take(sizeof(float) * 5 * (size_t)d->B * d->H * d->W);
+    pl.o_gfields = take(sizeof(float) * (size_t)d->B * pl.G.fld_per_image);
+    pl.o_bzero = o;
+    pl.o_acc = take(sizeof(float) * 12 * (size_t)std::max<long long>(BN, 1));
+    pl.o_gbg = take(sizeof(float) * 4 * (size_t)d->B);
+    pl.bz_len = o - pl.o_bzero;
+    pl.total_bytes = o;
+}
+
+template <typename T>
+T *at(void *ws, size_t off) { return reinterpret_cast<T *>(reinterpret_cast<char *>(ws) + off); }
+
+int launch_fields_fwd(const Plan &pl, void *ws, cudaStream_t st) {
+    const RenderGeom &G = pl.G;
+    dim3 grid((unsigned)((long long)G.B * G.tiles_per_image));
+    auto rec = at<SplatRec>(ws, pl.o_rec);
+    auto rng = at<int2>(ws, pl.o_ranges);
+    const int *vals = at<int>(ws, (pl.passes % 2) ? pl.o_vals_b : pl.o_vals_a);
+    auto fld = at<float>(ws, pl.o_fields);
+    if (G.tile == 8) k_fields_fwd<8, 4><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
+    else if (G.tile == 16) k_fields_fwd<16, 4><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
+    else k_fields_fwd<4, 4><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
+    GS_CHECK_LAUNCH("k_fields_fwd");
+    return GS_OK;
+}
+
+int run_preprocess(const Plan &pl, const float *mu, const float *ls, const float *col, const float *op,
+                   const float *th, void *ws, cudaStream_t st) {
+    const RenderGeom &G = pl.G;
+    cudaError_t e = cudaMemsetAsync(at<char>(ws, pl.o_zero), 0, pl.z_len, st);
+    GS_COUNT(1);
+    if (e != cudaSuccess) return set_cuda_error(e, "memset");
+    k_preprocess<<<pl.nblk_pre, 256, 0, st>>>(G, mu, ls, col, op, G.has_theta ? th : nullptr, at<SplatRec>(ws, pl.o_rec),
+                                              at<int4>(ws, pl.o_meta), at<int>(ws, pl.o_counts),
+                                              at<int>(ws, pl.o_bsum), at<unsigned long long>(ws, pl.o_gpairs),
+                                              at<int>(ws, pl.o_gsplats));
+    GS_CHECK_LAUNCH("k_preprocess");
+    return GS_OK;
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------------------------------------------
+// C ABI
+
+extern "C" {
+
+int64_t gs_render_pair_bound(const gs_render_desc *d) {
+    if (validate(d) != GS_OK) return -1;
+    RenderGeom G;
+    make_geom(d, G);
+    return pair_bound(d, G);
+}
+
+size_t gs_render_workspace_size(const gs_render_desc *d, int with_backward) {
+    if (validate(d) != GS_OK) return 0;
+    Plan pl;
+    make_plan(d, pl);
+    return with_backward ? pl.total_bytes : pl.fwd_bytes;
+}
+
+int gs_render_count(const gs_render_desc *d, const float *mu, const float *log_scale, void *workspace,
+                    size_t workspace_bytes, int64_t *counts_host, int32_t *groups_out, void *stream) {
+    int st = validate(d);
+    if (st != GS_OK) return st;
+    if (!mu || !log_scale || !counts_host) return GS_ERR_BAD_ARGUMENT;
+    gs_render_desc dd = *d;
+    dd.pair_capacity = 1;
+    Plan pl;
+    make_plan(&dd, pl);
+    if (workspace_bytes < pl.o_keys_a) return GS_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    // colour/opacity are not needed for counting: point them at the positions (any readable floats)
+    const float *dummy = mu;
+    pl.G.C = 1;
+    pl.G.has_theta = 0;
+    st = run_preprocess(pl, mu, log_scale, dummy, dummy, nullptr, workspace, s);
+    if (st != GS_OK) return st;
+    int n = d->B * pl.ngroups;
+    unsigned long long *tmp = new unsigned long long[n];
+    cudaError_t e = cudaMemcpyAsync(tmp, at<unsigned long long>(workspace, pl.o_gpairs), sizeof(unsigned long long) * n,
+                                    cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        delete[] tmp;
+        return set_cuda_error(e, "gs_render_count");
+    }
+    for (int i = 0; i < n; i++) counts_host[i] = (int64_t)tmp[i];
+    delete[] tmp;
+    if (groups_out) *groups_out = pl.ngroups;
+    return GS_OK;
+}
+
+int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_scale, const float *color,
+                  const float *opacity, const float *bg, const float *theta, float *out, void *workspace,
+                  size_t workspace_bytes, void *stream) {
+    int st = validate(d);
+    if (st != GS_OK) return st;
+    if (!bg || !out) return GS_ERR_BAD_ARGUMENT;
+    if (d->N > 0 && (!mu || !log_scale || !color || !opacity || (d->has_theta && !theta))) return GS_ERR_BAD_ARGUMENT;
+    Plan pl;
+    make_plan(d, pl);
+    if (!workspace || workspace_bytes < pl.fwd_bytes) return GS_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    const RenderGeom &G = pl.G;
+    std::unique_ptr<ProfScope> bin_scope(new ProfScope(PR_BIN, s));
+    st = run_preprocess(pl, mu, log_scale, color, opacity, theta, workspace, s);
+    if (st != GS_OK) return st;
+    long long *total = at<long long>(workspace, pl.o_misc);
+    int *status = at<int>(workspace, pl.o_misc + 8);
+    if (d->mode != GS_MODE_EXACT && d->N > 0) {
+        k_scan_blocks<<<1, 1024, 0, s>>>(at<int>(workspace, pl.o_bsum), pl.nblk_pre, total);
+        GS_CHECK_LAUNCH("k_scan_blocks");
+        k_emit<<<pl.nblk_pre, 256, 0, s>>>(G, at<int4>(workspace, pl.o_meta), at<int>(workspace, pl.o_counts),
+                                           at<int>(workspace, pl.o_bsum), at<unsigned>(workspace, pl.o_keys_a),
+                                           at<int>(workspace, pl.o_vals_a), status);
+        GS_CHECK_LAUNCH("k_emit");
+        unsigned *ka = at<unsigned>(workspace, pl.o_keys_a), *kb = at<unsigned>(workspace, pl.o_keys_b);
+        int *va = at<int>(workspace, pl.o_vals_a), *vb = at<int>(workspace, pl.o_vals_b);
+        int radix = 1 << pl.radix_bits;
+        for (int p = 0; p < pl.passes; p++) {
+            int shift = p * pl.radix_bits;
+            k_radix_upsweep<<<pl.nblk_sort, RS_THREADS, 0, s>>>(ka, total, pl.cap, shift, radix,
+                                                                at<int>(workspace, pl.o_hist), pl.nblk_sort);
+            GS_CHECK_LAUNCH("k_radix_upsweep");
+            k_radix_scan<<<radix, 256, 0, s>>>(at<int>(workspace, pl.o_hist), total, pl.cap, pl.nblk_sort,
+                                               at<int>(workspace, pl.o_dtot));
+            GS_CHECK_LAUNCH("k_radix_scan");
+            k_radix_downsweep<<<pl.nblk_sort, RS_THREADS, 0, s>>>(ka, va, kb, vb, total, pl.cap, shift, radix,
+                                                                  at<int>(workspace, pl.o_hist), pl.nblk_sort,
+                                                                  at<int>(workspace, pl.o_dtot));
+            GS_CHECK_LAUNCH("k_radix_downsweep");
+            std::swap(ka, kb);
+            std::swap(va, vb);
+        }
+        unsigned nrb = (unsigned)std::max<long long>(1, (pl.cap + 255) / 256);
+        k_ranges<<<nrb, 256, 0, s>>>(ka, total, pl.cap, at<int2>(workspace, pl.o_ranges));
+        GS_CHECK_LAUNCH("k_ranges");
+    }
+    bin_scope.reset();
+    {
+        ProfScope ps(PR_FIELDS_FWD, s);
+        st = launch_fields_fwd(pl, workspace, s);
+        if (st != GS_OK) return st;
+    }
+    long long P = (long long)d->H * d->W;
+    dim3 cg((unsigned)((P + 255) / 256), (unsigned)d->B);
+    {
+        ProfScope ps(PR_COMPOSITE, s);
+        k_composite<<<cg, 256, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,
+                                       out, at<float>(workspace, pl.o_F));
+        GS_CHECK_LAUNCH("k_composite");
+    }
+    return GS_OK;
+}
+
+int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_scale, const float *color,
+                  const float *opacity, const float *bg, const float *theta, const float *grad_out, float *g_mu,
+                  float *g_log_scale, float *g_color, float *g_opacity, float *g_bg, float *g_theta,
+                  void *workspace, size_t workspace_bytes, void *stream) {
+    int st = validate(d);
+    if (st != GS_OK) return st;
+    if (!grad_out || !g_bg) return GS_ERR_BAD_ARGUMENT;
+    if (d->N > 0 && (!g_mu || !g_log_scale || !g_color || !g_opacity || !log_scale)) return GS_ERR_BAD_ARGUMENT;
+    (void)mu; (void)color; (void)opacity;
+    Plan pl;
+    make_plan(d, pl);
+    if (!workspace || workspace_bytes < pl.total_bytes) return GS_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    const RenderGeom &G = pl.G;
+    cudaError_t e = cudaMemsetAsync(at<char>(workspace, pl.o_bzero), 0, pl.bz_len, s);
+    GS_COUNT(1);
+    if (e != cudaSuccess) return set_cuda_error(e, "memset");
+    long long P = (long long)d->H * d->W;
+    dim3 cg((unsigned)((P + 255) / 256), (unsigned)d->B);
+    int clamp_mask = (d->mode == GS_MODE_OCTAVE || d->mode == GS_MODE_MULTIRES) ? 1 : 0;
+    std::unique_ptr<ProfScope> cb_scope(new ProfScope(PR_COMPOSITE_BWD, s));
+    k_composite_bwd<<<cg, 256, 0, s>>>(G, at<float>(workspace, pl.o_F), bg, grad_out, at<float>(workspace, pl.o_G),
+                                       at<float>(workspace, pl.o_gbg), clamp_mask);
+    GS_CHECK_LAUNCH("k_composite_bwd");
+    bool any_coarse = false;
+    for (int g = 0; g < G.ngroups; g++)
+        if (!(G.g[g].H == G.H && G.g[g].W == G.W)) any_coarse = true;
+    if (any_coarse) {
+        long long tex = 0;
+        for (int g = 0; g < G.ngroups; g++) tex += (long long)G.g[g].H * G.g[g].W;
+        dim3 ag((unsigned)((tex + 255) / 256), (unsigned)d->B);
+        k_adjoint<<<ag, 256, 0, s>>>(G, at<int>(workspace, pl.o_gsplats), at<float>(workspace, pl.o_G),
+                                     at<float>(workspace, pl.o_gfields));
+        GS_CHECK_LAUNCH("k_adjoint");
+    }
+    cb_scope.reset();
+    dim3 grid((unsigned)((long long)G.B * G.tiles_per_image));
+    auto rec = at<SplatRec>(workspace, pl.o_rec);
+    auto rng = at<int2>(workspace, pl.o_ranges);
+    const int *vals = at<int>(workspace, (pl.passes % 2) ? pl.o_vals_b : pl.o_vals_a);
+    auto Gn = at<float>(workspace, pl.o_G);
+    auto gf = at<float>(workspace, pl.o_gfields);
+    auto acc = at<float>(workspace, pl.o_acc);
+    if (d->N > 0) {
+        ProfScope ps(PR_FIELDS_BWD, s);
+        if (G.tile == 8) k_fields_bwd<8, 4><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
+        else if (G.tile == 16) k_fields_bwd<16, 4><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
+        else k_fields_bwd<4, 4><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
+        GS_CHECK_LAUNCH("k_fields_bwd");
+    }
+    long long nfin = std::max<long long>((long long)d->B * d->N, (long long)d->B * d->C);
+    ProfScope ps(PR_FINALIZE, s);
+    k_finalize<<<(unsigned)((nfin + 255) / 256), 256, 0, s>>>(G, log_scale, d->has_theta ? theta : nullptr, acc,
+                                                              at<float>(workspace, pl.o_gbg), g_mu, g_log_scale,
+                                                              g_color, g_opacity, g_bg, g_theta);
+    GS_CHECK_LAUNCH("k_finalize");
+    return GS_OK;
+}
+
+int gs_render_debug_bins(const gs_render_desc *d, const void *workspace, int64_t *total_pairs,
+                         int32_t *tiles_per_image, int32_t *geom_host, int32_t *tile_ranges_host,
+                         int32_t *splat_ids_host, int32_t *octave_host) {
+    int st = validate(d);
+    if (st != GS_OK) return st;
+    Plan pl;
+    make_plan(d, pl);
+    void *ws = const_cast<void *>(workspace);
+    long long tot = 0;
+    cudaError_t e = cudaMemcpy(&tot, at<long long>(ws, pl.o_misc), sizeof(long long), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return set_cuda_error(e, "debug_bins");
+    if (total_pairs) *total_pairs = tot;
+    if (tiles_per_image) *tiles_per_image = pl.G.tiles_per_image;
+    if (geom_host)
+        for (int g = 0; g < pl.ngroups; g++) {
+            geom_host[g * 5 + 0] = pl.G.g[g].H;
+            geom_host[g * 5 + 1] = pl.G.g[g].W;
+            geom_host[g * 5 + 2] = pl.G.g[g].ntx;
+            geom_host[g * 5 + 3] = pl.G.g[g].nty;
+            geom_host[g * 5 + 4] = pl.G.g[g].tile_off;
+        }
+    if (tile_ranges_host) {
+        e = cudaMemcpy(tile_ranges_host, at<int2>(ws, pl.o_ranges), sizeof(int2) * (size_t)d->B * pl.G.tiles_per_image,
+                       cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return set_cuda_error(e, "debug_bins");
+    }
+    if (splat_ids_host && tot > 0) {
+        const int *vals = at<int>(ws, (pl.passes % 2) ? pl.o_vals_b : pl.o_vals_a);
+        e = cudaMemcpy(splat_ids_host, vals, sizeof(int) * (size_t)std::min<long long>(tot, pl.cap),
+                       cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return set_cuda_error(e, "debug_bins");
+    }
+    if (octave_host) {
+        long long BN = (long long)d->B * d->N;
+        int4 *m = new int4[std::max<long long>(BN, 1)];
+        e = cudaMemcpy(m, at<int4>(ws, pl.o_meta), sizeof(int4) * (size_t)BN, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess)
+            for (long long i = 0; i < BN; i++) octave_host[i] = m[i].y >> 24;
+        delete[] m;
+        if (e != cudaSuccess) return set_cuda_error(e, "debug_bins");
+    }
+    int status = 0;
+    e = cudaMemcpy(&status, at<int>(ws, pl.o_misc + 8), sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return set_cuda_error(e, "debug_bins");
+    return status ? GS_ERR_PAIR_BUDGET : GS_OK;
+}
+
+int gs_activate_scale(const float *log_scale, float *out, int64_t n, void *stream) {
+    if (!log_scale || !out || n < 0) return GS_ERR_BAD_ARGUMENT;
+    if (n == 0) return GS_OK;
+    k_activate_scale<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(log_scale, out, n);
+    GS_CHECK_LAUNCH("k_activate_scale");
+    return GS_OK;
+}
+
+const char *gs_last_error(void) { return g_last_error; }
+
+uint64_t gs_kernel_launches(void) { return __atomic_load_n(&g_launches, __ATOMIC_RELAXED); }
+
+void gs_profile_enable(int on) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_prof_on = on != 0;
+}
+
+int gs_profile_collect(double *ms_out, int64_t *count_out) {
+    std::vector<ProfEvent> evs;
+    {
+        std::lock_guard<std::mutex> lk(g_prof_mu);
+        evs.swap(g_prof);
+    }
+    for (int r = 0; r < PR_N; r++) {
+        if (ms_out) ms_out[r] = 0.0;
+        if (count_out) count_out[r] = 0;
+    }
+    int st = GS_OK;
+    for (auto &e : evs) {
+        float ms = 0.f;
+        cudaError_t err = cudaEventSynchronize(e.b);
+        if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e.a, e.b);
+        if (err != cudaSuccess) st = set_cuda_error(err, "gs_profile_collect");
+        if (ms_out) ms_out[e.region] += ms;
+        if (count_out) count_out[e.region] += 1;
+        cudaEventDestroy(e.a);
+        cudaEventDestroy(e.b);
+    }
+    return st;
+}
+
+int gs_build_arch(void) { return 100; }
+
+}  // extern "C"

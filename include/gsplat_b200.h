@@ -1,0 +1,128 @@
+/*
+ * gsplat_b200.h -- C ABI of libgsplat_b200.so, the B200 (sm_100a) kernels behind the
+ * gaussian_2d_splat_encoder_b200 Python package.
+ *
+ * The reference (bigwolfeman/gaussian-2d-splat-encoder) exposes this hot path as Python functions on
+ * torch tensors; these entry points are what its wrappers would bind through ctypes/cffi instead of
+ * launching Triton kernels.  Each declaration names the reference interface it replaces.
+ *
+ * Conventions for every entry point:
+ *   - pointers are DEVICE pointers (fp32 unless stated), tightly packed in the reference's layouts:
+ *       mu [B][N][2] as (y,x) in normalised [0,1] image units; log_scale [B][N][2] pre-softplus;
+ *       color [B][N][C]; opacity [B][N] in (0,1); theta [B][N] (may be NULL); bg [B][C];
+ *       images [B][C][H][W].
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).  Every call only
+ *     enqueues work on that stream; none synchronises it except gs_render_count.
+ *   - the return value is a gs_status; nothing aborts the process.
+ *   - workspaces are caller-owned device memory of at least the size the matching *_workspace_size
+ *     query returns; their contents are private to the library and must stay untouched between a
+ *     forward and its backward.
+ */
+#ifndef GSPLAT_B200_H
+#define GSPLAT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    GS_OK = 0,
+    GS_ERR_PAIR_BUDGET = 1,  /* reference: PairBudgetExceeded (render_triton.py:51-54) */
+    GS_ERR_BAD_ARGUMENT = 2, /* reference: ValueError / NotImplementedError / assert */
+    GS_ERR_TIMEOUT = 3,      /* a bounded device wait gave up */
+    GS_ERR_CUDA = 4,         /* a CUDA runtime call failed (see gs_last_error) */
+    GS_ERR_WORKSPACE = 5     /* workspace smaller than the size query asked for */
+} gs_status;
+
+/* Render modes: which reference entry point a descriptor describes. */
+typedef enum {
+    GS_MODE_OCTAVE = 0,   /* render_alpha_octave            render_triton.py:935-980 */
+    GS_MODE_CULL = 1,     /* render_alpha_full_triton(cull=True)  render_triton.py:326-347, 538-567 */
+    GS_MODE_MULTIRES = 2, /* render_alpha_multires          render_triton.py:879-922 */
+    GS_MODE_EXACT = 3     /* render_alpha_full_triton(cull=False) / render.render_alpha_full */
+} gs_render_mode;
+
+typedef struct {
+    int32_t mode;          /* gs_render_mode */
+    int32_t B, N, C;       /* images, splats per image, colour channels (1..3) */
+    int32_t H, W;          /* output resolution */
+    int32_t tile;          /* TILE: 4, 8 or 16 (reference default 8) */
+    int32_t odds;          /* 1: odds weights w = a/(1-a) (render_triton.py:494-499) */
+    int32_t has_theta;     /* 0: theta pointer ignored (axis-aligned splats) */
+    int32_t max_octaves;   /* octave mode (reference default 6) */
+    int32_t n_coarse;      /* multires mode; <=0 or >=N -> single full-resolution group */
+    int32_t coarse_factor; /* multires mode (reference default 8) */
+    float cutoff;          /* bbox radius in sigmas (reference default 3.0) */
+    float base_texels;     /* octave mode (reference default 8.0) */
+    int64_t max_pairs;     /* per (image, group) pair budget; < 0 disables the check */
+    int64_t pair_capacity; /* pairs the workspace holds for the whole batch; 0 -> gs_render_pair_bound */
+} gs_render_desc;
+
+/* Upper bound on the (tile, splat) pairs of the whole batch, computed on the host from the
+ * descriptor alone (no device access).  Replaces the pair-count .item() sync of _build_tiles
+ * (render_triton.py:378-391) whenever the bound is within budget. */
+int64_t gs_render_pair_bound(const gs_render_desc *d);
+
+/* Workspace bytes for a forward (with_backward = 0) or a forward + backward (with_backward = 1). */
+size_t gs_render_workspace_size(const gs_render_desc *d, int with_backward);
+
+/* Exact pair counts per (image, group) into counts_host[B * groups] (groups = max_octaves + 1 in octave
+ * mode, 2 in multires mode, 1 otherwise); *groups_out receives the group count.  Runs the
+ * preprocessing kernel and SYNCHRONISES the stream: the analogue of _build_tiles's budget check
+ * (render_triton.py:378-385), used only when the host bound exceeds the budget. */
+int gs_render_count(const gs_render_desc *d, const float *mu, const float *log_scale, void *workspace,
+                    size_t workspace_bytes, int64_t *counts_host, int32_t *groups_out, void *stream);
+
+/* Forward render: out [B][C][H][W].  Replaces _forward_cull / _forward_cull_fields + the octave loop
+ * of render_alpha_octave / render_alpha_multires + the exact _forward (render_triton.py:128-157,
+ * 538-600, 879-980).  Keeps the state its backward needs in the workspace. */
+int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_scale, const float *color,
+                  const float *opacity, const float *bg, const float *theta, float *out, void *workspace,
+                  size_t workspace_bytes, void *stream);
+
+/* Backward of gs_render_fwd for upstream gradient grad_out [B][C][H][W]: gradients of all six
+ * leaves (g_theta may be NULL).  Replaces _backward / _backward_cull / _backward_cull_fields and the
+ * torch autograd of the upsample + composite (render_triton.py:269-303, 723-810, 864-980). */
+int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_scale, const float *color,
+                  const float *opacity, const float *bg, const float *theta, const float *grad_out, float *g_mu,
+                  float *g_log_scale, float *g_color, float *g_opacity, float *g_bg, float *g_theta,
+                  void *workspace, size_t workspace_bytes, void *stream);
+
+/* Debug/parity accessors for the binning held in a forward's workspace (octave/cull/multires):
+ * copies (SYNCHRONOUSLY) the total pair count, the per-group geometry and the sorted CSR so tests can
+ * compare it bit-exactly with the reference's _build_tiles (render_triton.py:351-409).
+ * tile_ranges_host receives [B * tiles_per_image][2] (begin, end); splat_ids_host receives
+ * [total_pairs] global splat ids (b * N + i); geom_host receives per group
+ * {H, W, ntx, nty, tile_offset}. Any output pointer may be NULL. */
+int gs_render_debug_bins(const gs_render_desc *d, const void *workspace, int64_t *total_pairs,
+                         int32_t *tiles_per_image, int32_t *geom_host, int32_t *tile_ranges_host,
+                         int32_t *splat_ids_host, int32_t *octave_host);
+
+/* activate_scale (params.py:18-28): out = softplus(log_scale) + 1e-4, n elements. */
+int gs_activate_scale(const float *log_scale, float *out, int64_t n, void *stream);
+
+/* Text of the last CUDA error seen by the calling thread (empty when none). */
+const char *gs_last_error(void);
+
+/* Number of kernels (memsets included) this library has enqueued since it was loaded; benchmarks
+ * read it before and after a timed region to report their launch count. */
+uint64_t gs_kernel_launches(void);
+
+/* Device-time profiling of the render stages.  While enabled, gs_render_fwd/bwd record CUDA events
+ * on their stream around each stage; gs_profile_collect waits for them and returns per-stage totals
+ * (ms) and call counts in slots 0 binning (preprocess..tile ranges), 1 fields forward, 2 composite,
+ * 3 composite backward + upsample adjoint, 4 fields backward, 5 finalize (arrays of 8). */
+void gs_profile_enable(int on);
+int gs_profile_collect(double *ms_out, int64_t *count_out);
+
+/* Library version and the compute capability it was built for (100 = sm_100a). */
+int gs_build_arch(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSPLAT_B200_H */

@@ -1,0 +1,76 @@
+"""The C-ABI library loads and exports every entry point include/gsplat_b200.h declares; the host-only
+queries (bounds, workspace sizes) answer without touching a GPU."""
+
+import ctypes as C
+import re
+import subprocess
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared(header="gsplat_b200.h"):
+    txt = (ROOT / "include" / header).read_text()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return set(re.findall(r"\b(gs_[a-z0-9_]+)\s*\(", txt))
+
+
+def test_header_symbols_exported(lib):
+    from gaussian_2d_splat_encoder_b200 import _lib
+
+    names = declared()
+    assert names, "no declarations parsed"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r" T (gs_\w+)", out))
+    missing = names - exported
+    assert not missing, f"declared but not exported: {missing}"
+    for n in names:
+        assert hasattr(lib, n)
+    assert names <= set(_lib.SIGNATURES), "python binding misses a declared entry point"
+
+
+def test_build_arch(lib):
+    assert lib.gs_build_arch() == 100
+
+
+def _desc(**kw):
+    from gaussian_2d_splat_encoder_b200.render_triton import _desc as mk
+
+    return mk(**kw)
+
+
+def test_pair_bound_and_workspace_host_only(lib):
+    from gaussian_2d_splat_encoder_b200 import _lib
+
+    d = _desc(mode=_lib.MODE_OCTAVE, B=1, N=92160, C=3, H=768, W=768, TILE=8, odds=True, has_theta=True,
+              cutoff=3.0, base_texels=8.0, max_octaves=6, max_pairs=48_000_000)
+    bound = lib.gs_render_pair_bound(C.byref(d))
+    # octaves 0..5: sigma <= 8 texels -> bbox <= 8 x 8 tiles; octave 6 at 12x12 px -> 2 x 2 tiles
+    assert bound == 64 * 92160
+    ws_f = lib.gs_render_workspace_size(C.byref(d), 0)
+    ws_b = lib.gs_render_workspace_size(C.byref(d), 1)
+    assert 0 < ws_f < ws_b < (1 << 31)
+    d.tile = 5
+    assert lib.gs_render_workspace_size(C.byref(d), 0) == 0
+    assert lib.gs_render_pair_bound(C.byref(d)) == -1
+
+
+def test_bad_arguments_rejected_without_gpu(lib):
+    from gaussian_2d_splat_encoder_b200 import _lib
+
+    d = _desc(mode=_lib.MODE_EXACT, B=1, N=4, C=3, H=8, W=8, TILE=8, odds=True, has_theta=False, cutoff=3.0)
+    assert lib.gs_render_fwd(C.byref(d), *([None] * 8), 0, None) == _lib.GS_ERR_BAD_ARGUMENT
+    assert lib.gs_activate_scale(None, None, 4, None) == _lib.GS_ERR_BAD_ARGUMENT
+
+
+def test_no_cpu_fallback():
+    """CPU tensors are refused loudly; the product has no CPU or Triton path."""
+    import pytest
+    import torch
+
+    from gaussian_2d_splat_encoder_b200 import render_triton as rt
+
+    t = torch.zeros(1, 4, 2)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        rt.render_alpha_octave(t, t, torch.zeros(1, 4, 3), torch.zeros(1, 4), torch.zeros(1, 3), 16, 16)
