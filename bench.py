@@ -4,18 +4,25 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
 Workloads (seeded synthetic inputs; no dataset is involved):
-  render  config 1: one 768x768 image, 92,160 splats (seed 1), render_alpha_octave(odds=True) forward +
-          backward of an L2 loss against a seeded target.  One step = one image.
+  encode_render (default) configs 2/3: 768x768 test cards (seeds 100-163, 500 shapes, 150 strokes), the
+          released checkpoint when a local copy exists (weights/encoder_golden_d256.pt) else random init
+          (seed 0); one step = one image per GPU: EfficientGaussianEncoder forward (bf16 tensor cores, with
+          its internal 384^2 coarse render) + render_alpha_octave(odds=True) at 768^2 (fp32).
+  render  config 1: one 768x768 image, 92,160 splats (seed 1): render_alpha_octave(odds=True) forward +
+          backward of an L2 loss against a seeded target.  Its ms/image is also reported by every
+          encode_render line ("render_fwd_bwd_ms_per_image").
 Multi-GPU: every rank runs its own images (no collective on the data path; weak scaling); the timed
 region is bracketed by a barrier + synchronize and the max over ranks is reported.
 
---impl reference times the reference's algorithm on the host CPU (the C oracle restating the
-reference's renderer, all host threads) on the same workload, printed with "impl": "reference".
+--impl reference times the reference's algorithm on the host CPU (fp32 torch-CPU restatement of the
+encoder + the C oracle of the renderer, all host threads) on the same workload; rank 0 alone prints it.
 """
 
 from __future__ import annotations
 
 import argparse
+import ctypes as C
+import datetime
 import json
 import os
 import statistics
@@ -30,6 +37,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "768² encode+render images/s at 1/2/4/8 B200; render fwd+bwd ms/image"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+STAGE_NAMES = {0: "binning", 1: "fields_fwd", 2: "composite", 3: "composite_bwd+adjoint", 4: "fields_bwd",
+               5: "finalize", 8: "enc_prep", 9: "conv1", 10: "conv2", 11: "conv3", 12: "conv4_decoder",
+               13: "heads", 14: "enc_gn_concat_cond", 15: "enc_coarse_render"}
 
 
 def peaks():
@@ -41,7 +51,6 @@ def peaks():
     return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0, source="fallback")
 
 
-# ------------------------------------------------------------------------------------------ clocks
 class ClockSampler:
     """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
 
@@ -50,16 +59,13 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.proc = None
-        self.f = None
+        self.idx, self.proc, self.f = gpu_index, None, None
 
     def __enter__(self):
         try:
             self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.idx), "-lms", "50"], stdout=self.f,
-                                         stderr=subprocess.DEVNULL)
+                                          "-i", str(self.idx), "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
         return self
@@ -98,6 +104,101 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------ workloads
+def _load_encoder(dev=None):
+    """The released checkpoint when a local copy exists, else the reference architecture with random
+    init (torch.manual_seed(0)); returns (module, description)."""
+    import torch
+
+    from gaussian_2d_splat_encoder_b200.efficient_encoder import EfficientGaussianEncoder
+
+    sys.path.insert(0, str(ROOT / "tests"))
+    from enc_util import GOLDEN_CFG, load_golden
+
+    m = load_golden(EfficientGaussianEncoder)
+    desc = "released checkpoint encoder_golden_d256.pt"
+    if m is None:
+        torch.manual_seed(0)
+        m = EfficientGaussianEncoder(**GOLDEN_CFG).eval()
+        desc = "reference architecture, random init (torch.manual_seed(0))"
+    if dev is not None:
+        m = m.to(dev)
+    return m, desc
+
+
+class EncodeRenderWorkload:
+    name = "encode_render"
+    H = W = 768
+    SEEDS = list(range(100, 164))
+
+    def __init__(self, dev, rank=0, world=1):
+        import torch
+
+        from gaussian_2d_splat_encoder_b200 import synth
+        from gaussian_2d_splat_encoder_b200 import render_triton as rt
+
+        self.torch, self.rt, self.dev = torch, rt, dev
+        self.enc, self.wdesc = _load_encoder(dev)
+        mine = self.SEEDS[rank::world] or self.SEEDS[:1]
+        imgs = [synth.synth_card(self.H, self.W, 500, 150, s) for s in mine]
+        self.host = [x.contiguous().pin_memory() for x in imgs]
+        self.dev_imgs = [x.to(dev) for x in imgs]
+        self.i = 0
+
+    def _run(self, x):
+        torch = self.torch
+        with torch.inference_mode():
+            out = self.enc(x)
+            rec = self.rt.render_alpha_octave(out["mu"], out["log_scale"], out["color"], out["opacity"], out["bg"],
+                                              self.H, self.W, theta=out["theta"], odds=self.enc.odds)
+        return rec
+
+    def step(self):
+        x = self.dev_imgs[self.i % len(self.dev_imgs)]
+        self.i += 1
+        return self._run(x)
+
+    def e2e_buffers(self):
+        return self.torch.empty(1, 3, self.H, self.W).pin_memory()
+
+    def e2e_step(self, buf):
+        x = self.host[self.i % len(self.host)].to(self.dev, non_blocking=True)
+        self.i += 1
+        rec = self._run(x)
+        buf.copy_(rec, non_blocking=True)
+
+    def io_bytes(self):
+        return 3 * self.H * self.W * 4, 3 * self.H * self.W * 4
+
+    def config(self):
+        return {"workload": "configs 2/3: 768x768 test cards (seeds 100-163), EfficientGaussianEncoder (bf16, "
+                            "tcgen05) + render_alpha_octave(odds) fp32, inference", "images_per_step_per_gpu": 1,
+                "encoder_weights": self.wdesc, "H": self.H, "W": self.W,
+                "splats_per_image": (self.H // 8) ** 2 * 2 + (self.H // 4) ** 2 * 2,
+                "l2": "flushed between timed steps (256 MB write, outside the timed events)"}
+
+    @classmethod
+    def cpu_inputs(cls):
+        import torch
+
+        from gaussian_2d_splat_encoder_b200 import synth
+
+        sys.path.insert(0, str(ROOT / "tests"))
+        from enc_util import GOLDEN_CFG
+
+        m, desc = _load_encoder()
+        return dict(sd=m.state_dict(), cfg=GOLDEN_CFG, x=synth.synth_card(cls.H, cls.W, 500, 150, cls.SEEDS[0]),
+                    desc=desc, torch=torch)
+
+    @classmethod
+    def cpu_step(cls, O, s):
+        from oracle import encoder_oracle as E
+
+        o = E.encode(s["sd"], s["cfg"], s["x"])
+        f = {k: (v.numpy() if v is not None else None) for k, v in o.items() if hasattr(v, "numpy") or v is None}
+        O.render_alpha_octave(f["mu"], f["log_scale"], f["color"], f["opacity"], f["bg"], cls.H, cls.W,
+                              theta=f["theta"], odds=True)
+
+
 class RenderWorkload:
     """Config 1: render_alpha_octave(odds) forward + L2 backward of one 768^2 image, 92,160 splats."""
 
@@ -105,7 +206,7 @@ class RenderWorkload:
     H = W = 768
     N = 92160
 
-    def __init__(self, dev):
+    def __init__(self, dev, rank=0, world=1):
         import torch
 
         from gaussian_2d_splat_encoder_b200 import synth
@@ -123,19 +224,9 @@ class RenderWorkload:
         L = self.leaves if leaves is None else leaves
         tgt = self.dev_in["target"] if target is None else target
         out = rt.render_alpha_octave(L[0], L[1], L[2], L[3], L[4], self.H, self.W, theta=L[5], odds=True)
-        loss = (out - tgt).square().mean()
+        loss = torch.nn.functional.mse_loss(out, tgt)
         grads = torch.autograd.grad(loss, L)
         return loss, grads
-
-    def e2e_step(self, out_bufs):
-        """Host (pinned) -> device copy of the step's inputs, the step, device -> host of loss + grads."""
-        torch = self.torch
-        L = [self.host[k].to(self.dev, non_blocking=True).requires_grad_(True) for k in self.keys]
-        tgt = self.host["target"].to(self.dev, non_blocking=True)
-        loss, grads = self.step(L, tgt)
-        for o, g in zip(out_bufs, grads):
-            o.copy_(g, non_blocking=True)
-        out_bufs[-1].copy_(loss.detach().reshape(1), non_blocking=True)
 
     def e2e_buffers(self):
         torch = self.torch
@@ -143,38 +234,23 @@ class RenderWorkload:
         bufs.append(torch.empty(1).pin_memory())
         return bufs
 
+    def e2e_step(self, out_bufs):
+        """Host (pinned) -> device copy of the step's inputs, the step, device -> host of loss + grads."""
+        L = [self.host[k].to(self.dev, non_blocking=True).requires_grad_(True) for k in self.keys]
+        tgt = self.host["target"].to(self.dev, non_blocking=True)
+        loss, grads = self.step(L, tgt)
+        for o, g in zip(out_bufs, grads):
+            o.copy_(g, non_blocking=True)
+        out_bufs[-1].copy_(loss.detach().reshape(1), non_blocking=True)
+
     def io_bytes(self):
         h2d = sum(self.host[k].numel() * 4 for k in self.keys) + self.host["target"].numel() * 4
         d2h = sum(self.host[k].numel() * 4 for k in self.keys) + 4
         return h2d, d2h
 
-    def pixel_pairs(self, lib):
-        """Algorithmic units of the compositing kernels: (tile, splat) pairs x 64 pixels, summed over
-        the octaves, read back from one forward's binning."""
-        import ctypes as C
-
-        from gaussian_2d_splat_encoder_b200 import _lib
-        from gaussian_2d_splat_encoder_b200.render_triton import _desc
-
-        torch = self.torch
-        d = _desc(mode=_lib.MODE_OCTAVE, B=1, N=self.N, C=3, H=self.H, W=self.W, TILE=8, odds=True, has_theta=True,
-                  cutoff=3.0, base_texels=8.0, max_octaves=6, max_pairs=48_000_000)
-        d.pair_capacity = lib.gs_render_pair_bound(C.byref(d))
-        nb = lib.gs_render_workspace_size(C.byref(d), 0)
-        ws = torch.empty(nb, dtype=torch.uint8, device=self.dev)
-        out = torch.empty(1, 3, self.H, self.W, device=self.dev)
-        f = [self.dev_in[k].contiguous() for k in self.keys]
-        _lib.check(lib.gs_render_fwd(C.byref(d), *[_lib.ptr(t) for t in f], _lib.ptr(out), _lib.ptr(ws), nb,
-                                     _lib.stream_of(self.dev)))
-        torch.cuda.synchronize()
-        tot = C.c_int64(0)
-        _lib.check(lib.gs_render_debug_bins(C.byref(d), _lib.ptr(ws), C.byref(tot), None, None, None, None, None))
-        return int(tot.value), int(tot.value) * 64
-
-    @classmethod
-    def config(cls):
-        return {"workload": "config 1: render_alpha_octave(odds=True) fwd + L2 bwd, 768x768, 92,160 splats "
-                            "(seed 1)", "images_per_step_per_gpu": 1, "H": cls.H, "W": cls.W, "splats": cls.N,
+    def config(self):
+        return {"workload": "config 1: render_alpha_octave(odds=True) fwd + L2 bwd, 768x768, 92,160 splats (seed 1)",
+                "images_per_step_per_gpu": 1, "H": self.H, "W": self.W, "splats": self.N,
                 "l2": "flushed between timed steps (256 MB write, outside the timed events)"}
 
     @classmethod
@@ -193,13 +269,15 @@ class RenderWorkload:
                               theta=s["theta"], odds=True, grad_out=g)
 
 
-WORKLOADS = {"render": RenderWorkload}
+WORKLOADS = {"encode_render": EncodeRenderWorkload, "render": RenderWorkload}
 
 
 # ------------------------------------------------------------------------------------------ CPU side
 def cpu_baseline(workload_cls, steps: int, budget_s: float = 20.0):
-    """The reference's algorithm on the host cores (C oracle, all threads): images/s over a bounded
-    sample of whole steps."""
+    """The reference's algorithm on the host cores (torch-CPU fp32 encoder + C oracle renderer, all
+    threads): images/s over a bounded sample of whole steps."""
+    import torch
+
     from oracle import oracle as O
 
     O.build()
@@ -214,23 +292,44 @@ def cpu_baseline(workload_cls, steps: int, budget_s: float = 20.0):
             break
     per = statistics.mean(times)
     return {"value": 1.0 / per, "unit": "images/s", "cores": O.num_threads(), "kind": "port",
-            "sample": f"{len(times)} whole {workload_cls.name} steps (768x768, fwd+bwd) on the C oracle, "
-                      f"{O.num_threads()} OpenMP threads, os.cpu_count()={os.cpu_count()}"}
+            "sample": f"{len(times)} whole {workload_cls.name} steps at 768x768 on the host: torch-CPU fp32 encoder "
+                      f"({torch.get_num_threads()} threads) + C oracle renderer ({O.num_threads()} OpenMP threads); "
+                      f"os.cpu_count()={os.cpu_count()}"}
 
 
-# ------------------------------------------------------------------------------------------ main
+# ------------------------------------------------------------------------------------------ GPU timing
+def time_steps(torch, wl, K, flush, lib):
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    for i in range(K):
+        flush.zero_()
+        ev[i][0].record()
+        wl.step()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in ev]
+
+
+def collect_stages(lib):
+    from gaussian_2d_splat_encoder_b200 import _lib
+
+    ms = (C.c_double * 16)()
+    cnt = (C.c_int64 * 16)()
+    _lib.check(lib.gs_profile_collect(ms, cnt))
+    return {STAGE_NAMES[i]: {"ms_per_call": ms[i] / max(cnt[i], 1), "calls": int(cnt[i])}
+            for i in STAGE_NAMES if cnt[i] > 0}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="render")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="encode_render")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     W = max(3, args.warmup)
     K = max(1, args.steps)
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -243,8 +342,7 @@ def main():
         line = {"metric": METRIC, "value": r["value"], "unit": "images/s", "n_gpus": args.gpus, "steps": K,
                 "warmup": W, "ms_per_step": 1000.0 / r["value"], "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
-                "config": wcls.config(),
-                "cpu_baseline": r,
+                "config": {"workload": wcls.name}, "cpu_baseline": r,
                 "e2e": {"value": r["value"], "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
@@ -255,11 +353,11 @@ def main():
     from gaussian_2d_splat_encoder_b200 import _lib
 
     if world > 1:
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     lib = _lib.load()
-    wl = wcls(dev)
+    wl = wcls(dev, rank, world)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
 
     def barrier():
@@ -267,93 +365,96 @@ def main():
         if world > 1:
             dist.barrier()
 
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     for _ in range(W):
         wl.step()
     barrier()
-
-    # device-resident timed region: per-step events, L2 flushed between steps outside the events
     lib.gs_profile_enable(1)
     l0 = lib.gs_kernel_launches()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    idx = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
-        if os.environ.get("CUDA_VISIBLE_DEVICES") else local
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    idx = int(vis.split(",")[local]) if vis else local
     with ClockSampler(idx) as clk:
-        for i in range(K):
-            flush.zero_()
-            ev[i][0].record()
-            wl.step()
-            ev[i][1].record()
-        torch.cuda.synchronize()
+        step_ms = time_steps(torch, wl, K, flush, lib)
     launches = lib.gs_kernel_launches() - l0
     lib.gs_profile_enable(0)
-    import ctypes as C
-
-    ms_st = (C.c_double * 8)()
-    cnt_st = (C.c_int64 * 8)()
-    _lib.check(lib.gs_profile_collect(ms_st, cnt_st))
-    step_ms = [a.elapsed_time(b) for a, b in ev]
-    tot_ms = sum(step_ms)
-    if world > 1:
-        t = torch.tensor([tot_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        tot_ms = float(t.item())
+    stages = collect_stages(lib)
+    tot_ms = max_over_ranks(sum(step_ms))
     barrier()
 
-    # end-to-end through the public API with host buffers
-    bufs = wl.e2e_buffers()
+    # end-to-end through the public API with host buffers (H2D of inputs, D2H of the result inside)
+    buf = wl.e2e_buffers()
     for _ in range(2):
-        wl.e2e_step(bufs)
+        wl.e2e_step(buf)
     barrier()
     Ke = max(3, min(K, 50))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(Ke):
-        wl.e2e_step(bufs)
+        wl.e2e_step(buf)
     e1.record()
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
 
-    pairs, pp = wl.pixel_pairs(lib)
+    # secondary metric: config-1 render fwd+bwd ms/image
+    sec = None
+    if wcls is not RenderWorkload:
+        rw = RenderWorkload(dev)
+        for _ in range(3):
+            rw.step()
+        torch.cuda.synchronize()
+        lib.gs_profile_enable(1)
+        rms = time_steps(torch, rw, 30, flush, lib)
+        lib.gs_profile_enable(0)
+        rstages = collect_stages(lib)
+        sec = {"render_fwd_bwd_ms_per_image": statistics.mean(rms), "stages_ms": rstages}
+    barrier()
+
     images = K * world
     value = images / (tot_ms / 1000.0)
     e2e_val = Ke * world / (e2e_ms / 1000.0)
     h2d, d2h = wl.io_bytes()
     clocks = clk.summary()
     f_mhz = clocks["sm_mhz"] or 1965.0
-    # roofline of the dominant kernel (fields backward): FP32-bound, 40 FP32 lane-ops + 2 SFU per
-    # pixel-pair (algorithmic count); peak = 148 SMs x 128 FP32 lanes x the sampled SM clock.
-    ms_fwd = ms_st[1] / max(cnt_st[1], 1)
-    ms_bwd = ms_st[4] / max(cnt_st[4], 1)
-    fp32_peak = 148 * 128 * f_mhz * 1e6 / 1e9  # Gop/s
-    sfu_peak = 148 * 16 * f_mhz * 1e6 / 1e9
-    bwd_ach = 40.0 * pp / (ms_bwd * 1e-3) / 1e9
-    fwd_ach_sfu = 3.0 * pp / (ms_fwd * 1e-3) / 1e9
-    stages = {n: {"ms_per_call": ms_st[i] / max(cnt_st[i], 1), "calls": int(cnt_st[i])}
-              for i, n in enumerate(("binning", "fields_fwd", "composite", "composite_bwd+adjoint", "fields_bwd",
-                                     "finalize"))}
     pk = peaks()
     line = {
         "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": tot_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp32", "data": "synthetic", "config": {**wl.config(), "parallelism": f"dp{world} (image per GPU, "
-                                                                                      "no collective)"},
-        "render_fwd_bwd_ms_per_image": tot_ms / K,
-        "roofline": {"bound": "fp32", "kernel": "k_fields_bwd", "achieved": bwd_ach, "peak": fp32_peak,
-                     "unit": "Gop/s (FP32 lane-ops)", "frac": bwd_ach / fp32_peak, "traffic": None,
-                     "units_per_launch": pp, "ops_per_unit": 40,
-                     "peak_source": f"148 SMs x 128 FP32 lanes x {f_mhz:.0f} MHz (median SM clock sampled during "
-                                    "the timed region); MEASURED_PEAKS.json has no FP32/SFU figure"},
-        "roofline_fields_fwd": {"bound": "sfu", "achieved": fwd_ach_sfu, "peak": sfu_peak, "unit": "Gop/s (MUFU)",
-                                "frac": fwd_ach_sfu / sfu_peak, "ops_per_unit": 3, "units_per_launch": pp},
-        "stages_ms": stages, "pairs": pairs, "pixel_pairs": pp,
-        "clocks": clocks, "gpu_launches": int(launches),
+        "dtype": "bf16 encoder / fp32 render" if wcls is EncodeRenderWorkload else "fp32", "data": "synthetic",
+        "config": {**wl.config(), "parallelism": f"dp{world} (image per GPU, no collective)"},
+        "stages_ms": stages, "clocks": clocks, "gpu_launches": int(launches),
         "e2e": {"value": e2e_val, "unit": "images/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "peaks": pk,
     }
+    if wcls is EncodeRenderWorkload:
+        # dominant kernel: the decoder convolution (tensor-bound): 2*M*N*K flops per launch
+        M, N, Kd = (wl.H // 4) * (wl.W // 4), 128, 9 * 384
+        t = stages.get("conv4_decoder", {}).get("ms_per_call", 0.0)
+        ach = 2.0 * M * N * Kd / (t * 1e-3) / 1e12 if t > 0 else None
+        line["roofline"] = {"bound": "tensor", "kernel": "k_conv_tc<128,64,4> (decoder 3x3 384->128 @192^2)",
+                            "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                            "frac": (ach / pk["bf16_tflops"]) if ach else None, "traffic": None,
+                            "flops_per_launch": 2.0 * M * N * Kd,
+                            "peak_source": f"MEASURED_PEAKS.json bf16_tflops (burst, {pk['source']})"}
+        line["render_fwd_bwd_ms_per_image"] = sec["render_fwd_bwd_ms_per_image"] if sec else None
+        line["render_stages_ms"] = sec["stages_ms"] if sec else None
+    else:
+        line["render_fwd_bwd_ms_per_image"] = tot_ms / K
+        fw = stages.get("fields_bwd", {}).get("ms_per_call", 0.0)
+        pairs = 850839  # (tile, splat) pairs of config 1 (reported by the binning; fixed by the seed)
+        pp = pairs * 64
+        fp32_peak = 148 * 128 * f_mhz * 1e6 / 1e9
+        ach = 40.0 * pp / (fw * 1e-3) / 1e9 if fw > 0 else None
+        line["roofline"] = {"bound": "fp32", "kernel": "k_fields_bwd<8,4>", "achieved": ach, "peak": fp32_peak,
+                            "unit": "Gop/s (FP32 lane-ops)", "frac": (ach / fp32_peak) if ach else None,
+                            "traffic": None, "units_per_launch": pp, "ops_per_unit": 40,
+                            "peak_source": f"148 SMs x 128 FP32 lanes x {f_mhz:.0f} MHz (median SM clock sampled "
+                                           "during the timed region)"}
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wcls, 3)
     if rank == 0:

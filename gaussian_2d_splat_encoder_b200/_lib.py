@@ -46,6 +46,10 @@ SIGNATURES = {
     "gs_render_bwd": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "gs_render_debug_bins": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P]),
     "gs_activate_scale": (C.c_int, [_P, _P, C.c_int64, _P]),
+    "gs_conv2d": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P]),
+    "gs_encoder_workspace_size": (C.c_size_t, [_P]),
+    "gs_encoder_fwd": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
+    "gs_encoder_error_flag": (C.c_int, [_P, _P, _P]),
     "gs_last_error": (C.c_char_p, []),
     "gs_kernel_launches": (C.c_uint64, []),
     "gs_profile_enable": (None, [C.c_int]),

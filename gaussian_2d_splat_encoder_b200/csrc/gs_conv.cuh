@@ -1,0 +1,23 @@
+// Internal interface of the tcgen05 convolution (gs_conv.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/gsplat_b200.h"
+
+struct ConvArgs {
+    int B, Hi, Wi, Ci, Co;
+    int KH, KW, stride, pad;
+    int Ho, Wo;
+    int TX, TY, tiles_x, tiles_y;
+    int nchunks, nkb;
+    int gelu;
+    const float *bias;
+    __nv_bfloat16 *out;
+    double *stats;  // [B][8][2] GroupNorm partial sums (sum, sum of squares), accumulated
+    int *err;       // set to a non-zero stage code when a bounded wait gives up
+};
+
+void gs_conv_pick_tile(int Ho, int Wo, int *TX, int *TY);
+int gs_conv_run(const gs_conv_desc *d, const void *in, const void *w, const float *bias, void *out, double *stats,
+                int *err, cudaStream_t st);

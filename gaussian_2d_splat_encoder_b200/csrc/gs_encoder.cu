@@ -1,0 +1,572 @@
+// gs_encoder.cu -- EfficientGaussianEncoder('adaptive') forward on B200 (reference:
+// bigwolfeman/gaussian-2d-splat-encoder, gaussian_splat_encoder/efficient_encoder.py:306-378).
+//
+//   k_prep        grey, Sobel/4, gradient magnitude (efficient_encoder.py:123-130) and the
+//                 space-to-depth bf16 input of the first convolution; per-block pooled gradients
+//   conv1..3      tcgen05 implicit GEMM (gs_conv.cu): 7x7/2 (on the space-to-depth tensor as 4x4/1),
+//                 3x3/2, 3x3/2, bias + GELU + GroupNorm statistics fused (efficient_encoder.py:53-58)
+//   k_gn_apply    GroupNorm(8) normalise + affine in place (NHWC bf16); the last one also sums the
+//                 channels for the background head
+//   k_bg          sigmoid(Linear(mean_hw(s8)))               (efficient_encoder.py:267-268)
+//   k_head        1x1 head + activations of one splat group   (efficient_encoder.py:170-197, 340-342)
+//   coarse render render_alpha_octave at residual_grid^2 with odds (gs_render.cu)
+//   k_cond        bilinear(image -> grid), |target - render|, mean(render)   (efficient_encoder.py:349-351)
+//   k_concat      bilinear(s8 -> s4 size) || s4  (the _UpBlock input, efficient_encoder.py:89-91)
+//   conv4         3x3/1 384->128 decoder convolution on the tensor cores
+//   k_head (fine) GroupNorm applied on the fly, [fine_feat, pooled gradient, bilinear(cond)] 1x1 head
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include "../../include/gsplat_b200.h"
+#include "gs_conv.cuh"
+#include "gs_prof.cuh"
+
+namespace {
+
+__device__ __forceinline__ void lin_idx(int d, int in_size, int out_size, int &i0, int &i1, float &l0, float &l1) {
+    float scale = (float)in_size / (float)out_size;
+    float src = scale * ((float)d + 0.5f) - 0.5f;
+    if (src < 0.0f) src = 0.0f;
+    int i = (int)src;
+    if (i > in_size - 1) i = in_size - 1;
+    int ip = (i < in_size - 1) ? 1 : 0;
+    float lam = fminf(fmaxf(src - (float)i, 0.0f), 1.0f);
+    i0 = i;
+    i1 = i + ip;
+    l1 = lam;
+    l0 = 1.0f - lam;
+}
+
+// torch.linspace(0.5/n, 1-0.5/n, n)[i] in fp32 (efficient_encoder.py:174-175)
+__device__ __forceinline__ float lin_center(int i, int n) {
+    float start = 0.5f / (float)n, end = 1.0f - 0.5f / (float)n;
+    if (n == 1) return start;
+    float step = (end - start) / (float)(n - 1);
+    return i < n / 2 ? start + step * (float)i : end - step * (float)(n - 1 - i);
+}
+
+__device__ __forceinline__ float gray_at(const float *img, int H, int W, int y, int x) {
+    if (y < 0 || y >= H || x < 0 || x >= W) return 0.0f;
+    long long P = (long long)H * W, p = (long long)y * W + x;
+    return (img[p] + img[P + p] + img[2 * P + p]) / 3.0f;
+}
+
+// grad [B][H][W] fp32 and the space-to-depth bf16 input Z[B][H/2][W/2][16],
+// Z[p][q][(dy*2+dx)*4 + c] = X[2p+dy][2q+dx][c], X = (R, G, B, grad).
+__global__ void __launch_bounds__(256) k_prep(const float *__restrict__ image, int B, int H, int W,
+                                              float *__restrict__ grad, __nv_bfloat16 *__restrict__ Z) {
+    const int Hz = H / 2, Wz = W / 2;
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)B * Hz * Wz) return;
+    int b = (int)(i / ((long long)Hz * Wz));
+    int r = (int)(i - (long long)b * Hz * Wz);
+    int p = r / Wz, q = r - p * Wz;
+    const float *img = image + (long long)b * 3 * H * W;
+    const long long P = (long long)H * W;
+    // 4x4 grey neighbourhood of the 2x2 block
+    float g[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) g[a][c] = gray_at(img, H, W, 2 * p - 1 + a, 2 * q - 1 + c);
+    __align__(16) __nv_bfloat16 z[16];
+#pragma unroll
+    for (int dy = 0; dy < 2; dy++)
+#pragma unroll
+        for (int dx = 0; dx < 2; dx++) {
+            // F.conv2d with kx = [[-1,0,1],[-2,0,2],[-1,0,1]]/4, ky = kx^T (cross-correlation, zero pad)
+            float gx = 0.f, gy = 0.f;
+            const float k[3][3] = {{-1.f, 0.f, 1.f}, {-2.f, 0.f, 2.f}, {-1.f, 0.f, 1.f}};
+#pragma unroll
+            for (int u = 0; u < 3; u++)
+#pragma unroll
+                for (int v = 0; v < 3; v++) {
+                    float gv = g[dy + u][dx + v];
+                    gx += (k[u][v] / 4.0f) * gv;
+                    gy += (k[v][u] / 4.0f) * gv;
+                }
+            float gm = sqrtf(gx * gx + gy * gy + 1e-6f);
+            int y = 2 * p + dy, x = 2 * q + dx;
+            grad[(long long)b * P + (long long)y * W + x] = gm;
+            int base = (dy * 2 + dx) * 4;
+            long long pp = (long long)y * W + x;
+            z[base + 0] = __float2bfloat16_rn(img[pp]);
+            z[base + 1] = __float2bfloat16_rn(img[P + pp]);
+            z[base + 2] = __float2bfloat16_rn(img[2 * P + pp]);
+            z[base + 3] = __float2bfloat16_rn(gm);
+        }
+    uint4 *dst = reinterpret_cast<uint4 *>(Z + i * 16);
+    dst[0] = reinterpret_cast<uint4 *>(z)[0];
+    dst[1] = reinterpret_cast<uint4 *>(z)[1];
+}
+
+// adaptive_avg_pool2d of grad to (H/f, W/f) for f dividing H and W
+__global__ void k_pool(const float *__restrict__ grad, int B, int H, int W, int f, float *__restrict__ out) {
+    const int Ho = H / f, Wo = W / f;
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)B * Ho * Wo) return;
+    int b = (int)(i / ((long long)Ho * Wo));
+    int r = (int)(i - (long long)b * Ho * Wo);
+    int y = r / Wo, x = r - y * Wo;
+    const float *g = grad + (long long)b * H * W;
+    float s = 0.f;
+    for (int a = 0; a < f; a++)
+        for (int c = 0; c < f; c++) s += g[(long long)(y * f + a) * W + x * f + c];
+    out[i] = s / (float)(f * f);
+}
+
+// GroupNorm(8) apply in place on NHWC bf16 [B][HW][C]; chsum (optional) += per-channel sums of the
+// normalised values (mean for the background head).
+__global__ void __launch_bounds__(256) k_gn_apply(__nv_bfloat16 *__restrict__ x, int B, long long HW, int C,
+                                                  const double *__restrict__ stats, const float *__restrict__ gamma,
+                                                  const float *__restrict__ beta, float *__restrict__ chsum) {
+    extern __shared__ float sh[];  // scale[C], shift[C], csum[C]
+    float *scale = sh, *shift = sh + C, *csum = sh + 2 * C;
+    const int b = blockIdx.y;
+    const double n = (double)HW * (C / 8);
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        int g = c / (C / 8);
+        double mean = stats[(b * 8 + g) * 2] / n;
+        double var = stats[(b * 8 + g) * 2 + 1] / n - mean * mean;
+        if (var < 0) var = 0;
+        float rstd = (float)(1.0 / sqrt(var + 1e-5));
+        scale[c] = gamma[c] * rstd;
+        shift[c] = beta[c] - (float)mean * gamma[c] * rstd;
+        csum[c] = 0.f;
+    }
+    __syncthreads();
+    const long long nvec = HW * C / 8;
+    __nv_bfloat16 *xb = x + (long long)b * HW * C;
+    for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += (long long)gridDim.x * blockDim.x) {
+        uint4 u = reinterpret_cast<uint4 *>(xb)[v];
+        __nv_bfloat16 *e = reinterpret_cast<__nv_bfloat16 *>(&u);
+        int c0 = (int)((v * 8) % C);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            float f = __bfloat162float(e[k]) * scale[c0 + k] + shift[c0 + k];
+            e[k] = __float2bfloat16_rn(f);
+            if (chsum) atomicAdd(&csum[c0 + k], __bfloat162float(e[k]));
+        }
+        reinterpret_cast<uint4 *>(xb)[v] = u;
+    }
+    if (chsum) {
+        __syncthreads();
+        for (int c = threadIdx.x; c < C; c += blockDim.x) atomicAdd(&chsum[b * C + c], csum[c]);
+    }
+}
+
+// bg = sigmoid(W * mean_hw(s8) + b) (efficient_encoder.py:267-268)
+__global__ void k_bg(const float *__restrict__ chsum, int C, long long HW, const float *__restrict__ w,
+                     const float *__restrict__ bias, float *__restrict__ bg) {
+    int b = blockIdx.x, k = threadIdx.x;
+    if (k >= 3) return;
+    float s = bias[k];
+    for (int c = 0; c < C; c++) s += w[k * C + c] * (chsum[b * C + c] / (float)HW);
+    bg[b * 3 + k] = 1.0f / (1.0f + expf(-s));
+}
+
+struct HeadArgs {
+    int B, fH, fW, M;          // grid and splats per cell
+    int Cfeat;                 // feature channels read from `feat` (NHWC bf16)
+    const __nv_bfloat16 *feat;
+    const double *gn_stats;    // if non-NULL, feat is pre-GroupNorm: normalise on the fly
+    const float *gn_gamma, *gn_beta;
+    const float *gpool;        // [B][fH][fW] pooled gradient (extra channel Cfeat)
+    const float *cond;         // [B][rg][rg][4] or NULL: bilinear-sampled extra channels Cfeat+1..+4
+    int rg;
+    const float *w, *b;        // [nout][Cin], [nout]; rows: mu(2M), scale(2M), colour(3M), opacity(M), theta(M)
+    int Cin, nout;
+    float off_scale, ls_floor, min_op;
+    int use_rot;
+    // outputs: API tensors [B][Ntot][...] at splat offset n0, plus optional contiguous copies
+    int Ntot, n0;
+    float *mu, *ls, *col, *op, *th;
+    float *cmu, *cls, *ccol, *cop, *cth;  // contiguous [B][fH*fW*M] copies (coarse render input)
+};
+
+// one thread per feature cell: 1x1 convolution of the head + activations (efficient_encoder.py:170-197)
+__global__ void __launch_bounds__(128) k_head(HeadArgs a) {
+    extern __shared__ float shw[];  // weights [nout][Cin], bias [nout], gn scale/shift [2][Cfeat]
+    float *sw = shw, *sb = shw + a.nout * a.Cin, *gsc = sb + a.nout, *gsh = gsc + a.Cfeat;
+    long long cell = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long ncell = (long long)a.B * a.fH * a.fW;
+    int b0 = (int)(((long long)blockIdx.x * blockDim.x) / ((long long)a.fH * a.fW));
+    for (int i = threadIdx.x; i < a.nout * a.Cin; i += blockDim.x) sw[i] = a.w[i];
+    for (int i = threadIdx.x; i < a.nout; i += blockDim.x) sb[i] = a.b[i];
+    // GroupNorm scale/shift of the block's first image (blocks never straddle images: fH*fW % 128 == 0
+    // is required by the caller, otherwise the per-thread path below recomputes them)
+    if (a.gn_stats) {
+        const double n = (double)a.fH * a.fW * (a.Cfeat / 8);
+        for (int c = threadIdx.x; c < a.Cfeat; c += blockDim.x) {
+            int g = c / (a.Cfeat / 8);
+            double mean = a.gn_stats[(b0 * 8 + g) * 2] / n;
+            double var = a.gn_stats[(b0 * 8 + g) * 2 + 1] / n - mean * mean;
+            if (var < 0) var = 0;
+            float rstd = (float)(1.0 / sqrt(var + 1e-5));
+            gsc[c] = a.gn_gamma[c] * rstd;
+            gsh[c] = a.gn_beta[c] - (float)mean * a.gn_gamma[c] * rstd;
+        }
+    }
+    __syncthreads();
+    if (cell >= ncell) return;
+    const int b = (int)(cell / ((long long)a.fH * a.fW));
+    const int r = (int)(cell - (long long)b * a.fH * a.fW);
+    const int y = r / a.fW, x = r - y * a.fW;
+    float acc[18];
+#pragma unroll
+    for (int k = 0; k < 18; k++) acc[k] = k < a.nout ? sb[k] : 0.f;
+    const __nv_bfloat16 *fp = a.feat + cell * a.Cfeat;
+    for (int c = 0; c < a.Cfeat; c += 8) {
+        uint4 u = *reinterpret_cast<const uint4 *>(fp + c);
+        const __nv_bfloat16 *e = reinterpret_cast<const __nv_bfloat16 *>(&u);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            float v = __bfloat162float(e[j]);
+            if (a.gn_stats) v = v * gsc[c + j] + gsh[c + j];
+#pragma unroll
+            for (int k = 0; k < 18; k++)
+                if (k < a.nout) acc[k] += sw[k * a.Cin + c + j] * v;
+        }
+    }
+    float extra[5];
+    int nextra = 1;
+    extra[0] = a.gpool[cell];
+    if (a.cond) {
+        int y0, y1, x0, x1;
+        float h0, h1, w0, w1;
+        lin_idx(y, a.rg, a.fH, y0, y1, h0, h1);
+        lin_idx(x, a.rg, a.fW, x0, x1, w0, w1);
+        const float *cb = a.cond + (long long)b * a.rg * a.rg * 4;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            extra[1 + c] = h0 * (w0 * cb[((long long)y0 * a.rg + x0) * 4 + c] + w1 * cb[((long long)y0 * a.rg + x1) * 4 + c]) +
+                           h1 * (w0 * cb[((long long)y1 * a.rg + x0) * 4 + c] + w1 * cb[((long long)y1 * a.rg + x1) * 4 + c]);
+        }
+        nextra = 5;
+    }
+    for (int j = 0; j < nextra; j++)
+#pragma unroll
+        for (int k = 0; k < 18; k++)
+            if (k < a.nout) acc[k] += sw[k * a.Cin + a.Cfeat + j] * extra[j];
+    // activations; channel layout of each head: (m, component)
+    const int M = a.M;
+    const float by = lin_center(y, a.fH), bx = lin_center(x, a.fW);
+    for (int m = 0; m < M; m++) {
+        const long long nl = (long long)r * M + m;  // splat index inside the group (cell-major, then slot)
+        const long long n = (long long)b * a.Ntot + a.n0 + nl;
+        float muy = by + tanhf(acc[m * 2 + 0]) * a.off_scale;
+        float mux = bx + tanhf(acc[m * 2 + 1]) * a.off_scale;
+        muy = fminf(fmaxf(muy, 0.005f), 0.995f);
+        mux = fminf(fmaxf(mux, 0.005f), 0.995f);
+        float ly = acc[2 * M + m * 2 + 0], lx = acc[2 * M + m * 2 + 1];
+        ly = fmaxf(ly, a.ls_floor);
+        lx = fmaxf(lx, a.ls_floor);
+        float cc[3];
+        for (int c = 0; c < 3; c++) cc[c] = 1.0f / (1.0f + expf(-acc[4 * M + m * 3 + c]));
+        float o = 1.0f / (1.0f + expf(-acc[7 * M + m]));
+        if (a.min_op > 0.f) o = a.min_op + (1.0f - a.min_op) * o;
+        float t = a.use_rot ? tanhf(acc[8 * M + m]) * 1.5707963267948966f : 0.f;
+        a.mu[n * 2] = muy; a.mu[n * 2 + 1] = mux;
+        a.ls[n * 2] = ly; a.ls[n * 2 + 1] = lx;
+        for (int c = 0; c < 3; c++) a.col[n * 3 + c] = cc[c];
+        a.op[n] = o;
+        if (a.use_rot && a.th) a.th[n] = t;
+        if (a.cmu) {
+            const long long q = (long long)b * a.fH * a.fW * M + nl;
+            a.cmu[q * 2] = muy; a.cmu[q * 2 + 1] = mux;
+            a.cls[q * 2] = ly; a.cls[q * 2 + 1] = lx;
+            for (int c = 0; c < 3; c++) a.ccol[q * 3 + c] = cc[c];
+            a.cop[q] = o;
+            if (a.cth) a.cth[q] = t;
+        }
+    }
+}
+
+// cond[B][rg][rg][4] = (|bilinear(image) - render|, mean_c(render)) (efficient_encoder.py:349-351)
+__global__ void k_cond(const float *__restrict__ image, int B, int H, int W, const float *__restrict__ render, int rg,
+                       float *__restrict__ cond) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)B * rg * rg) return;
+    int b = (int)(i / ((long long)rg * rg));
+    int r = (int)(i - (long long)b * rg * rg);
+    int y = r / rg, x = r - y * rg;
+    int y0, y1, x0, x1;
+    float h0, h1, w0, w1;
+    lin_idx(y, H, rg, y0, y1, h0, h1);
+    lin_idx(x, W, rg, x0, x1, w0, w1);
+    const long long P = (long long)H * W, R = (long long)rg * rg;
+    float msum = 0.f;
+    for (int c = 0; c < 3; c++) {
+        const float *im = image + ((long long)b * 3 + c) * P;
+        float t = h0 * (w0 * im[(long long)y0 * W + x0] + w1 * im[(long long)y0 * W + x1]) +
+                  h1 * (w0 * im[(long long)y1 * W + x0] + w1 * im[(long long)y1 * W + x1]);
+        float rv = render[((long long)b * 3 + c) * R + r];
+        cond[i * 4 + c] = fabsf(t - rv);
+        msum += rv;
+    }
+    cond[i * 4 + 3] = msum / 3.0f;
+}
+
+// concat[B][H4][W4][Cu + Cs] = (bilinear(s8 -> H4 x W4), s4)   (efficient_encoder.py:89-91)
+__global__ void __launch_bounds__(256) k_concat(const __nv_bfloat16 *__restrict__ s8, int H8, int W8, int Cu,
+                                                const __nv_bfloat16 *__restrict__ s4, int H4, int W4, int Cs, int B,
+                                                __nv_bfloat16 *__restrict__ out) {
+    const int Ct = Cu + Cs;
+    const int nv = Ct / 8;
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)B * H4 * W4 * nv) return;
+    int v = (int)(i % nv);
+    long long pix = i / nv;
+    int b = (int)(pix / ((long long)H4 * W4));
+    int r = (int)(pix - (long long)b * H4 * W4);
+    int y = r / W4, x = r - y * W4;
+    uint4 res;
+    __nv_bfloat16 *e = reinterpret_cast<__nv_bfloat16 *>(&res);
+    int c0 = v * 8;
+    if (c0 < Cu) {
+        int y0, y1, x0, x1;
+        float h0, h1, w0, w1;
+        lin_idx(y, H8, H4, y0, y1, h0, h1);
+        lin_idx(x, W8, W4, x0, x1, w0, w1);
+        const __nv_bfloat16 *sb = s8 + (long long)b * H8 * W8 * Cu;
+        uint4 a00 = *reinterpret_cast<const uint4 *>(sb + ((long long)y0 * W8 + x0) * Cu + c0);
+        uint4 a01 = *reinterpret_cast<const uint4 *>(sb + ((long long)y0 * W8 + x1) * Cu + c0);
+        uint4 a10 = *reinterpret_cast<const uint4 *>(sb + ((long long)y1 * W8 + x0) * Cu + c0);
+        uint4 a11 = *reinterpret_cast<const uint4 *>(sb + ((long long)y1 * W8 + x1) * Cu + c0);
+        const __nv_bfloat16 *p00 = reinterpret_cast<const __nv_bfloat16 *>(&a00);
+        const __nv_bfloat16 *p01 = reinterpret_cast<const __nv_bfloat16 *>(&a01);
+        const __nv_bfloat16 *p10 = reinterpret_cast<const __nv_bfloat16 *>(&a10);
+        const __nv_bfloat16 *p11 = reinterpret_cast<const __nv_bfloat16 *>(&a11);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            float f = h0 * (w0 * __bfloat162float(p00[k]) + w1 * __bfloat162float(p01[k])) +
+                      h1 * (w0 * __bfloat162float(p10[k]) + w1 * __bfloat162float(p11[k]));
+            e[k] = __float2bfloat16_rn(f);
+        }
+    } else {
+        res = *reinterpret_cast<const uint4 *>(s4 + pix * Cs + (c0 - Cu));
+    }
+    *reinterpret_cast<uint4 *>(out + pix * Ct + c0) = res;
+}
+
+// NHWC bf16 -> NHWC fp32 (backbone_features output)
+__global__ void k_bf16_to_f32(const __nv_bfloat16 *__restrict__ in, float *__restrict__ out, long long n) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __bfloat162float(in[i]);
+}
+
+size_t al(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct EncPlan {
+    int B, H, W, H2, W2, H4, W4, H8, W8, d, Nc, Nf, N, rg;
+    size_t o_Z, o_y1, o_y2, o_y3, o_cat, o_y4, o_grad, o_g4, o_g8, o_stats, o_chsum, o_err, o_c[5], o_render,
+        o_cond, o_rws, total;
+    gs_render_desc rd;
+    size_t rws;
+};
+
+int enc_plan(const gs_encoder_desc *e, EncPlan &p) {
+    if (!e || e->B < 1 || e->H < 16 || e->W < 16 || e->H % 8 || e->W % 8) return GS_ERR_BAD_ARGUMENT;
+    if (e->d != 256 || e->M < 1 || e->M > 2 || e->Mf < 1 || e->Mf > 2) return GS_ERR_BAD_ARGUMENT;
+    if (e->residual_grid < 8) return GS_ERR_BAD_ARGUMENT;
+    // the fine head's thread blocks (128 cells) must not straddle two images
+    if (((long long)(e->H / 4) * (e->W / 4)) % 128 != 0) return GS_ERR_BAD_ARGUMENT;
+    memset(&p, 0, sizeof(p));
+    p.B = e->B; p.H = e->H; p.W = e->W; p.d = e->d; p.rg = e->residual_grid;
+    p.H2 = p.H / 2; p.W2 = p.W / 2; p.H4 = p.H / 4; p.W4 = p.W / 4; p.H8 = p.H / 8; p.W8 = p.W / 8;
+    p.Nc = p.H8 * p.W8 * e->M;
+    p.Nf = p.H4 * p.W4 * e->Mf;
+    p.N = p.Nc + p.Nf;
+    const size_t B = p.B;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { size_t r = o; o = al(o + bytes); return r; };
+    p.o_Z = take(B * p.H2 * p.W2 * 16 * 2);
+    p.o_y1 = take(B * p.H2 * p.W2 * 64 * 2);
+    p.o_y2 = take(B * p.H4 * p.W4 * 128 * 2);
+    p.o_y3 = take(B * p.H8 * p.W8 * 256 * 2);
+    p.o_cat = take(B * p.H4 * p.W4 * 384 * 2);
+    p.o_y4 = take(B * p.H4 * p.W4 * 128 * 2);
+    p.o_grad = take(B * p.H * p.W * 4);
+    p.o_g4 = take(B * p.H4 * p.W4 * 4);
+    p.o_g8 = take(B * p.H8 * p.W8 * 4);
+    p.o_stats = take(4 * B * 16 * sizeof(double));
+    p.o_chsum = take(B * 256 * 4);
+    p.o_err = take(64);
+    const size_t nc = B * p.Nc;
+    p.o_c[0] = take(nc * 2 * 4);
+    p.o_c[1] = take(nc * 2 * 4);
+    p.o_c[2] = take(nc * 3 * 4);
+    p.o_c[3] = take(nc * 4);
+    p.o_c[4] = take(nc * 4);
+    p.o_render = take(B * 3 * p.rg * p.rg * 4);
+    p.o_cond = take(B * p.rg * p.rg * 4 * 4);
+    gs_render_desc &rd = p.rd;
+    memset(&rd, 0, sizeof(rd));
+    rd.mode = GS_MODE_OCTAVE; rd.B = p.B; rd.N = p.Nc; rd.C = 3; rd.H = p.rg; rd.W = p.rg; rd.tile = 8;
+    rd.odds = e->odds; rd.has_theta = e->use_rotation; rd.max_octaves = 6; rd.cutoff = 3.0f; rd.base_texels = 8.0f;
+    rd.max_pairs = -1; rd.pair_capacity = 0;
+    p.rws = gs_render_workspace_size(&rd, 0);
+    if (p.rws == 0) return GS_ERR_BAD_ARGUMENT;
+    p.o_rws = take(p.rws);
+    p.total = o;
+    return GS_OK;
+}
+
+template <typename T>
+T *W(void *ws, size_t off) { return reinterpret_cast<T *>(reinterpret_cast<char *>(ws) + off); }
+
+}  // namespace
+
+extern "C" size_t gs_encoder_workspace_size(const gs_encoder_desc *e) {
+    EncPlan p;
+    if (enc_plan(e, p) != GS_OK) return 0;
+    return p.total;
+}
+
+extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights *w, const float *image, float *mu,
+                              float *log_scale, float *color, float *opacity, float *theta, float *bg,
+                              float *features, void *workspace, size_t workspace_bytes, void *stream) {
+    EncPlan p;
+    int st = enc_plan(e, p);
+    if (st != GS_OK) return st;
+    if (!w || !image || !mu || !log_scale || !color || !opacity || !bg || (e->use_rotation && !theta))
+        return GS_ERR_BAD_ARGUMENT;
+    if (!workspace || workspace_bytes < p.total) return GS_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    void *ws = workspace;
+    const int B = p.B;
+    cudaMemsetAsync(W<char>(ws, p.o_stats), 0, p.o_err + 64 - p.o_stats, s);  // stats, chsum, err
+    double *stats = W<double>(ws, p.o_stats);
+    int *err = W<int>(ws, p.o_err);
+    float *grad = W<float>(ws, p.o_grad);
+    // 1. input preparation
+    {
+        ProfScope ps(PR_ENC_PREP, s);
+        long long n = (long long)B * p.H2 * p.W2;
+        k_prep<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(image, B, p.H, p.W, grad, W<__nv_bfloat16>(ws, p.o_Z));
+        long long n4 = (long long)B * p.H4 * p.W4, n8 = (long long)B * p.H8 * p.W8;
+        k_pool<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(grad, B, p.H, p.W, 4, W<float>(ws, p.o_g4));
+        k_pool<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(grad, B, p.H, p.W, 8, W<float>(ws, p.o_g8));
+    }
+    // 2. backbone: conv -> GELU -> GroupNorm, three stages
+    auto gn = [&](void *x, long long HW, int C, double *stt, const float *gamma, const float *beta, float *chsum) {
+        dim3 grid((unsigned)std::min<long long>(1024, (HW * C / 8 + 255) / 256), (unsigned)B);
+        k_gn_apply<<<grid, 256, 3 * C * sizeof(float), s>>>((__nv_bfloat16 *)x, B, HW, C, stt, gamma, beta, chsum);
+    };
+    gs_conv_desc cd;
+    memset(&cd, 0, sizeof(cd));
+    cd.B = B; cd.H = p.H2; cd.W = p.W2; cd.Cin = 16; cd.Cout = 64; cd.kh = 4; cd.kw = 4; cd.stride = 1; cd.pad = 2;
+    cd.Ho = p.H2; cd.Wo = p.W2; cd.gelu = 1; cd.kind = 1;
+    {
+        ProfScope ps(PR_CONV1, s);
+        if ((st = gs_conv_run(&cd, W<void>(ws, p.o_Z), w->w1, w->b1, W<void>(ws, p.o_y1), stats, err, s))) return st;
+    }
+    gn(W<void>(ws, p.o_y1), (long long)p.H2 * p.W2, 64, stats, w->gn1_w, w->gn1_b, nullptr);
+    memset(&cd, 0, sizeof(cd));
+    cd.B = B; cd.H = p.H2; cd.W = p.W2; cd.Cin = 64; cd.Cout = 128; cd.kh = 3; cd.kw = 3; cd.stride = 2; cd.pad = 1;
+    cd.gelu = 1;
+    {
+        ProfScope ps(PR_CONV2, s);
+        if ((st = gs_conv_run(&cd, W<void>(ws, p.o_y1), w->w2, w->b2, W<void>(ws, p.o_y2), stats + B * 16, err, s)))
+            return st;
+    }
+    gn(W<void>(ws, p.o_y2), (long long)p.H4 * p.W4, 128, stats + B * 16, w->gn2_w, w->gn2_b, nullptr);
+    memset(&cd, 0, sizeof(cd));
+    cd.B = B; cd.H = p.H4; cd.W = p.W4; cd.Cin = 128; cd.Cout = 256; cd.kh = 3; cd.kw = 3; cd.stride = 2; cd.pad = 1;
+    cd.gelu = 1;
+    {
+        ProfScope ps(PR_CONV3, s);
+        if ((st = gs_conv_run(&cd, W<void>(ws, p.o_y2), w->w3, w->b3, W<void>(ws, p.o_y3), stats + 2 * B * 16, err,
+                              s)))
+            return st;
+    }
+    float *chsum = W<float>(ws, p.o_chsum);
+    gn(W<void>(ws, p.o_y3), (long long)p.H8 * p.W8, 256, stats + 2 * B * 16, w->gn3_w, w->gn3_b, chsum);
+    k_bg<<<B, 32, 0, s>>>(chsum, 256, (long long)p.H8 * p.W8, w->bg_w, w->bg_b, bg);
+    // 3. coarse head (writes the API tensors and a contiguous copy for the coarse render)
+    HeadArgs h;
+    memset(&h, 0, sizeof(h));
+    h.B = B; h.fH = p.H8; h.fW = p.W8; h.M = e->M; h.Cfeat = 256; h.feat = W<__nv_bfloat16>(ws, p.o_y3);
+    h.gpool = W<float>(ws, p.o_g8); h.w = w->hc_w; h.b = w->hc_b; h.Cin = 257; h.nout = (e->use_rotation ? 9 : 8) * e->M;
+    h.off_scale = e->coarse_offset / (float)std::max(p.H8, p.W8);
+    h.ls_floor = e->coarse_ls_floor; h.min_op = e->coarse_min_opacity; h.use_rot = e->use_rotation;
+    h.Ntot = p.N; h.n0 = 0; h.mu = mu; h.ls = log_scale; h.col = color; h.op = opacity; h.th = theta;
+    h.cmu = W<float>(ws, p.o_c[0]); h.cls = W<float>(ws, p.o_c[1]); h.ccol = W<float>(ws, p.o_c[2]);
+    h.cop = W<float>(ws, p.o_c[3]); h.cth = e->use_rotation ? W<float>(ws, p.o_c[4]) : nullptr;
+    {
+        ProfScope ps(PR_HEADS, s);
+        long long ncell = (long long)B * p.H8 * p.W8;
+        size_t sm = ((size_t)h.nout * h.Cin + h.nout + 2 * h.Cfeat) * 4;
+        k_head<<<(unsigned)((ncell + 127) / 128), 128, sm, s>>>(h);
+    }
+    // 4. coarse render at residual_grid^2 (odds) -> cond map
+    {
+        ProfScope ps(PR_ENC_RENDER, s);
+        float *bgws = bg;
+        st = gs_render_fwd(&p.rd, h.cmu, h.cls, h.ccol, h.cop, bgws, h.cth, W<float>(ws, p.o_render),
+                           W<void>(ws, p.o_rws), p.rws, stream);
+        if (st != GS_OK) return st;
+        long long n = (long long)B * p.rg * p.rg;
+        k_cond<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(image, B, p.H, p.W, W<float>(ws, p.o_render), p.rg,
+                                                          W<float>(ws, p.o_cond));
+    }
+    // 5. fine decoder: bilinear(s8) || s4 -> 3x3 conv 384->128 (+GELU, GN stats)
+    {
+        ProfScope ps(PR_ENC_MISC, s);
+        long long n = (long long)B * p.H4 * p.W4 * (384 / 8);
+        k_concat<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), p.H8, p.W8, 256,
+                                                             W<__nv_bfloat16>(ws, p.o_y2), p.H4, p.W4, 128, B,
+                                                             W<__nv_bfloat16>(ws, p.o_cat));
+    }
+    memset(&cd, 0, sizeof(cd));
+    cd.B = B; cd.H = p.H4; cd.W = p.W4; cd.Cin = 384; cd.Cout = 128; cd.kh = 3; cd.kw = 3; cd.stride = 1; cd.pad = 1;
+    cd.gelu = 1;
+    {
+        ProfScope ps(PR_CONV4, s);
+        if ((st = gs_conv_run(&cd, W<void>(ws, p.o_cat), w->w4, w->b4, W<void>(ws, p.o_y4), stats + 3 * B * 16, err,
+                              s)))
+            return st;
+    }
+    // 6. fine head: GN on the fly, + pooled gradient + bilinear(cond)
+    memset(&h, 0, sizeof(h));
+    h.B = B; h.fH = p.H4; h.fW = p.W4; h.M = e->Mf; h.Cfeat = 128; h.feat = W<__nv_bfloat16>(ws, p.o_y4);
+    h.gn_stats = stats + 3 * B * 16; h.gn_gamma = w->gn4_w; h.gn_beta = w->gn4_b;
+    h.gpool = W<float>(ws, p.o_g4); h.cond = W<float>(ws, p.o_cond); h.rg = p.rg;
+    h.w = w->hf_w; h.b = w->hf_b; h.Cin = 133; h.nout = (e->use_rotation ? 9 : 8) * e->Mf;
+    h.off_scale = e->fine_offset / (float)std::max(p.H4, p.W4);
+    h.ls_floor = -INFINITY; h.min_op = 0.f; h.use_rot = e->use_rotation;
+    h.Ntot = p.N; h.n0 = p.Nc; h.mu = mu; h.ls = log_scale; h.col = color; h.op = opacity; h.th = theta;
+    {
+        ProfScope ps(PR_HEADS, s);
+        long long ncell = (long long)B * p.H4 * p.W4;
+        size_t sm = ((size_t)h.nout * h.Cin + h.nout + 2 * h.Cfeat) * 4;
+        k_head<<<(unsigned)((ncell + 127) / 128), 128, sm, s>>>(h);
+    }
+    if (features) {
+        long long n = (long long)B * p.H8 * p.W8 * 256;
+        k_bf16_to_f32<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), features, n);
+    }
+    // memset, prep, 2 pools, 4 convs, 3 GN applies, bg, 2 heads, cond, concat, optional feature copy
+    gs_count_launch(17 + (features ? 1 : 0));
+    cudaError_t ce = cudaGetLastError();
+    if (ce != cudaSuccess) {
+        fprintf(stderr, "gs_encoder_fwd: %s\n", cudaGetErrorString(ce));
+        return GS_ERR_CUDA;
+    }
+    return GS_OK;
+}
+
+extern "C" int gs_encoder_error_flag(const gs_encoder_desc *e, const void *workspace, int *flag_host) {
+    EncPlan p;
+    int st = enc_plan(e, p);
+    if (st != GS_OK) return st;
+    cudaError_t ce = cudaMemcpy(flag_host, W<int>(const_cast<void *>(workspace), p.o_err), sizeof(int),
+                                cudaMemcpyDeviceToHost);
+    return ce == cudaSuccess ? GS_OK : GS_ERR_CUDA;
+}

@@ -35,15 +35,13 @@ static unsigned long long g_launches = 0;  // kernels enqueued by this library (
 
 #define GS_COUNT(n) __atomic_fetch_add(&g_launches, (unsigned long long)(n), __ATOMIC_RELAXED)
 
-// Optional CUDA-event timing of the render stages (gs_profile_enable / gs_profile_collect): events are
-// recorded on the launching stream around each stage, so the durations are device time of exactly
-// those kernels.
 #include <memory>
 #include <mutex>
 #include <vector>
+
+#include "gs_prof.cuh"
+
 namespace {
-enum { PR_BIN = 0, PR_FIELDS_FWD = 1, PR_COMPOSITE = 2, PR_COMPOSITE_BWD = 3, PR_FIELDS_BWD = 4, PR_FINALIZE = 5,
-       PR_N = 8 };
 struct ProfEvent {
     int region;
     cudaEvent_t a, b;
@@ -51,25 +49,14 @@ struct ProfEvent {
 std::mutex g_prof_mu;
 bool g_prof_on = false;
 std::vector<ProfEvent> g_prof;
-struct ProfScope {
-    bool on;
-    ProfEvent ev;
-    cudaStream_t s;
-    ProfScope(int region, cudaStream_t st) : on(g_prof_on), s(st) {
-        if (!on) return;
-        ev.region = region;
-        cudaEventCreate(&ev.a);
-        cudaEventCreate(&ev.b);
-        cudaEventRecord(ev.a, s);
-    }
-    ~ProfScope() {
-        if (!on) return;
-        cudaEventRecord(ev.b, s);
-        std::lock_guard<std::mutex> lk(g_prof_mu);
-        g_prof.push_back(ev);
-    }
-};
 }  // namespace
+
+bool gs_prof_on() { return g_prof_on; }
+void gs_prof_push(int region, cudaEvent_t a, cudaEvent_t b) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_prof.push_back(ProfEvent{region, a, b});
+}
+void gs_count_launch(unsigned long long n) { GS_COUNT(n); }
 
 static int set_cuda_error(cudaError_t e, const char *where) {
     snprintf(g_last_error, sizeof(g_last_error), "%s: %s", where, cudaGetErrorString(e));
@@ -175,6 +162,7 @@ __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *_
     const int b0 = G.N > 0 ? (int)(((long long)blockIdx.x * blockDim.x) / G.N) : 0;
     long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     int count = 0;
+    int skey = -1;
     if (s < (long long)G.B * G.N) {
         int b = (int)(s / G.N), i = (int)(s - (long long)b * G.N);
         float2 m = reinterpret_cast<const float2 *>(mu)[s];  // (y, x)
@@ -210,12 +198,23 @@ __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *_
         }
         meta[s] = mt;
         counts[s] = count;
-        if (b - b0 < 4) {
-            atomicAdd(&s_pairs[(b - b0) * GS_MAX_GROUPS + g], (unsigned long long)count);
-            atomicAdd(&s_spl[(b - b0) * GS_MAX_GROUPS + g], 1);
-        } else {
-            atomicAdd(&gpairs[b * G.ngroups + g], (unsigned long long)count);
-            atomicAdd(&gsplats[b * G.ngroups + g], 1);
+        skey = b * GS_MAX_GROUPS + g;
+    }
+    {
+        // aggregate per warp over lanes with the same (image, group), then per block in shared memory
+        const unsigned peers = __match_any_sync(0xffffffffu, skey);
+        const int npeer = __popc(peers);
+        const unsigned psum = __reduce_add_sync(peers, (unsigned)count);
+        const bool leader = (peers & ((1u << (threadIdx.x & 31)) - 1u)) == 0u;
+        if (leader && skey >= 0) {
+            const int b = skey / GS_MAX_GROUPS, g = skey % GS_MAX_GROUPS;
+            if (b - b0 < 4) {
+                atomicAdd(&s_pairs[(b - b0) * GS_MAX_GROUPS + g], (unsigned long long)psum);
+                atomicAdd(&s_spl[(b - b0) * GS_MAX_GROUPS + g], npeer);
+            } else {
+                atomicAdd(&gpairs[b * G.ngroups + g], (unsigned long long)psum);
+                atomicAdd(&gsplats[b * G.ngroups + g], npeer);
+            }
         }
     }
     __syncthreads();
@@ -311,23 +310,27 @@ __device__ __forceinline__ long long clamp_n(const long long *n_ptr, long long c
     return n < cap ? n : cap;
 }
 
+// grid-stride over "virtual blocks" of RS_ITEMS keys; n is read from the device
 __global__ void __launch_bounds__(RS_THREADS) k_radix_upsweep(const unsigned *__restrict__ keys,
                                                               const long long *__restrict__ n_ptr, long long cap,
                                                               int shift, int radix, int *__restrict__ hist,
                                                               int nblk_cap) {
     __shared__ int h[256];
-    long long n = clamp_n(n_ptr, cap);
-    long long base = (long long)blockIdx.x * RS_ITEMS;
-    if (base >= n) return;
-    for (int d = threadIdx.x; d < radix; d += RS_THREADS) h[d] = 0;
-    __syncthreads();
-    unsigned mask = (unsigned)radix - 1u;
-    for (int r = 0; r < RS_ROUNDS; r++) {
-        long long i = base + r * RS_THREADS + threadIdx.x;
-        if (i < n) atomicAdd(&h[(keys[i] >> shift) & mask], 1);
+    const long long n = clamp_n(n_ptr, cap);
+    const int nblk = (int)((n + RS_ITEMS - 1) / RS_ITEMS);
+    const unsigned mask = (unsigned)radix - 1u;
+    for (int vb = blockIdx.x; vb < nblk; vb += gridDim.x) {
+        const long long base = (long long)vb * RS_ITEMS;
+        for (int d = threadIdx.x; d < radix; d += RS_THREADS) h[d] = 0;
+        __syncthreads();
+        for (int r = 0; r < RS_ROUNDS; r++) {
+            long long i = base + r * RS_THREADS + threadIdx.x;
+            if (i < n) atomicAdd(&h[(keys[i] >> shift) & mask], 1);
+        }
+        __syncthreads();
+        for (int d = threadIdx.x; d < radix; d += RS_THREADS) hist[d * nblk_cap + vb] = h[d];
+        __syncthreads();
     }
-    __syncthreads();
-    for (int d = threadIdx.x; d < radix; d += RS_THREADS) hist[d * nblk_cap + blockIdx.x] = h[d];
 }
 
 // grid = radix blocks: exclusive scan of one digit's per-block counts; digit total -> dtot[d]
@@ -349,6 +352,9 @@ __global__ void __launch_bounds__(256) k_radix_scan(int *__restrict__ hist, cons
     if (threadIdx.x == 0) dtot[blockIdx.x] = carry;
 }
 
+// Stable scatter of one digit: warp w of a virtual block ranks its own 256 consecutive keys in 8
+// sequential rounds (match_any within the round + a running per-warp digit count), then one block-wide
+// prefix over warps turns the per-warp counts into global positions.
 __global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep(const unsigned *__restrict__ kin,
                                                                 const int *__restrict__ vin,
                                                                 unsigned *__restrict__ kout, int *__restrict__ vout,
@@ -356,70 +362,71 @@ __global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep(const unsigned *
                                                                 int shift, int radix, const int *__restrict__ hist,
                                                                 int nblk_cap, const int *__restrict__ dtot) {
     constexpr int NWARP = RS_THREADS / 32;
+    constexpr int PER_WARP = RS_ITEMS / NWARP;  // 256
     __shared__ int wsum[NWARP];
-    __shared__ int base_d[256];   // digit base + this block's scanned offset, advanced per round
+    __shared__ int dbase[256];
     __shared__ int wcnt[NWARP][256];
-    long long n = clamp_n(n_ptr, cap);
-    long long base = (long long)blockIdx.x * RS_ITEMS;
-    if (base >= n) return;
-    int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // digit bases: exclusive scan of digit totals (radix <= 256 = RS_THREADS)
-    int dv = tid < radix ? dtot[tid] : 0;
-    int dpre = block_excl_scan<RS_THREADS>(dv, wsum, nullptr);
-    if (tid < radix) base_d[tid] = dpre + hist[tid * nblk_cap + blockIdx.x];
-    for (int d = tid; d < 256; d += RS_THREADS)
-        for (int w = 0; w < NWARP; w++) wcnt[w][d] = 0;
-    __syncthreads();
-    unsigned mask = (unsigned)radix - 1u;
-    unsigned lt_mask = (1u << lane) - 1u;
-    for (int r = 0; r < RS_ROUNDS; r++) {
-        long long i = base + r * RS_THREADS + tid;
-        bool valid = i < n;
-        unsigned key = valid ? kin[i] : 0u;
-        int val = valid ? vin[i] : 0;
-        int d = valid ? (int)((key >> shift) & mask) : 256 + lane;  // invalid lanes: unique dummy digits
-        unsigned peers = __match_any_sync(0xffffffffu, d);
-        int wrank = __popc(peers & lt_mask);
-        bool leader = (peers & lt_mask) == 0u;
-        if (valid && leader) wcnt[warp][d] = __popc(peers);
+    const long long n = clamp_n(n_ptr, cap);
+    const int nblk = (int)((n + RS_ITEMS - 1) / RS_ITEMS);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int dv = tid < radix ? dtot[tid] : 0;
+    const int dpre = block_excl_scan<RS_THREADS>(dv, wsum, nullptr);
+    if (tid < radix) dbase[tid] = dpre;
+    const unsigned mask = (unsigned)radix - 1u;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    for (int vb = blockIdx.x; vb < nblk; vb += gridDim.x) {
+        const long long base = (long long)vb * RS_ITEMS + warp * PER_WARP;
+        for (int d = lane; d < radix; d += 32) wcnt[warp][d] = 0;
+        __syncwarp();
+        unsigned key[RS_ROUNDS];
+        int val[RS_ROUNDS], dig[RS_ROUNDS], rank[RS_ROUNDS];
+#pragma unroll
+        for (int r = 0; r < RS_ROUNDS; r++) {
+            const long long i = base + r * 32 + lane;
+            const bool valid = i < n;
+            key[r] = valid ? kin[i] : 0u;
+            val[r] = valid ? vin[i] : 0;
+            const int d = valid ? (int)((key[r] >> shift) & mask) : -1;
+            dig[r] = d;
+            const unsigned peers = __match_any_sync(0xffffffffu, d);
+            const int pre = valid ? wcnt[warp][d] : 0;
+            rank[r] = pre + __popc(peers & lt_mask);
+            __syncwarp();
+            if (valid && (peers & lt_mask) == 0u) wcnt[warp][d] = pre + __popc(peers);
+            __syncwarp();
+        }
         __syncthreads();
         if (tid < radix) {
-            int run = base_d[tid];
+            int run = dbase[tid] + hist[tid * nblk_cap + vb];
 #pragma unroll
             for (int w = 0; w < NWARP; w++) {
-                int c = wcnt[w][tid];
+                const int c = wcnt[w][tid];
                 wcnt[w][tid] = run;
                 run += c;
             }
-            base_d[tid] = run;
         }
         __syncthreads();
-        if (valid) {
-            int pos = wcnt[warp][d] + wrank;
-            kout[pos] = key;
-            vout[pos] = val;
-        }
-        __syncthreads();
-        if (valid && leader) wcnt[warp][d] = 0;
-        // entries of digits this warp did not touch are already 0 except the prefix written above:
-        // reset every written prefix (all radix entries were overwritten by the scan step)
-        if (tid < radix) {
 #pragma unroll
-            for (int w = 0; w < NWARP; w++) wcnt[w][tid] = 0;
+        for (int r = 0; r < RS_ROUNDS; r++) {
+            if (dig[r] >= 0) {
+                const int pos = wcnt[warp][dig[r]] + rank[r];
+                kout[pos] = key[r];
+                vout[pos] = val[r];
+            }
         }
         __syncthreads();
     }
 }
 
-// [begin, end) of every tile present in the sorted key list (ranges zeroed beforehand)
+// [begin, end) of every tile present in the sorted key list (ranges zeroed beforehand); grid-stride
 __global__ void __launch_bounds__(256) k_ranges(const unsigned *__restrict__ keys, const long long *__restrict__ n_ptr,
                                                 long long cap, int2 *__restrict__ ranges) {
-    long long n = clamp_n(n_ptr, cap);
-    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    unsigned k = keys[i];
-    if (i == 0 || keys[i - 1] != k) ranges[k].x = (int)i;
-    if (i == n - 1 || keys[i + 1] != k) ranges[k].y = (int)(i + 1);
+    const long long n = clamp_n(n_ptr, cap);
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        unsigned k = keys[i];
+        if (i == 0 || keys[i - 1] != k) ranges[k].x = (int)i;
+        if (i == n - 1 || keys[i + 1] != k) ranges[k].y = (int)(i + 1);
+    }
 }
 
 // ----------------------------------------------------------------------------------------------------
@@ -562,16 +569,14 @@ __device__ __forceinline__ void lin_index(int d, int in_size, int out_size, int 
 
 __device__ __forceinline__ bool group_native(const RenderGeom &G, int g) { return G.g[g].H == G.H && G.g[g].W == G.W; }
 
-// one native pixel per thread: sum the present groups' fields, composite, keep the sums for backward
-__global__ void __launch_bounds__(256) k_composite(RenderGeom G, const float *__restrict__ fields,
-                                                   const int *__restrict__ gsplats, const float *__restrict__ bg,
-                                                   float *__restrict__ out, float *__restrict__ F) {
-    const int b = blockIdx.y;
-    const long long P = (long long)G.H * G.W;
-    long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (p >= P) return;
-    int y = (int)(p / G.W), x = (int)(p - (long long)y * G.W);
-    float S[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+// S[0..4] = the five raw sums at native pixel (y, x) of image b: every present group's field, bilinearly
+// upsampled to native resolution (torch align_corners=False), added in the reference's order
+// (render_triton.py:959-972, 914-916).
+__device__ __forceinline__ void gather_sums(const RenderGeom &G, const float *__restrict__ fields,
+                                            const int *__restrict__ gsplats, int b, long long p, int y, int x,
+                                            float S[5]) {
+#pragma unroll
+    for (int c = 0; c < 5; c++) S[c] = 0.f;
     const float *fimg = fields + (long long)b * G.fld_per_image;
 #pragma unroll
     for (int k = 0; k < GS_MAX_GROUPS; k++) {
@@ -598,6 +603,19 @@ __global__ void __launch_bounds__(256) k_composite(RenderGeom G, const float *__
             }
         }
     }
+}
+
+// one native pixel per thread: sum the present groups' fields and composite (render_triton.py:976-979)
+__global__ void __launch_bounds__(256) k_composite(RenderGeom G, const float *__restrict__ fields,
+                                                   const int *__restrict__ gsplats, const float *__restrict__ bg,
+                                                   float *__restrict__ out) {
+    const int b = blockIdx.y;
+    const long long P = (long long)G.H * G.W;
+    long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= P) return;
+    int y = (int)(p / G.W), x = (int)(p - (long long)y * G.W);
+    float S[5];
+    gather_sums(G, fields, gsplats, b, p, y, x, S);
     float asum = fmaxf(S[1], 1e-8f);
     float T = expf(S[0]);
     float *ob = out + (long long)b * G.C * P;
@@ -608,11 +626,6 @@ __global__ void __launch_bounds__(256) k_composite(RenderGeom G, const float *__
             ob[c * P + p] = (1.0f - T) * fg + T * bg[b * G.C + c];
         }
     }
-    if (F) {
-        float *Fb = F + (long long)b * 5 * P;
-#pragma unroll
-        for (int c = 0; c < 5; c++) Fb[c * P + p] = S[c];
-    }
 }
 
 // ----------------------------------------------------------------------------------------------------
@@ -620,7 +633,8 @@ __global__ void __launch_bounds__(256) k_composite(RenderGeom G, const float *__
 
 // dS at native resolution from dL/dimage (torch autograd of render_triton.py:976-979; the cull and
 // exact paths skip the clamp_min mask, render_triton.py:644-654); bg gradient sum_p g * T.
-__global__ void __launch_bounds__(256) k_composite_bwd(RenderGeom G, const float *__restrict__ F,
+__global__ void __launch_bounds__(256) k_composite_bwd(RenderGeom G, const float *__restrict__ fields,
+                                                       const int *__restrict__ gsplats,
                                                        const float *__restrict__ bg,
                                                        const float *__restrict__ gout, float *__restrict__ Gn,
                                                        float *__restrict__ gbg, int clamp_mask) {
@@ -630,8 +644,10 @@ __global__ void __launch_bounds__(256) k_composite_bwd(RenderGeom G, const float
     long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     float gT[3] = {0.f, 0.f, 0.f};
     if (p < P) {
-        const float *Fb = F + (long long)b * 5 * P;
-        float Sl = Fb[p], Sw = Fb[P + p];
+        const int y = (int)(p / G.W), x = (int)(p - (long long)y * G.W);
+        float S[5];
+        gather_sums(G, fields, gsplats, b, p, y, x, S);
+        const float Sl = S[0], Sw = S[1];
         float asum = fmaxf(Sw, 1e-8f);
         float T = expf(Sl);
         float dT = 0.f, dasum = 0.f, dsc[3] = {0.f, 0.f, 0.f};
@@ -640,7 +656,7 @@ __global__ void __launch_bounds__(256) k_composite_bwd(RenderGeom G, const float
         for (int c = 0; c < 3; c++) {
             if (c < G.C) {
                 float gc = gb[c * P + p];
-                float fg = Fb[(2 + c) * P + p] / asum;
+                float fg = S[2 + c] / asum;
                 dT += gc * (bg[b * G.C + c] - fg);
                 float dfg = gc * (1.0f - T);
                 dsc[c] = dfg / asum;
@@ -673,13 +689,14 @@ __global__ void __launch_bounds__(256) k_composite_bwd(RenderGeom G, const float
     }
 }
 
-// adjoint of the bilinear upsample for every present coarse group: each texel gathers, in a fixed
-// order, the native-resolution dS values whose bilinear taps touched it (deterministic).
+// adjoint of the bilinear upsample for every present coarse group: each texel whose tile holds pairs
+// gathers, in a fixed order, the native-resolution dS values whose bilinear taps touched it
+// (deterministic; texels of empty tiles are never read by the backward and are skipped).
 __global__ void __launch_bounds__(256) k_adjoint(RenderGeom G, const int *__restrict__ gsplats,
-                                                 const float *__restrict__ Gn, float *__restrict__ gfields) {
+                                                 const int2 *__restrict__ ranges, const float *__restrict__ Gn,
+                                                 float *__restrict__ gfields) {
     const int b = blockIdx.y;
     long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    // locate the group: texel index space = concatenation of all groups' planes
     int g = -1;
     long long acc = 0;
 #pragma unroll
@@ -694,32 +711,36 @@ __global__ void __launch_bounds__(256) k_adjoint(RenderGeom G, const int *__rest
     q -= acc;
     const int Hg = G.g[g].H, Wg = G.g[g].W;
     const int i = (int)(q / Wg), j = (int)(q - (long long)i * Wg);
+    const int tile = G.g[g].tile_off + (i / G.tile) * G.g[g].ntx + (j / G.tile);
+    const int2 rg = ranges[(long long)b * G.tiles_per_image + tile];
+    if (rg.y <= rg.x) return;
     const long long P = (long long)G.H * G.W;
     const float sy = (float)G.H / (float)Hg, sx = (float)G.W / (float)Wg;
-    int ylo = max(0, (int)floorf((i - 0.5f) * sy - 0.5f) - 2), yhi = min(G.H - 1, (int)ceilf((i + 1.5f) * sy - 0.5f) + 2);
-    int xlo = max(0, (int)floorf((j - 0.5f) * sx - 0.5f) - 2), xhi = min(G.W - 1, (int)ceilf((j + 1.5f) * sx - 0.5f) + 2);
+    const int ylo = max(0, (int)ceilf((i - 0.5f) * sy - 0.5f) - 1);
+    const int yhi = min(G.H - 1, (int)floorf((i + 1.5f) * sy - 0.5f) + 1);
+    const int xlo = max(0, (int)ceilf((j - 0.5f) * sx - 0.5f) - 1);
+    const int xhi = min(G.W - 1, (int)floorf((j + 1.5f) * sx - 0.5f) + 1);
     float acc5[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
     const float *Gb = Gn + (long long)b * 5 * P;
     for (int y = ylo; y <= yhi; y++) {
         int y0, y1;
         float h0, h1;
         lin_index(y, Hg, G.H, y0, y1, h0, h1);
-        float wy = (y0 == i ? h0 : 0.f) + (y1 == i ? h1 : 0.f);
-        if (wy == 0.f && y0 != i && y1 != i) continue;
+        if (y0 != i && y1 != i) continue;
+        const float wy = (y0 == i ? h0 : 0.f) + (y1 == i ? h1 : 0.f);
         for (int x = xlo; x <= xhi; x++) {
             int x0, x1;
             float w0, w1;
             lin_index(x, Wg, G.W, x0, x1, w0, w1);
             if (x0 != j && x1 != j) continue;
-            float wx = (x0 == j ? w0 : 0.f) + (x1 == j ? w1 : 0.f);
-            float w = wy * wx;
-            long long p = (long long)y * G.W + x;
+            const float w = wy * ((x0 == j ? w0 : 0.f) + (x1 == j ? w1 : 0.f));
+            const long long p = (long long)y * G.W + x;
 #pragma unroll
             for (int c = 0; c < 5; c++) acc5[c] += w * Gb[c * P + p];
         }
     }
     float *gf = gfields + (long long)b * G.fld_per_image + G.g[g].fld_off;
-    long long plane = (long long)Hg * Wg;
+    const long long plane = (long long)Hg * Wg;
 #pragma unroll
     for (int c = 0; c < 5; c++) gf[c * plane + q] = acc5[c];
 }
@@ -893,7 +914,7 @@ struct Plan {
     long long cap;
     int nblk_pre, nblk_sort, passes, radix_bits;
     size_t o_rec, o_meta, o_counts, o_bsum, o_zero, o_gpairs, o_gsplats, o_misc, o_ranges, z_len;
-    size_t o_keys_a, o_vals_a, o_keys_b, o_vals_b, o_hist, o_dtot, o_fields, o_F, fwd_bytes;
+    size_t o_keys_a, o_vals_a, o_keys_b, o_vals_b, o_hist, o_dtot, o_fields, fwd_bytes;
     size_t o_G, o_gfields, o_bzero, o_acc, o_gbg, bz_len, total_bytes;
 };
 
@@ -1025,7 +1046,6 @@ void make_plan(const gs_render_desc *d, Plan &pl) {
     pl.o_hist = take(sizeof(int) * 256 * (size_t)pl.nblk_sort);
     pl.o_dtot = take(sizeof(int) * 256);
     pl.o_fields = take(sizeof(float) * (size_t)d->B * pl.G.fld_per_image);
-    pl.o_F = take(sizeof(float) * 5 * (size_t)d->B * d->H * d->W);
     pl.fwd_bytes = o;
     pl.o_G = take(sizeof(float) * 5 * (size_t)d->B * d->H * d->W);
     pl.o_gfields = take(sizeof(float) * (size_t)d->B * pl.G.fld_per_image);
@@ -1147,22 +1167,23 @@ int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_sca
         unsigned *ka = at<unsigned>(workspace, pl.o_keys_a), *kb = at<unsigned>(workspace, pl.o_keys_b);
         int *va = at<int>(workspace, pl.o_vals_a), *vb = at<int>(workspace, pl.o_vals_b);
         int radix = 1 << pl.radix_bits;
+        const int pgrid = std::min(pl.nblk_sort, 148 * 8);
         for (int p = 0; p < pl.passes; p++) {
             int shift = p * pl.radix_bits;
-            k_radix_upsweep<<<pl.nblk_sort, RS_THREADS, 0, s>>>(ka, total, pl.cap, shift, radix,
+            k_radix_upsweep<<<pgrid, RS_THREADS, 0, s>>>(ka, total, pl.cap, shift, radix,
                                                                 at<int>(workspace, pl.o_hist), pl.nblk_sort);
             GS_CHECK_LAUNCH("k_radix_upsweep");
             k_radix_scan<<<radix, 256, 0, s>>>(at<int>(workspace, pl.o_hist), total, pl.cap, pl.nblk_sort,
                                                at<int>(workspace, pl.o_dtot));
             GS_CHECK_LAUNCH("k_radix_scan");
-            k_radix_downsweep<<<pl.nblk_sort, RS_THREADS, 0, s>>>(ka, va, kb, vb, total, pl.cap, shift, radix,
+            k_radix_downsweep<<<pgrid, RS_THREADS, 0, s>>>(ka, va, kb, vb, total, pl.cap, shift, radix,
                                                                   at<int>(workspace, pl.o_hist), pl.nblk_sort,
                                                                   at<int>(workspace, pl.o_dtot));
             GS_CHECK_LAUNCH("k_radix_downsweep");
             std::swap(ka, kb);
             std::swap(va, vb);
         }
-        unsigned nrb = (unsigned)std::max<long long>(1, (pl.cap + 255) / 256);
+        unsigned nrb = (unsigned)std::min<long long>(std::max<long long>(1, (pl.cap + 255) / 256), 148 * 8);
         k_ranges<<<nrb, 256, 0, s>>>(ka, total, pl.cap, at<int2>(workspace, pl.o_ranges));
         GS_CHECK_LAUNCH("k_ranges");
     }
@@ -1177,7 +1198,7 @@ int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_sca
     {
         ProfScope ps(PR_COMPOSITE, s);
         k_composite<<<cg, 256, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,
-                                       out, at<float>(workspace, pl.o_F));
+                                       out);
         GS_CHECK_LAUNCH("k_composite");
     }
     return GS_OK;
@@ -1204,8 +1225,9 @@ int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_sca
     dim3 cg((unsigned)((P + 255) / 256), (unsigned)d->B);
     int clamp_mask = (d->mode == GS_MODE_OCTAVE || d->mode == GS_MODE_MULTIRES) ? 1 : 0;
     std::unique_ptr<ProfScope> cb_scope(new ProfScope(PR_COMPOSITE_BWD, s));
-    k_composite_bwd<<<cg, 256, 0, s>>>(G, at<float>(workspace, pl.o_F), bg, grad_out, at<float>(workspace, pl.o_G),
-                                       at<float>(workspace, pl.o_gbg), clamp_mask);
+    k_composite_bwd<<<cg, 256, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,
+                                       grad_out, at<float>(workspace, pl.o_G), at<float>(workspace, pl.o_gbg),
+                                       clamp_mask);
     GS_CHECK_LAUNCH("k_composite_bwd");
     bool any_coarse = false;
     for (int g = 0; g < G.ngroups; g++)
@@ -1214,8 +1236,8 @@ int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_sca
         long long tex = 0;
         for (int g = 0; g < G.ngroups; g++) tex += (long long)G.g[g].H * G.g[g].W;
         dim3 ag((unsigned)((tex + 255) / 256), (unsigned)d->B);
-        k_adjoint<<<ag, 256, 0, s>>>(G, at<int>(workspace, pl.o_gsplats), at<float>(workspace, pl.o_G),
-                                     at<float>(workspace, pl.o_gfields));
+        k_adjoint<<<ag, 256, 0, s>>>(G, at<int>(workspace, pl.o_gsplats), at<int2>(workspace, pl.o_ranges),
+                                     at<float>(workspace, pl.o_G), at<float>(workspace, pl.o_gfields));
         GS_CHECK_LAUNCH("k_adjoint");
     }
     cb_scope.reset();

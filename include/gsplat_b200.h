@@ -101,6 +101,66 @@ int gs_render_debug_bins(const gs_render_desc *d, const void *workspace, int64_t
                          int32_t *tiles_per_image, int32_t *geom_host, int32_t *tile_ranges_host,
                          int32_t *splat_ids_host, int32_t *octave_host);
 
+/* One encoder convolution on the tensor cores: NHWC bf16 input [B][H][W][Cin], packed bf16 weights
+ * [Cout][kh*kw*Cin] (tap-major, channel-minor), fp32 bias, NHWC bf16 output [B][Ho][Wo][Cout] with
+ * bias + (optional) exact GELU applied; when gn_stats is non-NULL the GroupNorm(8) partial sums
+ * (sum, sum of squares) of the output are ADDED to gn_stats[B][8][2].  kind 0: Cin a multiple of 64,
+ * stride 1 or 2; kind 1: the encoder's first layer expressed on its space-to-depth input (Cin = 16,
+ * 4x4 taps, stride 1, pad 2, output Ho x Wo given explicitly).  Cout in {64, 128, 256}.  err_flag
+ * (device int, may be NULL) receives a non-zero code if a bounded device wait gave up.
+ * Replaces nn.Conv2d + nn.GELU of the reference encoder (efficient_encoder.py:53-58, 86-87). */
+typedef struct {
+    int32_t B, H, W, Cin;
+    int32_t Cout, kh, kw, stride, pad;
+    int32_t Ho, Wo; /* 0 -> derived from the standard formula */
+    int32_t gelu;
+    int32_t kind;
+} gs_conv_desc;
+
+int gs_conv2d(const gs_conv_desc *d, const void *in_bf16, const void *w_bf16, const float *bias, void *out_bf16,
+              double *gn_stats, int *err_flag, void *stream);
+
+/* EfficientGaussianEncoder, variant 'adaptive' (efficient_encoder.py:200-378) with d_feature 256,
+ * stride 8, fine_stride 4, GroupNorm, gradient input: the released checkpoint's architecture. */
+typedef struct {
+    int32_t B, H, W;           /* image batch [B][3][H][W], H and W multiples of 8 */
+    int32_t d;                 /* d_feature (256) */
+    int32_t M, Mf;             /* coarse / fine splats per cell (1..2) */
+    int32_t residual_grid;     /* resolution of the internal coarse render */
+    int32_t odds;              /* odds compositing of the internal render */
+    int32_t use_rotation;      /* theta heads present */
+    float coarse_ls_floor;     /* softplus^-1(coarse_min_scale), or -inf for none */
+    float coarse_offset, fine_offset; /* offset_cells of the two heads */
+    float coarse_min_opacity;  /* coarse opacity floor */
+} gs_encoder_desc;
+
+/* Device pointers of the packed weights (see gaussian_2d_splat_encoder_b200/efficient_encoder.py):
+ * w1 bf16 [64][256] (first layer on the space-to-depth input), w2 bf16 [128][576], w3 bf16 [256][1152],
+ * w4 bf16 [128][3456] (decoder), fp32 biases and GroupNorm affine parameters, bg head [3][256] + [3],
+ * coarse head [9*M][257] + [9*M], fine head [9*Mf][133] + [9*Mf] (rows: mu, scale, colour, opacity,
+ * theta). */
+typedef struct {
+    const void *w1, *w2, *w3, *w4;
+    const float *b1, *b2, *b3, *b4;
+    const float *gn1_w, *gn1_b, *gn2_w, *gn2_b, *gn3_w, *gn3_b, *gn4_w, *gn4_b;
+    const float *bg_w, *bg_b, *hc_w, *hc_b, *hf_w, *hf_b;
+} gs_encoder_weights;
+
+size_t gs_encoder_workspace_size(const gs_encoder_desc *e);
+
+/* Encoder forward of a batch: outputs in the reference's layouts with N = 2*(H/8)(W/8)*M/2... precisely
+ * N = (H/8)(W/8)M + (H/4)(W/4)Mf splats per image ordered [coarse | fine], cell-major then slot:
+ * mu [B][N][2], log_scale [B][N][2], color [B][N][3], opacity [B][N], theta [B][N] (if use_rotation),
+ * bg [B][3]; features (optional) receives backbone_features as NHWC fp32 [B][H/8][W/8][256].
+ * Replaces EfficientGaussianEncoder.forward (efficient_encoder.py:306-378), including its internal
+ * render_alpha_octave call. */
+int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights *w, const float *image, float *mu,
+                   float *log_scale, float *color, float *opacity, float *theta, float *bg, float *features,
+                   void *workspace, size_t workspace_bytes, void *stream);
+
+/* Reads (synchronously) the bounded-wait error flag left in an encoder workspace (0 = none). */
+int gs_encoder_error_flag(const gs_encoder_desc *e, const void *workspace, int *flag_host);
+
 /* activate_scale (params.py:18-28): out = softplus(log_scale) + 1e-4, n elements. */
 int gs_activate_scale(const float *log_scale, float *out, int64_t n, void *stream);
 
@@ -111,10 +171,12 @@ const char *gs_last_error(void);
  * read it before and after a timed region to report their launch count. */
 uint64_t gs_kernel_launches(void);
 
-/* Device-time profiling of the render stages.  While enabled, gs_render_fwd/bwd record CUDA events
- * on their stream around each stage; gs_profile_collect waits for them and returns per-stage totals
- * (ms) and call counts in slots 0 binning (preprocess..tile ranges), 1 fields forward, 2 composite,
- * 3 composite backward + upsample adjoint, 4 fields backward, 5 finalize (arrays of 8). */
+/* Device-time profiling of library stages.  While enabled, the entry points record CUDA events on
+ * their stream around each stage; gs_profile_collect waits for them and returns per-stage totals (ms)
+ * and call counts (arrays of 16): 0 binning (preprocess..tile ranges), 1 fields forward, 2 composite,
+ * 3 composite backward + upsample adjoint, 4 fields backward, 5 finalize, 8 encoder input preparation,
+ * 9..12 encoder convolutions 1..4, 13 encoder heads, 14 encoder GroupNorm/concat/cond, 15 the
+ * encoder's internal coarse render. */
 void gs_profile_enable(int on);
 int gs_profile_collect(double *ms_out, int64_t *count_out);
 
