@@ -133,46 +133,44 @@ class EncodeRenderWorkload:
     def __init__(self, dev, rank=0, world=1):
         import torch
 
-        from gaussian_2d_splat_encoder_b200 import synth
-        from gaussian_2d_splat_encoder_b200 import render_triton as rt
+        from gaussian_2d_splat_encoder_b200 import pipeline, synth
 
-        self.torch, self.rt, self.dev = torch, rt, dev
+        self.torch, self.dev = torch, dev
         self.enc, self.wdesc = _load_encoder(dev)
         mine = self.SEEDS[rank::world] or self.SEEDS[:1]
         imgs = [synth.synth_card(self.H, self.W, 500, 150, s) for s in mine]
         self.host = [x.contiguous().pin_memory() for x in imgs]
         self.dev_imgs = [x.to(dev) for x in imgs]
+        self.pipe = pipeline.EncodeRender(self.enc, 1, self.H, self.W, dev)
         self.i = 0
 
-    def _run(self, x):
-        torch = self.torch
-        with torch.inference_mode():
-            out = self.enc(x)
-            rec = self.rt.render_alpha_octave(out["mu"], out["log_scale"], out["color"], out["opacity"], out["bg"],
-                                              self.H, self.W, theta=out["theta"], odds=self.enc.odds)
-        return rec
+    def capture(self, profile=False):
+        self.pipe.x.copy_(self.dev_imgs[0])
+        self.pipe.capture(profile)
+
+    def stage(self):
+        """Put the next image into the pipeline's input buffer (outside the timed events)."""
+        self.pipe.x.copy_(self.dev_imgs[self.i % len(self.dev_imgs)], non_blocking=True)
+        self.i += 1
 
     def step(self):
-        x = self.dev_imgs[self.i % len(self.dev_imgs)]
-        self.i += 1
-        return self._run(x)
+        return self.pipe.replay()
 
     def e2e_buffers(self):
         return self.torch.empty(1, 3, self.H, self.W).pin_memory()
 
     def e2e_step(self, buf):
-        x = self.host[self.i % len(self.host)].to(self.dev, non_blocking=True)
+        rec = self.pipe(self.host[self.i % len(self.host)])     # H2D from pinned memory + replay
         self.i += 1
-        rec = self._run(x)
-        buf.copy_(rec, non_blocking=True)
+        buf.copy_(rec, non_blocking=True)                       # D2H of the reconstruction
 
     def io_bytes(self):
         return 3 * self.H * self.W * 4, 3 * self.H * self.W * 4
 
     def config(self):
         return {"workload": "configs 2/3: 768x768 test cards (seeds 100-163), EfficientGaussianEncoder (bf16, "
-                            "tcgen05) + render_alpha_octave(odds) fp32, inference", "images_per_step_per_gpu": 1,
-                "encoder_weights": self.wdesc, "H": self.H, "W": self.W,
+                            "tcgen05) + render_alpha_octave(odds) fp32, inference, one CUDA graph per step",
+                "images_per_step_per_gpu": 1, "encoder_weights": self.wdesc, "H": self.H, "W": self.W,
                 "splats_per_image": (self.H // 8) ** 2 * 2 + (self.H // 4) ** 2 * 2,
                 "l2": "flushed between timed steps (256 MB write, outside the timed events)"}
 
@@ -209,24 +207,24 @@ class RenderWorkload:
     def __init__(self, dev, rank=0, world=1):
         import torch
 
-        from gaussian_2d_splat_encoder_b200 import synth
-        from gaussian_2d_splat_encoder_b200 import render_triton as rt
+        from gaussian_2d_splat_encoder_b200 import pipeline, synth
 
-        self.torch, self.rt, self.dev = torch, rt, dev
+        self.torch, self.dev = torch, dev
         s = synth.synth_splats_cfg1(self.N, self.H, self.W, seed=1)
         self.host = {k: v.contiguous().pin_memory() for k, v in s.items()}
         self.keys = ("mu", "log_scale", "color", "opacity", "bg", "theta")
         self.dev_in = {k: v.to(dev) for k, v in s.items()}
-        self.leaves = [self.dev_in[k].clone().requires_grad_(True) for k in self.keys]
+        self.pipe = pipeline.RenderFitStep(self.N, self.H, self.W, dev)
 
-    def step(self, leaves=None, target=None):
-        torch, rt = self.torch, self.rt
-        L = self.leaves if leaves is None else leaves
-        tgt = self.dev_in["target"] if target is None else target
-        out = rt.render_alpha_octave(L[0], L[1], L[2], L[3], L[4], self.H, self.W, theta=L[5], odds=True)
-        loss = torch.nn.functional.mse_loss(out, tgt)
-        grads = torch.autograd.grad(loss, L)
-        return loss, grads
+    def capture(self, profile=False):
+        self.stage()
+        self.pipe.capture(profile)
+
+    def stage(self):
+        self.pipe.load(*[self.dev_in[k] for k in self.keys], self.dev_in["target"])
+
+    def step(self):
+        return self.pipe.replay()
 
     def e2e_buffers(self):
         torch = self.torch
@@ -236,9 +234,8 @@ class RenderWorkload:
 
     def e2e_step(self, out_bufs):
         """Host (pinned) -> device copy of the step's inputs, the step, device -> host of loss + grads."""
-        L = [self.host[k].to(self.dev, non_blocking=True).requires_grad_(True) for k in self.keys]
-        tgt = self.host["target"].to(self.dev, non_blocking=True)
-        loss, grads = self.step(L, tgt)
+        self.pipe.load(*[self.host[k] for k in self.keys], self.host["target"])
+        loss, grads = self.pipe.replay()
         for o, g in zip(out_bufs, grads):
             o.copy_(g, non_blocking=True)
         out_bufs[-1].copy_(loss.detach().reshape(1), non_blocking=True)
@@ -298,10 +295,13 @@ def cpu_baseline(workload_cls, steps: int, budget_s: float = 20.0):
 
 
 # ------------------------------------------------------------------------------------------ GPU timing
-def time_steps(torch, wl, K, flush, lib):
+def time_steps(torch, wl, K, flush):
+    """K graph replays, each bracketed by CUDA events on the replay stream; the L2 flush and the
+    staging of the step's input happen between the events."""
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     for i in range(K):
         flush.zero_()
+        wl.stage()
         ev[i][0].record()
         wl.step()
         ev[i][1].record()
@@ -309,14 +309,28 @@ def time_steps(torch, wl, K, flush, lib):
     return [a.elapsed_time(b) for a, b in ev]
 
 
-def collect_stages(lib):
+def profile_stages(torch, lib, wl_cls, dev, flush, reps=20):
+    """Per-stage device time from CUDA events the library records on its own stream around each stage,
+    captured as event nodes into a separate graph of the same step and read after every replay."""
     from gaussian_2d_splat_encoder_b200 import _lib
 
+    wl = wl_cls(dev)
+    wl.capture(profile=True)
+    acc = {}
     ms = (C.c_double * 16)()
     cnt = (C.c_int64 * 16)()
-    _lib.check(lib.gs_profile_collect(ms, cnt))
-    return {STAGE_NAMES[i]: {"ms_per_call": ms[i] / max(cnt[i], 1), "calls": int(cnt[i])}
-            for i in STAGE_NAMES if cnt[i] > 0}
+    for _ in range(reps):
+        flush.zero_()
+        wl.stage()
+        wl.step()
+        torch.cuda.synchronize()
+        _lib.check(lib.gs_profile_collect2(ms, cnt, 1))
+        for i, n in STAGE_NAMES.items():
+            if cnt[i] > 0:
+                a = acc.setdefault(n, [0.0, int(cnt[i])])
+                a[0] += ms[i]
+    lib.gs_profile_collect2(None, None, 0)
+    return {n: {"ms_per_replay": v[0] / reps, "calls_per_replay": v[1]} for n, v in acc.items()}
 
 
 def main():
@@ -372,18 +386,17 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    wl.capture()
+    per_replay = wl.pipe.launches_per_replay  # our kernels (memsets included) in one graph replay
     for _ in range(W):
+        wl.stage()
         wl.step()
     barrier()
-    lib.gs_profile_enable(1)
-    l0 = lib.gs_kernel_launches()
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     idx = int(vis.split(",")[local]) if vis else local
     with ClockSampler(idx) as clk:
-        step_ms = time_steps(torch, wl, K, flush, lib)
-    launches = lib.gs_kernel_launches() - l0
-    lib.gs_profile_enable(0)
-    stages = collect_stages(lib)
+        step_ms = time_steps(torch, wl, K, flush)
+    launches = per_replay * K
     tot_ms = max_over_ranks(sum(step_ms))
     barrier()
 
@@ -401,18 +414,18 @@ def main():
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
 
-    # secondary metric: config-1 render fwd+bwd ms/image
+    # per-stage device times (separate profiled graph) and the secondary config-1 metric
+    stages = profile_stages(torch, lib, wcls, dev, flush)
     sec = None
     if wcls is not RenderWorkload:
         rw = RenderWorkload(dev)
+        rw.capture()
         for _ in range(3):
+            rw.stage()
             rw.step()
-        torch.cuda.synchronize()
-        lib.gs_profile_enable(1)
-        rms = time_steps(torch, rw, 30, flush, lib)
-        lib.gs_profile_enable(0)
-        rstages = collect_stages(lib)
-        sec = {"render_fwd_bwd_ms_per_image": statistics.mean(rms), "stages_ms": rstages}
+        rms = time_steps(torch, rw, 50, flush)
+        sec = {"render_fwd_bwd_ms_per_image": statistics.mean(rms),
+               "stages_ms": profile_stages(torch, lib, RenderWorkload, dev, flush)}
     barrier()
 
     images = K * world
@@ -434,7 +447,7 @@ def main():
     if wcls is EncodeRenderWorkload:
         # dominant kernel: the decoder convolution (tensor-bound): 2*M*N*K flops per launch
         M, N, Kd = (wl.H // 4) * (wl.W // 4), 128, 9 * 384
-        t = stages.get("conv4_decoder", {}).get("ms_per_call", 0.0)
+        t = stages.get("conv4_decoder", {}).get("ms_per_replay", 0.0)
         ach = 2.0 * M * N * Kd / (t * 1e-3) / 1e12 if t > 0 else None
         line["roofline"] = {"bound": "tensor", "kernel": "k_conv_tc<128,64,4> (decoder 3x3 384->128 @192^2)",
                             "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
@@ -445,7 +458,7 @@ def main():
         line["render_stages_ms"] = sec["stages_ms"] if sec else None
     else:
         line["render_fwd_bwd_ms_per_image"] = tot_ms / K
-        fw = stages.get("fields_bwd", {}).get("ms_per_call", 0.0)
+        fw = stages.get("fields_bwd", {}).get("ms_per_replay", 0.0)
         pairs = 850839  # (tile, splat) pairs of config 1 (reported by the binning; fixed by the seed)
         pp = pairs * 64
         fp32_peak = 148 * 128 * f_mhz * 1e6 / 1e9

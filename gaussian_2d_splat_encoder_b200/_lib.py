@@ -54,6 +54,7 @@ SIGNATURES = {
     "gs_kernel_launches": (C.c_uint64, []),
     "gs_profile_enable": (None, [C.c_int]),
     "gs_profile_collect": (C.c_int, [_P, _P]),
+    "gs_profile_collect2": (C.c_int, [_P, _P, C.c_int]),
     "gs_build_arch": (C.c_int, []),
 }
 

@@ -13,24 +13,32 @@ enum {
 };
 
 bool gs_prof_on();
-void gs_prof_push(int region, cudaEvent_t a, cudaEvent_t b);
+// Takes an event pair from a pre-created pool (NULL events when the pool is exhausted).
+void gs_prof_take(int region, cudaEvent_t *a, cudaEvent_t *b);
 void gs_count_launch(unsigned long long n);
+
+// Records on a capturing stream become external event-record nodes of the graph, so a graph replay
+// re-records them and gs_profile_collect reads the last replay's durations.
+inline void gs_prof_record(cudaEvent_t e, cudaStream_t s) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(s, &cs);
+    if (cs == cudaStreamCaptureStatusActive) cudaEventRecordWithFlags(e, s, cudaEventRecordExternal);
+    else cudaEventRecord(e, s);
+}
 
 struct ProfScope {
     bool on;
-    int region;
     cudaEvent_t a, b;
     cudaStream_t s;
-    ProfScope(int r, cudaStream_t st) : on(gs_prof_on()), region(r), s(st) {
+    ProfScope(int r, cudaStream_t st) : on(gs_prof_on()), a(nullptr), b(nullptr), s(st) {
         if (!on) return;
-        cudaEventCreate(&a);
-        cudaEventCreate(&b);
-        cudaEventRecord(a, s);
+        gs_prof_take(r, &a, &b);
+        if (!a) { on = false; return; }
+        gs_prof_record(a, s);
     }
     void stop() {
         if (!on) return;
-        cudaEventRecord(b, s);
-        gs_prof_push(region, a, b);
+        gs_prof_record(b, s);
         on = false;
     }
     ~ProfScope() { stop(); }

@@ -48,13 +48,21 @@ struct ProfEvent {
 };
 std::mutex g_prof_mu;
 bool g_prof_on = false;
-std::vector<ProfEvent> g_prof;
+std::vector<ProfEvent> g_prof_pool;  // pre-created events
+size_t g_prof_used = 0;
 }  // namespace
 
 bool gs_prof_on() { return g_prof_on; }
-void gs_prof_push(int region, cudaEvent_t a, cudaEvent_t b) {
+void gs_prof_take(int region, cudaEvent_t *a, cudaEvent_t *b) {
     std::lock_guard<std::mutex> lk(g_prof_mu);
-    g_prof.push_back(ProfEvent{region, a, b});
+    if (g_prof_used >= g_prof_pool.size()) {
+        *a = *b = nullptr;
+        return;
+    }
+    ProfEvent &e = g_prof_pool[g_prof_used++];
+    e.region = region;
+    *a = e.a;
+    *b = e.b;
 }
 void gs_count_launch(unsigned long long n) { GS_COUNT(n); }
 
@@ -1325,32 +1333,46 @@ uint64_t gs_kernel_launches(void) { return __atomic_load_n(&g_launches, __ATOMIC
 
 void gs_profile_enable(int on) {
     std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (on && g_prof_pool.empty()) {
+        g_prof_pool.resize(4096);
+        for (auto &e : g_prof_pool) {
+            cudaEventCreate(&e.a);
+            cudaEventCreate(&e.b);
+            e.region = -1;
+        }
+    }
     g_prof_on = on != 0;
 }
 
-int gs_profile_collect(double *ms_out, int64_t *count_out) {
-    std::vector<ProfEvent> evs;
-    {
-        std::lock_guard<std::mutex> lk(g_prof_mu);
-        evs.swap(g_prof);
-    }
+// Durations of the events recorded since the last collect (or, for events recorded by a CUDA graph,
+// of its last replay); the pool is then recycled unless `keep` is set, in which case the same event
+// slots stay assigned so a captured graph can be replayed and collected again.
+int gs_profile_collect2(double *ms_out, int64_t *count_out, int keep) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
     for (int r = 0; r < PR_N; r++) {
         if (ms_out) ms_out[r] = 0.0;
         if (count_out) count_out[r] = 0;
     }
     int st = GS_OK;
-    for (auto &e : evs) {
+    for (size_t i = 0; i < g_prof_used; i++) {
+        ProfEvent &e = g_prof_pool[i];
         float ms = 0.f;
         cudaError_t err = cudaEventSynchronize(e.b);
         if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e.a, e.b);
-        if (err != cudaSuccess) st = set_cuda_error(err, "gs_profile_collect");
-        if (ms_out) ms_out[e.region] += ms;
-        if (count_out) count_out[e.region] += 1;
-        cudaEventDestroy(e.a);
-        cudaEventDestroy(e.b);
+        if (err != cudaSuccess) {
+            st = set_cuda_error(err, "gs_profile_collect");
+            continue;
+        }
+        if (e.region >= 0 && e.region < PR_N) {
+            if (ms_out) ms_out[e.region] += ms;
+            if (count_out) count_out[e.region] += 1;
+        }
     }
+    if (!keep) g_prof_used = 0;
     return st;
 }
+
+int gs_profile_collect(double *ms_out, int64_t *count_out) { return gs_profile_collect2(ms_out, count_out, 0); }
 
 int gs_build_arch(void) { return 100; }
 

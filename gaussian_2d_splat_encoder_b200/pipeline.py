@@ -1,0 +1,128 @@
+"""CUDA-graph pipelines over the encode-and-render path.
+
+Every kernel of the path is launched from host code (Python wrappers + the C ABI), which costs a few
+microseconds of CPU per launch; at 768^2 the GPU work of one image is well under a millisecond, so an
+eagerly launched step is bound by the host.  These classes capture a whole step once per input shape
+into a CUDA graph and replay it: the same kernels, the same numerics, one launch.
+
+* ``EncodeRender`` -- ``EfficientGaussianEncoder`` forward + ``render_alpha_octave`` of its splats
+  (examples/encode_and_render.py:31-38 of the reference), inference.
+* ``RenderFitStep`` -- ``render_alpha_octave`` forward + an L2 loss + the gradients of the six splat
+  leaves (the fitting step of configs 1 and 4).
+
+Outputs live in static buffers that the next call overwrites; clone them to keep them.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+from .render_triton import render_alpha_octave
+
+
+class EncodeRender:
+    def __init__(self, encoder, batch: int, H: int, W: int, device=None, warmup: int = 2):
+        self.enc = encoder
+        self.dev = torch.device(device) if device is not None else next(encoder.parameters()).device
+        self.shape = (batch, 3, H, W)
+        self.x = torch.zeros(self.shape, device=self.dev)
+        self.graph = None
+        self.out = None
+        self.rec = None
+        self.warmup = warmup
+
+    def _body(self):
+        out = self.enc(self.x)
+        rec = render_alpha_octave(out["mu"], out["log_scale"], out["color"], out["opacity"], out["bg"],
+                                  self.shape[2], self.shape[3], theta=out["theta"], odds=self.enc.odds)
+        return out, rec
+
+    def capture(self, profile: bool = False):
+        """Warm up eagerly, then capture one step.  profile=True captures the library's stage events
+        (gs_profile_enable) into the graph so every replay re-records them."""
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.inference_mode(), torch.cuda.stream(s):
+            for _ in range(self.warmup):
+                self._body()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        L = _lib.load()
+        if profile:
+            L.gs_profile_collect2(None, None, 0)
+            L.gs_profile_enable(1)
+        n0 = L.gs_kernel_launches()
+        with torch.inference_mode(), torch.cuda.graph(self.graph):
+            self.out, self.rec = self._body()
+        self.launches_per_replay = int(L.gs_kernel_launches() - n0)
+        if profile:
+            L.gs_profile_enable(0)
+        return self
+
+    def __call__(self, image: torch.Tensor):
+        """image [B,3,H,W] (device or pinned host memory) -> reconstruction [B,3,H,W] (static buffer).
+        The encoder outputs of the same call are in ``self.out``."""
+        if self.graph is None:
+            self.capture()
+        self.x.copy_(image, non_blocking=True)
+        self.graph.replay()
+        return self.rec
+
+    def replay(self):
+        self.graph.replay()
+        return self.rec
+
+
+class RenderFitStep:
+    def __init__(self, N: int, H: int, W: int, device, batch: int = 1, odds: bool = True, warmup: int = 2):
+        self.dev = torch.device(device)
+        self.H, self.W, self.odds = H, W, odds
+        self.leaves = [torch.zeros(batch, N, 2, device=self.dev), torch.zeros(batch, N, 2, device=self.dev),
+                       torch.zeros(batch, N, 3, device=self.dev), torch.zeros(batch, N, device=self.dev),
+                       torch.zeros(batch, 3, device=self.dev), torch.zeros(batch, N, device=self.dev)]
+        for t in self.leaves:
+            t.requires_grad_(True)
+        self.target = torch.zeros(batch, 3, H, W, device=self.dev)
+        self.graph = None
+        self.warmup = warmup
+
+    def load(self, mu, log_scale, color, opacity, bg, theta, target):
+        with torch.no_grad():
+            for dst, src in zip(self.leaves, (mu, log_scale, color, opacity, bg, theta)):
+                dst.copy_(src, non_blocking=True)
+            self.target.copy_(target, non_blocking=True)
+
+    def _body(self):
+        L = self.leaves
+        out = render_alpha_octave(L[0], L[1], L[2], L[3], L[4], self.H, self.W, theta=L[5], odds=self.odds)
+        loss = F.mse_loss(out, self.target)
+        grads = torch.autograd.grad(loss, L)
+        return loss, grads
+
+    def capture(self, profile: bool = False):
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(self.warmup):
+                self._body()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        L = _lib.load()
+        if profile:
+            L.gs_profile_collect2(None, None, 0)
+            L.gs_profile_enable(1)
+        n0 = L.gs_kernel_launches()
+        with torch.cuda.graph(self.graph):
+            self.loss, self.grads = self._body()
+        self.launches_per_replay = int(L.gs_kernel_launches() - n0)
+        if profile:
+            L.gs_profile_enable(0)
+        return self
+
+    def replay(self):
+        if self.graph is None:
+            self.capture()
+        self.graph.replay()
+        return self.loss, self.grads

@@ -179,6 +179,9 @@ uint64_t gs_kernel_launches(void);
  * encoder's internal coarse render. */
 void gs_profile_enable(int on);
 int gs_profile_collect(double *ms_out, int64_t *count_out);
+/* As gs_profile_collect; keep != 0 leaves the event slots assigned (for a captured CUDA graph that
+ * records them on every replay). */
+int gs_profile_collect2(double *ms_out, int64_t *count_out, int keep);
 
 /* Library version and the compute capability it was built for (100 = sm_100a). */
 int gs_build_arch(void);
