@@ -341,6 +341,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="encode_render")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="warm-up + K graph replays and nothing else (for ncu launch lists)")
     args = ap.parse_args()
     W = max(3, args.warmup)
     K = max(1, args.steps)
@@ -392,6 +394,11 @@ def main():
         wl.stage()
         wl.step()
     barrier()
+    if args.kernels_only:
+        time_steps(torch, wl, K, flush)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     idx = int(vis.split(",")[local]) if vis else local
     with ClockSampler(idx) as clk:
