@@ -266,7 +266,118 @@ class RenderWorkload:
                               theta=s["theta"], odds=True, grad_out=g)
 
 
-WORKLOADS = {"encode_render": EncodeRenderWorkload, "render": RenderWorkload}
+class FitWorkload:
+    """Config 4: fitting loop on one 2048x2048 card (seed 4) with 655,360 splats initialised by the encoder.
+    Rank r renders native rows [r*H/R, (r+1)*H/R) (render_alpha_octave row_band), the L2 loss is normalised
+    by the global pixel count, the splat-parameter gradients (9 floats per splat + bg) are summed across
+    ranks with one NCCL all-reduce, and every rank applies the same fused Adam step (lr 1e-2).  One step =
+    one CUDA graph replay (render fwd + bwd + all-reduce + Adam)."""
+
+    name = "fit"
+    H = W = 2048
+
+    def __init__(self, dev, rank=0, world=1):
+        import torch
+        import torch.distributed as dist
+
+        from gaussian_2d_splat_encoder_b200 import synth
+
+        self.torch, self.dev, self.rank, self.world = torch, dev, rank, world
+        self.dist = dist if world > 1 else None
+        enc, self.wdesc = _load_encoder(dev)
+        img = synth.card_for_config(4).to(dev)
+        with torch.inference_mode():
+            o = enc(img)
+        self.keys = ("mu", "log_scale", "color", "opacity", "bg", "theta")
+        self.init = {k: o[k].clone() for k in self.keys}
+        self.leaves = [self.init[k].clone().requires_grad_(True) for k in self.keys]
+        self.target = img.clone()
+        self.N = self.init["mu"].shape[1]
+        from gaussian_2d_splat_encoder_b200 import shard
+
+        self.band = shard.row_bands(self.H, world)[rank]
+        self.opt = torch.optim.Adam(self.leaves, lr=1e-2, fused=True, capturable=True)
+        self.flat = torch.zeros(sum(t.numel() for t in self.leaves), device=dev)
+        self.graph = None
+
+        class _P:  # launches_per_replay holder, like the pipelines
+            pass
+
+        self.pipe = _P()
+
+    def _body(self):
+        from gaussian_2d_splat_encoder_b200 import shard
+
+        L = self.leaves
+        out = self.rt.render_alpha_octave(L[0], L[1], L[2], L[3], L[4], self.H, self.W, theta=L[5], odds=True,
+                                          row_band=self.band)
+        loss = shard.band_mse(out, self.target, self.band, self.H, self.W)
+        grads = self.torch.autograd.grad(loss, L)
+        for t, g in zip(L, shard.allreduce_grads(grads, self.flat)):
+            t.grad = g
+        self.opt.step()
+        return loss
+
+    def capture(self, profile=False):
+        torch = self.torch
+        from gaussian_2d_splat_encoder_b200 import _lib
+        from gaussian_2d_splat_encoder_b200 import render_triton as rt
+
+        self.rt = rt
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._body()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        L = _lib.load()
+        if profile:
+            L.gs_profile_collect2(None, None, 0)
+            L.gs_profile_enable(1)
+        n0 = L.gs_kernel_launches()
+        with torch.cuda.graph(self.graph):
+            self.loss = self._body()
+        self.pipe.launches_per_replay = int(L.gs_kernel_launches() - n0)
+        self.pipe.graph = self.graph
+        if profile:
+            L.gs_profile_enable(0)
+
+    def stage(self):
+        pass
+
+    def step(self):
+        self.graph.replay()
+        return self.loss
+
+    def reset(self):
+        with self.torch.no_grad():
+            for t, k in zip(self.leaves, self.keys):
+                t.copy_(self.init[k])
+
+    def e2e_buffers(self):
+        return self.torch.empty(1).pin_memory()
+
+    def e2e_step(self, buf):
+        self.graph.replay()
+        buf.copy_(self.loss.detach().reshape(1), non_blocking=True)
+
+    def io_bytes(self):
+        return 0, 4
+
+    def config(self):
+        return {"workload": "config 4: 2048x2048 card (seed 4), 655,360 encoder-initialised splats, render_alpha_octave"
+                            "(odds) fwd+bwd on a native-row band per rank, NCCL all-reduce of the splat gradients, "
+                            "fused Adam lr 1e-2; one CUDA graph per step", "splats": self.N, "H": self.H,
+                "W": self.W, "band_rows": list(self.band), "encoder_weights": self.wdesc,
+                "l2": "flushed between timed steps (256 MB write, outside the timed events)"}
+
+    def release(self):
+        self.graph = None
+        self.pipe.graph = None
+
+
+WORKLOADS = {"encode_render": EncodeRenderWorkload, "render": RenderWorkload, "fit": FitWorkload}
 
 
 # ------------------------------------------------------------------------------------------ CPU side
@@ -309,12 +420,34 @@ def time_steps(torch, wl, K, flush):
     return [a.elapsed_time(b) for a, b in ev]
 
 
-def profile_stages(torch, lib, wl_cls, dev, flush, reps=20):
+def count_pairs(torch, lib, dev, ins, H, W, row_band=None):
+    """(tile, splat) pairs of one octave-odds render of `ins` (read back from the binning)."""
+    from gaussian_2d_splat_encoder_b200 import _lib
+    from gaussian_2d_splat_encoder_b200.render_triton import _desc
+
+    keys = ("mu", "log_scale", "color", "opacity", "bg", "theta")
+    f = [ins[k].detach().contiguous().float() for k in keys]
+    B, N = f[0].shape[0], f[0].shape[1]
+    d = _desc(mode=_lib.MODE_OCTAVE, B=B, N=N, C=3, H=H, W=W, TILE=8, odds=True, has_theta=True, cutoff=3.0,
+              base_texels=8.0, max_octaves=6, max_pairs=-1, row_band=row_band)
+    d.pair_capacity = lib.gs_render_pair_bound(C.byref(d))
+    nb = lib.gs_render_workspace_size(C.byref(d), 0)
+    ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+    out = torch.empty(B, 3, H, W, device=dev)
+    _lib.check(lib.gs_render_fwd(C.byref(d), *[_lib.ptr(t) for t in f], _lib.ptr(out), _lib.ptr(ws), nb,
+                                 _lib.stream_of(dev)))
+    torch.cuda.synchronize()
+    tot = C.c_int64(0)
+    _lib.check(lib.gs_render_debug_bins(C.byref(d), _lib.ptr(ws), C.byref(tot), None, None, None, None, None))
+    return int(tot.value)
+
+
+def profile_stages(torch, lib, wl_cls, dev, flush, reps=20, rank=0, world=1):
     """Per-stage device time from CUDA events the library records on its own stream around each stage,
     captured as event nodes into a separate graph of the same step and read after every replay."""
     from gaussian_2d_splat_encoder_b200 import _lib
 
-    wl = wl_cls(dev)
+    wl = wl_cls(dev, rank, world)
     wl.capture(profile=True)
     acc = {}
     ms = (C.c_double * 16)()
@@ -330,6 +463,8 @@ def profile_stages(torch, lib, wl_cls, dev, flush, reps=20):
                 a = acc.setdefault(n, [0.0, int(cnt[i])])
                 a[0] += ms[i]
     lib.gs_profile_collect2(None, None, 0)
+    if hasattr(wl, "release"):
+        wl.release()
     return {n: {"ms_per_replay": v[0] / reps, "calls_per_replay": v[1]} for n, v in acc.items()}
 
 
@@ -396,6 +531,8 @@ def main():
     barrier()
     if args.kernels_only:
         time_steps(torch, wl, K, flush)
+        if hasattr(wl, "release"):
+            wl.release()
         if world > 1:
             dist.destroy_process_group()
         return
@@ -422,9 +559,9 @@ def main():
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
 
     # per-stage device times (separate profiled graph) and the secondary config-1 metric
-    stages = profile_stages(torch, lib, wcls, dev, flush)
+    stages = profile_stages(torch, lib, wcls, dev, flush, rank=rank, world=world)
     sec = None
-    if wcls is not RenderWorkload:
+    if wcls is EncodeRenderWorkload:
         rw = RenderWorkload(dev)
         rw.capture()
         for _ in range(3):
@@ -464,21 +601,31 @@ def main():
         line["render_fwd_bwd_ms_per_image"] = sec["render_fwd_bwd_ms_per_image"] if sec else None
         line["render_stages_ms"] = sec["stages_ms"] if sec else None
     else:
-        line["render_fwd_bwd_ms_per_image"] = tot_ms / K
+        if wcls is RenderWorkload:
+            line["render_fwd_bwd_ms_per_image"] = tot_ms / K
+            pairs = count_pairs(torch, lib, dev, wl.dev_in, wl.H, wl.W)
+        else:
+            line.update(unit="steps/s", scaling="strong", dtype="fp32",
+                        metric="config 4: 2048^2 fitting step (render fwd+bwd + NCCL all-reduce + Adam) steps/s")
+            line["value"] = K / (tot_ms / 1000.0)
+            line["e2e"]["value"] = Ke / (e2e_ms / 1000.0)
+            line["e2e"]["unit"] = "steps/s"
+            pairs = count_pairs(torch, lib, dev, {k: wl.init[k] for k in wl.keys}, wl.H, wl.W, wl.band)
         fw = stages.get("fields_bwd", {}).get("ms_per_replay", 0.0)
-        pairs = 850839  # (tile, splat) pairs of config 1 (reported by the binning; fixed by the seed)
         pp = pairs * 64
         fp32_peak = 148 * 128 * f_mhz * 1e6 / 1e9
         ach = 40.0 * pp / (fw * 1e-3) / 1e9 if fw > 0 else None
         line["roofline"] = {"bound": "fp32", "kernel": "k_fields_bwd<8,4>", "achieved": ach, "peak": fp32_peak,
                             "unit": "Gop/s (FP32 lane-ops)", "frac": (ach / fp32_peak) if ach else None,
-                            "traffic": None, "units_per_launch": pp, "ops_per_unit": 40,
+                            "traffic": None, "units_per_launch": pp, "ops_per_unit": 40, "pairs": pairs,
                             "peak_source": f"148 SMs x 128 FP32 lanes x {f_mhz:.0f} MHz (median SM clock sampled "
                                            "during the timed region)"}
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wcls, 3)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if hasattr(wl, "release"):
+        wl.release()
     if world > 1:
         dist.destroy_process_group()
 

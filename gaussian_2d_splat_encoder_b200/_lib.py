@@ -32,7 +32,8 @@ class GsRenderDesc(C.Structure):
                 ("H", C.c_int32), ("W", C.c_int32), ("tile", C.c_int32), ("odds", C.c_int32),
                 ("has_theta", C.c_int32), ("max_octaves", C.c_int32), ("n_coarse", C.c_int32),
                 ("coarse_factor", C.c_int32), ("cutoff", C.c_float), ("base_texels", C.c_float),
-                ("max_pairs", C.c_int64), ("pair_capacity", C.c_int64)]
+                ("max_pairs", C.c_int64), ("pair_capacity", C.c_int64), ("row_begin", C.c_int32),
+                ("row_end", C.c_int32)]
 
 
 # every exported symbol of include/gsplat_b200.h, with its ctypes signature
@@ -48,7 +49,7 @@ SIGNATURES = {
     "gs_activate_scale": (C.c_int, [_P, _P, C.c_int64, _P]),
     "gs_conv2d": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P]),
     "gs_encoder_workspace_size": (C.c_size_t, [_P]),
-    "gs_encoder_fwd": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
+    "gs_encoder_fwd": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "gs_encoder_error_flag": (C.c_int, [_P, _P, _P]),
     "gs_last_error": (C.c_char_p, []),
     "gs_kernel_launches": (C.c_uint64, []),

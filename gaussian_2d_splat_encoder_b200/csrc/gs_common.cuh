@@ -38,11 +38,12 @@ struct GroupGeom {
     int ntx, nty;  // tiles
     int tile_off;  // first tile of this group inside an image's tile range
     int fld_off;   // first float of this group's 5 planar fields inside an image's field block
-    int pad0, pad1;
+    int ty_lo, ty_hi;  // tile rows this call needs (the native row band's bilinear footprint)
 };
 
 struct RenderGeom {
     int mode, B, N, C, H, W, tile, odds, has_theta, max_oct, n_coarse, ngroups;
+    int y0, y1;  // native row band
     float cutoff, base_texels, rep;
     int tiles_per_image;
     long long fld_per_image;  // floats of group fields per image

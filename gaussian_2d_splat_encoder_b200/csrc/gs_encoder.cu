@@ -355,6 +355,24 @@ __global__ void __launch_bounds__(256) k_concat(const __nv_bfloat16 *__restrict_
     *reinterpret_cast<uint4 *>(out + pix * Ct + c0) = res;
 }
 
+// GroupNorm(8) applied to NHWC bf16 [B][HW][C] written as NHWC fp32 (the fine decoder's normalised
+// features: splat_features of forward(return_latents=True))
+__global__ void k_gn_to_f32(const __nv_bfloat16 *__restrict__ x, int B, long long HW, int C,
+                            const double *__restrict__ stats, const float *__restrict__ gamma,
+                            const float *__restrict__ beta, float *__restrict__ out) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)B * HW * C) return;
+    int c = (int)(i % C);
+    int b = (int)(i / (HW * C));
+    int g = c / (C / 8);
+    const double n = (double)HW * (C / 8);
+    double mean = stats[(b * 8 + g) * 2] / n;
+    double var = stats[(b * 8 + g) * 2 + 1] / n - mean * mean;
+    if (var < 0) var = 0;
+    float rstd = (float)(1.0 / sqrt(var + 1e-5));
+    out[i] = (__bfloat162float(x[i]) - (float)mean) * rstd * gamma[c] + beta[c];
+}
+
 // NHWC bf16 -> NHWC fp32 (backbone_features output)
 __global__ void k_bf16_to_f32(const __nv_bfloat16 *__restrict__ in, float *__restrict__ out, long long n) {
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -431,7 +449,8 @@ extern "C" size_t gs_encoder_workspace_size(const gs_encoder_desc *e) {
 
 extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights *w, const float *image, float *mu,
                               float *log_scale, float *color, float *opacity, float *theta, float *bg,
-                              float *features, void *workspace, size_t workspace_bytes, void *stream) {
+                              float *features, float *latents, void *workspace, size_t workspace_bytes,
+                              void *stream) {
     EncPlan p;
     int st = enc_plan(e, p);
     if (st != GS_OK) return st;
@@ -547,6 +566,13 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
         long long ncell = (long long)B * p.H4 * p.W4;
         size_t sm = ((size_t)h.nout * h.Cin + h.nout + 2 * h.Cfeat) * 4;
         k_head<<<(unsigned)((ncell + 127) / 128), 128, sm, s>>>(h);
+    }
+    if (latents) {
+        long long n = (long long)B * p.H4 * p.W4 * 128;
+        k_gn_to_f32<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y4), B,
+                                                                (long long)p.H4 * p.W4, 128, stats + 3 * B * 16,
+                                                                w->gn4_w, w->gn4_b, latents);
+        gs_count_launch(1);
     }
     if (features) {
         long long n = (long long)B * p.H8 * p.W8 * 256;

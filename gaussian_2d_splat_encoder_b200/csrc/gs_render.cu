@@ -198,8 +198,10 @@ __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *_
             GroupGeom gg = G.g[g];
             int x0, x1, y0, y1;
             tile_rect(m.x, m.y, sy, sx, gg.H, gg.W, G.tile, G.cutoff, gg.ntx, gg.nty, x0, x1, y0, y1);
+            y0 = max(y0, gg.ty_lo);
+            y1 = min(y1, gg.ty_hi);
             int w = x1 - x0 + 1;
-            count = w * (y1 - y0 + 1);
+            count = y1 >= y0 ? w * (y1 - y0 + 1) : 0;
             mt = make_int4(b * G.tiles_per_image + gg.tile_off + y0 * gg.ntx + x0, w | (g << 24), gg.ntx, count);
         } else {
             mt.y = g << 24;
@@ -619,8 +621,8 @@ __global__ void __launch_bounds__(256) k_composite(RenderGeom G, const float *__
                                                    float *__restrict__ out) {
     const int b = blockIdx.y;
     const long long P = (long long)G.H * G.W;
-    long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (p >= P) return;
+    long long p = (long long)G.y0 * G.W + (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= (long long)G.y1 * G.W) return;
     int y = (int)(p / G.W), x = (int)(p - (long long)y * G.W);
     float S[5];
     gather_sums(G, fields, gsplats, b, p, y, x, S);
@@ -649,9 +651,9 @@ __global__ void __launch_bounds__(256) k_composite_bwd(RenderGeom G, const float
     __shared__ float red[3][8];
     const int b = blockIdx.y;
     const long long P = (long long)G.H * G.W;
-    long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    long long p = (long long)G.y0 * G.W + (long long)blockIdx.x * blockDim.x + threadIdx.x;
     float gT[3] = {0.f, 0.f, 0.f};
-    if (p < P) {
+    if (p < (long long)G.y1 * G.W) {
         const int y = (int)(p / G.W), x = (int)(p - (long long)y * G.W);
         float S[5];
         gather_sums(G, fields, gsplats, b, p, y, x, S);
@@ -724,8 +726,8 @@ __global__ void __launch_bounds__(256) k_adjoint(RenderGeom G, const int *__rest
     if (rg.y <= rg.x) return;
     const long long P = (long long)G.H * G.W;
     const float sy = (float)G.H / (float)Hg, sx = (float)G.W / (float)Wg;
-    const int ylo = max(0, (int)ceilf((i - 0.5f) * sy - 0.5f) - 1);
-    const int yhi = min(G.H - 1, (int)floorf((i + 1.5f) * sy - 0.5f) + 1);
+    const int ylo = max(G.y0, (int)ceilf((i - 0.5f) * sy - 0.5f) - 1);
+    const int yhi = min(G.y1 - 1, (int)floorf((i + 1.5f) * sy - 0.5f) + 1);
     const int xlo = max(0, (int)ceilf((j - 0.5f) * sx - 0.5f) - 1);
     const int xhi = min(G.W - 1, (int)floorf((j + 1.5f) * sx - 0.5f) + 1);
     float acc5[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
@@ -792,7 +794,8 @@ __global__ void __launch_bounds__(NW * 32) k_fields_bwd(RenderGeom G, const Spla
         int yp = ty * TILE + q / TILE, xp = tx * TILE + q % TILE;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         float v4 = 0.f;
-        if (yp < Hg && xp < Wg) {
+        const bool inband = !group_native(G, g) || (yp >= G.y0 && yp < G.y1);
+        if (yp < Hg && xp < Wg && inband) {
             long long p = (long long)yp * Wg + xp;
             v = make_float4(src[p], src[plane + p], src[2 * plane + p], src[3 * plane + p]);
             v4 = src[4 * plane + p];
@@ -936,6 +939,8 @@ int validate(const gs_render_desc *d) {
     if (d->mode == GS_MODE_EXACT && d->odds) return GS_ERR_BAD_ARGUMENT;
     if (!(d->cutoff > 0.0f)) return GS_ERR_BAD_ARGUMENT;
     if ((long long)d->B * d->N >= (1LL << 31)) return GS_ERR_BAD_ARGUMENT;
+    if (d->row_end > 0 && (d->row_begin < 0 || d->row_begin >= d->row_end || d->row_end > d->H))
+        return GS_ERR_BAD_ARGUMENT;
     return GS_OK;
 }
 
@@ -990,6 +995,24 @@ void make_geom(const gs_render_desc *d, RenderGeom &G) {
     }
     G.tiles_per_image = toff;
     G.fld_per_image = foff;
+    G.y0 = std::max(0, d->row_begin);
+    G.y1 = d->row_end > 0 ? std::min(d->H, d->row_end) : d->H;
+    for (int k = 0; k < ng; k++) {
+        GroupGeom &gg = G.g[k];
+        int lo, hi;  // texel rows of group k sampled by native rows [y0, y1) (+1 row of margin)
+        if (gg.H == d->H) {
+            lo = G.y0;
+            hi = G.y1 - 1;
+        } else {
+            double sc = (double)gg.H / (double)d->H;
+            lo = (int)std::floor(sc * (G.y0 + 0.5) - 0.5) - 1;
+            hi = (int)std::floor(sc * (G.y1 - 1 + 0.5) - 0.5) + 2;
+        }
+        lo = std::max(0, lo);
+        hi = std::min(gg.H - 1, hi);
+        gg.ty_lo = lo / T;
+        gg.ty_hi = hi >= lo ? hi / T : -1;
+    }
 }
 
 // per-splat upper bound on the tiles of group g (see gs_render_pair_bound)
@@ -1201,8 +1224,8 @@ int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_sca
         st = launch_fields_fwd(pl, workspace, s);
         if (st != GS_OK) return st;
     }
-    long long P = (long long)d->H * d->W;
-    dim3 cg((unsigned)((P + 255) / 256), (unsigned)d->B);
+    long long Pb = (long long)(G.y1 - G.y0) * d->W;
+    dim3 cg((unsigned)std::max<long long>(1, (Pb + 255) / 256), (unsigned)d->B);
     {
         ProfScope ps(PR_COMPOSITE, s);
         k_composite<<<cg, 256, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,
@@ -1229,8 +1252,8 @@ int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_sca
     cudaError_t e = cudaMemsetAsync(at<char>(workspace, pl.o_bzero), 0, pl.bz_len, s);
     GS_COUNT(1);
     if (e != cudaSuccess) return set_cuda_error(e, "memset");
-    long long P = (long long)d->H * d->W;
-    dim3 cg((unsigned)((P + 255) / 256), (unsigned)d->B);
+    long long Pb = (long long)(G.y1 - G.y0) * d->W;
+    dim3 cg((unsigned)std::max<long long>(1, (Pb + 255) / 256), (unsigned)d->B);
     int clamp_mask = (d->mode == GS_MODE_OCTAVE || d->mode == GS_MODE_MULTIRES) ? 1 : 0;
     std::unique_ptr<ProfScope> cb_scope(new ProfScope(PR_COMPOSITE_BWD, s));
     k_composite_bwd<<<cg, 256, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,

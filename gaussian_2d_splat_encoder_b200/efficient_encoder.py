@@ -307,8 +307,6 @@ class EfficientGaussianEncoder(nn.Module):
         if not self._cuda_supported():
             raise NotImplementedError("the CUDA encoder implements the released 'adaptive' architecture "
                                       "(d_feature=256, stride 8, fine_stride 4, GroupNorm, gradient input)")
-        if return_latents:
-            raise NotImplementedError("return_latents is not implemented by the CUDA encoder yet")
         dev = _lib.require_cuda(image)
         if image.dim() != 4 or image.shape[1] != 3:
             raise ValueError("image must be [B,3,H,W]")
@@ -331,12 +329,15 @@ class EfficientGaussianEncoder(nn.Module):
                      theta=torch.empty(B, N, device=dev) if self.use_rotation else None,
                      bg=torch.empty(B, 3, device=dev))
             feat = torch.empty(B, H // 8, W // 8, self.d_feature, device=dev)
+            lat = torch.empty(B, H // 4, W // 4, self.fine_decoder.out_ch, device=dev) if return_latents else None
             ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
             p = _lib.ptr
             _lib.check(L.gs_encoder_fwd(C.byref(d), C.byref(wst), p(x), p(o["mu"]), p(o["log_scale"]), p(o["color"]),
-                                        p(o["opacity"]), p(o["theta"]), p(o["bg"]), p(feat), p(ws), nbytes,
+                                        p(o["opacity"]), p(o["theta"]), p(o["bg"]), p(feat), p(lat), p(ws), nbytes,
                                         _lib.stream_of(dev)), "gs_encoder_fwd")
         o["n_gaussians"] = N
         o["n_coarse"] = Nc
         o["backbone_features"] = feat.permute(0, 3, 1, 2)
+        if return_latents:
+            o["splat_features"] = lat.permute(0, 3, 1, 2)
         return o

@@ -35,7 +35,7 @@ _BOUND_SYNC_THRESHOLD = 1 << 26
 
 
 def _desc(mode, B, N, C, H, W, TILE, odds, has_theta, cutoff, base_texels=8.0, max_octaves=6, n_coarse=-1,
-          coarse_factor=8, max_pairs=-1, capacity=0):
+          coarse_factor=8, max_pairs=-1, capacity=0, row_band=None):
     d = _lib.GsRenderDesc()
     d.mode, d.B, d.N, d.C, d.H, d.W = int(mode), int(B), int(N), int(C), int(H), int(W)
     d.tile, d.odds, d.has_theta = int(TILE), int(bool(odds)), int(bool(has_theta))
@@ -43,6 +43,8 @@ def _desc(mode, B, N, C, H, W, TILE, odds, has_theta, cutoff, base_texels=8.0, m
     d.cutoff, d.base_texels = float(cutoff), float(base_texels)
     d.max_pairs = -1 if max_pairs is None else int(max_pairs)
     d.pair_capacity = int(capacity)
+    if row_band is not None:
+        d.row_begin, d.row_end = int(row_band[0]), int(row_band[1])
     return d
 
 
@@ -143,17 +145,22 @@ def _render(mode, mu, log_scale, color, opacity, bg, H, W, theta, kw):
 
 
 def render_alpha_octave(mu, log_scale, color, opacity, bg, H, W, theta=None, cutoff=3.0, TILE=8,
-                        base_texels=8.0, max_octaves=6, max_pairs=48_000_000, odds=False):
+                        base_texels=8.0, max_octaves=6, max_pairs=48_000_000, odds=False, row_band=None):
     """Memory-bounded differentiable render with scale-routed octave LOD (render_triton.py:935-980).
 
     Each splat renders at octave o = clamp(ceil(log2(max(sigma_px / base_texels, 1e-6))), 0, max_octaves)
     at resolution max(8, H >> o) x max(8, W >> o); the octaves' raw sums are bilinearly upsampled
     (align_corners=False), summed and composited once with bg.  Returns [B,C,H,W] float32.
-    Raises PairBudgetExceeded when one image's octave would hold more than max_pairs pairs."""
+    Raises PairBudgetExceeded when one image's octave would hold more than max_pairs pairs.
+
+    row_band=(y0, y1) (an extension for tile-row sharding across GPUs) renders only native rows
+    [y0, y1): only the splats whose footprint reaches those rows are binned, output rows outside the band
+    are left unwritten, and the backward reads grad_out only inside the band, so the gradients are the
+    band's partial sums (summing them over a partition of the rows gives the full gradient)."""
     if not 0 <= int(max_octaves) <= 7:
         raise ValueError("max_octaves must be in 0..7")
     kw = dict(TILE=TILE, odds=odds, cutoff=cutoff, base_texels=base_texels, max_octaves=max_octaves,
-              max_pairs=max_pairs)
+              max_pairs=max_pairs, row_band=row_band)
     return _render(_lib.MODE_OCTAVE, mu, log_scale, color, opacity, bg, H, W, theta, kw)
 
 

@@ -59,6 +59,9 @@ typedef struct {
     float base_texels;     /* octave mode (reference default 8.0) */
     int64_t max_pairs;     /* per (image, group) pair budget; < 0 disables the check */
     int64_t pair_capacity; /* pairs the workspace holds for the whole batch; 0 -> gs_render_pair_bound */
+    int32_t row_begin;     /* native row band [row_begin, row_end) this call renders (tile-row sharding); */
+    int32_t row_end;       /* row_end <= 0 -> all rows.  Output rows outside the band are not written and
+                              the backward reads grad_out only inside it. */
 } gs_render_desc;
 
 /* Upper bound on the (tile, splat) pairs of the whole batch, computed on the host from the
@@ -151,12 +154,14 @@ size_t gs_encoder_workspace_size(const gs_encoder_desc *e);
 /* Encoder forward of a batch: outputs in the reference's layouts with N = 2*(H/8)(W/8)*M/2... precisely
  * N = (H/8)(W/8)M + (H/4)(W/4)Mf splats per image ordered [coarse | fine], cell-major then slot:
  * mu [B][N][2], log_scale [B][N][2], color [B][N][3], opacity [B][N], theta [B][N] (if use_rotation),
- * bg [B][3]; features (optional) receives backbone_features as NHWC fp32 [B][H/8][W/8][256].
+ * bg [B][3]; features (optional) receives backbone_features as NHWC fp32 [B][H/8][W/8][256]; latents
+ * (optional) receives the normalised fine-decoder features, NHWC fp32 [B][H/4][W/4][128]
+ * (splat_features of forward(return_latents=True)).
  * Replaces EfficientGaussianEncoder.forward (efficient_encoder.py:306-378), including its internal
  * render_alpha_octave call. */
 int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights *w, const float *image, float *mu,
                    float *log_scale, float *color, float *opacity, float *theta, float *bg, float *features,
-                   void *workspace, size_t workspace_bytes, void *stream);
+                   float *latents, void *workspace, size_t workspace_bytes, void *stream);
 
 /* Reads (synchronously) the bounded-wait error flag left in an encoder workspace (0 = none). */
 int gs_encoder_error_flag(const gs_encoder_desc *e, const void *workspace, int *flag_host);

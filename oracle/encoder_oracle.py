@@ -108,6 +108,7 @@ def encode(state_dict, cfg: dict, image: torch.Tensor) -> dict:
     out["n_gaussians"] = out["mu"].shape[1]
     out["n_coarse"] = coarse["mu"].shape[1]
     out["backbone_features"] = s8
+    out["splat_features"] = fine_feat
     out["coarse_render"] = c_render
     return out
 

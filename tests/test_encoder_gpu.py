@@ -91,3 +91,26 @@ def test_reconstruction_psnr_gate(lib, card):
 
 def Path_stem(p):
     return p.rsplit("/", 1)[-1].rsplit(".", 1)[0]
+
+
+def test_return_latents_and_gather(lib):
+    """forward(return_latents=True) exposes the normalised fine-decoder map; gather_splat_latents aligns it
+    with the splat axis (coarse splats -> zeros) (efficient_encoder.py:270-296)."""
+    from gaussian_2d_splat_encoder_b200.efficient_encoder import EfficientGaussianEncoder
+    from oracle import encoder_oracle as E
+
+    torch.manual_seed(0)
+    m = EfficientGaussianEncoder(**GOLDEN_CFG).eval()
+    x = torch.from_numpy(np.load(GOLDEN / "encoder_cfg0.npz")["image"])
+    ref = E.encode(m.state_dict(), GOLDEN_CFG, x)
+    m = m.cuda()
+    with torch.no_grad():
+        o = m(x.cuda(), return_latents=True)
+    sf = o["splat_features"].float().cpu()
+    r = ref["splat_features"]
+    assert sf.shape == r.shape
+    rel = float((sf - r).square().mean().sqrt() / r.square().mean().sqrt())
+    assert rel < 0.03, rel
+    lat = m.gather_splat_latents(o)
+    assert lat.shape == (1, o["n_gaussians"], 128)
+    assert float(lat[:, :o["n_coarse"]].abs().max()) == 0.0
