@@ -306,13 +306,10 @@ class FitWorkload:
         self.pipe = _P()
 
     def _body(self):
-        from gaussian_2d_splat_encoder_b200 import shard
+        from gaussian_2d_splat_encoder_b200 import pipeline, shard
 
         L = self.leaves
-        out = self.rt.render_alpha_octave(L[0], L[1], L[2], L[3], L[4], self.H, self.W, theta=L[5], odds=True,
-                                          row_band=self.band)
-        loss = shard.band_mse(out, self.target, self.band, self.H, self.W)
-        grads = self.torch.autograd.grad(loss, L)
+        loss, grads = pipeline.render_l2_grads(L, self.target, self.H, self.W, True, self.band)
         for t, g in zip(L, shard.allreduce_grads(grads, self.flat)):
             t.grad = g
         self.opt.step()

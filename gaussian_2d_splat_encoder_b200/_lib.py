@@ -47,6 +47,8 @@ SIGNATURES = {
     "gs_render_bwd": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "gs_render_debug_bins": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P]),
     "gs_activate_scale": (C.c_int, [_P, _P, C.c_int64, _P]),
+    "gs_l2_loss_grad": (C.c_int, [_P, _P, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_float, _P, _P,
+                                  _P]),
     "gs_conv2d": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P]),
     "gs_encoder_workspace_size": (C.c_size_t, [_P]),
     "gs_encoder_fwd": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),

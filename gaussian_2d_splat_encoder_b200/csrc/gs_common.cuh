@@ -39,6 +39,9 @@ struct GroupGeom {
     int tile_off;  // first tile of this group inside an image's tile range
     int fld_off;   // first float of this group's 5 planar fields inside an image's field block
     int ty_lo, ty_hi;  // tile rows this call needs (the native row band's bilinear footprint)
+    float up_sy, up_sx;  // bilinear source-index scales group/native, (float)Hg / (float)H as torch computes
+    int adj_off;         // first texel of this group in the adjoint launch (coarse groups only), -1 if none
+    int pad;
 };
 
 struct RenderGeom {

@@ -393,9 +393,13 @@ __global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep(const unsigned *
 #pragma unroll
         for (int r = 0; r < RS_ROUNDS; r++) {
             const long long i = base + r * 32 + lane;
+            key[r] = i < n ? __ldg(kin + i) : 0u;
+            val[r] = i < n ? __ldg(vin + i) : 0;
+        }
+#pragma unroll
+        for (int r = 0; r < RS_ROUNDS; r++) {
+            const long long i = base + r * 32 + lane;
             const bool valid = i < n;
-            key[r] = valid ? kin[i] : 0u;
-            val[r] = valid ? vin[i] : 0;
             const int d = valid ? (int)((key[r] >> shift) & mask) : -1;
             dig[r] = d;
             const unsigned peers = __match_any_sync(0xffffffffu, d);
@@ -563,6 +567,19 @@ __global__ void __launch_bounds__(NW * 32) k_fields_fwd(RenderGeom G, const Spla
 // ----------------------------------------------------------------------------------------------------
 // bilinear upsample with torch's align_corners=False source-index rule
 
+__device__ __forceinline__ void lin_index_s(int d, int in_size, float scale, int &i0, int &i1, float &l0, float &l1) {
+    float src = __fsub_rn(__fmul_rn(scale, __fadd_rn((float)d, 0.5f)), 0.5f);
+    if (src < 0.0f) src = 0.0f;
+    int i = (int)src;
+    if (i > in_size - 1) i = in_size - 1;
+    int ip = (i < in_size - 1) ? 1 : 0;
+    float lam = fminf(fmaxf(src - (float)i, 0.0f), 1.0f);
+    i0 = i;
+    i1 = i + ip;
+    l1 = lam;
+    l0 = 1.0f - lam;
+}
+
 __device__ __forceinline__ void lin_index(int d, int in_size, int out_size, int &i0, int &i1, float &l0, float &l1) {
     float scale = __fdiv_rn((float)in_size, (float)out_size);
     float src = __fsub_rn(__fmul_rn(scale, __fadd_rn((float)d, 0.5f)), 0.5f);
@@ -602,13 +619,14 @@ __device__ __forceinline__ void gather_sums(const RenderGeom &G, const float *__
         } else {
             int y0, y1, x0, x1;
             float h0, h1, w0, w1;
-            lin_index(y, Hg, G.H, y0, y1, h0, h1);
-            lin_index(x, Wg, G.W, x0, x1, w0, w1);
+            lin_index_s(y, Hg, G.g[g].up_sy, y0, y1, h0, h1);
+            lin_index_s(x, Wg, G.g[g].up_sx, x0, x1, w0, w1);
+            const long long a00 = (long long)y0 * Wg + x0, a01 = (long long)y0 * Wg + x1;
+            const long long a10 = (long long)y1 * Wg + x0, a11 = (long long)y1 * Wg + x1;
 #pragma unroll
             for (int c = 0; c < 5; c++) {
                 const float *fc = f + c * plane;
-                float v = h0 * (w0 * fc[(long long)y0 * Wg + x0] + w1 * fc[(long long)y0 * Wg + x1]) +
-                          h1 * (w0 * fc[(long long)y1 * Wg + x0] + w1 * fc[(long long)y1 * Wg + x1]);
+                float v = h0 * (w0 * fc[a00] + w1 * fc[a01]) + h1 * (w0 * fc[a10] + w1 * fc[a11]);
                 S[c] += v;
             }
         }
@@ -706,47 +724,51 @@ __global__ void __launch_bounds__(256) k_adjoint(RenderGeom G, const int *__rest
                                                  const int2 *__restrict__ ranges, const float *__restrict__ Gn,
                                                  float *__restrict__ gfields) {
     const int b = blockIdx.y;
-    long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long q0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     int g = -1;
-    long long acc = 0;
 #pragma unroll
-    for (int k = 0; k < GS_MAX_GROUPS; k++) {
-        if (k < G.ngroups && g < 0) {
-            long long np = (long long)G.g[k].H * G.g[k].W;
-            if (q < acc + np) g = k; else acc += np;
-        }
-    }
-    if (g < 0) return;
-    if (group_native(G, g) || gsplats[b * G.ngroups + g] == 0) return;
-    q -= acc;
+    for (int k = 0; k < GS_MAX_GROUPS; k++)
+        if (k < G.ngroups && G.g[k].adj_off >= 0 && q0 >= G.g[k].adj_off &&
+            q0 < G.g[k].adj_off + (long long)G.g[k].H * G.g[k].W)
+            g = k;
+    if (g < 0 || gsplats[b * G.ngroups + g] == 0) return;
+    const long long q = q0 - G.g[g].adj_off;
     const int Hg = G.g[g].H, Wg = G.g[g].W;
     const int i = (int)(q / Wg), j = (int)(q - (long long)i * Wg);
     const int tile = G.g[g].tile_off + (i / G.tile) * G.g[g].ntx + (j / G.tile);
     const int2 rg = ranges[(long long)b * G.tiles_per_image + tile];
     if (rg.y <= rg.x) return;
     const long long P = (long long)G.H * G.W;
-    const float sy = (float)G.H / (float)Hg, sx = (float)G.W / (float)Wg;
-    const int ylo = max(G.y0, (int)ceilf((i - 0.5f) * sy - 0.5f) - 1);
-    const int yhi = min(G.y1 - 1, (int)floorf((i + 1.5f) * sy - 0.5f) + 1);
-    const int xlo = max(0, (int)ceilf((j - 0.5f) * sx - 0.5f) - 1);
-    const int xhi = min(G.W - 1, (int)floorf((j + 1.5f) * sx - 0.5f) + 1);
+    const float inv_sy = (float)G.H / (float)Hg, inv_sx = (float)G.W / (float)Wg;
+    const int ylo = max(G.y0, (int)ceilf((i - 0.5f) * inv_sy - 0.5f) - 1);
+    const int yhi = min(G.y1 - 1, (int)floorf((i + 1.5f) * inv_sy - 0.5f) + 1);
+    const int xlo = max(0, (int)ceilf((j - 0.5f) * inv_sx - 0.5f) - 1);
+    const int xhi = min(G.W - 1, (int)floorf((j + 1.5f) * inv_sx - 0.5f) + 1);
+    const float usy = G.g[g].up_sy, usx = G.g[g].up_sx;
+    // column weights of texel j, computed once per texel
+    constexpr int MAXW = 264;  // 2 * (W / Wg) + 3 with W / Wg <= 128 (max_octaves <= 7)
+    float wx[MAXW];
+    const int nx = min(xhi - xlo + 1, MAXW);
+    for (int t = 0; t < nx; t++) {
+        int x0, x1;
+        float w0, w1;
+        lin_index_s(xlo + t, Wg, usx, x0, x1, w0, w1);
+        wx[t] = (x0 == j ? w0 : 0.f) + (x1 == j ? w1 : 0.f);
+    }
     float acc5[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
     const float *Gb = Gn + (long long)b * 5 * P;
     for (int y = ylo; y <= yhi; y++) {
         int y0, y1;
         float h0, h1;
-        lin_index(y, Hg, G.H, y0, y1, h0, h1);
-        if (y0 != i && y1 != i) continue;
+        lin_index_s(y, Hg, usy, y0, y1, h0, h1);
         const float wy = (y0 == i ? h0 : 0.f) + (y1 == i ? h1 : 0.f);
-        for (int x = xlo; x <= xhi; x++) {
-            int x0, x1;
-            float w0, w1;
-            lin_index(x, Wg, G.W, x0, x1, w0, w1);
-            if (x0 != j && x1 != j) continue;
-            const float w = wy * ((x0 == j ? w0 : 0.f) + (x1 == j ? w1 : 0.f));
-            const long long p = (long long)y * G.W + x;
+        if (wy == 0.f) continue;
+        const long long rowp = (long long)y * G.W + xlo;
+        for (int t = 0; t < nx; t++) {
+            const float w = wy * wx[t];
+            if (w == 0.f) continue;
 #pragma unroll
-            for (int c = 0; c < 5; c++) acc5[c] += w * Gb[c * P + p];
+            for (int c = 0; c < 5; c++) acc5[c] += w * Gb[c * P + rowp + t];
         }
     }
     float *gf = gfields + (long long)b * G.fld_per_image + G.g[g].fld_off;
@@ -907,6 +929,33 @@ __global__ void __launch_bounds__(256) k_finalize(RenderGeom G, const float *__r
     if (G.has_theta && g_th) g_th[s] = -(sx / sy - sy / sx) * Suv * invK2;
 }
 
+// L2 loss of a [planes][H][W] image against a target over rows [y0, y1): grad = 2*scale*(out - target)
+// inside the band (rows outside are not written), loss += scale * sum (out - target)^2.
+__global__ void __launch_bounds__(256) k_l2_grad(const float *__restrict__ out, const float *__restrict__ target,
+                                                 long long planes, int H, int W, int y0, int y1, float scale,
+                                                 float *__restrict__ grad, float *__restrict__ loss) {
+    __shared__ float red[8];
+    const long long per = (long long)(y1 - y0) * W;
+    float acc = 0.f;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < planes * per;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long pl = i / per, r = i - pl * per;
+        const long long idx = pl * H * W + (long long)y0 * W + r;
+        const float d = out[idx] - target[idx];
+        grad[idx] = 2.0f * scale * d;
+        acc = fmaf(d, d, acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red[w];
+        atomicAdd(loss, t * scale);
+    }
+}
+
 __global__ void k_activate_scale(const float *__restrict__ ls, float *__restrict__ out, long long n) {
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) out[i] = gs_softplus_eps(ls[i]);
@@ -995,6 +1044,20 @@ void make_geom(const gs_render_desc *d, RenderGeom &G) {
     }
     G.tiles_per_image = toff;
     G.fld_per_image = foff;
+    {
+        long long adj = 0;
+        for (int k = 0; k < ng; k++) {
+            GroupGeom &gg = G.g[k];
+            gg.up_sy = (float)gg.H / (float)d->H;
+            gg.up_sx = (float)gg.W / (float)d->W;
+            if (gg.H == d->H && gg.W == d->W) {
+                gg.adj_off = -1;
+            } else {
+                gg.adj_off = (int)adj;
+                adj += (long long)gg.H * gg.W;
+            }
+        }
+    }
     G.y0 = std::max(0, d->row_begin);
     G.y1 = d->row_end > 0 ? std::min(d->H, d->row_end) : d->H;
     for (int k = 0; k < ng; k++) {
@@ -1265,7 +1328,8 @@ int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_sca
         if (!(G.g[g].H == G.H && G.g[g].W == G.W)) any_coarse = true;
     if (any_coarse) {
         long long tex = 0;
-        for (int g = 0; g < G.ngroups; g++) tex += (long long)G.g[g].H * G.g[g].W;
+        for (int g = 0; g < G.ngroups; g++)
+            if (G.g[g].adj_off >= 0) tex += (long long)G.g[g].H * G.g[g].W;
         dim3 ag((unsigned)((tex + 255) / 256), (unsigned)d->B);
         k_adjoint<<<ag, 256, 0, s>>>(G, at<int>(workspace, pl.o_gsplats), at<int2>(workspace, pl.o_ranges),
                                      at<float>(workspace, pl.o_G), at<float>(workspace, pl.o_gfields));
@@ -1340,6 +1404,22 @@ int gs_render_debug_bins(const gs_render_desc *d, const void *workspace, int64_t
     e = cudaMemcpy(&status, at<int>(ws, pl.o_misc + 8), sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return set_cuda_error(e, "debug_bins");
     return status ? GS_ERR_PAIR_BUDGET : GS_OK;
+}
+
+int gs_l2_loss_grad(const float *out, const float *target, int64_t planes, int32_t H, int32_t W, int32_t row_begin,
+                    int32_t row_end, float scale, float *grad, float *loss, void *stream) {
+    if (!out || !target || !grad || !loss || planes < 0 || H < 1 || W < 1) return GS_ERR_BAD_ARGUMENT;
+    int y0 = std::max(0, row_begin), y1 = row_end > 0 ? std::min(H, row_end) : H;
+    if (y1 <= y0) return GS_ERR_BAD_ARGUMENT;
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t e = cudaMemsetAsync(loss, 0, sizeof(float), s);
+    GS_COUNT(1);
+    if (e != cudaSuccess) return set_cuda_error(e, "gs_l2_loss_grad");
+    long long n = planes * (long long)(y1 - y0) * W;
+    unsigned grid = (unsigned)std::min<long long>(148 * 8, std::max<long long>(1, (n + 255) / 256));
+    k_l2_grad<<<grid, 256, 0, s>>>(out, target, planes, H, W, y0, y1, scale, grad, loss);
+    GS_CHECK_LAUNCH("k_l2_grad");
+    return GS_OK;
 }
 
 int gs_activate_scale(const float *log_scale, float *out, int64_t n, void *stream) {

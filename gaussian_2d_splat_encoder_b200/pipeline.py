@@ -16,7 +16,6 @@ Outputs live in static buffers that the next call overwrites; clone them to keep
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from . import _lib
 from .render_triton import render_alpha_octave
@@ -75,6 +74,25 @@ class EncodeRender:
         return self.rec
 
 
+def render_l2_grads(leaves, target, H: int, W: int, odds: bool = True, row_band=None):
+    """One fitting step's loss and gradients: render_alpha_octave forward, the fused L2 kernel
+    (gs_l2_loss_grad: mse over the whole image, or a row band's share of it), and the render backward
+    seeded with that gradient.  Returns (loss [1] device tensor, grads of the six leaves)."""
+    L = leaves
+    out = render_alpha_octave(L[0], L[1], L[2], L[3], L[4], H, W, theta=L[5], odds=odds, row_band=row_band)
+    dev = out.device
+    gout = torch.zeros_like(out) if row_band is not None else torch.empty_like(out)
+    loss = torch.empty(1, device=dev)
+    y0, y1 = row_band if row_band is not None else (0, H)
+    planes = out.shape[0] * out.shape[1]
+    tgt = target.contiguous().float()
+    _lib.check(_lib.load().gs_l2_loss_grad(_lib.ptr(out), _lib.ptr(tgt), planes, H, W, y0, y1,
+                                           1.0 / float(planes * H * W), _lib.ptr(gout), _lib.ptr(loss),
+                                           _lib.stream_of(dev)), "gs_l2_loss_grad")
+    grads = torch.autograd.grad(out, L, grad_outputs=gout)
+    return loss, grads
+
+
 class RenderFitStep:
     def __init__(self, N: int, H: int, W: int, device, batch: int = 1, odds: bool = True, warmup: int = 2):
         self.dev = torch.device(device)
@@ -95,11 +113,7 @@ class RenderFitStep:
             self.target.copy_(target, non_blocking=True)
 
     def _body(self):
-        L = self.leaves
-        out = render_alpha_octave(L[0], L[1], L[2], L[3], L[4], self.H, self.W, theta=L[5], odds=self.odds)
-        loss = F.mse_loss(out, self.target)
-        grads = torch.autograd.grad(loss, L)
-        return loss, grads
+        return render_l2_grads(self.leaves, self.target, self.H, self.W, self.odds)
 
     def capture(self, profile: bool = False):
         s = torch.cuda.Stream(self.dev)

@@ -166,6 +166,14 @@ int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights *w, const 
 /* Reads (synchronously) the bounded-wait error flag left in an encoder workspace (0 = none). */
 int gs_encoder_error_flag(const gs_encoder_desc *e, const void *workspace, int *flag_host);
 
+/* Fused L2 loss of a fitting step over rows [row_begin, row_end) (row_end <= 0: all rows) of `planes`
+ * H x W fp32 images: grad = 2*scale*(out - target) inside the band (other rows untouched) and
+ * *loss = scale * sum (out - target)^2 (loss is a device float, zeroed by the call).  With
+ * scale = 1/(planes*H*W) this is mse_loss and its gradient (the loss of the reference's fitting
+ * configurations); with a band it is that band's share. */
+int gs_l2_loss_grad(const float *out, const float *target, int64_t planes, int32_t H, int32_t W, int32_t row_begin,
+                    int32_t row_end, float scale, float *grad, float *loss, void *stream);
+
 /* activate_scale (params.py:18-28): out = softplus(log_scale) + 1e-4, n elements. */
 int gs_activate_scale(const float *log_scale, float *out, int64_t n, void *stream);
 
