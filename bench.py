@@ -505,8 +505,12 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     lib = _lib.load()
+    if args.kernels_only:
+        # lean process for ncu (it saves and restores device memory between passes): one input image and
+        # no L2-flush buffer (ncu flushes caches itself)
+        EncodeRenderWorkload.SEEDS = EncodeRenderWorkload.SEEDS[:1]
     wl = wcls(dev, rank, world)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4 if not args.kernels_only else 1024, dtype=torch.float32, device=dev)
 
     def barrier():
         torch.cuda.synchronize()

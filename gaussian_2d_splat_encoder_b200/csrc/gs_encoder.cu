@@ -161,14 +161,29 @@ __global__ void __launch_bounds__(256) k_gn_apply(__nv_bfloat16 *__restrict__ x,
     }
 }
 
-// bg = sigmoid(W * mean_hw(s8) + b) (efficient_encoder.py:267-268)
+// bg = sigmoid(W * mean_hw(s8) + b) (efficient_encoder.py:267-268); one warp per image, lanes split the
+// channels and reduce with shuffles
 __global__ void k_bg(const float *__restrict__ chsum, int C, long long HW, const float *__restrict__ w,
                      const float *__restrict__ bias, float *__restrict__ bg) {
-    int b = blockIdx.x, k = threadIdx.x;
-    if (k >= 3) return;
-    float s = bias[k];
-    for (int c = 0; c < C; c++) s += w[k * C + c] * (chsum[b * C + c] / (float)HW);
-    bg[b * 3 + k] = 1.0f / (1.0f + expf(-s));
+    const int b = blockIdx.x, lane = threadIdx.x;
+    const float inv = 1.0f / (float)HW;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+    for (int c = lane; c < C; c += 32) {
+        const float m = chsum[b * C + c] * inv;
+        s0 = fmaf(w[c], m, s0);
+        s1 = fmaf(w[C + c], m, s1);
+        s2 = fmaf(w[2 * C + c], m, s2);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    if (lane < 3) {
+        const float s = (lane == 0 ? s0 : lane == 1 ? s1 : s2) + bias[lane];
+        bg[b * 3 + lane] = 1.0f / (1.0f + expf(-s));
+    }
 }
 
 struct HeadArgs {
@@ -190,17 +205,23 @@ struct HeadArgs {
     float *cmu, *cls, *ccol, *cop, *cth;  // contiguous [B][fH*fW*M] copies (coarse render input)
 };
 
-// one thread per feature cell: 1x1 convolution of the head + activations (efficient_encoder.py:170-197)
-__global__ void __launch_bounds__(128) k_head(HeadArgs a) {
-    extern __shared__ float shw[];  // weights [nout][Cin], bias [nout], gn scale/shift [2][Cfeat]
-    float *sw = shw, *sb = shw + a.nout * a.Cin, *gsc = sb + a.nout, *gsh = gsc + a.Cfeat;
+// one thread per feature cell: 1x1 convolution of the head + activations (efficient_encoder.py:170-197).
+// Weights sit transposed in shared memory, [Cin][20] (18 outputs padded to 20), so one input channel is
+// 5 broadcast 16-byte loads for 18 FMAs.
+#define HEAD_NP 20
+__global__ void __launch_bounds__(64) k_head(HeadArgs a) {
+    extern __shared__ __align__(16) float shw[];  // wT [Cin][20], bias [20], gn scale/shift [2][Cfeat]
+    float *wT = shw, *sb = shw + a.Cin * HEAD_NP, *gsc = sb + HEAD_NP, *gsh = gsc + a.Cfeat;
     long long cell = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const long long ncell = (long long)a.B * a.fH * a.fW;
     int b0 = (int)(((long long)blockIdx.x * blockDim.x) / ((long long)a.fH * a.fW));
-    for (int i = threadIdx.x; i < a.nout * a.Cin; i += blockDim.x) sw[i] = a.w[i];
-    for (int i = threadIdx.x; i < a.nout; i += blockDim.x) sb[i] = a.b[i];
-    // GroupNorm scale/shift of the block's first image (blocks never straddle images: fH*fW % 128 == 0
-    // is required by the caller, otherwise the per-thread path below recomputes them)
+    for (int i = threadIdx.x; i < a.Cin * HEAD_NP; i += blockDim.x) {
+        const int c = i / HEAD_NP, k = i - c * HEAD_NP;
+        wT[i] = k < a.nout ? a.w[k * a.Cin + c] : 0.f;
+    }
+    for (int i = threadIdx.x; i < HEAD_NP; i += blockDim.x) sb[i] = i < a.nout ? a.b[i] : 0.f;
+    // GroupNorm scale/shift of the block's image (blocks never straddle images: the caller requires
+    // fH*fW to be a multiple of the block size when gn_stats is used)
     if (a.gn_stats) {
         const double n = (double)a.fH * a.fW * (a.Cfeat / 8);
         for (int c = threadIdx.x; c < a.Cfeat; c += blockDim.x) {
@@ -218,9 +239,20 @@ __global__ void __launch_bounds__(128) k_head(HeadArgs a) {
     const int b = (int)(cell / ((long long)a.fH * a.fW));
     const int r = (int)(cell - (long long)b * a.fH * a.fW);
     const int y = r / a.fW, x = r - y * a.fW;
-    float acc[18];
+    float acc[HEAD_NP];
 #pragma unroll
-    for (int k = 0; k < 18; k++) acc[k] = k < a.nout ? sb[k] : 0.f;
+    for (int k = 0; k < HEAD_NP; k++) acc[k] = sb[k];
+    auto fma_channel = [&](int c, float v) {
+        const float4 *wc = reinterpret_cast<const float4 *>(wT + c * HEAD_NP);
+#pragma unroll
+        for (int q = 0; q < HEAD_NP / 4; q++) {
+            const float4 w4 = wc[q];
+            acc[4 * q + 0] = fmaf(w4.x, v, acc[4 * q + 0]);
+            acc[4 * q + 1] = fmaf(w4.y, v, acc[4 * q + 1]);
+            acc[4 * q + 2] = fmaf(w4.z, v, acc[4 * q + 2]);
+            acc[4 * q + 3] = fmaf(w4.w, v, acc[4 * q + 3]);
+        }
+    };
     const __nv_bfloat16 *fp = a.feat + cell * a.Cfeat;
     for (int c = 0; c < a.Cfeat; c += 8) {
         uint4 u = *reinterpret_cast<const uint4 *>(fp + c);
@@ -228,32 +260,26 @@ __global__ void __launch_bounds__(128) k_head(HeadArgs a) {
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             float v = __bfloat162float(e[j]);
-            if (a.gn_stats) v = v * gsc[c + j] + gsh[c + j];
-#pragma unroll
-            for (int k = 0; k < 18; k++)
-                if (k < a.nout) acc[k] += sw[k * a.Cin + c + j] * v;
+            if (a.gn_stats) v = fmaf(v, gsc[c + j], gsh[c + j]);
+            fma_channel(c + j, v);
         }
     }
-    float extra[5];
-    int nextra = 1;
-    extra[0] = a.gpool[cell];
+    fma_channel(a.Cfeat, a.gpool[cell]);
     if (a.cond) {
         int y0, y1, x0, x1;
         float h0, h1, w0, w1;
         lin_idx(y, a.rg, a.fH, y0, y1, h0, h1);
         lin_idx(x, a.rg, a.fW, x0, x1, w0, w1);
         const float *cb = a.cond + (long long)b * a.rg * a.rg * 4;
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-            extra[1 + c] = h0 * (w0 * cb[((long long)y0 * a.rg + x0) * 4 + c] + w1 * cb[((long long)y0 * a.rg + x1) * 4 + c]) +
-                           h1 * (w0 * cb[((long long)y1 * a.rg + x0) * 4 + c] + w1 * cb[((long long)y1 * a.rg + x1) * 4 + c]);
-        }
-        nextra = 5;
+        const float4 c00 = *reinterpret_cast<const float4 *>(cb + ((long long)y0 * a.rg + x0) * 4);
+        const float4 c01 = *reinterpret_cast<const float4 *>(cb + ((long long)y0 * a.rg + x1) * 4);
+        const float4 c10 = *reinterpret_cast<const float4 *>(cb + ((long long)y1 * a.rg + x0) * 4);
+        const float4 c11 = *reinterpret_cast<const float4 *>(cb + ((long long)y1 * a.rg + x1) * 4);
+        fma_channel(a.Cfeat + 1, h0 * (w0 * c00.x + w1 * c01.x) + h1 * (w0 * c10.x + w1 * c11.x));
+        fma_channel(a.Cfeat + 2, h0 * (w0 * c00.y + w1 * c01.y) + h1 * (w0 * c10.y + w1 * c11.y));
+        fma_channel(a.Cfeat + 3, h0 * (w0 * c00.z + w1 * c01.z) + h1 * (w0 * c10.z + w1 * c11.z));
+        fma_channel(a.Cfeat + 4, h0 * (w0 * c00.w + w1 * c01.w) + h1 * (w0 * c10.w + w1 * c11.w));
     }
-    for (int j = 0; j < nextra; j++)
-#pragma unroll
-        for (int k = 0; k < 18; k++)
-            if (k < a.nout) acc[k] += sw[k * a.Cin + a.Cfeat + j] * extra[j];
     // activations; channel layout of each head: (m, component)
     const int M = a.M;
     const float by = lin_center(y, a.fH), bx = lin_center(x, a.fW);
@@ -393,8 +419,8 @@ int enc_plan(const gs_encoder_desc *e, EncPlan &p) {
     if (!e || e->B < 1 || e->H < 16 || e->W < 16 || e->H % 8 || e->W % 8) return GS_ERR_BAD_ARGUMENT;
     if (e->d != 256 || e->M < 1 || e->M > 2 || e->Mf < 1 || e->Mf > 2) return GS_ERR_BAD_ARGUMENT;
     if (e->residual_grid < 8) return GS_ERR_BAD_ARGUMENT;
-    // the fine head's thread blocks (128 cells) must not straddle two images
-    if (((long long)(e->H / 4) * (e->W / 4)) % 128 != 0) return GS_ERR_BAD_ARGUMENT;
+    // the fine head's thread blocks (64 cells) must not straddle two images
+    if (((long long)(e->H / 4) * (e->W / 4)) % 64 != 0) return GS_ERR_BAD_ARGUMENT;
     memset(&p, 0, sizeof(p));
     p.B = e->B; p.H = e->H; p.W = e->W; p.d = e->d; p.rg = e->residual_grid;
     p.H2 = p.H / 2; p.W2 = p.W / 2; p.H4 = p.H / 4; p.W4 = p.W / 4; p.H8 = p.H / 8; p.W8 = p.W / 8;
@@ -521,8 +547,8 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     {
         ProfScope ps(PR_HEADS, s);
         long long ncell = (long long)B * p.H8 * p.W8;
-        size_t sm = ((size_t)h.nout * h.Cin + h.nout + 2 * h.Cfeat) * 4;
-        k_head<<<(unsigned)((ncell + 127) / 128), 128, sm, s>>>(h);
+        size_t sm = ((size_t)h.Cin * HEAD_NP + HEAD_NP + 2 * h.Cfeat) * 4;
+        k_head<<<(unsigned)((ncell + 63) / 64), 64, sm, s>>>(h);
     }
     // 4. coarse render at residual_grid^2 (odds) -> cond map
     {
@@ -564,8 +590,8 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     {
         ProfScope ps(PR_HEADS, s);
         long long ncell = (long long)B * p.H4 * p.W4;
-        size_t sm = ((size_t)h.nout * h.Cin + h.nout + 2 * h.Cfeat) * 4;
-        k_head<<<(unsigned)((ncell + 127) / 128), 128, sm, s>>>(h);
+        size_t sm = ((size_t)h.Cin * HEAD_NP + HEAD_NP + 2 * h.Cfeat) * 4;
+        k_head<<<(unsigned)((ncell + 63) / 64), 64, sm, s>>>(h);
     }
     if (latents) {
         long long n = (long long)B * p.H4 * p.W4 * 128;

@@ -11,7 +11,7 @@ outputs carry no autograd history.
 
 Supported configuration on the CUDA path: variant='adaptive', d_feature=256, stride=8, fine_stride=4,
 norm_type='group', use_grad_input=True, 1-2 splats per cell, H and W multiples of 8 with
-(H/4)(W/4) a multiple of 128 -- the released checkpoint's architecture.  Other configurations can be
+(H/4)(W/4) a multiple of 64 -- the released checkpoint's architecture.  Other configurations can be
 constructed (state-dict compatible) but their forward raises NotImplementedError.
 """
 
@@ -311,9 +311,9 @@ class EfficientGaussianEncoder(nn.Module):
         if image.dim() != 4 or image.shape[1] != 3:
             raise ValueError("image must be [B,3,H,W]")
         B, _, H, W = image.shape
-        if H % 8 or W % 8 or ((H // 4) * (W // 4)) % 128:
+        if H % 8 or W % 8 or ((H // 4) * (W // 4)) % 64:
             raise NotImplementedError(f"image size {H}x{W}: the CUDA encoder needs H, W multiples of 8 and "
-                                      "(H/4)(W/4) a multiple of 128")
+                                      "(H/4)(W/4) a multiple of 64")
         x = image.detach().contiguous().float()
         with torch.cuda.device(dev):
             L = _lib.load()
