@@ -44,6 +44,7 @@ SIGNATURES = {
     "gs_render_workspace_size": (C.c_size_t, [_DESC, C.c_int]),
     "gs_render_count": (C.c_int, [_DESC, _P, _P, _P, C.c_size_t, _P, _P, _P]),
     "gs_render_fwd": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
+    "gs_render_fwd_noalloc": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P, _P]),
     "gs_render_bwd": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "gs_render_debug_bins": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P]),
     "gs_activate_scale": (C.c_int, [_P, _P, C.c_int64, _P]),

@@ -72,6 +72,20 @@ int64_t gs_render_pair_bound(const gs_render_desc *d);
 /* Workspace bytes for a forward (with_backward = 0) or a forward + backward (with_backward = 1). */
 size_t gs_render_workspace_size(const gs_render_desc *d, int with_backward);
 
+/* Forward render without any caller-provided workspace (no counterpart in the reference).  For callers
+ * that cannot allocate device memory -- a host whose device memory belongs to an allocator it cannot
+ * call, or a latency-critical path that must not pay for cudaMalloc's implicit synchronisation -- the
+ * workspace of gs_render_fwd is taken from a fixed array inside the library instead.  Same arguments
+ * and result as gs_render_fwd minus the workspace.  Limits: a render whose forward workspace
+ * (gs_render_workspace_size(d, 0)) exceeds GS_NOALLOC_SCRATCH_BYTES is refused with
+ * GS_ERR_WORKSPACE before any launch; every GPU that loads the library holds the array until exit;
+ * all calls on a device share it, so calls that overlap on the GPU (other streams or threads) race and
+ * must be serialised by the caller; the first call on a device looks up the array's address and
+ * should come before any stream capture.  There is no backward variant. */
+#define GS_NOALLOC_SCRATCH_BYTES (32u << 20)
+int gs_render_fwd_noalloc(const gs_render_desc *d, const float *mu, const float *log_scale, const float *color,
+                          const float *opacity, const float *bg, const float *theta, float *out, void *stream);
+
 /* Exact pair counts per (image, group) into counts_host[B * groups] (groups = max_octaves + 1 in octave
  * mode, 2 in multires mode, 1 otherwise); *groups_out receives the group count.  Runs the
  * preprocessing kernel and SYNCHRONISES the stream: the analogue of _build_tiles's budget check
