@@ -1,16 +1,17 @@
 // gs_conv.cu -- implicit-GEMM convolution on the 5th-generation tensor cores (sm_100a).
 //
-// One CTA computes a 128-pixel x Cout output tile (M = 128 output pixels laid out as TY rows x TX
-// columns of one image, N = Cout <= 256, fp32 accumulator in TMEM).  The K loop runs over
-// (tap, input-channel chunk): for each k-block TMA brings the A tile (128 input pixels x KC channels,
-// NHWC bf16, zero fill outside the image = the convolution's zero padding) and the B tile (Cout x KC
-// slice of the packed weight matrix) into a STAGES-deep shared-memory ring; one thread issues
-// tcgen05.mma (kind::f16, bf16 x bf16 -> f32) and commits each stage back to the producer.  The
-// epilogue reads TMEM with tcgen05.ld (one output pixel per thread), adds the bias, applies the exact
-// GELU, accumulates the GroupNorm(8) partial sums of the tile and stores bf16 NHWC.
+// The output is cut into work items of MT vertically stacked M-tiles (each 128 output pixels laid out
+// as TY rows x TX columns of one image) times a BN-wide slice of the output channels; a persistent grid
+// strides over the items.  The K loop of an item runs over (tap, input-channel chunk): for each k-block
+// TMA brings the MT A tiles (128 input pixels x KC channels, NHWC bf16, zero fill outside the image =
+// the convolution's zero padding) and the B tile (BN x KC slice of the packed weight matrix) into a
+// STAGES-deep shared-memory ring; one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32) into
+// TMEM and commits each stage back to the producer.  Accumulators are double-buffered in TMEM, so the
+// epilogue warps (tcgen05.ld, bias, exact GELU, GroupNorm(8) partial sums, bf16 NHWC store) of one
+// item run while the tensor cores work on the next.
 //
 // Stride-2 convolutions read their input through a 5-D view (C, x parity, x/2, y, image) so the
-// 128 output pixels of a row map to TX consecutive elements of the x/2 axis; stride-1 convolutions
+// TX output pixels of a row map to TX consecutive elements of the x/2 axis; stride-1 convolutions
 // read a TY x TX box directly.  Replaces nn.Conv2d + nn.GELU (+ the statistics pass of nn.GroupNorm)
 // of the reference encoder (efficient_encoder.py:53-58, 86-87).
 #include <cuda.h>
@@ -30,42 +31,61 @@ using namespace gs_tc;
 
 namespace {
 
-template <int BN, int KC, int STAGES>
-__global__ void __launch_bounds__(128, 1) k_conv_tc(const __grid_constant__ CUtensorMap tmA,
-                                                    const __grid_constant__ CUtensorMap tmB, ConvArgs a) {
+// Persistent, warp-specialised convolution.  Work item = MT vertically stacked 128-pixel M-tiles x
+// one BN-wide slice of the output channels; CTAs stride over the items.
+//   warp 0        TMA producer (one lane): A tiles of the MT M-tiles + the B slice, STAGES-deep ring
+//   warp 1        TMEM owner + MMA issuer (one lane): MT accumulators of 128 x BN fp32 per item,
+//                 double-buffered in TMEM so the epilogue of item i overlaps the K loop of item i+1
+//   warps 2..     4*MT epilogue warps: warp w drains TMEM lanes 32*(w%4).. of accumulator (w-2)/4 --
+//                 bias, exact GELU, GroupNorm(8) partial sums, bf16 NHWC store
+// Every wait is bounded; a wait that gives up records its stage in *err and raises a CTA-wide abort
+// flag so the other roles stop issuing, then the CTA drains its copies and MMAs and frees TMEM.
+template <int BN, int KC, int STAGES, int MT, int CPG, int MINB>
+__global__ void __launch_bounds__(64 + 128 * MT, MINB)
+    k_conv_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, ConvArgs a) {
+    constexpr int NEPI = 4 * MT;
     constexpr uint32_t A_BYTES = 128u * KC * 2u;
     constexpr uint32_t B_BYTES = (uint32_t)BN * KC * 2u;
-    constexpr uint32_t STAGE = A_BYTES + B_BYTES;
-    constexpr uint32_t LAYOUT = KC == 64 ? 2u : 6u;       // SWIZZLE_128B : SWIZZLE_32B
-    constexpr uint32_t SBO = KC == 64 ? 1024u : 256u;     // 8 rows x row pitch
-    constexpr int CPG = BN / 8;                           // channels per GroupNorm group
+    constexpr uint32_t STAGE = MT * A_BYTES + B_BYTES;
+    constexpr uint32_t LAYOUT = KC == 64 ? 2u : 6u;    // SWIZZLE_128B : SWIZZLE_32B
+    constexpr uint32_t SBO = KC == 64 ? 1024u : 256u;  // 8 rows x row pitch
+    constexpr uint32_t ACC = (uint32_t)MT * BN;        // TMEM columns of one accumulator buffer
+    constexpr uint32_t TCOLS = 2 * ACC < 32 ? 32 : 2 * ACC;
+    static_assert((TCOLS & (TCOLS - 1)) == 0 && TCOLS <= 512, "TMEM columns");
+    static_assert(CPG % 8 == 0 && (CPG >= 16 ? CPG % 16 == 0 : true), "GroupNorm channels per group");
     extern __shared__ uint8_t dsmem[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
-    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], done;
+    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2], mdone;
     __shared__ uint32_t tmem_base;
-    __shared__ float gsum[4][8], gsq[4][8];
+    __shared__ volatile int abort_flag;
+    __shared__ int issued, consumed;
+    __shared__ __align__(16) float sbias[256];
+    __shared__ float sacc[NEPI][16];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int t = blockIdx.x;
-    const int tx = t % a.tiles_x;
-    t /= a.tiles_x;
-    const int ty = t % a.tiles_y;
-    const int b = t / a.tiles_y;
-    const int x0 = tx * a.TX, y0 = ty * a.TY;
+    const int nsplit = a.Co / BN;
+    const int n_items = a.B * a.tiles_y * a.tiles_x * nsplit;
 
-    if (warp == 0) {
-        tmem_alloc(&tmem_base, BN < 32 ? 32 : BN);
+    for (int i = threadIdx.x; i < a.Co; i += blockDim.x) sbias[i] = a.bias[i];
+    for (int i = threadIdx.x; i < NEPI * 16; i += blockDim.x) (&sacc[0][0])[i] = 0.f;
+    if (warp == 1) {
+        tmem_alloc(&tmem_base, TCOLS);
         tmem_relinquish();
     }
-    if (threadIdx.x == 32) {
+    if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(&done, 1);
+        for (int j = 0; j < 2; j++) {
+            mbar_init(&tfull[j], 1);
+            mbar_init(&tempty[j], NEPI);
+        }
+        mbar_init(&mdone, 1);
+        abort_flag = 0;
+        issued = 0;
+        consumed = 0;
         fence_barrier_init();
-    }
-    if (threadIdx.x == 64) {
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
     }
@@ -76,114 +96,213 @@ __global__ void __launch_bounds__(128, 1) k_conv_tc(const __grid_constant__ CUte
 
     if (warp == 0) {
         if (lane == 0) {
-            // TMA producer
-            for (int kb = 0; kb < a.nkb; kb++) {
-                const int s = kb % STAGES;
-                if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, a.err, 1)) break;
-                mbar_arrive_expect_tx(&full[s], STAGE);
-                uint8_t *sa = smem + s * STAGE;
-                uint8_t *sb = sa + A_BYTES;
-                const int tap = kb / a.nchunks, chunk = kb - tap * a.nchunks;
-                const int kh = tap / a.KW, kw = tap - kh * a.KW;
-                const int c0 = chunk * KC;
-                if (a.stride == 1) {
-                    tma_load_4d(sa, &tmA, &full[s], c0, x0 + kw - a.pad, y0 + kh - a.pad, b);
-                } else {
-                    const int xin = 2 * x0 + kw - a.pad;
-                    const int xp = xin & 1;
-                    const int xh = (xin - xp) / 2;
-                    for (int r = 0; r < a.TY; r++)
-                        tma_load_5d(sa + r * a.TX * KC * 2, &tmA, &full[s], c0, xp, xh, 2 * (y0 + r) + kh - a.pad,
-                                    b);
+            int it = 0;
+            for (int item = blockIdx.x; item < n_items && !abort_flag; item += gridDim.x) {
+                int t = item;
+                const int nb = t % nsplit;
+                t /= nsplit;
+                const int tx = t % a.tiles_x;
+                t /= a.tiles_x;
+                const int ty = t % a.tiles_y;
+                const int b = t / a.tiles_y;
+                const int x0 = tx * a.TX, y0 = ty * a.TY * MT;
+                for (int kb = 0; kb < a.nkb; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (it >= STAGES && !mbar_wait_or_abort(&empty[s], ((it / STAGES) - 1) & 1, &abort_flag, a.err, 1))
+                        break;
+                    if (abort_flag) break;
+                    mbar_arrive_expect_tx(&full[s], STAGE);
+                    uint8_t *sa = smem + s * STAGE;
+                    uint8_t *sb = sa + MT * A_BYTES;
+                    const int tap = kb / a.nchunks, chunk = kb - tap * a.nchunks;
+                    const int kh = tap / a.KW, kw = tap - kh * a.KW;
+                    const int c0 = chunk * KC;
+#pragma unroll
+                    for (int mt = 0; mt < MT; mt++) {
+                        const int ym = y0 + mt * a.TY;
+                        if (a.stride == 1) {
+                            tma_load_4d(sa + mt * A_BYTES, &tmA, &full[s], c0, x0 + kw - a.pad, ym + kh - a.pad, b);
+                        } else {
+                            const int xin = 2 * x0 + kw - a.pad;
+                            const int xp = xin & 1;
+                            const int xh = (xin - xp) / 2;
+                            for (int r = 0; r < a.TY; r++)
+                                tma_load_5d(sa + mt * A_BYTES + r * a.TX * KC * 2, &tmA, &full[s], c0, xp, xh,
+                                            2 * (ym + r) + kh - a.pad, b);
+                        }
+                    }
+                    tma_load_2d(sb, &tmB, &full[s], kb * KC, nb * BN);
+                    issued = it + 1;
                 }
-                tma_load_2d(sb, &tmB, &full[s], kb * KC, 0);
+                if (abort_flag) break;
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // MMA issuer
             constexpr uint32_t idesc = idesc_bf16_f32(128, BN);
-            for (int kb = 0; kb < a.nkb; kb++) {
-                const int s = kb % STAGES;
-                if (!mbar_wait(&full[s], (kb / STAGES) & 1, a.err, 2)) break;
+            int it = 0, tc = 0;
+            for (int item = blockIdx.x; item < n_items && !abort_flag; item += gridDim.x, tc++) {
+                const int buf = tc & 1;
+                if (tc >= 2 && !mbar_wait_or_abort(&tempty[buf], ((tc >> 1) - 1) & 1, &abort_flag, a.err, 2)) break;
                 tc_fence_after();
-                const uint32_t sa = smem_u32(smem + s * STAGE);
-                const uint32_t sb = sa + A_BYTES;
+                const uint32_t dcol = tbase + (uint32_t)buf * ACC;
+                bool ok = true;
+                for (int kb = 0; kb < a.nkb; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait_or_abort(&full[s], (it / STAGES) & 1, &abort_flag, a.err, 3)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * STAGE);
+                    const uint32_t sb = sa + MT * A_BYTES;
 #pragma unroll
-                for (int k = 0; k < KC / 16; k++)
-                    mma_bf16(tbase, sdesc(sa + 32u * k, SBO, LAYOUT), sdesc(sb + 32u * k, SBO, LAYOUT), idesc,
-                             (kb | k) != 0 ? 1u : 0u);
-                mma_commit(&empty[s]);
+                    for (int k = 0; k < KC / 16; k++) {
+                        const uint64_t bd = sdesc(sb + 32u * k, SBO, LAYOUT);
+#pragma unroll
+                        for (int mt = 0; mt < MT; mt++)
+                            mma_bf16(dcol + (uint32_t)(mt * BN), sdesc(sa + mt * A_BYTES + 32u * k, SBO, LAYOUT), bd,
+                                     idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    mma_commit(&empty[s]);
+                    consumed = it + 1;
+                }
+                if (!ok) break;
+                mma_commit(&tfull[buf]);
             }
-            mma_commit(&done);
+            // all MMAs of this CTA (also those of an aborted item) have finished once mdone flips
+            mma_commit(&mdone);
+            mbar_wait(&mdone, 0, a.err, 4);
         }
+    } else {
+        // epilogue
+        const int e = warp - 2;
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int mt = e >> 2;
+        const int m = q * 32 + lane;
+        float *acc = sacc[e];
+        int cur_b = -1, tc = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x, tc++) {
+            int t = item;
+            const int nb = t % nsplit;
+            t /= nsplit;
+            const int tx = t % a.tiles_x;
+            t /= a.tiles_x;
+            const int ty = t % a.tiles_y;
+            const int b = t / a.tiles_y;
+            const int yy = ty * a.TY * MT + mt * a.TY + m / a.TX, xx = tx * a.TX + m % a.TX;
+            const bool valid = yy < a.Ho && xx < a.Wo;
+            const int buf = tc & 1;
+            if (!mbar_wait_or_abort(&tfull[buf], (tc >> 1) & 1, &abort_flag, a.err, 5)) break;
+            tc_fence_after();
+            if (a.stats && b != cur_b) {
+                if (cur_b >= 0 && lane < 16) {
+                    atomicAdd(&a.stats[cur_b * 16 + lane], (double)acc[lane]);
+                    acc[lane] = 0.f;
+                }
+                cur_b = b;
+                __syncwarp();
+            }
+            const int n0 = nb * BN;
+            __nv_bfloat16 *dst = a.out + (((long long)b * a.Ho + yy) * a.Wo + xx) * a.Co + n0;
+            const uint32_t taddr = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)buf * ACC + (uint32_t)(mt * BN);
+            float rs = 0.f, rq = 0.f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                float v[16];
+                tmem_ld16(taddr + (uint32_t)c0, v);
+                if (c0 + 16 == BN) {
+                    // the accumulator buffer is drained: hand it back to the MMA warp
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[buf]);
+                }
+                float s0 = 0.f, q0 = 0.f, s1 = 0.f, q1 = 0.f;
+                const float4 *bb = reinterpret_cast<const float4 *>(sbias + n0 + c0);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float4 bj = bb[j];
+                    v[4 * j] += bj.x;
+                    v[4 * j + 1] += bj.y;
+                    v[4 * j + 2] += bj.z;
+                    v[4 * j + 3] += bj.w;
+                }
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    float x = v[i];
+                    if (a.gelu) x = 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+                    v[i] = x;
+                    if (CPG == 8 && i >= 8) {
+                        s1 += x;
+                        q1 += x * x;
+                    } else {
+                        s0 += x;
+                        q0 += x * x;
+                    }
+                }
+                if (valid) {
+                    uint4 p0, p1;
+                    uint32_t *w0 = &p0.x, *w1 = &p1.x;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                        __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 + 2 * i], v[8 + 2 * i + 1]);
+                        w0[i] = *reinterpret_cast<uint32_t *>(&h0);
+                        w1[i] = *reinterpret_cast<uint32_t *>(&h1);
+                    }
+                    reinterpret_cast<uint4 *>(dst + c0)[0] = p0;
+                    reinterpret_cast<uint4 *>(dst + c0)[1] = p1;
+                }
+                if (a.stats) {
+                    if (!valid) s0 = q0 = s1 = q1 = 0.f;
+                    if (CPG == 8) {
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+                            q0 += __shfl_xor_sync(0xffffffffu, q0, o);
+                            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+                            q1 += __shfl_xor_sync(0xffffffffu, q1, o);
+                        }
+                        if (lane == 0) {
+                            const int g = (n0 + c0) / 8;
+                            acc[2 * g] += s0;
+                            acc[2 * g + 1] += q0;
+                            acc[2 * g + 2] += s1;
+                            acc[2 * g + 3] += q1;
+                        }
+                    } else {
+                        rs += s0;
+                        rq += q0;
+                        if ((c0 + 16) % CPG == 0) {
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) {
+                                rs += __shfl_xor_sync(0xffffffffu, rs, o);
+                                rq += __shfl_xor_sync(0xffffffffu, rq, o);
+                            }
+                            if (lane == 0) {
+                                const int g = (n0 + c0) / CPG;
+                                acc[2 * g] += rs;
+                                acc[2 * g + 1] += rq;
+                            }
+                            rs = rq = 0.f;
+                        }
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (a.stats && cur_b >= 0 && lane < 16) atomicAdd(&a.stats[cur_b * 16 + lane], (double)acc[lane]);
     }
-    __syncwarp();
 
-    // epilogue: thread = one output pixel (TMEM lane), BN channels in chunks of 16
-    const bool ok = mbar_wait(&done, 0, a.err, 3);
-    tc_fence_after();
-    const int m = warp * 32 + lane;
-    const int yy = y0 + m / a.TX, xx = x0 + m % a.TX;
-    const bool valid = ok && yy < a.Ho && xx < a.Wo;
-    float gs[8], gq[8];
-#pragma unroll
-    for (int g = 0; g < 8; g++) {
-        gs[g] = 0.f;
-        gq[g] = 0.f;
-    }
-    __nv_bfloat16 *dst = a.out + (((long long)b * a.Ho + yy) * a.Wo + xx) * BN;
-#pragma unroll
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            float x = v[i] + a.bias[c0 + i];
-            if (a.gelu) x = 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-            v[i] = x;
-            const int g = (c0 + i) / CPG;
-            gs[g] += x;
-            gq[g] += x * x;
-        }
-        if (valid) {
-            uint4 p0, p1;
-            uint32_t *q0 = &p0.x, *q1 = &p1.x;
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                __nv_bfloat162 h0 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-                __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 + 2 * i], v[8 + 2 * i + 1]);
-                q0[i] = *reinterpret_cast<uint32_t *>(&h0);
-                q1[i] = *reinterpret_cast<uint32_t *>(&h1);
-            }
-            reinterpret_cast<uint4 *>(dst + c0)[0] = p0;
-            reinterpret_cast<uint4 *>(dst + c0)[1] = p1;
-        }
-    }
-    if (a.stats) {
-#pragma unroll
-        for (int g = 0; g < 8; g++) {
-            float s = valid ? gs[g] : 0.f, q = valid ? gq[g] : 0.f;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                s += __shfl_xor_sync(0xffffffffu, s, o);
-                q += __shfl_xor_sync(0xffffffffu, q, o);
-            }
-            if (lane == 0) {
-                gsum[warp][g] = s;
-                gsq[warp][g] = q;
-            }
-        }
-    }
     tc_fence_before();
     __syncthreads();
-    if (a.stats && threadIdx.x < 16) {
-        const int g = threadIdx.x >> 1, which = threadIdx.x & 1;
-        float v = 0.f;
-        for (int w = 0; w < 4; w++) v += which ? gsq[w][g] : gsum[w][g];
-        atomicAdd(&a.stats[(b * 8 + g) * 2 + which], (double)v);
+    if (abort_flag && threadIdx.x == 0) {
+        // copies that were issued but never consumed still land in shared memory: wait for them
+        for (int j = consumed; j < issued; j++) mbar_wait(&full[j % STAGES], (j / STAGES) & 1, a.err, 6);
     }
-    if (warp == 0) tmem_dealloc(tbase, BN < 32 ? 32 : BN);
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tbase, TCOLS);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -210,26 +329,44 @@ int make_map(CUtensorMap *tm, const void *base, int rank, const uint64_t *dims, 
     return r == CUDA_SUCCESS ? GS_OK : GS_ERR_BAD_ARGUMENT;
 }
 
-template <int BN, int KC, int STAGES>
-int launch(const CUtensorMap &tA, const CUtensorMap &tB, const ConvArgs &a, int nblocks, cudaStream_t st) {
-    constexpr size_t SMEM = (size_t)STAGES * (128 * KC * 2 + BN * KC * 2) + 1024;
+int sm_count() {
+    static int n[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!n[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        n[dev] = v > 0 ? v : 148;
+    }
+    return n[dev];
+}
+
+template <int BN, int KC, int STAGES, int MT, int CPG, int MINB>
+int launch(const CUtensorMap &tA, const CUtensorMap &tB, const ConvArgs &a, cudaStream_t st) {
+    constexpr size_t SMEM = (size_t)STAGES * (MT * 128 * KC * 2 + BN * KC * 2) + 1024;
+    auto kern = k_conv_tc<BN, KC, STAGES, MT, CPG, MINB>;
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(k_conv_tc<BN, KC, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
         configured = true;
     }
-    k_conv_tc<BN, KC, STAGES><<<nblocks, 128, SMEM, st>>>(tA, tB, a);
+    const long long items = (long long)a.B * a.tiles_y * a.tiles_x * (a.Co / BN);
+    const long long slots = (long long)sm_count() * MINB;
+    const int grid = (int)(items < slots ? items : slots);
+    kern<<<grid, 64 + 128 * MT, SMEM, st>>>(tA, tB, a);
     return cudaGetLastError() == cudaSuccess ? GS_OK : GS_ERR_CUDA;
 }
 
 }  // namespace
 
-// Choose the TY x TX output tile (TX * TY = 128) that wastes the fewest pixels.
-void gs_conv_pick_tile(int Ho, int Wo, int *TX, int *TY) {
+// Choose the TY x TX M-tile (TX * TY = 128) whose MT-stacked cover of the output wastes the fewest
+// pixels; ties go to the wider tile.
+void gs_conv_pick_tile(int Ho, int Wo, int MT, int *TX, int *TY) {
     long long best = -1;
     int btx = 128;
     for (int tx = 128; tx >= 8; tx >>= 1) {
-        int ty = 128 / tx;
+        int ty = (128 / tx) * MT;
         long long cover = (long long)((Wo + tx - 1) / tx) * tx * ((Ho + ty - 1) / ty) * ty;
         long long waste = cover - (long long)Wo * Ho;
         if (best < 0 || waste < best) {
@@ -245,19 +382,25 @@ int gs_conv_run(const gs_conv_desc *d, const void *in, const void *w, const floa
                 int *err, cudaStream_t st) {
     if (!d || !in || !w || !bias || !out) return GS_ERR_BAD_ARGUMENT;
     const int B = d->B, Hi = d->H, Wi = d->W, Ci = d->Cin, Co = d->Cout;
+    if (B <= 0 || Hi <= 0 || Wi <= 0 || d->kh <= 0 || d->kw <= 0 || d->pad < 0) return GS_ERR_BAD_ARGUMENT;
     if (!(Co == 64 || Co == 128 || Co == 256)) return GS_ERR_BAD_ARGUMENT;
     const int KC = d->kind == 1 ? 16 : 64;
     if (Ci % KC != 0) return GS_ERR_BAD_ARGUMENT;
+    if (d->kind == 1 && Co != 64) return GS_ERR_BAD_ARGUMENT;
     if (d->stride == 2 && (Wi % 2 != 0)) return GS_ERR_BAD_ARGUMENT;
     if (d->stride != 1 && d->stride != 2) return GS_ERR_BAD_ARGUMENT;
+    // kernel shape per layer: MT stacked M-tiles per work item, BN output channels per item
+    const int MT = Co == 256 ? 1 : 2;
+    const int BN = Co == 256 ? 128 : Co;
     ConvArgs a;
     a.B = B; a.Hi = Hi; a.Wi = Wi; a.Ci = Ci; a.Co = Co;
     a.KH = d->kh; a.KW = d->kw; a.stride = d->stride; a.pad = d->pad;
     a.Ho = d->Ho > 0 ? d->Ho : (Hi + 2 * d->pad - d->kh) / d->stride + 1;
     a.Wo = d->Wo > 0 ? d->Wo : (Wi + 2 * d->pad - d->kw) / d->stride + 1;
-    gs_conv_pick_tile(a.Ho, a.Wo, &a.TX, &a.TY);
+    if (a.Ho <= 0 || a.Wo <= 0) return GS_ERR_BAD_ARGUMENT;
+    gs_conv_pick_tile(a.Ho, a.Wo, MT, &a.TX, &a.TY);
     a.tiles_x = (a.Wo + a.TX - 1) / a.TX;
-    a.tiles_y = (a.Ho + a.TY - 1) / a.TY;
+    a.tiles_y = (a.Ho + a.TY * MT - 1) / (a.TY * MT);
     a.nchunks = Ci / KC;
     a.nkb = d->kh * d->kw * a.nchunks;
     a.gelu = d->gelu;
@@ -284,15 +427,14 @@ int gs_conv_run(const gs_conv_desc *d, const void *in, const void *w, const floa
     {
         uint64_t dims[2] = {(uint64_t)K, (uint64_t)Co};
         uint64_t str[1] = {(uint64_t)K * 2};
-        uint32_t box[2] = {(uint32_t)KC, (uint32_t)Co};
+        uint32_t box[2] = {(uint32_t)KC, (uint32_t)BN};
         s = make_map(&tB, w, 2, dims, str, box, swz);
     }
     if (s != GS_OK) return s;
-    const int nblocks = B * a.tiles_x * a.tiles_y;
-    if (KC == 16) return launch<64, 16, 8>(tA, tB, a, nblocks, st);
-    if (Co == 64) return launch<64, 64, 4>(tA, tB, a, nblocks, st);
-    if (Co == 128) return launch<128, 64, 4>(tA, tB, a, nblocks, st);
-    return launch<256, 64, 4>(tA, tB, a, nblocks, st);
+    if (KC == 16) return launch<64, 16, 8, 2, 8, 2>(tA, tB, a, st);
+    if (Co == 64) return launch<64, 64, 5, 2, 8, 1>(tA, tB, a, st);
+    if (Co == 128) return launch<128, 64, 4, 2, 16, 1>(tA, tB, a, st);
+    return launch<128, 64, 6, 1, 32, 1>(tA, tB, a, st);
 }
 
 extern "C" int gs_conv2d(const gs_conv_desc *d, const void *in_bf16, const void *w_bf16, const float *bias,

@@ -18,6 +18,6 @@ struct ConvArgs {
     int *err;       // set to a non-zero stage code when a bounded wait gives up
 };
 
-void gs_conv_pick_tile(int Ho, int Wo, int *TX, int *TY);
+void gs_conv_pick_tile(int Ho, int Wo, int MT, int *TX, int *TY);
 int gs_conv_run(const gs_conv_desc *d, const void *in, const void *w, const float *bias, void *out, double *stats,
                 int *err, cudaStream_t st);
