@@ -263,15 +263,24 @@ __global__ void __launch_bounds__(1024) k_scan_blocks(int *__restrict__ data, in
     if (threadIdx.x == 0) *total = tot;
 }
 
-// pairs in splat order: key = global tile id, value = global splat id
+// pairs in splat order: key = global tile id, value = global splat id.  Splat block j (256 splats, the
+// preprocessing block) owns the output segment [bpre[j], bpre[j] + tot_j); `parts` emit blocks share it,
+// part p writing the sub-segment [bpre[j] + min(p*c, tot_j), bpre[j] + min((p+1)*c, tot_j)) with
+// c = ceil(tot_j / parts).  Each emit block also writes the digit-0 histogram of its sub-segment
+// (hist0 column = emit block), so the first radix pass needs no separate counting sweep.
 __global__ void __launch_bounds__(256) k_emit(RenderGeom G, const int4 *__restrict__ meta,
                                               const int *__restrict__ counts, const int *__restrict__ bpre,
-                                              unsigned *__restrict__ keys, int *__restrict__ vals,
-                                              int *__restrict__ status) {
+                                              int parts, unsigned *__restrict__ keys, int *__restrict__ vals,
+                                              int *__restrict__ status, int *__restrict__ hist0, int hist_stride,
+                                              int radix0) {
     __shared__ int wsum[8];
     __shared__ int soff[257];
     __shared__ int4 smeta[256];
-    long long s0 = (long long)blockIdx.x * 256;
+    __shared__ int shist[256];
+    if (hist0)
+        for (int d = threadIdx.x; d < radix0; d += 256) shist[d] = 0;
+    const int j = blockIdx.x / parts, part = blockIdx.x - j * parts;
+    long long s0 = (long long)j * 256;
     long long s = s0 + threadIdx.x;
     int c = 0;
     int4 mt = make_int4(0, 0, 1, 0);
@@ -285,8 +294,10 @@ __global__ void __launch_bounds__(256) k_emit(RenderGeom G, const int4 *__restri
     smeta[threadIdx.x] = mt;
     if (threadIdx.x == 0) soff[256] = tot;
     __syncthreads();
-    long long base = bpre[blockIdx.x];
-    for (int e = threadIdx.x; e < tot; e += 256) {
+    long long base = bpre[j];
+    const int chunk = (tot + parts - 1) / parts;
+    const int e_lo = min(part * chunk, tot), e_hi = min(e_lo + chunk, tot);
+    for (int e = e_lo + threadIdx.x; e < e_hi; e += 256) {
         // splat k of this block with soff[k] <= e < soff[k+1]
         int lo = 0, hi = 255;
         while (lo < hi) {
@@ -302,9 +313,15 @@ __global__ void __launch_bounds__(256) k_emit(RenderGeom G, const int4 *__restri
         if (pos < G.cap) {
             keys[pos] = tile;
             vals[pos] = (int)(s0 + lo);
+            if (hist0) atomicAdd(&shist[tile & (unsigned)(radix0 - 1)], 1);
         } else {
             atomicOr(status, 1);
         }
+    }
+    if (hist0) {
+        // digit-0 histogram of this block's output segment (the first radix pass scatters per segment)
+        __syncthreads();
+        for (int d = threadIdx.x; d < radix0; d += 256) hist0[d * hist_stride + blockIdx.x] = shist[d];
     }
 }
 
@@ -345,10 +362,11 @@ __global__ void __launch_bounds__(RS_THREADS) k_radix_upsweep(const unsigned *__
 
 // grid = radix blocks: exclusive scan of one digit's per-block counts; digit total -> dtot[d]
 __global__ void __launch_bounds__(256) k_radix_scan(int *__restrict__ hist, const long long *__restrict__ n_ptr,
-                                                    long long cap, int nblk_cap, int *__restrict__ dtot) {
+                                                    long long cap, int nblk_cap, int *__restrict__ dtot,
+                                                    int nblk_fixed) {
     __shared__ int wsum[8];
     long long n = clamp_n(n_ptr, cap);
-    int nblk = (int)((n + RS_ITEMS - 1) / RS_ITEMS);
+    int nblk = nblk_fixed > 0 ? nblk_fixed : (int)((n + RS_ITEMS - 1) / RS_ITEMS);
     int *h = hist + (long long)blockIdx.x * nblk_cap;
     int carry = 0;
     for (int c0 = 0; c0 < nblk; c0 += 256) {
@@ -429,6 +447,93 @@ __global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep(const unsigned *
             }
         }
         __syncthreads();
+    }
+}
+
+// First radix pass over the emit kernel's output sub-segments (one per emit block: part p of splat block
+// j, bounds as in k_emit), whose digit histograms k_emit already wrote.  Each sub-segment is ranked in
+// chunks of RS_ITEMS keys exactly like k_radix_downsweep, with the per-digit running position carried
+// across chunks.
+__global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep_seg(const unsigned *__restrict__ kin,
+                                                                    const int *__restrict__ vin,
+                                                                    unsigned *__restrict__ kout,
+                                                                    int *__restrict__ vout,
+                                                                    const int *__restrict__ bpre, int nblk_pre,
+                                                                    int parts, const long long *__restrict__ n_ptr,
+                                                                    long long cap, int shift, int radix,
+                                                                    const int *__restrict__ hist, int hist_stride,
+                                                                    const int *__restrict__ dtot) {
+    constexpr int NWARP = RS_THREADS / 32;
+    constexpr int PER_WARP = RS_ITEMS / NWARP;
+    __shared__ int wsum[NWARP];
+    __shared__ int dbase[256];
+    __shared__ int run_d[256];
+    __shared__ int wcnt[NWARP][256];
+    const long long n = clamp_n(n_ptr, cap);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int dv = tid < radix ? dtot[tid] : 0;
+    const int dpre = block_excl_scan<RS_THREADS>(dv, wsum, nullptr);
+    if (tid < radix) dbase[tid] = dpre;
+    const unsigned mask = (unsigned)radix - 1u;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    const int nseg = nblk_pre * parts;
+    for (int j = blockIdx.x; j < nseg; j += gridDim.x) {
+        const int sb = j / parts, part = j - sb * parts;
+        const long long beg = bpre[sb];
+        const long long end = sb + 1 < nblk_pre ? (long long)bpre[sb + 1] : n;
+        const long long tot = end - beg;
+        const long long chunk = (tot + parts - 1) / parts;
+        const long long b0 = min(beg + min(part * chunk, tot), n);
+        const long long b1 = min(beg + min((part + 1) * chunk, tot), n);
+        __syncthreads();
+        if (tid < radix) run_d[tid] = dbase[tid] + hist[tid * hist_stride + j];
+        for (long long c0 = b0; c0 < b1; c0 += RS_ITEMS) {
+            const long long base = c0 + warp * PER_WARP;
+            for (int d = lane; d < radix; d += 32) wcnt[warp][d] = 0;
+            __syncwarp();
+            unsigned key[RS_ROUNDS];
+            int val[RS_ROUNDS], dig[RS_ROUNDS], rank[RS_ROUNDS];
+#pragma unroll
+            for (int r = 0; r < RS_ROUNDS; r++) {
+                const long long i = base + r * 32 + lane;
+                key[r] = i < b1 ? __ldg(kin + i) : 0u;
+                val[r] = i < b1 ? __ldg(vin + i) : 0;
+            }
+#pragma unroll
+            for (int r = 0; r < RS_ROUNDS; r++) {
+                const long long i = base + r * 32 + lane;
+                const bool valid = i < b1;
+                const int d = valid ? (int)((key[r] >> shift) & mask) : -1;
+                dig[r] = d;
+                const unsigned peers = __match_any_sync(0xffffffffu, d);
+                const int pre = valid ? wcnt[warp][d] : 0;
+                rank[r] = pre + __popc(peers & lt_mask);
+                __syncwarp();
+                if (valid && (peers & lt_mask) == 0u) wcnt[warp][d] = pre + __popc(peers);
+                __syncwarp();
+            }
+            __syncthreads();
+            if (tid < radix) {
+                int run = run_d[tid];
+#pragma unroll
+                for (int w = 0; w < NWARP; w++) {
+                    const int c = wcnt[w][tid];
+                    wcnt[w][tid] = run;
+                    run += c;
+                }
+                run_d[tid] = run;
+            }
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < RS_ROUNDS; r++) {
+                if (dig[r] >= 0) {
+                    const int pos = wcnt[warp][dig[r]] + rank[r];
+                    kout[pos] = key[r];
+                    vout[pos] = val[r];
+                }
+            }
+            __syncthreads();
+        }
     }
 }
 
@@ -973,6 +1078,7 @@ struct Plan {
     int ngroups;
     long long cap;
     int nblk_pre, nblk_sort, passes, radix_bits;
+    int emit_parts;  // emit blocks per preprocessing block (>= 4 blocks per SM of 148 in all)
     size_t o_rec, o_meta, o_counts, o_bsum, o_zero, o_gpairs, o_gsplats, o_misc, o_ranges, z_len;
     size_t o_keys_a, o_vals_a, o_keys_b, o_vals_b, o_hist, o_dtot, o_fields, fwd_bytes;
     size_t o_G, o_gfields, o_bzero, o_acc, o_gbg, bz_len, total_bytes;
@@ -1115,6 +1221,7 @@ void make_plan(const gs_render_desc *d, Plan &pl) {
     long long BN = (long long)d->B * d->N;
     pl.nblk_pre = (int)std::max<long long>(1, (BN + 255) / 256);
     pl.nblk_sort = (int)std::max<long long>(1, (cap + RS_ITEMS - 1) / RS_ITEMS);
+    pl.emit_parts = std::min(8, std::max(1, (4 * 148 + pl.nblk_pre - 1) / pl.nblk_pre));
     long long ntiles = (long long)d->B * pl.G.tiles_per_image;
     int bits = 0;
     while ((1LL << bits) < ntiles) bits++;
@@ -1137,7 +1244,7 @@ void make_plan(const gs_render_desc *d, Plan &pl) {
     pl.o_vals_a = take(sizeof(int) * (size_t)std::max<long long>(cap, 1));
     pl.o_keys_b = take(sizeof(unsigned) * (size_t)std::max<long long>(cap, 1));
     pl.o_vals_b = take(sizeof(int) * (size_t)std::max<long long>(cap, 1));
-    pl.o_hist = take(sizeof(int) * 256 * (size_t)pl.nblk_sort);
+    pl.o_hist = take(sizeof(int) * 256 * (size_t)std::max(pl.nblk_sort, pl.nblk_pre * pl.emit_parts));
     pl.o_dtot = take(sizeof(int) * 256);
     pl.o_fields = take(sizeof(float) * (size_t)d->B * pl.G.fld_per_image);
     pl.fwd_bytes = o;
@@ -1254,26 +1361,36 @@ int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_sca
     if (d->mode != GS_MODE_EXACT && d->N > 0) {
         k_scan_blocks<<<1, 1024, 0, s>>>(at<int>(workspace, pl.o_bsum), pl.nblk_pre, total);
         GS_CHECK_LAUNCH("k_scan_blocks");
-        k_emit<<<pl.nblk_pre, 256, 0, s>>>(G, at<int4>(workspace, pl.o_meta), at<int>(workspace, pl.o_counts),
-                                           at<int>(workspace, pl.o_bsum), at<unsigned>(workspace, pl.o_keys_a),
-                                           at<int>(workspace, pl.o_vals_a), status);
+        int radix = 1 << pl.radix_bits;
+        int *hist = at<int>(workspace, pl.o_hist), *dtot = at<int>(workspace, pl.o_dtot);
+        const int nemit = pl.nblk_pre * pl.emit_parts;
+        k_emit<<<nemit, 256, 0, s>>>(G, at<int4>(workspace, pl.o_meta), at<int>(workspace, pl.o_counts),
+                                     at<int>(workspace, pl.o_bsum), pl.emit_parts, at<unsigned>(workspace, pl.o_keys_a),
+                                     at<int>(workspace, pl.o_vals_a), status, pl.passes > 0 ? hist : nullptr, nemit,
+                                     radix);
         GS_CHECK_LAUNCH("k_emit");
         unsigned *ka = at<unsigned>(workspace, pl.o_keys_a), *kb = at<unsigned>(workspace, pl.o_keys_b);
         int *va = at<int>(workspace, pl.o_vals_a), *vb = at<int>(workspace, pl.o_vals_b);
-        int radix = 1 << pl.radix_bits;
         const int pgrid = std::min(pl.nblk_sort, 148 * 8);
         for (int p = 0; p < pl.passes; p++) {
             int shift = p * pl.radix_bits;
-            k_radix_upsweep<<<pgrid, RS_THREADS, 0, s>>>(ka, total, pl.cap, shift, radix,
-                                                                at<int>(workspace, pl.o_hist), pl.nblk_sort);
-            GS_CHECK_LAUNCH("k_radix_upsweep");
-            k_radix_scan<<<radix, 256, 0, s>>>(at<int>(workspace, pl.o_hist), total, pl.cap, pl.nblk_sort,
-                                               at<int>(workspace, pl.o_dtot));
-            GS_CHECK_LAUNCH("k_radix_scan");
-            k_radix_downsweep<<<pgrid, RS_THREADS, 0, s>>>(ka, va, kb, vb, total, pl.cap, shift, radix,
-                                                                  at<int>(workspace, pl.o_hist), pl.nblk_sort,
-                                                                  at<int>(workspace, pl.o_dtot));
-            GS_CHECK_LAUNCH("k_radix_downsweep");
+            if (p == 0) {
+                // digit-0 histograms per emit segment come from k_emit
+                k_radix_scan<<<radix, 256, 0, s>>>(hist, total, pl.cap, nemit, dtot, nemit);
+                GS_CHECK_LAUNCH("k_radix_scan");
+                k_radix_downsweep_seg<<<std::min(nemit, 148 * 8), RS_THREADS, 0, s>>>(
+                    ka, va, kb, vb, at<int>(workspace, pl.o_bsum), pl.nblk_pre, pl.emit_parts, total, pl.cap, shift,
+                    radix, hist, nemit, dtot);
+                GS_CHECK_LAUNCH("k_radix_downsweep_seg");
+            } else {
+                k_radix_upsweep<<<pgrid, RS_THREADS, 0, s>>>(ka, total, pl.cap, shift, radix, hist, pl.nblk_sort);
+                GS_CHECK_LAUNCH("k_radix_upsweep");
+                k_radix_scan<<<radix, 256, 0, s>>>(hist, total, pl.cap, pl.nblk_sort, dtot, 0);
+                GS_CHECK_LAUNCH("k_radix_scan");
+                k_radix_downsweep<<<pgrid, RS_THREADS, 0, s>>>(ka, va, kb, vb, total, pl.cap, shift, radix, hist,
+                                                               pl.nblk_sort, dtot);
+                GS_CHECK_LAUNCH("k_radix_downsweep");
+            }
             std::swap(ka, kb);
             std::swap(va, vb);
         }
