@@ -157,12 +157,25 @@ class EncodeRenderWorkload:
         return self.pipe.replay()
 
     def e2e_buffers(self):
-        return self.torch.empty(1, 3, self.H, self.W).pin_memory()
+        """The streaming form of the public pipeline (EncodeRenderStream, two graph instances) and two
+        pinned output images."""
+        from gaussian_2d_splat_encoder_b200 import pipeline
 
-    def e2e_step(self, buf):
-        rec = self.pipe(self.host[self.i % len(self.host)])     # H2D from pinned memory + replay
+        if not hasattr(self, "stream"):
+            self.stream = pipeline.EncodeRenderStream(self.enc, self.H, self.W, self.dev).capture()
+        return [self.torch.empty(1, 3, self.H, self.W).pin_memory() for _ in range(2)]
+
+    def e2e_begin(self):
+        self.stream.start_after()
+
+    def e2e_step(self, bufs):
+        # H2D of this image from pinned memory, encode + render, D2H of its reconstruction; the copies of
+        # neighbouring images overlap the kernels
+        self.stream.submit(self.host[self.i % len(self.host)], bufs[self.i % 2])
         self.i += 1
-        buf.copy_(rec, non_blocking=True)                       # D2H of the reconstruction
+
+    def e2e_end(self):
+        self.stream.wait_into()
 
     def io_bytes(self):
         return 3 * self.H * self.W * 4, 3 * self.H * self.W * 4
@@ -172,6 +185,9 @@ class EncodeRenderWorkload:
                             "tcgen05) + render_alpha_octave(odds) fp32, inference, one CUDA graph per step",
                 "images_per_step_per_gpu": 1, "encoder_weights": self.wdesc, "H": self.H, "W": self.W,
                 "splats_per_image": (self.H // 8) ** 2 * 2 + (self.H // 4) ** 2 * 2,
+                "e2e_api": "pipeline.EncodeRenderStream: pinned host image -> H2D -> encode+render graph -> D2H "
+                           "of the reconstruction, per image; two graph instances so the copies of "
+                           "neighbouring images overlap the kernels",
                 "l2": "flushed between timed steps (256 MB write, outside the timed events)"}
 
     @classmethod
@@ -264,6 +280,35 @@ class RenderWorkload:
         g = (2.0 / out.size) * (out - s["target"])
         O.render_alpha_octave(s["mu"], s["log_scale"], s["color"], s["opacity"], s["bg"], cls.H, cls.W,
                               theta=s["theta"], odds=True, grad_out=g)
+
+
+def time_points(torch, dev, N=92160, P=3000, H=768, W=768, reps=20):
+    """render_alpha_subsampled (render.py:68-87) forward + backward of sum(out * g): config-1 splats at
+    P = 3000 sampled pixels (the released checkpoint's training n_pixels), eager calls timed with CUDA
+    events.  Returns (ms per fwd+bwd, pixel-pairs per call)."""
+    from gaussian_2d_splat_encoder_b200 import synth
+    from gaussian_2d_splat_encoder_b200.render import render_alpha_subsampled
+
+    s = synth.synth_splats_cfg1(N, H, W, seed=1)
+    L = [s[k].to(dev).requires_grad_(True) for k in ("mu", "log_scale", "color", "opacity", "bg", "theta")]
+    g = torch.Generator(device=dev).manual_seed(7)
+    idx = torch.randint(0, H * W, (1, P), device=dev, generator=g)
+    gout = torch.randn(1, 3, P, device=dev, generator=g)
+
+    def one():
+        out, _ = render_alpha_subsampled(*L[:5], H, W, theta=L[5], pixel_indices=idx)
+        return torch.autograd.grad(out, L, grad_outputs=gout)
+
+    for _ in range(3):
+        one()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        one()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps, N * P
 
 
 class FitWorkload:
@@ -552,9 +597,15 @@ def main():
     barrier()
     Ke = max(3, min(K, 50))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if hasattr(wl, "e2e_end"):
+        wl.e2e_end()
     e0.record()
+    if hasattr(wl, "e2e_begin"):
+        wl.e2e_begin()
     for _ in range(Ke):
         wl.e2e_step(buf)
+    if hasattr(wl, "e2e_end"):
+        wl.e2e_end()
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
@@ -571,6 +622,10 @@ def main():
         rms = time_steps(torch, rw, 50, flush)
         sec = {"render_fwd_bwd_ms_per_image": statistics.mean(rms),
                "stages_ms": profile_stages(torch, lib, RenderWorkload, dev, flush)}
+        pms, ppairs = time_points(torch, dev)
+        sec["points"] = {"workload": "render_alpha_subsampled fwd+bwd, 92,160 config-1 splats x 3,000 pixels",
+                         "ms_per_step": pms, "pixel_pairs": ppairs,
+                         "gpixel_pairs_per_s": ppairs / (pms * 1e-3) / 1e9}
     barrier()
 
     images = K * world
@@ -601,6 +656,7 @@ def main():
                             "peak_source": f"MEASURED_PEAKS.json bf16_tflops (burst, {pk['source']})"}
         line["render_fwd_bwd_ms_per_image"] = sec["render_fwd_bwd_ms_per_image"] if sec else None
         line["render_stages_ms"] = sec["stages_ms"] if sec else None
+        line["points_fwd_bwd"] = sec["points"] if sec else None
     else:
         if wcls is RenderWorkload:
             line["render_fwd_bwd_ms_per_image"] = tot_ms / K

@@ -46,6 +46,10 @@ SIGNATURES = {
     "gs_render_fwd": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "gs_render_fwd_noalloc": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P, _P]),
     "gs_render_bwd": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
+    "gs_render_points_workspace_size": (C.c_size_t, [_DESC, C.c_int32, C.c_int]),
+    "gs_render_points_fwd": (C.c_int, [_DESC, C.c_int32, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
+    "gs_render_points_bwd": (C.c_int, [_DESC, C.c_int32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                       C.c_size_t, _P]),
     "gs_render_debug_bins": (C.c_int, [_DESC, _P, _P, _P, _P, _P, _P, _P]),
     "gs_activate_scale": (C.c_int, [_P, _P, C.c_int64, _P]),
     "gs_l2_loss_grad": (C.c_int, [_P, _P, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_float, _P, _P,
@@ -54,6 +58,8 @@ SIGNATURES = {
     "gs_encoder_workspace_size": (C.c_size_t, [_P]),
     "gs_encoder_fwd": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "gs_encoder_error_flag": (C.c_int, [_P, _P, _P]),
+    "gs_encode_render_workspace_size": (C.c_size_t, [_P]),
+    "gs_encode_render_fwd": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "gs_last_error": (C.c_char_p, []),
     "gs_kernel_launches": (C.c_uint64, []),
     "gs_profile_enable": (None, [C.c_int]),

@@ -41,6 +41,8 @@ struct GroupGeom {
     int ty_lo, ty_hi;  // tile rows this call needs (the native row band's bilinear footprint)
     float up_sy, up_sx;  // bilinear source-index scales group/native, (float)Hg / (float)H as torch computes
     int adj_off;         // first texel of this group in the adjoint launch (coarse groups only), -1 if none
+    int prior_grp;       // group of a prior render whose fields this group reuses, -1 if none
+    int prior_off;       // first float of that group's fields inside the prior's per-image block
     int pad;
 };
 
@@ -52,6 +54,11 @@ struct RenderGeom {
     long long fld_per_image;  // floats of group fields per image
     long long cap;            // pair capacity of the workspace
     int order[GS_MAX_GROUPS]; // summation order of groups in the composite (the reference's order)
+    // reuse of a prior render's group fields: splats [0, skip_n) of each image whose octave at the prior's
+    // representative size prior_rep is the prior group mapped to their group here are not binned; the
+    // prior group's fields are added to this group's fields instead
+    int skip_n;
+    float prior_rep;
     GroupGeom g[GS_MAX_GROUPS];
 };
 

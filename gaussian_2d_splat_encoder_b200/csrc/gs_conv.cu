@@ -7,7 +7,7 @@
 // the convolution's zero padding) and the B tile (BN x KC slice of the packed weight matrix) into a
 // STAGES-deep shared-memory ring; one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32) into
 // TMEM and commits each stage back to the producer.  Accumulators are double-buffered in TMEM, so the
-// epilogue warps (tcgen05.ld, bias, exact GELU, GroupNorm(8) partial sums, bf16 NHWC store) of one
+// epilogue warps (tcgen05.ld, bias, GELU, GroupNorm(8) partial sums, bf16 NHWC store) of one
 // item run while the tensor cores work on the next.
 //
 // Stride-2 convolutions read their input through a 5-D view (C, x parity, x/2, y, image) so the
@@ -31,18 +31,47 @@ using namespace gs_tc;
 
 namespace {
 
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// GELU(x) = 0.5 x (1 + erf(x / sqrt 2)) with erf from the rational approximation of Abramowitz &
+// Stegun, Handbook of Mathematical Functions, formula 7.1.26: for z >= 0,
+// erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2), t = 1 / (1 + p z), |error| <= 1.5e-7.
+// 1 + erf(x / sqrt 2) is formed as 2 - q (x >= 0) or q (x < 0), q = t (...) exp(-z^2), so the negative
+// tail keeps its relative accuracy.  In fp32 the GELU error stays below 7e-7 absolute over [-12, 12],
+// far under the bf16 rounding of the stored activation.
+__device__ __forceinline__ float gelu_erf(float x) {
+    const float z = fabsf(x) * 0.70710678118654752f;
+    const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
+    float q = fmaf(1.061405429f, t, -1.453152027f);
+    q = fmaf(q, t, 1.421413741f);
+    q = fmaf(q, t, -0.284496736f);
+    q = fmaf(q, t, 0.254829592f);
+    q *= t * ex2_approx(-(z * z) * 1.4426950408889634f);
+    return 0.5f * x * (x >= 0.f ? 2.0f - q : q);
+}
+
 // Persistent, warp-specialised convolution.  Work item = MT vertically stacked 128-pixel M-tiles x
 // one BN-wide slice of the output channels; CTAs stride over the items.
 //   warp 0        TMA producer (one lane): A tiles of the MT M-tiles + the B slice, STAGES-deep ring
 //   warp 1        TMEM owner + MMA issuer (one lane): MT accumulators of 128 x BN fp32 per item,
 //                 double-buffered in TMEM so the epilogue of item i overlaps the K loop of item i+1
 //   warps 2..     4*MT epilogue warps: warp w drains TMEM lanes 32*(w%4).. of accumulator (w-2)/4 --
-//                 bias, exact GELU, GroupNorm(8) partial sums, bf16 NHWC store
+//                 bias, GELU (gelu_erf), GroupNorm(8) partial sums, bf16 NHWC store
 // Every wait is bounded; a wait that gives up records its stage in *err and raises a CTA-wide abort
 // flag so the other roles stop issuing, then the CTA drains its copies and MMAs and frees TMEM.
 template <int BN, int KC, int STAGES, int MT, int CPG, int MINB>
 __global__ void __launch_bounds__(64 + 128 * MT, MINB)
-    k_conv_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, ConvArgs a) {
+    k_conv_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+              const __grid_constant__ CUtensorMap tmB, ConvArgs a) {
     constexpr int NEPI = 4 * MT;
     constexpr uint32_t A_BYTES = 128u * KC * 2u;
     constexpr uint32_t B_BYTES = (uint32_t)BN * KC * 2u;
@@ -87,6 +116,7 @@ __global__ void __launch_bounds__(64 + 128 * MT, MINB)
         consumed = 0;
         fence_barrier_init();
         prefetch_tensormap(&tmA);
+        if (a.nchunks1 < a.nchunks) prefetch_tensormap(&tmA2);
         prefetch_tensormap(&tmB);
     }
     tc_fence_before();
@@ -106,6 +136,8 @@ __global__ void __launch_bounds__(64 + 128 * MT, MINB)
                 const int ty = t % a.tiles_y;
                 const int b = t / a.tiles_y;
                 const int x0 = tx * a.TX, y0 = ty * a.TY * MT;
+                // (kh, kw, chunk) of k-block kb, stepped without divisions
+                int kh = 0, kw = 0, chunk = 0;
                 for (int kb = 0; kb < a.nkb; kb++, it++) {
                     const int s = it % STAGES;
                     if (it >= STAGES && !mbar_wait_or_abort(&empty[s], ((it / STAGES) - 1) & 1, &abort_flag, a.err, 1))
@@ -114,25 +146,34 @@ __global__ void __launch_bounds__(64 + 128 * MT, MINB)
                     mbar_arrive_expect_tx(&full[s], STAGE);
                     uint8_t *sa = smem + s * STAGE;
                     uint8_t *sb = sa + MT * A_BYTES;
-                    const int tap = kb / a.nchunks, chunk = kb - tap * a.nchunks;
-                    const int kh = tap / a.KW, kw = tap - kh * a.KW;
-                    const int c0 = chunk * KC;
+                    // input channels [0, nchunks1*KC) come from tmA, the rest from tmA2 (a concatenation
+                    // the convolution reads in place)
+                    const bool first = chunk < a.nchunks1;
+                    const CUtensorMap *ma = first ? &tmA : &tmA2;
+                    const int c0 = (first ? chunk : chunk - a.nchunks1) * KC;
 #pragma unroll
                     for (int mt = 0; mt < MT; mt++) {
                         const int ym = y0 + mt * a.TY;
                         if (a.stride == 1) {
-                            tma_load_4d(sa + mt * A_BYTES, &tmA, &full[s], c0, x0 + kw - a.pad, ym + kh - a.pad, b);
+                            tma_load_4d(sa + mt * A_BYTES, ma, &full[s], c0, x0 + kw - a.pad, ym + kh - a.pad, b);
                         } else {
                             const int xin = 2 * x0 + kw - a.pad;
                             const int xp = xin & 1;
                             const int xh = (xin - xp) / 2;
                             for (int r = 0; r < a.TY; r++)
-                                tma_load_5d(sa + mt * A_BYTES + r * a.TX * KC * 2, &tmA, &full[s], c0, xp, xh,
+                                tma_load_5d(sa + mt * A_BYTES + r * a.TX * KC * 2, ma, &full[s], c0, xp, xh,
                                             2 * (ym + r) + kh - a.pad, b);
                         }
                     }
                     tma_load_2d(sb, &tmB, &full[s], kb * KC, nb * BN);
                     issued = it + 1;
+                    if (++chunk == a.nchunks) {
+                        chunk = 0;
+                        if (++kw == a.KW) {
+                            kw = 0;
+                            ++kh;
+                        }
+                    }
                 }
                 if (abort_flag) break;
             }
@@ -230,7 +271,7 @@ __global__ void __launch_bounds__(64 + 128 * MT, MINB)
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
                     float x = v[i];
-                    if (a.gelu) x = 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+                    if (a.gelu) x = gelu_erf(x);
                     v[i] = x;
                     if (CPG == 8 && i >= 8) {
                         s1 += x;
@@ -343,7 +384,8 @@ int sm_count() {
 }
 
 template <int BN, int KC, int STAGES, int MT, int CPG, int MINB>
-int launch(const CUtensorMap &tA, const CUtensorMap &tB, const ConvArgs &a, cudaStream_t st) {
+int launch(const CUtensorMap &tA, const CUtensorMap &tA2, const CUtensorMap &tB, const ConvArgs &a,
+           cudaStream_t st) {
     constexpr size_t SMEM = (size_t)STAGES * (MT * 128 * KC * 2 + BN * KC * 2) + 1024;
     auto kern = k_conv_tc<BN, KC, STAGES, MT, CPG, MINB>;
     static bool configured = false;
@@ -354,7 +396,7 @@ int launch(const CUtensorMap &tA, const CUtensorMap &tB, const ConvArgs &a, cuda
     const long long items = (long long)a.B * a.tiles_y * a.tiles_x * (a.Co / BN);
     const long long slots = (long long)sm_count() * MINB;
     const int grid = (int)(items < slots ? items : slots);
-    kern<<<grid, 64 + 128 * MT, SMEM, st>>>(tA, tB, a);
+    kern<<<grid, 64 + 128 * MT, SMEM, st>>>(tA, tA2, tB, a);
     return cudaGetLastError() == cudaSuccess ? GS_OK : GS_ERR_CUDA;
 }
 
@@ -380,12 +422,19 @@ void gs_conv_pick_tile(int Ho, int Wo, int MT, int *TX, int *TY) {
 
 int gs_conv_run(const gs_conv_desc *d, const void *in, const void *w, const float *bias, void *out, double *stats,
                 int *err, cudaStream_t st) {
+    return gs_conv_run2(d, in, d ? d->Cin : 0, nullptr, w, bias, out, stats, err, st);
+}
+
+int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in2, const void *w, const float *bias,
+                 void *out, double *stats, int *err, cudaStream_t st) {
     if (!d || !in || !w || !bias || !out) return GS_ERR_BAD_ARGUMENT;
     const int B = d->B, Hi = d->H, Wi = d->W, Ci = d->Cin, Co = d->Cout;
+    const int Ci2 = Ci - Cin1;
+    if (Cin1 <= 0 || Ci2 < 0 || (Ci2 > 0 && !in2)) return GS_ERR_BAD_ARGUMENT;
     if (B <= 0 || Hi <= 0 || Wi <= 0 || d->kh <= 0 || d->kw <= 0 || d->pad < 0) return GS_ERR_BAD_ARGUMENT;
     if (!(Co == 64 || Co == 128 || Co == 256)) return GS_ERR_BAD_ARGUMENT;
     const int KC = d->kind == 1 ? 16 : 64;
-    if (Ci % KC != 0) return GS_ERR_BAD_ARGUMENT;
+    if (Ci % KC != 0 || Cin1 % KC != 0) return GS_ERR_BAD_ARGUMENT;
     if (d->kind == 1 && Co != 64) return GS_ERR_BAD_ARGUMENT;
     if (d->stride == 2 && (Wi % 2 != 0)) return GS_ERR_BAD_ARGUMENT;
     if (d->stride != 1 && d->stride != 2) return GS_ERR_BAD_ARGUMENT;
@@ -402,27 +451,36 @@ int gs_conv_run(const gs_conv_desc *d, const void *in, const void *w, const floa
     a.tiles_x = (a.Wo + a.TX - 1) / a.TX;
     a.tiles_y = (a.Ho + a.TY * MT - 1) / (a.TY * MT);
     a.nchunks = Ci / KC;
+    a.nchunks1 = Cin1 / KC;
     a.nkb = d->kh * d->kw * a.nchunks;
     a.gelu = d->gelu;
     a.bias = bias;
     a.out = reinterpret_cast<__nv_bfloat16 *>(out);
     a.stats = stats;
     a.err = err;
-    CUtensorMap tA, tB;
+    CUtensorMap tA, tA2, tB;
     CUtensorMapSwizzle swz = KC == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B;
-    int s;
-    if (d->stride == 1) {
-        uint64_t dims[4] = {(uint64_t)Ci, (uint64_t)Wi, (uint64_t)Hi, (uint64_t)B};
-        uint64_t str[3] = {(uint64_t)Ci * 2, (uint64_t)Wi * Ci * 2, (uint64_t)Hi * Wi * Ci * 2};
-        uint32_t box[4] = {(uint32_t)KC, (uint32_t)a.TX, (uint32_t)a.TY, 1};
-        s = make_map(&tA, in, 4, dims, str, box, swz);
-    } else {
-        uint64_t dims[5] = {(uint64_t)Ci, 2, (uint64_t)(Wi / 2), (uint64_t)Hi, (uint64_t)B};
-        uint64_t str[4] = {(uint64_t)Ci * 2, (uint64_t)Ci * 4, (uint64_t)Wi * Ci * 2, (uint64_t)Hi * Wi * Ci * 2};
+    // NHWC input with Cm channels: a 4-D box for stride 1, a 5-D (C, x parity, x/2, y, image) view for stride 2
+    auto input_map = [&](CUtensorMap *tm, const void *ptr, int Cm) {
+        if (d->stride == 1) {
+            uint64_t dims[4] = {(uint64_t)Cm, (uint64_t)Wi, (uint64_t)Hi, (uint64_t)B};
+            uint64_t str[3] = {(uint64_t)Cm * 2, (uint64_t)Wi * Cm * 2, (uint64_t)Hi * Wi * Cm * 2};
+            uint32_t box[4] = {(uint32_t)KC, (uint32_t)a.TX, (uint32_t)a.TY, 1};
+            return make_map(tm, ptr, 4, dims, str, box, swz);
+        }
+        uint64_t dims[5] = {(uint64_t)Cm, 2, (uint64_t)(Wi / 2), (uint64_t)Hi, (uint64_t)B};
+        uint64_t str[4] = {(uint64_t)Cm * 2, (uint64_t)Cm * 4, (uint64_t)Wi * Cm * 2, (uint64_t)Hi * Wi * Cm * 2};
         uint32_t box[5] = {(uint32_t)KC, 1, (uint32_t)a.TX, 1, 1};
-        s = make_map(&tA, in, 5, dims, str, box, swz);
-    }
+        return make_map(tm, ptr, 5, dims, str, box, swz);
+    };
+    int s = input_map(&tA, in, Cin1);
     if (s != GS_OK) return s;
+    if (Ci2 > 0) {
+        s = input_map(&tA2, in2, Ci2);
+        if (s != GS_OK) return s;
+    } else {
+        tA2 = tA;
+    }
     const int K = d->kh * d->kw * Ci;
     {
         uint64_t dims[2] = {(uint64_t)K, (uint64_t)Co};
@@ -431,10 +489,10 @@ int gs_conv_run(const gs_conv_desc *d, const void *in, const void *w, const floa
         s = make_map(&tB, w, 2, dims, str, box, swz);
     }
     if (s != GS_OK) return s;
-    if (KC == 16) return launch<64, 16, 8, 2, 8, 2>(tA, tB, a, st);
-    if (Co == 64) return launch<64, 64, 5, 2, 8, 1>(tA, tB, a, st);
-    if (Co == 128) return launch<128, 64, 4, 2, 16, 1>(tA, tB, a, st);
-    return launch<128, 64, 6, 1, 32, 1>(tA, tB, a, st);
+    if (KC == 16) return launch<64, 16, 8, 2, 8, 2>(tA, tA2, tB, a, st);
+    if (Co == 64) return launch<64, 64, 5, 2, 8, 1>(tA, tA2, tB, a, st);
+    if (Co == 128) return launch<128, 64, 4, 2, 16, 1>(tA, tA2, tB, a, st);
+    return launch<128, 64, 6, 1, 32, 1>(tA, tA2, tB, a, st);
 }
 
 extern "C" int gs_conv2d(const gs_conv_desc *d, const void *in_bf16, const void *w_bf16, const float *bias,

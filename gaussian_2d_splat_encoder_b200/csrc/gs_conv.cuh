@@ -11,6 +11,7 @@ struct ConvArgs {
     int Ho, Wo;
     int TX, TY, tiles_x, tiles_y;
     int nchunks, nkb;
+    int nchunks1;  // input-channel chunks read from the first input (the rest from the second)
     int gelu;
     const float *bias;
     __nv_bfloat16 *out;
@@ -21,3 +22,7 @@ struct ConvArgs {
 void gs_conv_pick_tile(int Ho, int Wo, int MT, int *TX, int *TY);
 int gs_conv_run(const gs_conv_desc *d, const void *in, const void *w, const float *bias, void *out, double *stats,
                 int *err, cudaStream_t st);
+// The same convolution over the channel concatenation [in (Cin1 channels), in2 (d->Cin - Cin1 channels)],
+// both NHWC with the same B, H, W; neither is copied.
+int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in2, const void *w, const float *bias,
+                 void *out, double *stats, int *err, cudaStream_t st);

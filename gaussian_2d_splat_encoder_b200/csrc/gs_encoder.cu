@@ -2,7 +2,8 @@
 // bigwolfeman/gaussian-2d-splat-encoder, gaussian_splat_encoder/efficient_encoder.py:306-378).
 //
 //   k_prep        grey, Sobel/4, gradient magnitude (efficient_encoder.py:123-130) and the
-//                 space-to-depth bf16 input of the first convolution; per-block pooled gradients
+//                 space-to-depth bf16 input of the first convolution
+//   k_pool48      4x4 and 8x8 pooled gradients in one pass
 //   conv1..3      tcgen05 implicit GEMM (gs_conv.cu): 7x7/2 (on the space-to-depth tensor as 4x4/1),
 //                 3x3/2, 3x3/2, bias + GELU + GroupNorm statistics fused (efficient_encoder.py:53-58)
 //   k_gn_apply    GroupNorm(8) normalise + affine in place (NHWC bf16); the last one also sums the
@@ -11,8 +12,8 @@
 //   k_head        1x1 head + activations of one splat group   (efficient_encoder.py:170-197, 340-342)
 //   coarse render render_alpha_octave at residual_grid^2 with odds (gs_render.cu)
 //   k_cond        bilinear(image -> grid), |target - render|, mean(render)   (efficient_encoder.py:349-351)
-//   k_concat      bilinear(s8 -> s4 size) || s4  (the _UpBlock input, efficient_encoder.py:89-91)
-//   conv4         3x3/1 384->128 decoder convolution on the tensor cores
+//   k_upsample    bilinear(s8 -> s4 size)  (the _UpBlock input is [this, s4], efficient_encoder.py:89-91)
+//   conv4         3x3/1 384->128 decoder convolution on the tensor cores, reading [up, s4] in place
 //   k_head (fine) GroupNorm applied on the fly, [fine_feat, pooled gradient, bilinear(cond)] 1x1 head
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -26,6 +27,7 @@
 #include "../../include/gsplat_b200.h"
 #include "gs_conv.cuh"
 #include "gs_prof.cuh"
+#include "gs_render_internal.cuh"
 
 namespace {
 
@@ -106,73 +108,116 @@ __global__ void __launch_bounds__(256) k_prep(const float *__restrict__ image, i
     dst[1] = reinterpret_cast<uint4 *>(z)[1];
 }
 
-// adaptive_avg_pool2d of grad to (H/f, W/f) for f dividing H and W
-__global__ void k_pool(const float *__restrict__ grad, int B, int H, int W, int f, float *__restrict__ out) {
-    const int Ho = H / f, Wo = W / f;
-    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long long)B * Ho * Wo) return;
-    int b = (int)(i / ((long long)Ho * Wo));
-    int r = (int)(i - (long long)b * Ho * Wo);
-    int y = r / Wo, x = r - y * Wo;
-    const float *g = grad + (long long)b * H * W;
-    float s = 0.f;
-    for (int a = 0; a < f; a++)
-        for (int c = 0; c < f; c++) s += g[(long long)(y * f + a) * W + x * f + c];
-    out[i] = s / (float)(f * f);
+// adaptive_avg_pool2d of grad to (H/4, W/4) and (H/8, W/8) (H, W multiples of 8): eight consecutive
+// lanes own one 8x8 block, lane a loading row a with two 16-byte loads; row sums meet by shuffles.
+__global__ void __launch_bounds__(256) k_pool48(const float *__restrict__ grad, int B, int H, int W,
+                                                float *__restrict__ out4, float *__restrict__ out8) {
+    const int H8 = H / 8, W8 = W / 8;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const int i = t >> 3, a = t & 7;
+    const bool live = i < B * H8 * W8;
+    const int ii = live ? i : 0;
+    const int b = ii / (H8 * W8);
+    const int r = ii - b * H8 * W8;
+    const int y = r / W8, x = r - y * W8;
+    const float *g = grad + (long long)b * H * W + (long long)(8 * y + a) * W + 8 * x;
+    const float4 lo = *reinterpret_cast<const float4 *>(g);
+    const float4 hi = *reinterpret_cast<const float4 *>(g + 4);
+    float sl = ((lo.x + lo.y) + lo.z) + lo.w, sh = ((hi.x + hi.y) + hi.z) + hi.w;
+    // 4-row sums (rows 0-3 or 4-7 of the block), then the whole block
+    sl += __shfl_xor_sync(0xffffffffu, sl, 1);
+    sh += __shfl_xor_sync(0xffffffffu, sh, 1);
+    sl += __shfl_xor_sync(0xffffffffu, sl, 2);
+    sh += __shfl_xor_sync(0xffffffffu, sh, 2);
+    float s8 = sl + sh;
+    s8 += __shfl_xor_sync(0xffffffffu, s8, 4);
+    if (!live) return;
+    const int W4 = W / 4;
+    if ((a & 3) == 0) {
+        float *o4 = out4 + (long long)b * (H / 4) * W4 + (long long)(2 * y + (a >> 2)) * W4 + 2 * x;
+        o4[0] = sl / 16.0f;
+        o4[1] = sh / 16.0f;
+    }
+    if (a == 0) out8[i] = s8 / 64.0f;
 }
 
-// GroupNorm(8) apply in place on NHWC bf16 [B][HW][C]; chsum (optional) += per-channel sums of the
-// normalised values (mean for the background head).
-__global__ void __launch_bounds__(256) k_gn_apply(__nv_bfloat16 *__restrict__ x, int B, long long HW, int C,
+// GroupNorm(8) apply in place on NHWC bf16 [B][HW][C]; chsum (optional) receives this block's per-channel
+// sums of the normalised values, chsum[b][blockIdx.x][C] (k_bg reduces them in a fixed order, so the
+// background colour is reproducible bit for bit).  Each thread handles 8-channel vectors of one fixed
+// channel octet (the grid stride in channels, gridDim.x * 256 * 8, is a multiple of C), so its
+// scale/shift and its channel sums stay in registers.
+__global__ void __launch_bounds__(256) k_gn_apply(__nv_bfloat16 *__restrict__ x, int HW, int C,
                                                   const double *__restrict__ stats, const float *__restrict__ gamma,
                                                   const float *__restrict__ beta, float *__restrict__ chsum) {
-    extern __shared__ float sh[];  // scale[C], shift[C], csum[C]
-    float *scale = sh, *shift = sh + C, *csum = sh + 2 * C;
+    __shared__ float red[256][9];
     const int b = blockIdx.y;
+    const int nvec = HW * (C / 8);
+    const int stride = gridDim.x * blockDim.x;
+    int v = blockIdx.x * blockDim.x + threadIdx.x;
+    const int c0 = (v * 8) % C;
+    const int g = c0 / (C / 8);
     const double n = (double)HW * (C / 8);
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        int g = c / (C / 8);
-        double mean = stats[(b * 8 + g) * 2] / n;
-        double var = stats[(b * 8 + g) * 2 + 1] / n - mean * mean;
-        if (var < 0) var = 0;
-        float rstd = (float)(1.0 / sqrt(var + 1e-5));
-        scale[c] = gamma[c] * rstd;
-        shift[c] = beta[c] - (float)mean * gamma[c] * rstd;
-        csum[c] = 0.f;
+    const double mean = stats[(b * 8 + g) * 2] / n;
+    double var = stats[(b * 8 + g) * 2 + 1] / n - mean * mean;
+    if (var < 0) var = 0;
+    const float rstd = (float)(1.0 / sqrt(var + 1e-5));
+    float sc[8], sh[8], cs[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        sc[k] = gamma[c0 + k] * rstd;
+        sh[k] = beta[c0 + k] - (float)mean * gamma[c0 + k] * rstd;
+        cs[k] = 0.f;
     }
-    __syncthreads();
-    const long long nvec = HW * C / 8;
-    __nv_bfloat16 *xb = x + (long long)b * HW * C;
-    for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += (long long)gridDim.x * blockDim.x) {
-        uint4 u = reinterpret_cast<uint4 *>(xb)[v];
+    uint4 *xb = reinterpret_cast<uint4 *>(x + (long long)b * HW * C);
+    auto apply = [&](uint4 &u) {
         __nv_bfloat16 *e = reinterpret_cast<__nv_bfloat16 *>(&u);
-        int c0 = (int)((v * 8) % C);
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            float f = __bfloat162float(e[k]) * scale[c0 + k] + shift[c0 + k];
-            e[k] = __float2bfloat16_rn(f);
-            if (chsum) atomicAdd(&csum[c0 + k], __bfloat162float(e[k]));
+            e[k] = __float2bfloat16_rn(fmaf(__bfloat162float(e[k]), sc[k], sh[k]));
+            cs[k] += __bfloat162float(e[k]);
         }
-        reinterpret_cast<uint4 *>(xb)[v] = u;
+    };
+    for (; v + stride < nvec; v += 2 * stride) {
+        uint4 u0 = xb[v], u1 = xb[v + stride];
+        apply(u0);
+        apply(u1);
+        xb[v] = u0;
+        xb[v + stride] = u1;
+    }
+    if (v < nvec) {
+        uint4 u0 = xb[v];
+        apply(u0);
+        xb[v] = u0;
     }
     if (chsum) {
+        // threads t, t + C/8, t + 2C/8, ... share a channel octet: sum their registers in thread order
+#pragma unroll
+        for (int k = 0; k < 8; k++) red[threadIdx.x][k] = cs[k];
         __syncthreads();
-        for (int c = threadIdx.x; c < C; c += blockDim.x) atomicAdd(&chsum[b * C + c], csum[c]);
+        const int oct = C / 8;
+        for (int c = threadIdx.x; c < C; c += blockDim.x) {
+            float t = 0.f;
+            for (int j = c / 8; j < (int)blockDim.x; j += oct) t += red[j][c % 8];
+            chsum[((long long)b * gridDim.x + blockIdx.x) * C + c] = t;
+        }
     }
 }
 
-// bg = sigmoid(W * mean_hw(s8) + b) (efficient_encoder.py:267-268); one warp per image, lanes split the
-// channels and reduce with shuffles
-__global__ void k_bg(const float *__restrict__ chsum, int C, long long HW, const float *__restrict__ w,
-                     const float *__restrict__ bias, float *__restrict__ bg) {
-    const int b = blockIdx.x, lane = threadIdx.x;
-    const float inv = 1.0f / (float)HW;
+// bg = sigmoid(W * mean_hw(s8) + b) (efficient_encoder.py:308-309); one block of C threads per image: thread
+// c sums channel c's nblk block partials in order, then the three dot products reduce over the block
+__global__ void __launch_bounds__(256) k_bg(const float *__restrict__ chsum, int nblk, int C, long long HW,
+                                            const float *__restrict__ w, const float *__restrict__ bias,
+                                            float *__restrict__ bg) {
+    __shared__ float red[3][8];
+    const int b = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
     float s0 = 0.f, s1 = 0.f, s2 = 0.f;
-    for (int c = lane; c < C; c += 32) {
-        const float m = chsum[b * C + c] * inv;
-        s0 = fmaf(w[c], m, s0);
-        s1 = fmaf(w[C + c], m, s1);
-        s2 = fmaf(w[2 * C + c], m, s2);
+    if (c < C) {
+        float t = 0.f;
+        for (int k = 0; k < nblk; k++) t += chsum[((long long)b * nblk + k) * C + c];
+        const float m = t / (float)HW;
+        s0 = w[c] * m;
+        s1 = w[C + c] * m;
+        s2 = w[2 * C + c] * m;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -180,11 +225,20 @@ __global__ void k_bg(const float *__restrict__ chsum, int C, long long HW, const
         s1 += __shfl_xor_sync(0xffffffffu, s1, o);
         s2 += __shfl_xor_sync(0xffffffffu, s2, o);
     }
-    if (lane < 3) {
-        const float s = (lane == 0 ? s0 : lane == 1 ? s1 : s2) + bias[lane];
-        bg[b * 3 + lane] = 1.0f / (1.0f + expf(-s));
+    if (lane == 0) {
+        red[0][warp] = s0;
+        red[1][warp] = s1;
+        red[2][warp] = s2;
+    }
+    __syncthreads();
+    if (c < 3) {
+        float s = bias[c];
+        for (int k = 0; k < (int)(blockDim.x >> 5); k++) s += red[c][k];
+        bg[b * 3 + c] = 1.0f / (1.0f + expf(-s));
     }
 }
+
+#define GN_BG_BLOCKS 128  // blocks of the GroupNorm launch that also sums channels for the background head
 
 struct HeadArgs {
     int B, fH, fW, M;          // grid and splats per cell
@@ -205,23 +259,51 @@ struct HeadArgs {
     float *cmu, *cls, *ccol, *cop, *cth;  // contiguous [B][fH*fW*M] copies (coarse render input)
 };
 
-// one thread per feature cell: 1x1 convolution of the head + activations (efficient_encoder.py:170-197).
-// Weights sit transposed in shared memory, [Cin][20] (18 outputs padded to 20), so one input channel is
-// 5 broadcast 16-byte loads for 18 FMAs.
+// 1x1 convolution of the head + activations (efficient_encoder.py:170-197).  A block takes HEAD_CELLS
+// feature cells (lane = cell) and HEAD_PARTS warps, each warp accumulating its slice of the feature
+// channels; partial sums meet in shared memory and warp m (m < M) adds the extra channels (pooled
+// gradient, bilinear cond) and applies the activations of splat slot m.  Weights sit transposed in shared memory, [Cin][20] (18
+// outputs padded to 20), so one input channel is 5 broadcast 16-byte loads for 18 FMAs.
 #define HEAD_NP 20
-__global__ void __launch_bounds__(64) k_head(HeadArgs a) {
-    extern __shared__ __align__(16) float shw[];  // wT [Cin][20], bias [20], gn scale/shift [2][Cfeat]
+#define HEAD_CELLS 32
+#define HEAD_PARTS 8
+template <int M>
+__global__ void __launch_bounds__(32 * HEAD_PARTS) k_head(HeadArgs a) {
+    // wT [Cin][20], bias [20], gn scale/shift [2][Cfeat], partial sums [HEAD_PARTS][HEAD_CELLS][20]
+    extern __shared__ __align__(16) float shw[];
     float *wT = shw, *sb = shw + a.Cin * HEAD_NP, *gsc = sb + HEAD_NP, *gsh = gsc + a.Cfeat;
-    long long cell = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    float *red = gsh + a.Cfeat;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long cell0 = (long long)blockIdx.x * HEAD_CELLS;
     const long long ncell = (long long)a.B * a.fH * a.fW;
-    int b0 = (int)(((long long)blockIdx.x * blockDim.x) / ((long long)a.fH * a.fW));
-    for (int i = threadIdx.x; i < a.Cin * HEAD_NP; i += blockDim.x) {
-        const int c = i / HEAD_NP, k = i - c * HEAD_NP;
-        wT[i] = k < a.nout ? a.w[k * a.Cin + c] : 0.f;
+    const int b0 = (int)(cell0 / ((long long)a.fH * a.fW));
+    {
+        // coalesced read of w [nout][Cin], 8 independent loads in flight per thread
+        const int n = a.nout * a.Cin;
+        for (int i0 = threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = i0 + u * blockDim.x;
+                v[u] = i < n ? __ldg(a.w + i) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = i0 + u * blockDim.x;
+                if (i < n) {
+                    const int k = i / a.Cin, c = i - k * a.Cin;
+                    wT[c * HEAD_NP + k] = v[u];
+                }
+            }
+        }
+    }
+    for (int i = threadIdx.x; i < a.Cin * (HEAD_NP - a.nout); i += blockDim.x) {
+        const int c = i / (HEAD_NP - a.nout), k = a.nout + i % (HEAD_NP - a.nout);
+        wT[c * HEAD_NP + k] = 0.f;
     }
     for (int i = threadIdx.x; i < HEAD_NP; i += blockDim.x) sb[i] = i < a.nout ? a.b[i] : 0.f;
     // GroupNorm scale/shift of the block's image (blocks never straddle images: the caller requires
-    // fH*fW to be a multiple of the block size when gn_stats is used)
+    // fH*fW to be a multiple of HEAD_CELLS when gn_stats is used)
     if (a.gn_stats) {
         const double n = (double)a.fH * a.fW * (a.Cfeat / 8);
         for (int c = threadIdx.x; c < a.Cfeat; c += blockDim.x) {
@@ -235,13 +317,11 @@ __global__ void __launch_bounds__(64) k_head(HeadArgs a) {
         }
     }
     __syncthreads();
-    if (cell >= ncell) return;
-    const int b = (int)(cell / ((long long)a.fH * a.fW));
-    const int r = (int)(cell - (long long)b * a.fH * a.fW);
-    const int y = r / a.fW, x = r - y * a.fW;
+    const long long cell = cell0 + lane;
+    const bool live = cell < ncell;
     float acc[HEAD_NP];
 #pragma unroll
-    for (int k = 0; k < HEAD_NP; k++) acc[k] = sb[k];
+    for (int k = 0; k < HEAD_NP; k++) acc[k] = 0.f;
     auto fma_channel = [&](int c, float v) {
         const float4 *wc = reinterpret_cast<const float4 *>(wT + c * HEAD_NP);
 #pragma unroll
@@ -253,17 +333,57 @@ __global__ void __launch_bounds__(64) k_head(HeadArgs a) {
             acc[4 * q + 3] = fmaf(w4.w, v, acc[4 * q + 3]);
         }
     };
-    const __nv_bfloat16 *fp = a.feat + cell * a.Cfeat;
-    for (int c = 0; c < a.Cfeat; c += 8) {
-        uint4 u = *reinterpret_cast<const uint4 *>(fp + c);
-        const __nv_bfloat16 *e = reinterpret_cast<const __nv_bfloat16 *>(&u);
+    const int per = ((a.Cfeat / 8 + HEAD_PARTS - 1) / HEAD_PARTS) * 8;
+    const int c_lo = warp * per, c_hi = min(a.Cfeat, c_lo + per);
+    if (live) {
+        // the warp's slice, up to 4 vectors of 8 channels at a time, loaded before any arithmetic
+        const __nv_bfloat16 *fp = a.feat + cell * a.Cfeat;
+        for (int c1 = c_lo; c1 < c_hi; c1 += 32) {
+            uint4 u[4];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            float v = __bfloat162float(e[j]);
-            if (a.gn_stats) v = fmaf(v, gsc[c + j], gsh[c + j]);
-            fma_channel(c + j, v);
+            for (int q = 0; q < 4; q++)
+                if (c1 + 8 * q < c_hi) u[q] = __ldg(reinterpret_cast<const uint4 *>(fp + c1 + 8 * q));
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                if (c1 + 8 * q >= c_hi) break;
+                const int c = c1 + 8 * q;
+                const __nv_bfloat16 *e = reinterpret_cast<const __nv_bfloat16 *>(&u[q]);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    float v = __bfloat162float(e[j]);
+                    if (a.gn_stats) v = fmaf(v, gsc[c + j], gsh[c + j]);
+                    fma_channel(c + j, v);
+                }
+            }
         }
     }
+    {
+        float4 *rp = reinterpret_cast<float4 *>(red + (warp * HEAD_CELLS + lane) * HEAD_NP);
+#pragma unroll
+        for (int q = 0; q < HEAD_NP / 4; q++) rp[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+    }
+    __syncthreads();
+    // warp m < M finishes splat slot m of the 32 cells (partials summed in a fixed order)
+    if (warp >= M || !live) return;
+#pragma unroll
+    for (int k = 0; k < HEAD_NP; k++) acc[k] = 0.f;
+#pragma unroll
+    for (int p = 0; p < HEAD_PARTS; p++) {
+        const float4 *rp = reinterpret_cast<const float4 *>(red + (p * HEAD_CELLS + lane) * HEAD_NP);
+#pragma unroll
+        for (int q = 0; q < HEAD_NP / 4; q++) {
+            const float4 t = rp[q];
+            acc[4 * q] += t.x;
+            acc[4 * q + 1] += t.y;
+            acc[4 * q + 2] += t.z;
+            acc[4 * q + 3] += t.w;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < HEAD_NP; k++) acc[k] += sb[k];
+    const int b = (int)(cell / ((long long)a.fH * a.fW));
+    const int r = (int)(cell - (long long)b * a.fH * a.fW);
+    const int y = r / a.fW, x = r - y * a.fW;
     fma_channel(a.Cfeat, a.gpool[cell]);
     if (a.cond) {
         int y0, y1, x0, x1;
@@ -281,9 +401,11 @@ __global__ void __launch_bounds__(64) k_head(HeadArgs a) {
         fma_channel(a.Cfeat + 4, h0 * (w0 * c00.w + w1 * c01.w) + h1 * (w0 * c10.w + w1 * c11.w));
     }
     // activations; channel layout of each head: (m, component)
-    const int M = a.M;
+    // M (splats per cell) is a template parameter so every acc[] index is static and acc stays in registers
     const float by = lin_center(y, a.fH), bx = lin_center(x, a.fW);
+#pragma unroll
     for (int m = 0; m < M; m++) {
+        if (m != warp) continue;
         const long long nl = (long long)r * M + m;  // splat index inside the group (cell-major, then slot)
         const long long n = (long long)b * a.Ntot + a.n0 + nl;
         float muy = by + tanhf(acc[m * 2 + 0]) * a.off_scale;
@@ -294,12 +416,14 @@ __global__ void __launch_bounds__(64) k_head(HeadArgs a) {
         ly = fmaxf(ly, a.ls_floor);
         lx = fmaxf(lx, a.ls_floor);
         float cc[3];
+#pragma unroll
         for (int c = 0; c < 3; c++) cc[c] = 1.0f / (1.0f + expf(-acc[4 * M + m * 3 + c]));
         float o = 1.0f / (1.0f + expf(-acc[7 * M + m]));
         if (a.min_op > 0.f) o = a.min_op + (1.0f - a.min_op) * o;
         float t = a.use_rot ? tanhf(acc[8 * M + m]) * 1.5707963267948966f : 0.f;
         a.mu[n * 2] = muy; a.mu[n * 2 + 1] = mux;
         a.ls[n * 2] = ly; a.ls[n * 2 + 1] = lx;
+#pragma unroll
         for (int c = 0; c < 3; c++) a.col[n * 3 + c] = cc[c];
         a.op[n] = o;
         if (a.use_rot && a.th) a.th[n] = t;
@@ -307,6 +431,7 @@ __global__ void __launch_bounds__(64) k_head(HeadArgs a) {
             const long long q = (long long)b * a.fH * a.fW * M + nl;
             a.cmu[q * 2] = muy; a.cmu[q * 2 + 1] = mux;
             a.cls[q * 2] = ly; a.cls[q * 2 + 1] = lx;
+#pragma unroll
             for (int c = 0; c < 3; c++) a.ccol[q * 3 + c] = cc[c];
             a.cop[q] = o;
             if (a.cth) a.cth[q] = t;
@@ -339,46 +464,38 @@ __global__ void k_cond(const float *__restrict__ image, int B, int H, int W, con
     cond[i * 4 + 3] = msum / 3.0f;
 }
 
-// concat[B][H4][W4][Cu + Cs] = (bilinear(s8 -> H4 x W4), s4)   (efficient_encoder.py:89-91)
-__global__ void __launch_bounds__(256) k_concat(const __nv_bfloat16 *__restrict__ s8, int H8, int W8, int Cu,
-                                                const __nv_bfloat16 *__restrict__ s4, int H4, int W4, int Cs, int B,
-                                                __nv_bfloat16 *__restrict__ out) {
-    const int Ct = Cu + Cs;
-    const int nv = Ct / 8;
-    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long long)B * H4 * W4 * nv) return;
-    int v = (int)(i % nv);
-    long long pix = i / nv;
-    int b = (int)(pix / ((long long)H4 * W4));
-    int r = (int)(pix - (long long)b * H4 * W4);
-    int y = r / W4, x = r - y * W4;
+// up[B][H4][W4][Cu] = bilinear(s8 -> H4 x W4) (the upsampled half of the _UpBlock input,
+// efficient_encoder.py:89-91; the decoder convolution reads [up, s4] as two inputs, so the
+// concatenation is never materialised).  grid = (row blocks, H4, B); one thread per 8-channel vector.
+__global__ void __launch_bounds__(256) k_upsample(const __nv_bfloat16 *__restrict__ s8, int H8, int W8, int Cu,
+                                                  int H4, int W4, __nv_bfloat16 *__restrict__ up) {
+    const int nv = Cu / 8;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= W4 * nv) return;
+    const int y = blockIdx.y, b = blockIdx.z;
+    const int x = i / nv, c0 = (i - x * nv) * 8;
+    int y0, y1, x0, x1;
+    float h0, h1, w0, w1;
+    lin_idx(y, H8, H4, y0, y1, h0, h1);
+    lin_idx(x, W8, W4, x0, x1, w0, w1);
+    const __nv_bfloat16 *sb = s8 + (long long)b * H8 * W8 * Cu + c0;
+    const uint4 a00 = *reinterpret_cast<const uint4 *>(sb + (y0 * W8 + x0) * Cu);
+    const uint4 a01 = *reinterpret_cast<const uint4 *>(sb + (y0 * W8 + x1) * Cu);
+    const uint4 a10 = *reinterpret_cast<const uint4 *>(sb + (y1 * W8 + x0) * Cu);
+    const uint4 a11 = *reinterpret_cast<const uint4 *>(sb + (y1 * W8 + x1) * Cu);
+    const __nv_bfloat16 *p00 = reinterpret_cast<const __nv_bfloat16 *>(&a00);
+    const __nv_bfloat16 *p01 = reinterpret_cast<const __nv_bfloat16 *>(&a01);
+    const __nv_bfloat16 *p10 = reinterpret_cast<const __nv_bfloat16 *>(&a10);
+    const __nv_bfloat16 *p11 = reinterpret_cast<const __nv_bfloat16 *>(&a11);
     uint4 res;
     __nv_bfloat16 *e = reinterpret_cast<__nv_bfloat16 *>(&res);
-    int c0 = v * 8;
-    if (c0 < Cu) {
-        int y0, y1, x0, x1;
-        float h0, h1, w0, w1;
-        lin_idx(y, H8, H4, y0, y1, h0, h1);
-        lin_idx(x, W8, W4, x0, x1, w0, w1);
-        const __nv_bfloat16 *sb = s8 + (long long)b * H8 * W8 * Cu;
-        uint4 a00 = *reinterpret_cast<const uint4 *>(sb + ((long long)y0 * W8 + x0) * Cu + c0);
-        uint4 a01 = *reinterpret_cast<const uint4 *>(sb + ((long long)y0 * W8 + x1) * Cu + c0);
-        uint4 a10 = *reinterpret_cast<const uint4 *>(sb + ((long long)y1 * W8 + x0) * Cu + c0);
-        uint4 a11 = *reinterpret_cast<const uint4 *>(sb + ((long long)y1 * W8 + x1) * Cu + c0);
-        const __nv_bfloat16 *p00 = reinterpret_cast<const __nv_bfloat16 *>(&a00);
-        const __nv_bfloat16 *p01 = reinterpret_cast<const __nv_bfloat16 *>(&a01);
-        const __nv_bfloat16 *p10 = reinterpret_cast<const __nv_bfloat16 *>(&a10);
-        const __nv_bfloat16 *p11 = reinterpret_cast<const __nv_bfloat16 *>(&a11);
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            float f = h0 * (w0 * __bfloat162float(p00[k]) + w1 * __bfloat162float(p01[k])) +
-                      h1 * (w0 * __bfloat162float(p10[k]) + w1 * __bfloat162float(p11[k]));
-            e[k] = __float2bfloat16_rn(f);
-        }
-    } else {
-        res = *reinterpret_cast<const uint4 *>(s4 + pix * Cs + (c0 - Cu));
+    for (int k = 0; k < 8; k++) {
+        float f = h0 * (w0 * __bfloat162float(p00[k]) + w1 * __bfloat162float(p01[k])) +
+                  h1 * (w0 * __bfloat162float(p10[k]) + w1 * __bfloat162float(p11[k]));
+        e[k] = __float2bfloat16_rn(f);
     }
-    *reinterpret_cast<uint4 *>(out + pix * Ct + c0) = res;
+    *reinterpret_cast<uint4 *>(up + (((long long)b * H4 + y) * W4 + x) * Cu + c0) = res;
 }
 
 // GroupNorm(8) applied to NHWC bf16 [B][HW][C] written as NHWC fp32 (the fine decoder's normalised
@@ -399,10 +516,23 @@ __global__ void k_gn_to_f32(const __nv_bfloat16 *__restrict__ x, int B, long lon
     out[i] = (__bfloat162float(x[i]) - (float)mean) * rstd * gamma[c] + beta[c];
 }
 
-// NHWC bf16 -> NHWC fp32 (backbone_features output)
+// NHWC bf16 -> NHWC fp32 (backbone_features output), 8 elements per thread (n a multiple of 8)
 __global__ void k_bf16_to_f32(const __nv_bfloat16 *__restrict__ in, float *__restrict__ out, long long n) {
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) out[i] = __bfloat162float(in[i]);
+    if (i * 8 >= n) return;
+    uint4 u = reinterpret_cast<const uint4 *>(in)[i];
+    const __nv_bfloat16 *e = reinterpret_cast<const __nv_bfloat16 *>(&u);
+    float4 *o = reinterpret_cast<float4 *>(out) + 2 * i;
+    o[0] = make_float4(__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3]));
+    o[1] = make_float4(__bfloat162float(e[4]), __bfloat162float(e[5]), __bfloat162float(e[6]), __bfloat162float(e[7]));
+}
+
+void launch_head(const HeadArgs &h, long long ncell, size_t smem, cudaStream_t s) {
+    const unsigned grid = (unsigned)((ncell + HEAD_CELLS - 1) / HEAD_CELLS);
+    if (h.M == 1)
+        k_head<1><<<grid, 32 * HEAD_PARTS, smem, s>>>(h);
+    else
+        k_head<2><<<grid, 32 * HEAD_PARTS, smem, s>>>(h);
 }
 
 size_t al(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -434,13 +564,13 @@ int enc_plan(const gs_encoder_desc *e, EncPlan &p) {
     p.o_y1 = take(B * p.H2 * p.W2 * 64 * 2);
     p.o_y2 = take(B * p.H4 * p.W4 * 128 * 2);
     p.o_y3 = take(B * p.H8 * p.W8 * 256 * 2);
-    p.o_cat = take(B * p.H4 * p.W4 * 384 * 2);
+    p.o_cat = take(B * p.H4 * p.W4 * 256 * 2);  // bilinear(s8) at the s4 size, the decoder's first input
     p.o_y4 = take(B * p.H4 * p.W4 * 128 * 2);
     p.o_grad = take(B * p.H * p.W * 4);
     p.o_g4 = take(B * p.H4 * p.W4 * 4);
     p.o_g8 = take(B * p.H8 * p.W8 * 4);
     p.o_stats = take(4 * B * 16 * sizeof(double));
-    p.o_chsum = take(B * 256 * 4);
+    p.o_chsum = take(B * GN_BG_BLOCKS * 256 * 4);  // per-block channel sums of the normalised s8
     p.o_err = take(64);
     const size_t nc = B * p.Nc;
     p.o_c[0] = take(nc * 2 * 4);
@@ -495,14 +625,16 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
         ProfScope ps(PR_ENC_PREP, s);
         long long n = (long long)B * p.H2 * p.W2;
         k_prep<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(image, B, p.H, p.W, grad, W<__nv_bfloat16>(ws, p.o_Z));
-        long long n4 = (long long)B * p.H4 * p.W4, n8 = (long long)B * p.H8 * p.W8;
-        k_pool<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(grad, B, p.H, p.W, 4, W<float>(ws, p.o_g4));
-        k_pool<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(grad, B, p.H, p.W, 8, W<float>(ws, p.o_g8));
+        long long n8 = (long long)B * p.H8 * p.W8 * 8;
+        k_pool48<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(grad, B, p.H, p.W, W<float>(ws, p.o_g4),
+                                                             W<float>(ws, p.o_g8));
     }
     // 2. backbone: conv -> GELU -> GroupNorm, three stages
     auto gn = [&](void *x, long long HW, int C, double *stt, const float *gamma, const float *beta, float *chsum) {
-        dim3 grid((unsigned)std::min<long long>(1024, (HW * C / 8 + 255) / 256), (unsigned)B);
-        k_gn_apply<<<grid, 256, 3 * C * sizeof(float), s>>>((__nv_bfloat16 *)x, B, HW, C, stt, gamma, beta, chsum);
+        // with channel sums every block ends in C global atomics: keep the grid small for that launch
+        // with channel sums the grid is fixed (GN_BG_BLOCKS per image): k_bg reduces exactly that many partials
+        dim3 grid((unsigned)(chsum ? GN_BG_BLOCKS : std::min<long long>(1024, (HW * C / 8 + 255) / 256)), (unsigned)B);
+        k_gn_apply<<<grid, 256, 0, s>>>((__nv_bfloat16 *)x, (int)HW, C, stt, gamma, beta, chsum);
     };
     gs_conv_desc cd;
     memset(&cd, 0, sizeof(cd));
@@ -533,7 +665,7 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     }
     float *chsum = W<float>(ws, p.o_chsum);
     gn(W<void>(ws, p.o_y3), (long long)p.H8 * p.W8, 256, stats + 2 * B * 16, w->gn3_w, w->gn3_b, chsum);
-    k_bg<<<B, 32, 0, s>>>(chsum, 256, (long long)p.H8 * p.W8, w->bg_w, w->bg_b, bg);
+    k_bg<<<B, 256, 0, s>>>(chsum, GN_BG_BLOCKS, 256, (long long)p.H8 * p.W8, w->bg_w, w->bg_b, bg);
     // 3. coarse head (writes the API tensors and a contiguous copy for the coarse render)
     HeadArgs h;
     memset(&h, 0, sizeof(h));
@@ -547,8 +679,8 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     {
         ProfScope ps(PR_HEADS, s);
         long long ncell = (long long)B * p.H8 * p.W8;
-        size_t sm = ((size_t)h.Cin * HEAD_NP + HEAD_NP + 2 * h.Cfeat) * 4;
-        k_head<<<(unsigned)((ncell + 63) / 64), 64, sm, s>>>(h);
+        size_t sm = ((size_t)h.Cin * HEAD_NP + HEAD_NP + 2 * h.Cfeat + HEAD_PARTS * HEAD_CELLS * HEAD_NP) * 4;
+        launch_head(h, ncell, sm, s);
     }
     // 4. coarse render at residual_grid^2 (odds) -> cond map
     {
@@ -564,18 +696,17 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     // 5. fine decoder: bilinear(s8) || s4 -> 3x3 conv 384->128 (+GELU, GN stats)
     {
         ProfScope ps(PR_ENC_MISC, s);
-        long long n = (long long)B * p.H4 * p.W4 * (384 / 8);
-        k_concat<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), p.H8, p.W8, 256,
-                                                             W<__nv_bfloat16>(ws, p.o_y2), p.H4, p.W4, 128, B,
-                                                             W<__nv_bfloat16>(ws, p.o_cat));
+        dim3 ug((unsigned)((p.W4 * (256 / 8) + 255) / 256), (unsigned)p.H4, (unsigned)B);
+        k_upsample<<<ug, 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), p.H8, p.W8, 256, p.H4, p.W4,
+                                      W<__nv_bfloat16>(ws, p.o_cat));
     }
     memset(&cd, 0, sizeof(cd));
     cd.B = B; cd.H = p.H4; cd.W = p.W4; cd.Cin = 384; cd.Cout = 128; cd.kh = 3; cd.kw = 3; cd.stride = 1; cd.pad = 1;
     cd.gelu = 1;
     {
         ProfScope ps(PR_CONV4, s);
-        if ((st = gs_conv_run(&cd, W<void>(ws, p.o_cat), w->w4, w->b4, W<void>(ws, p.o_y4), stats + 3 * B * 16, err,
-                              s)))
+        if ((st = gs_conv_run2(&cd, W<void>(ws, p.o_cat), 256, W<void>(ws, p.o_y2), w->w4, w->b4,
+                               W<void>(ws, p.o_y4), stats + 3 * B * 16, err, s)))
             return st;
     }
     // 6. fine head: GN on the fly, + pooled gradient + bilinear(cond)
@@ -590,8 +721,8 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     {
         ProfScope ps(PR_HEADS, s);
         long long ncell = (long long)B * p.H4 * p.W4;
-        size_t sm = ((size_t)h.Cin * HEAD_NP + HEAD_NP + 2 * h.Cfeat) * 4;
-        k_head<<<(unsigned)((ncell + 63) / 64), 64, sm, s>>>(h);
+        size_t sm = ((size_t)h.Cin * HEAD_NP + HEAD_NP + 2 * h.Cfeat + HEAD_PARTS * HEAD_CELLS * HEAD_NP) * 4;
+        launch_head(h, ncell, sm, s);
     }
     if (latents) {
         long long n = (long long)B * p.H4 * p.W4 * 128;
@@ -602,16 +733,61 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     }
     if (features) {
         long long n = (long long)B * p.H8 * p.W8 * 256;
-        k_bf16_to_f32<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), features, n);
+        k_bf16_to_f32<<<(unsigned)((n / 8 + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), features, n);
     }
-    // memset, prep, 2 pools, 4 convs, 3 GN applies, bg, 2 heads, cond, concat, optional feature copy
-    gs_count_launch(17 + (features ? 1 : 0));
+    // memset, prep, pool, 4 convs, 3 GN applies, bg, 2 heads, cond, upsample, optional feature copy
+    gs_count_launch(16 + (features ? 1 : 0));
     cudaError_t ce = cudaGetLastError();
     if (ce != cudaSuccess) {
         fprintf(stderr, "gs_encoder_fwd: %s\n", cudaGetErrorString(ce));
         return GS_ERR_CUDA;
     }
     return GS_OK;
+}
+
+// The final render of gs_encode_render_fwd: render_alpha_octave's defaults at the image size.
+static int final_render_desc(const gs_encoder_desc *e, const EncPlan &p, gs_render_desc &fd) {
+    memset(&fd, 0, sizeof(fd));
+    fd.mode = GS_MODE_OCTAVE; fd.B = p.B; fd.N = p.N; fd.C = 3; fd.H = p.H; fd.W = p.W; fd.tile = 8;
+    fd.odds = e->odds; fd.has_theta = e->use_rotation; fd.max_octaves = 6; fd.cutoff = 3.0f; fd.base_texels = 8.0f;
+    fd.n_coarse = -1; fd.coarse_factor = 8; fd.max_pairs = 48000000;
+    const int64_t bound = gs_render_pair_bound(&fd);
+    if (bound < 0) return GS_ERR_BAD_ARGUMENT;
+    // the reference checks the budget per image and octave; the host bound is per image here
+    if (bound / p.B > fd.max_pairs) return GS_ERR_PAIR_BUDGET;
+    fd.pair_capacity = std::max<int64_t>(bound, 1);
+    return GS_OK;
+}
+
+extern "C" size_t gs_encode_render_workspace_size(const gs_encoder_desc *e) {
+    EncPlan p;
+    if (enc_plan(e, p) != GS_OK) return 0;
+    gs_render_desc fd;
+    if (final_render_desc(e, p, fd) != GS_OK) return 0;
+    const size_t r = gs_render_workspace_size(&fd, 0);
+    return r ? al(p.total) + r : 0;
+}
+
+extern "C" int gs_encode_render_fwd(const gs_encoder_desc *e, const gs_encoder_weights *w, const float *image,
+                                    float *mu, float *log_scale, float *color, float *opacity, float *theta,
+                                    float *bg, float *features, float *latents, float *out, void *workspace,
+                                    size_t workspace_bytes, void *stream) {
+    EncPlan p;
+    int st = enc_plan(e, p);
+    if (st != GS_OK) return st;
+    gs_render_desc fd;
+    if ((st = final_render_desc(e, p, fd)) != GS_OK) return st;
+    if (!out) return GS_ERR_BAD_ARGUMENT;
+    const size_t rws = gs_render_workspace_size(&fd, 0);
+    if (!workspace || workspace_bytes < al(p.total) + rws) return GS_ERR_WORKSPACE;
+    st = gs_encoder_fwd(e, w, image, mu, log_scale, color, opacity, theta, bg, features, latents, workspace, p.total,
+                        stream);
+    if (st != GS_OK) return st;
+    // the coarse splats' octave fields of the encoder's internal render carry over when the texel grids agree
+    GsPrior prior;
+    const int mapped = gs_render_prior_map(&p.rd, W<void>(workspace, p.o_rws), &fd, p.Nc, &prior);
+    return gs_render_fwd_prior(&fd, mu, log_scale, color, opacity, bg, theta, out, mapped ? &prior : nullptr,
+                               W<void>(workspace, al(p.total)), rws, stream);
 }
 
 extern "C" int gs_encoder_error_flag(const gs_encoder_desc *e, const void *workspace, int *flag_host) {

@@ -40,6 +40,7 @@ static unsigned long long g_launches = 0;  // kernels enqueued by this library (
 #include <vector>
 
 #include "gs_prof.cuh"
+#include "gs_render_internal.cuh"
 
 namespace {
 struct ProfEvent {
@@ -151,6 +152,31 @@ __device__ __forceinline__ int group_of_splat(const RenderGeom &G, int i, float 
 // ----------------------------------------------------------------------------------------------------
 // forward: preprocessing
 
+// Render record of splat s (activate_scale of params.py:18-28, the rotation of render.py:21-26 and the
+// opacity), with the activated scales returned in sy, sx.
+__device__ __forceinline__ SplatRec make_rec(long long s, int C, int has_theta, const float *__restrict__ mu,
+                                             const float *__restrict__ ls, const float *__restrict__ col,
+                                             const float *__restrict__ op, const float *__restrict__ th, float &sy,
+                                             float &sx) {
+    float2 m = reinterpret_cast<const float2 *>(mu)[s];  // (y, x)
+    float2 l = reinterpret_cast<const float2 *>(ls)[s];
+    sy = gs_softplus_eps(l.x);
+    sx = gs_softplus_eps(l.y);
+    float o = op[s];
+    float cth = 1.0f, sth = 0.0f;
+    if (has_theta) sincosf(th[s], &sth, &cth);
+    float c0 = 0.f, c1 = 0.f, c2 = 0.f;
+    if (C > 0) c0 = col[s * C + 0];
+    if (C > 1) c1 = col[s * C + 1];
+    if (C > 2) c2 = col[s * C + 2];
+    float iy = GS_K / sy, ix = GS_K / sx;
+    SplatRec r;
+    r.a = make_float4(m.x, m.y, cth * iy, sth * iy);
+    r.b = make_float4(-sth * ix, cth * ix, o, log2f(o));
+    r.c = make_float4(c0, c1, c2, o <= GS_DEAD_OP ? 1.0f : 0.0f);
+    return r;
+}
+
 // meta = {global tile id of the rectangle's top-left, width | group << 24, ntx of the group, count}
 __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *__restrict__ mu,
                                                     const float *__restrict__ ls, const float *__restrict__ col,
@@ -174,24 +200,8 @@ __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *_
     if (s < (long long)G.B * G.N) {
         int b = (int)(s / G.N), i = (int)(s - (long long)b * G.N);
         float2 m = reinterpret_cast<const float2 *>(mu)[s];  // (y, x)
-        float2 l = reinterpret_cast<const float2 *>(ls)[s];
-        float sy = gs_softplus_eps(l.x), sx = gs_softplus_eps(l.y);
-        float o = op[s];
-        float cth = 1.0f, sth = 0.0f;
-        if (G.has_theta) {
-            float t = th[s];
-            sincosf(t, &sth, &cth);
-        }
-        float c0 = 0.f, c1 = 0.f, c2 = 0.f;
-        if (G.C > 0) c0 = col[s * G.C + 0];
-        if (G.C > 1) c1 = col[s * G.C + 1];
-        if (G.C > 2) c2 = col[s * G.C + 2];
-        float iy = GS_K / sy, ix = GS_K / sx;
-        SplatRec r;
-        r.a = make_float4(m.x, m.y, cth * iy, sth * iy);
-        r.b = make_float4(-sth * ix, cth * ix, o, log2f(o));
-        r.c = make_float4(c0, c1, c2, o <= GS_DEAD_OP ? 1.0f : 0.0f);
-        rec[s] = r;
+        float sy, sx;
+        rec[s] = make_rec(s, G.C, G.has_theta, mu, ls, col, op, th, sy, sx);
         int g = group_of_splat(G, i, sy, sx);
         int4 mt = make_int4(0, 0, 1, 0);
         if (G.mode != GS_MODE_EXACT) {
@@ -202,6 +212,10 @@ __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *_
             y1 = min(y1, gg.ty_hi);
             int w = x1 - x0 + 1;
             count = y1 >= y0 ? w * (y1 - y0 + 1) : 0;
+            // a splat whose contribution arrives with a prior render's fields is not binned again
+            if (i < G.skip_n && gg.prior_grp >= 0 &&
+                octave_of(sy, sx, G.prior_rep, G.base_texels, G.max_oct) == gg.prior_grp)
+                count = 0;
             mt = make_int4(b * G.tiles_per_image + gg.tile_off + y0 * gg.ntx + x0, w | (g << 24), gg.ntx, count);
         } else {
             mt.y = g << 24;
@@ -380,80 +394,116 @@ __global__ void __launch_bounds__(256) k_radix_scan(int *__restrict__ hist, cons
     if (threadIdx.x == 0) dtot[blockIdx.x] = carry;
 }
 
-// Stable scatter of one digit: warp w of a virtual block ranks its own 256 consecutive keys in 8
-// sequential rounds (match_any within the round + a running per-warp digit count), then one block-wide
-// prefix over warps turns the per-warp counts into global positions.
+// Shared memory of one radix scatter block.
+struct RsSmem {
+    int wsum[RS_THREADS / 32];
+    int wcnt[RS_THREADS / 32][256];  // per warp and digit: count, then the warp's start inside the chunk
+    int lbase[256];                  // start of each digit inside the chunk's digit-sorted order
+    int gbase[256];                  // global output position of each digit's first key of the chunk
+    unsigned skey[RS_ITEMS];         // the chunk, stably sorted by digit
+    int sval[RS_ITEMS];
+};
+
+// One chunk [c0, c1) (at most RS_ITEMS keys) of a stable LSD pass.  Warp w ranks its own 256 consecutive
+// keys in 8 sequential rounds (match_any within the round + a running per-warp digit count); a block-wide
+// scan over digits turns the counts into chunk-local positions, the chunk is staged in shared memory in
+// digit order, and each digit's run is then written to gbase[d] onwards with consecutive threads on
+// consecutive positions (coalesced).  gbase[d] advances by the chunk's digit-d count.
+__device__ __forceinline__ void rs_chunk(RsSmem &sm, const unsigned *__restrict__ kin, const int *__restrict__ vin,
+                                         unsigned *__restrict__ kout, int *__restrict__ vout, long long c0,
+                                         long long c1, int shift, int radix) {
+    constexpr int NWARP = RS_THREADS / 32;
+    constexpr int PER_WARP = RS_ITEMS / NWARP;  // 256
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned mask = (unsigned)radix - 1u;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    const long long base = c0 + warp * PER_WARP;
+    for (int d = lane; d < radix; d += 32) sm.wcnt[warp][d] = 0;
+    __syncwarp();
+    unsigned key[RS_ROUNDS];
+    int val[RS_ROUNDS], dig[RS_ROUNDS], rank[RS_ROUNDS];
+#pragma unroll
+    for (int r = 0; r < RS_ROUNDS; r++) {
+        const long long i = base + r * 32 + lane;
+        key[r] = i < c1 ? __ldg(kin + i) : 0u;
+        val[r] = i < c1 ? __ldg(vin + i) : 0;
+    }
+#pragma unroll
+    for (int r = 0; r < RS_ROUNDS; r++) {
+        const long long i = base + r * 32 + lane;
+        const bool valid = i < c1;
+        const int d = valid ? (int)((key[r] >> shift) & mask) : -1;
+        dig[r] = d;
+        const unsigned peers = __match_any_sync(0xffffffffu, d);
+        const int pre = valid ? sm.wcnt[warp][d] : 0;
+        rank[r] = pre + __popc(peers & lt_mask);
+        __syncwarp();
+        if (valid && (peers & lt_mask) == 0u) sm.wcnt[warp][d] = pre + __popc(peers);
+        __syncwarp();
+    }
+    __syncthreads();
+    int tot = 0;
+    if (tid < radix) {
+#pragma unroll
+        for (int w = 0; w < NWARP; w++) {
+            const int c = sm.wcnt[w][tid];
+            sm.wcnt[w][tid] = tot;
+            tot += c;
+        }
+    }
+    const int lb = block_excl_scan<RS_THREADS>(tot, sm.wsum, nullptr);  // ends with a block barrier
+    if (tid < radix) sm.lbase[tid] = lb;
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < RS_ROUNDS; r++) {
+        if (dig[r] >= 0) {
+            const int local = sm.lbase[dig[r]] + sm.wcnt[warp][dig[r]] + rank[r];
+            sm.skey[local] = key[r];
+            sm.sval[local] = val[r];
+        }
+    }
+    __syncthreads();
+    const int n = (int)(c1 - c0);
+    for (int t = tid; t < n; t += RS_THREADS) {
+        const unsigned k = sm.skey[t];
+        const int d = (int)((k >> shift) & mask);
+        const long long pos = (long long)sm.gbase[d] + (t - sm.lbase[d]);
+        kout[pos] = k;
+        vout[pos] = sm.sval[t];
+    }
+    __syncthreads();
+    if (tid < radix) sm.gbase[tid] += tot;
+    __syncthreads();
+}
+
+// Stable scatter of one digit over "virtual blocks" of RS_ITEMS keys (grid-stride); the per-block digit
+// counts come from k_radix_upsweep, scanned by k_radix_scan.
 __global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep(const unsigned *__restrict__ kin,
                                                                 const int *__restrict__ vin,
                                                                 unsigned *__restrict__ kout, int *__restrict__ vout,
                                                                 const long long *__restrict__ n_ptr, long long cap,
                                                                 int shift, int radix, const int *__restrict__ hist,
                                                                 int nblk_cap, const int *__restrict__ dtot) {
-    constexpr int NWARP = RS_THREADS / 32;
-    constexpr int PER_WARP = RS_ITEMS / NWARP;  // 256
-    __shared__ int wsum[NWARP];
+    extern __shared__ __align__(16) unsigned char rs_dsmem[];
+    RsSmem &sm = *reinterpret_cast<RsSmem *>(rs_dsmem);
     __shared__ int dbase[256];
-    __shared__ int wcnt[NWARP][256];
     const long long n = clamp_n(n_ptr, cap);
     const int nblk = (int)((n + RS_ITEMS - 1) / RS_ITEMS);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     const int dv = tid < radix ? dtot[tid] : 0;
-    const int dpre = block_excl_scan<RS_THREADS>(dv, wsum, nullptr);
+    const int dpre = block_excl_scan<RS_THREADS>(dv, sm.wsum, nullptr);
     if (tid < radix) dbase[tid] = dpre;
-    const unsigned mask = (unsigned)radix - 1u;
-    const unsigned lt_mask = (1u << lane) - 1u;
     for (int vb = blockIdx.x; vb < nblk; vb += gridDim.x) {
-        const long long base = (long long)vb * RS_ITEMS + warp * PER_WARP;
-        for (int d = lane; d < radix; d += 32) wcnt[warp][d] = 0;
-        __syncwarp();
-        unsigned key[RS_ROUNDS];
-        int val[RS_ROUNDS], dig[RS_ROUNDS], rank[RS_ROUNDS];
-#pragma unroll
-        for (int r = 0; r < RS_ROUNDS; r++) {
-            const long long i = base + r * 32 + lane;
-            key[r] = i < n ? __ldg(kin + i) : 0u;
-            val[r] = i < n ? __ldg(vin + i) : 0;
-        }
-#pragma unroll
-        for (int r = 0; r < RS_ROUNDS; r++) {
-            const long long i = base + r * 32 + lane;
-            const bool valid = i < n;
-            const int d = valid ? (int)((key[r] >> shift) & mask) : -1;
-            dig[r] = d;
-            const unsigned peers = __match_any_sync(0xffffffffu, d);
-            const int pre = valid ? wcnt[warp][d] : 0;
-            rank[r] = pre + __popc(peers & lt_mask);
-            __syncwarp();
-            if (valid && (peers & lt_mask) == 0u) wcnt[warp][d] = pre + __popc(peers);
-            __syncwarp();
-        }
-        __syncthreads();
-        if (tid < radix) {
-            int run = dbase[tid] + hist[tid * nblk_cap + vb];
-#pragma unroll
-            for (int w = 0; w < NWARP; w++) {
-                const int c = wcnt[w][tid];
-                wcnt[w][tid] = run;
-                run += c;
-            }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int r = 0; r < RS_ROUNDS; r++) {
-            if (dig[r] >= 0) {
-                const int pos = wcnt[warp][dig[r]] + rank[r];
-                kout[pos] = key[r];
-                vout[pos] = val[r];
-            }
-        }
-        __syncthreads();
+        if (tid < radix) sm.gbase[tid] = dbase[tid] + hist[tid * nblk_cap + vb];
+        // (rs_chunk reads gbase only after several block barriers)
+        const long long c0 = (long long)vb * RS_ITEMS;
+        rs_chunk(sm, kin, vin, kout, vout, c0, min(c0 + RS_ITEMS, n), shift, radix);
     }
 }
 
 // First radix pass over the emit kernel's output sub-segments (one per emit block: part p of splat block
-// j, bounds as in k_emit), whose digit histograms k_emit already wrote.  Each sub-segment is ranked in
-// chunks of RS_ITEMS keys exactly like k_radix_downsweep, with the per-digit running position carried
-// across chunks.
+// j, bounds as in k_emit), whose digit histograms k_emit already wrote.  Each sub-segment is scattered
+// in chunks of RS_ITEMS keys, the per-digit output position carried across its chunks.
 __global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep_seg(const unsigned *__restrict__ kin,
                                                                     const int *__restrict__ vin,
                                                                     unsigned *__restrict__ kout,
@@ -463,19 +513,14 @@ __global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep_seg(const unsign
                                                                     long long cap, int shift, int radix,
                                                                     const int *__restrict__ hist, int hist_stride,
                                                                     const int *__restrict__ dtot) {
-    constexpr int NWARP = RS_THREADS / 32;
-    constexpr int PER_WARP = RS_ITEMS / NWARP;
-    __shared__ int wsum[NWARP];
+    extern __shared__ __align__(16) unsigned char rs_dsmem[];
+    RsSmem &sm = *reinterpret_cast<RsSmem *>(rs_dsmem);
     __shared__ int dbase[256];
-    __shared__ int run_d[256];
-    __shared__ int wcnt[NWARP][256];
     const long long n = clamp_n(n_ptr, cap);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     const int dv = tid < radix ? dtot[tid] : 0;
-    const int dpre = block_excl_scan<RS_THREADS>(dv, wsum, nullptr);
+    const int dpre = block_excl_scan<RS_THREADS>(dv, sm.wsum, nullptr);
     if (tid < radix) dbase[tid] = dpre;
-    const unsigned mask = (unsigned)radix - 1u;
-    const unsigned lt_mask = (1u << lane) - 1u;
     const int nseg = nblk_pre * parts;
     for (int j = blockIdx.x; j < nseg; j += gridDim.x) {
         const int sb = j / parts, part = j - sb * parts;
@@ -485,55 +530,9 @@ __global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep_seg(const unsign
         const long long chunk = (tot + parts - 1) / parts;
         const long long b0 = min(beg + min(part * chunk, tot), n);
         const long long b1 = min(beg + min((part + 1) * chunk, tot), n);
+        if (tid < radix) sm.gbase[tid] = dbase[tid] + hist[tid * hist_stride + j];
+        for (long long c0 = b0; c0 < b1; c0 += RS_ITEMS) rs_chunk(sm, kin, vin, kout, vout, c0, min(c0 + RS_ITEMS, b1), shift, radix);
         __syncthreads();
-        if (tid < radix) run_d[tid] = dbase[tid] + hist[tid * hist_stride + j];
-        for (long long c0 = b0; c0 < b1; c0 += RS_ITEMS) {
-            const long long base = c0 + warp * PER_WARP;
-            for (int d = lane; d < radix; d += 32) wcnt[warp][d] = 0;
-            __syncwarp();
-            unsigned key[RS_ROUNDS];
-            int val[RS_ROUNDS], dig[RS_ROUNDS], rank[RS_ROUNDS];
-#pragma unroll
-            for (int r = 0; r < RS_ROUNDS; r++) {
-                const long long i = base + r * 32 + lane;
-                key[r] = i < b1 ? __ldg(kin + i) : 0u;
-                val[r] = i < b1 ? __ldg(vin + i) : 0;
-            }
-#pragma unroll
-            for (int r = 0; r < RS_ROUNDS; r++) {
-                const long long i = base + r * 32 + lane;
-                const bool valid = i < b1;
-                const int d = valid ? (int)((key[r] >> shift) & mask) : -1;
-                dig[r] = d;
-                const unsigned peers = __match_any_sync(0xffffffffu, d);
-                const int pre = valid ? wcnt[warp][d] : 0;
-                rank[r] = pre + __popc(peers & lt_mask);
-                __syncwarp();
-                if (valid && (peers & lt_mask) == 0u) wcnt[warp][d] = pre + __popc(peers);
-                __syncwarp();
-            }
-            __syncthreads();
-            if (tid < radix) {
-                int run = run_d[tid];
-#pragma unroll
-                for (int w = 0; w < NWARP; w++) {
-                    const int c = wcnt[w][tid];
-                    wcnt[w][tid] = run;
-                    run += c;
-                }
-                run_d[tid] = run;
-            }
-            __syncthreads();
-#pragma unroll
-            for (int r = 0; r < RS_ROUNDS; r++) {
-                if (dig[r] >= 0) {
-                    const int pos = wcnt[warp][dig[r]] + rank[r];
-                    kout[pos] = key[r];
-                    vout[pos] = val[r];
-                }
-            }
-            __syncthreads();
-        }
     }
 }
 
@@ -565,7 +564,7 @@ __device__ __forceinline__ void renorm(float &P, int &E) {
     P = __int_as_float((bits & 0x807fffff) | 0x3f000000);
 }
 
-template <int TILE, int NW>
+template <int TILE, int NW, bool ODDS>
 __global__ void __launch_bounds__(NW * 32) k_fields_fwd(RenderGeom G, const SplatRec *__restrict__ rec,
                                                         const int2 *__restrict__ ranges,
                                                         const int *__restrict__ vals, float *__restrict__ fields) {
@@ -591,14 +590,16 @@ __global__ void __launch_bounds__(NW * 32) k_fields_fwd(RenderGeom G, const Spla
         p1 = rg.y;
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float py[PPL], px[PPL];
+    // the PPL pixels of a lane share one column (32 is a multiple of TILE), so the x terms of the
+    // quadratic form are computed once per splat and lane
+    static_assert(NPIX < 32 || 32 % TILE == 0, "lane pixels must share a column");
+    float py[PPL];
 #pragma unroll
     for (int j = 0; j < PPL; j++) {
         int q = lane + 32 * j;
-        int ly = q / TILE, lx = q % TILE;
-        py[j] = __fdiv_rn((float)(ty * TILE + ly) + 0.5f, (float)Hg);
-        px[j] = __fdiv_rn((float)(tx * TILE + lx) + 0.5f, (float)Wg);
+        py[j] = __fdiv_rn((float)(ty * TILE + q / TILE) + 0.5f, (float)Hg);
     }
+    const float pxl = __fdiv_rn((float)(tx * TILE + lane % TILE) + 0.5f, (float)Wg);
     float P[PPL], Sw[PPL], S0[PPL], S1[PPL], S2[PPL];
     int E[PPL];
 #pragma unroll
@@ -606,41 +607,54 @@ __global__ void __launch_bounds__(NW * 32) k_fields_fwd(RenderGeom G, const Spla
         P[j] = 1.0f; E[j] = 0; Sw[j] = 0.f; S0[j] = 0.f; S1[j] = 0.f; S2[j] = 0.f;
     }
     const int n = p1 - p0;
-    const bool odds = G.odds != 0;
-    for (int base = warp * 32; base < n; base += NW * 32) {
-        int k = base + lane;
-        if (k < n) {
-            int sid = dense ? b * G.N + k : vals[p0 + k];
-            srec[warp][lane] = rec[sid];
-        }
-        __syncwarp();
-        const int nb = min(32, n - base);
-        for (int i = 0; i < nb; ++i) {
-            const float4 A = srec[warp][i].a, Bv = srec[warp][i].b, Cv = srec[warp][i].c;
-            const bool series = odds && Cv.w != 0.0f;
+    // one splat at the lane's PPL pixels; the weight form (alpha, odds by rcp, odds by series for dead
+    // splats) is chosen once per splat; the record is the same for every lane, and the warp vote makes
+    // that branch uniform for the compiler too
+    auto step = [&](const SplatRec &r) {
+        const float4 A = r.a, Bv = r.b, Cv = r.c;
+        const float dx = pxl - A.y;
+        const float ux = A.w * dx, vx = Bv.y * dx;
+        auto body = [&](auto weight) {
 #pragma unroll
             for (int j = 0; j < PPL; j++) {
-                float dy = py[j] - A.x, dx = px[j] - A.y;
-                float u = fmaf(A.z, dy, A.w * dx);
-                float v = fmaf(Bv.x, dy, Bv.y * dx);
+                float dy = py[j] - A.x;
+                float u = fmaf(A.z, dy, ux);
+                float v = fmaf(Bv.x, dy, vx);
                 float arg = fmaf(-u, u, fmaf(-v, v, Bv.w));
                 float a = fminf(gs_ex2(arg), GS_ALPHA_MAX);
                 float om = 1.0f - a;
                 P[j] *= om;
-                float w;
-                if (!odds) w = a;
-                else if (series) w = a * fmaf(a, fmaf(a, fmaf(a, 1.0f, 1.0f), 1.0f), 1.0f);
-                else w = a * gs_rcp(om);
+                float w = weight(a, om);
                 Sw[j] += w;
                 S0[j] = fmaf(w, Cv.x, S0[j]);
                 S1[j] = fmaf(w, Cv.y, S1[j]);
                 S2[j] = fmaf(w, Cv.z, S2[j]);
             }
-            if ((i & 7) == 7) {
+        };
+        if (!ODDS) body([](float a, float) { return a; });
+        else if (__all_sync(0xffffffffu, Cv.w != 0.0f))
+            body([](float a, float) { return a * fmaf(a, fmaf(a, fmaf(a, 1.0f, 1.0f), 1.0f), 1.0f); });
+        else body([](float a, float om) { return a * gs_rcp(om); });
+    };
+    // records of the next batch are fetched into registers while the current one is composited
+    SplatRec nxt;
+    int kb = warp * 32 + lane;
+    if (kb < n) nxt = rec[dense ? b * G.N + kb : vals[p0 + kb]];
+    for (int base = warp * 32; base < n; base += NW * 32) {
+        if (base + lane < n) srec[warp][lane] = nxt;
+        __syncwarp();
+        kb = base + NW * 32 + lane;
+        if (kb < n) nxt = rec[dense ? b * G.N + kb : vals[p0 + kb]];
+        const int nb = min(32, n - base);
+        int i = 0;
+        // (1 - a) >= 1e-4, so 8 factors stay normal in fp32: renormalise after every 8 splats
+        for (; i + 8 <= nb; i += 8) {
 #pragma unroll
-                for (int j = 0; j < PPL; j++) renorm(P[j], E[j]);
-            }
+            for (int ii = 0; ii < 8; ii++) step(srec[warp][i + ii]);
+#pragma unroll
+            for (int j = 0; j < PPL; j++) renorm(P[j], E[j]);
         }
+        for (; i < nb; ++i) step(srec[warp][i]);
 #pragma unroll
         for (int j = 0; j < PPL; j++) renorm(P[j], E[j]);
         __syncwarp();
@@ -759,6 +773,19 @@ __global__ void __launch_bounds__(256) k_composite(RenderGeom G, const float *__
             ob[c * P + p] = (1.0f - T) * fg + T * bg[b * G.C + c];
         }
     }
+}
+
+// fields of group g += the mapped prior group's fields (every group with prior_off >= 0, all images);
+// grid = (texel blocks, groups, images)
+__global__ void __launch_bounds__(256) k_add_prior(RenderGeom G, const float *__restrict__ prior,
+                                                   long long prior_per_image, float *__restrict__ fields) {
+    const GroupGeom &gg = G.g[blockIdx.y];
+    if (gg.prior_off < 0) return;
+    const long long n = 5LL * gg.H * gg.W;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int b = blockIdx.z;
+    fields[(long long)b * G.fld_per_image + gg.fld_off + i] += prior[(long long)b * prior_per_image + gg.prior_off + i];
 }
 
 // ----------------------------------------------------------------------------------------------------
@@ -885,7 +912,7 @@ __global__ void __launch_bounds__(256) k_adjoint(RenderGeom G, const int *__rest
 // one CTA per tile; lane = one (tile, splat) pair looping over the tile's pixels
 // (render_triton.py:602-720 with FIELDS=True; the index_add_ of render_triton.py:757-761/803-807
 // becomes three 16-byte vector atomics per pair into the per-splat sums).
-template <int TILE, int NW>
+template <int TILE, int NW, bool ODDS>
 __global__ void __launch_bounds__(NW * 32) k_fields_bwd(RenderGeom G, const SplatRec *__restrict__ rec,
                                                         const int2 *__restrict__ ranges,
                                                         const int *__restrict__ vals, const float *__restrict__ Gn,
@@ -935,7 +962,6 @@ __global__ void __launch_bounds__(NW * 32) k_fields_bwd(RenderGeom G, const Spla
         spx[threadIdx.x] = __fdiv_rn((float)(tx * TILE + threadIdx.x) + 0.5f, (float)Wg);
     }
     __syncthreads();
-    const bool odds = G.odds != 0;
     const int n = p1 - p0;
     for (int k = threadIdx.x; k < ((n + 31) & ~31); k += NW * 32) {
         if (k >= n) continue;  // whole-warp granularity: tail lanes idle
@@ -952,7 +978,8 @@ __global__ void __launch_bounds__(NW * 32) k_fields_bwd(RenderGeom G, const Spla
             vx[lx] = D * dx;
         }
         float Su = 0.f, Sv = 0.f, Suu = 0.f, Svv = 0.f, Suv = 0.f, Sf = 0.f, Sc0 = 0.f, Sc1 = 0.f, Sc2 = 0.f;
-#pragma unroll
+        // rows rolled, columns unrolled: the loop body stays small enough for the instruction cache
+#pragma unroll 1
         for (int ly = 0; ly < TILE; ly++) {
             const float dy = spy[ly] - muy;
             const float uy = A * dy, vy = Cc * dy;
@@ -970,7 +997,7 @@ __global__ void __launch_bounds__(NW * 32) k_fields_bwd(RenderGeom G, const Spla
                 const float rr = gs_rcp(om);
                 const float col_term = fmaf(d4.z, c0, fmaf(d4.w, c1, dS2 * c2));
                 float da, cw;
-                if (odds) {
+                if (ODDS) {
                     da = fmaf(d4.y + col_term, rr, -d4.x) * rr;
                     cw = a * rr;
                 } else {
@@ -1032,6 +1059,218 @@ __global__ void __launch_bounds__(256) k_finalize(RenderGeom G, const float *__r
     if (G.C > 1) g_col[s * G.C + 1] = a1.w;
     if (G.C > 2) g_col[s * G.C + 2] = a2.x;
     if (G.has_theta && g_th) g_th[s] = -(sx / sy - sy / sx) * Suv * invK2;
+}
+
+// ----------------------------------------------------------------------------------------------------
+// pixel-list render (render.py:68-87, render_alpha_subsampled): alpha compositing of all N splats of an
+// image at P listed pixels (flat indices y*W + x), dense (no binning), alpha mode, autograd of
+// render.py:30-36 including the clamp_min(1e-8) mask.  CTA = PT_PIX pixels x one slice of the splats.
+
+#define PT_PIX 64
+#define PT_SLICE 2048
+
+__device__ __forceinline__ void point_coords(const long long *__restrict__ px_idx, int P, int W, int H, int b, int p,
+                                             float &py, float &px) {
+    long long idx = p < P ? px_idx[(long long)b * P + p] : 0;
+    long long y = idx / W, x = idx - y * W;
+    py = __fdiv_rn((float)y + 0.5f, (float)H);  // ((idx // W) + 0.5) / H as torch computes it
+    px = __fdiv_rn((float)x + 0.5f, (float)W);
+}
+
+// partial sums (log T, S_w, S_c[3]) of splats [slice*PT_SLICE, ...) at the CTA's pixels:
+// part[slice][b][5][P]
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) k_points_fwd(int N, int H, int W, int P,
+                                                        const long long *__restrict__ px_idx,
+                                                        const SplatRec *__restrict__ rec, float *__restrict__ part) {
+    constexpr int PPL = PT_PIX / 32;
+    __shared__ SplatRec srec[NW][32];
+    __shared__ float red[NW][5][PT_PIX];
+    const int b = blockIdx.z, slice = blockIdx.y;
+    const int pbase = blockIdx.x * PT_PIX;
+    const int n0 = slice * PT_SLICE, n1 = min(N, n0 + PT_SLICE);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float py[PPL], px[PPL], Pp[PPL], Sw[PPL], S0[PPL], S1[PPL], S2[PPL];
+    int E[PPL];
+#pragma unroll
+    for (int j = 0; j < PPL; j++) {
+        point_coords(px_idx, P, W, H, b, pbase + lane + 32 * j, py[j], px[j]);
+        Pp[j] = 1.0f; E[j] = 0; Sw[j] = 0.f; S0[j] = 0.f; S1[j] = 0.f; S2[j] = 0.f;
+    }
+    const SplatRec *rb = rec + (long long)b * N;
+    for (int base = n0 + warp * 32; base < n1; base += NW * 32) {
+        if (base + lane < n1) srec[warp][lane] = rb[base + lane];
+        __syncwarp();
+        const int nb = min(32, n1 - base);
+        for (int i = 0; i < nb; ++i) {
+            const float4 A = srec[warp][i].a, Bv = srec[warp][i].b, Cv = srec[warp][i].c;
+#pragma unroll
+            for (int j = 0; j < PPL; j++) {
+                float dy = py[j] - A.x, dx = px[j] - A.y;
+                float u = fmaf(A.z, dy, A.w * dx);
+                float v = fmaf(Bv.x, dy, Bv.y * dx);
+                float a = fminf(gs_ex2(fmaf(-u, u, fmaf(-v, v, Bv.w))), GS_ALPHA_MAX);
+                Pp[j] *= 1.0f - a;
+                Sw[j] += a;
+                S0[j] = fmaf(a, Cv.x, S0[j]);
+                S1[j] = fmaf(a, Cv.y, S1[j]);
+                S2[j] = fmaf(a, Cv.z, S2[j]);
+            }
+            if ((i & 7) == 7) {
+#pragma unroll
+                for (int j = 0; j < PPL; j++) renorm(Pp[j], E[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < PPL; j++) renorm(Pp[j], E[j]);
+        __syncwarp();
+    }
+#pragma unroll
+    for (int j = 0; j < PPL; j++) {
+        const int q = lane + 32 * j;
+        red[warp][0][q] = logf(Pp[j]) + (float)E[j] * GS_LN2;
+        red[warp][1][q] = Sw[j];
+        red[warp][2][q] = S0[j];
+        red[warp][3][q] = S1[j];
+        red[warp][4][q] = S2[j];
+    }
+    __syncthreads();
+    const int B = gridDim.z;
+    for (int t = threadIdx.x; t < 5 * PT_PIX; t += NW * 32) {
+        const int c = t / PT_PIX, q = t - c * PT_PIX, p = pbase + q;
+        if (p >= P) continue;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; w++) v += red[w][c][q];
+        part[(((long long)slice * B + b) * 5 + c) * P + p] = v;
+    }
+}
+
+// fields[b][5][p] = sum over slices (fixed order), then the composite of render.py:30-36:
+// out[b][c][p] = (1 - T) * S_c / max(S_w, 1e-8) + T * bg[b][c]
+__global__ void __launch_bounds__(256) k_points_composite(int B, int C, int P, int nslices,
+                                                          const float *__restrict__ part,
+                                                          const float *__restrict__ bg, float *__restrict__ fields,
+                                                          float *__restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)B * P) return;
+    const int b = (int)(i / P), p = (int)(i - (long long)b * P);
+    float S[5];
+#pragma unroll
+    for (int c = 0; c < 5; c++) {
+        float v = 0.f;
+        for (int sl = 0; sl < nslices; sl++) v += part[(((long long)sl * B + b) * 5 + c) * P + p];
+        S[c] = v;
+        fields[((long long)b * 5 + c) * P + p] = v;
+    }
+    const float T = expf(S[0]);
+    const float asum = fmaxf(S[1], 1e-8f);
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+        if (c < C) out[((long long)b * C + c) * P + p] = (1.0f - T) * (S[2 + c] / asum) + T * bg[b * C + c];
+}
+
+// backward: the composite's adjoint for the CTA's pixels (fused), then lane = splat of the slice looping
+// over the pixels; the per-splat sums are those of k_fields_bwd, finished by k_finalize.
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) k_points_bwd(int N, int C, int H, int W, int P,
+                                                        const long long *__restrict__ px_idx,
+                                                        const SplatRec *__restrict__ rec,
+                                                        const float *__restrict__ fields, const float *__restrict__ bg,
+                                                        const float *__restrict__ gout, float *__restrict__ acc,
+                                                        float *__restrict__ gbg) {
+    __shared__ float4 sxy[PT_PIX];  // (py, px, dS_c2, -)
+    __shared__ float4 sds[PT_PIX];  // (dS_log, dS_w, dS_c0, dS_c1)
+    __shared__ float red[3][NW];
+    const int b = blockIdx.z, slice = blockIdx.y;
+    const int pbase = blockIdx.x * PT_PIX;
+    float gT[3] = {0.f, 0.f, 0.f};
+    if (threadIdx.x < PT_PIX) {
+        const int q = threadIdx.x, p = pbase + q;
+        float py, px;
+        point_coords(px_idx, P, W, H, b, p, py, px);
+        float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
+        float d2 = 0.f;
+        if (p < P) {
+            float S[5];
+#pragma unroll
+            for (int c = 0; c < 5; c++) S[c] = fields[((long long)b * 5 + c) * P + p];
+            const float Sw = S[1], asum = fmaxf(Sw, 1e-8f), T = expf(S[0]);
+            float dT = 0.f, dasum = 0.f, dsc[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < 3; c++) {
+                if (c < C) {
+                    const float gc = gout[((long long)b * C + c) * P + p];
+                    const float fg = S[2 + c] / asum;
+                    dT += gc * (bg[b * C + c] - fg);
+                    const float dfg = gc * (1.0f - T);
+                    dsc[c] = dfg / asum;
+                    dasum += dfg * fg;
+                    gT[c] = gc * T;
+                }
+            }
+            const float dsw = Sw >= 1e-8f ? -dasum / asum : 0.0f;  // clamp_min(1e-8) passes no gradient
+            d = make_float4(dT * T, dsw, dsc[0], dsc[1]);
+            d2 = dsc[2];
+        }
+        sxy[q] = make_float4(py, px, d2, 0.f);
+        sds[q] = d;
+    }
+    if (slice == 0) {  // the background gradient, once per pixel
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+            float v = gT[c];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) red[c][warp] = v;
+        }
+    }
+    __syncthreads();
+    if (slice == 0 && threadIdx.x < 3 && threadIdx.x < C) {
+        float v = 0.f;
+        for (int w = 0; w < NW; w++) v += red[threadIdx.x][w];
+        atomicAdd(&gbg[b * 4 + threadIdx.x], v);
+    }
+    const int npix = min(PT_PIX, P - pbase);
+    const int n0 = slice * PT_SLICE, n1 = min(N, n0 + PT_SLICE);
+    for (int k = n0 + threadIdx.x; k < n1; k += NW * 32) {
+        const long long sid = (long long)b * N + k;
+        const SplatRec r = rec[sid];
+        const float muy = r.a.x, mux = r.a.y, A = r.a.z, Bc = r.a.w;
+        const float Cc = r.b.x, D = r.b.y, op = r.b.z;
+        const float c0 = r.c.x, c1 = r.c.y, c2 = r.c.z;
+        float Su = 0.f, Sv = 0.f, Suu = 0.f, Svv = 0.f, Suv = 0.f, Sf = 0.f, Sc0 = 0.f, Sc1 = 0.f, Sc2 = 0.f;
+        for (int q = 0; q < npix; q++) {
+            const float4 xy = sxy[q];
+            const float4 d4 = sds[q];
+            const float dy = xy.x - muy, dx = xy.y - mux;
+            const float u = fmaf(A, dy, Bc * dx);
+            const float v = fmaf(Cc, dy, D * dx);
+            const float f = gs_ex2(-fmaf(u, u, v * v));
+            const float fo = op * f;
+            const float a = fminf(fo, GS_ALPHA_MAX);
+            const float rr = gs_rcp(1.0f - a);
+            const float col_term = fmaf(d4.z, c0, fmaf(d4.w, c1, xy.z * c2));
+            const float da = fmaf(-d4.x, rr, d4.y + col_term);
+            Sc0 = fmaf(a, d4.z, Sc0);
+            Sc1 = fmaf(a, d4.w, Sc1);
+            Sc2 = fmaf(a, xy.z, Sc2);
+            const float dafo = fo < GS_ALPHA_MAX ? da : 0.0f;
+            Sf = fmaf(dafo, f, Sf);
+            const float Gm = dafo * fo;
+            const float Gu = Gm * u, Gv = Gm * v;
+            Su += Gu;
+            Sv += Gv;
+            Suu = fmaf(Gu, u, Suu);
+            Svv = fmaf(Gv, v, Svv);
+            Suv = fmaf(Gu, v, Suv);
+        }
+        float *ap = acc + sid * 12;
+        gs_red_add_v4(ap, Su, Sv, Suu, Svv);
+        gs_red_add_v4(ap + 4, Suv, Sf, Sc0, Sc1);
+        gs_red_add_v4(ap + 8, Sc2, 0.f, 0.f, 0.f);
+    }
 }
 
 // L2 loss of a [planes][H][W] image against a target over rows [y0, y1): grad = 2*scale*(out - target)
@@ -1147,6 +1386,8 @@ void make_geom(const gs_render_desc *d, RenderGeom &G) {
     for (int k = 0; k < ng; k++) {
         G.g[k].fld_off = (int)foff;
         foff += 5LL * G.g[k].H * G.g[k].W;
+        G.g[k].prior_grp = -1;
+        G.g[k].prior_off = -1;
     }
     G.tiles_per_image = toff;
     G.fld_per_image = foff;
@@ -1267,9 +1508,15 @@ int launch_fields_fwd(const Plan &pl, void *ws, cudaStream_t st) {
     auto rng = at<int2>(ws, pl.o_ranges);
     const int *vals = at<int>(ws, (pl.passes % 2) ? pl.o_vals_b : pl.o_vals_a);
     auto fld = at<float>(ws, pl.o_fields);
-    if (G.tile == 8) k_fields_fwd<8, 4><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
-    else if (G.tile == 16) k_fields_fwd<16, 4><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
-    else k_fields_fwd<4, 4><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
+    if (G.odds) {
+        if (G.tile == 8) k_fields_fwd<8, 4, true><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
+        else if (G.tile == 16) k_fields_fwd<16, 4, true><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
+        else k_fields_fwd<4, 4, true><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
+    } else {
+        if (G.tile == 8) k_fields_fwd<8, 4, false><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
+        else if (G.tile == 16) k_fields_fwd<16, 4, false><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
+        else k_fields_fwd<4, 4, false><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
+    }
     GS_CHECK_LAUNCH("k_fields_fwd");
     return GS_OK;
 }
@@ -1286,6 +1533,45 @@ int run_preprocess(const Plan &pl, const float *mu, const float *ls, const float
                                               at<int>(ws, pl.o_gsplats));
     GS_CHECK_LAUNCH("k_preprocess");
     return GS_OK;
+}
+
+// ---- pixel-list render (render_alpha_subsampled)
+
+__global__ void __launch_bounds__(256) k_points_prep(long long BN, int C, int has_theta, const float *__restrict__ mu,
+                                                     const float *__restrict__ ls, const float *__restrict__ col,
+                                                     const float *__restrict__ op, const float *__restrict__ th,
+                                                     SplatRec *__restrict__ rec) {
+    const long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= BN) return;
+    float sy, sx;
+    rec[s] = make_rec(s, C, has_theta, mu, ls, col, op, th, sy, sx);
+}
+
+struct PointsPlan {
+    int nslices;
+    size_t o_rec, o_part, o_fields, o_acc, o_gbg, fwd_bytes, total_bytes;
+};
+
+int points_validate(const gs_render_desc *d, int P) {
+    int st = validate(d);
+    if (st != GS_OK) return st;
+    if (d->mode != GS_MODE_EXACT || d->odds || P < 1) return GS_ERR_BAD_ARGUMENT;
+    if ((long long)d->B * P >= (1LL << 31)) return GS_ERR_BAD_ARGUMENT;
+    return GS_OK;
+}
+
+void points_plan(const gs_render_desc *d, int P, PointsPlan &pp) {
+    const long long BN = (long long)d->B * d->N;
+    pp.nslices = (int)std::max<long long>(1, (d->N + PT_SLICE - 1) / PT_SLICE);
+    size_t o = 0;
+    auto take = [&](size_t bytes) { size_t r = o; o = align256(o + bytes); return r; };
+    pp.o_rec = take(sizeof(SplatRec) * (size_t)std::max<long long>(BN, 1));
+    pp.o_part = take(sizeof(float) * 5 * (size_t)pp.nslices * d->B * P);
+    pp.o_fields = take(sizeof(float) * 5 * (size_t)d->B * P);
+    pp.fwd_bytes = o;
+    pp.o_acc = take(sizeof(float) * 12 * (size_t)std::max<long long>(BN, 1));
+    pp.o_gbg = take(sizeof(float) * 4 * (size_t)d->B);
+    pp.total_bytes = o;
 }
 
 }  // namespace
@@ -1344,6 +1630,50 @@ int gs_render_count(const gs_render_desc *d, const float *mu, const float *log_s
 int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_scale, const float *color,
                   const float *opacity, const float *bg, const float *theta, float *out, void *workspace,
                   size_t workspace_bytes, void *stream) {
+    return gs_render_fwd_prior(d, mu, log_scale, color, opacity, bg, theta, out, nullptr, workspace,
+                               workspace_bytes, stream);
+}
+
+}  // extern "C"
+
+int gs_render_prior_map(const gs_render_desc *prior_d, const void *prior_ws, const gs_render_desc *d, int n_prior,
+                        GsPrior *out) {
+    if (!out) return 0;
+    memset(out, 0, sizeof(*out));
+    for (int k = 0; k < GS_MAX_GROUPS; k++) out->grp[k] = out->off[k] = -1;
+    if (validate(prior_d) != GS_OK || validate(d) != GS_OK || !prior_ws) return 0;
+    if (prior_d->mode != GS_MODE_OCTAVE || d->mode != GS_MODE_OCTAVE) return 0;
+    if (prior_d->B != d->B || prior_d->tile != d->tile || prior_d->cutoff != d->cutoff ||
+        prior_d->base_texels != d->base_texels || prior_d->max_octaves != d->max_octaves ||
+        prior_d->odds != d->odds || prior_d->has_theta != d->has_theta || prior_d->C != d->C)
+        return 0;
+    if (n_prior <= 0 || n_prior != prior_d->N || n_prior > d->N || prior_d->row_end > 0 || d->row_end > 0) return 0;
+    const int rep_p = std::min(prior_d->H, prior_d->W), rep = std::min(d->H, d->W);
+    if (rep != 2 * rep_p) return 0;  // the octave index then shifts by exactly one
+    Plan pp;
+    make_plan(prior_d, pp);
+    RenderGeom G;
+    make_geom(d, G);
+    int mapped = 0;
+    for (int k = 2; k <= d->max_octaves; k++) {
+        const int kp = k - 1;
+        if (kp >= prior_d->max_octaves) continue;  // the prior's clamped last octave also holds larger splats
+        if (G.g[k].H != pp.G.g[kp].H || G.g[k].W != pp.G.g[kp].W) continue;
+        out->grp[k] = kp;
+        out->off[k] = pp.G.g[kp].fld_off;
+        mapped++;
+    }
+    if (!mapped) return 0;
+    out->fields = reinterpret_cast<const float *>(reinterpret_cast<const char *>(prior_ws) + pp.o_fields);
+    out->fld_per_image = pp.G.fld_per_image;
+    out->skip_n = n_prior;
+    out->rep = (float)rep_p;
+    return mapped;
+}
+
+int gs_render_fwd_prior(const gs_render_desc *d, const float *mu, const float *log_scale, const float *color,
+                        const float *opacity, const float *bg, const float *theta, float *out, const GsPrior *prior,
+                        void *workspace, size_t workspace_bytes, void *stream) {
     int st = validate(d);
     if (st != GS_OK) return st;
     if (!bg || !out) return GS_ERR_BAD_ARGUMENT;
@@ -1352,6 +1682,14 @@ int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_sca
     make_plan(d, pl);
     if (!workspace || workspace_bytes < pl.fwd_bytes) return GS_ERR_WORKSPACE;
     cudaStream_t s = (cudaStream_t)stream;
+    if (prior && prior->fields) {
+        pl.G.skip_n = prior->skip_n;
+        pl.G.prior_rep = prior->rep;
+        for (int k = 0; k < pl.G.ngroups; k++) {
+            pl.G.g[k].prior_grp = prior->grp[k];
+            pl.G.g[k].prior_off = prior->off[k];
+        }
+    }
     const RenderGeom &G = pl.G;
     std::unique_ptr<ProfScope> bin_scope(new ProfScope(PR_BIN, s));
     st = run_preprocess(pl, mu, log_scale, color, opacity, theta, workspace, s);
@@ -1378,7 +1716,7 @@ int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_sca
                 // digit-0 histograms per emit segment come from k_emit
                 k_radix_scan<<<radix, 256, 0, s>>>(hist, total, pl.cap, nemit, dtot, nemit);
                 GS_CHECK_LAUNCH("k_radix_scan");
-                k_radix_downsweep_seg<<<std::min(nemit, 148 * 8), RS_THREADS, 0, s>>>(
+                k_radix_downsweep_seg<<<std::min(nemit, 148 * 8), RS_THREADS, sizeof(RsSmem), s>>>(
                     ka, va, kb, vb, at<int>(workspace, pl.o_bsum), pl.nblk_pre, pl.emit_parts, total, pl.cap, shift,
                     radix, hist, nemit, dtot);
                 GS_CHECK_LAUNCH("k_radix_downsweep_seg");
@@ -1387,8 +1725,8 @@ int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_sca
                 GS_CHECK_LAUNCH("k_radix_upsweep");
                 k_radix_scan<<<radix, 256, 0, s>>>(hist, total, pl.cap, pl.nblk_sort, dtot, 0);
                 GS_CHECK_LAUNCH("k_radix_scan");
-                k_radix_downsweep<<<pgrid, RS_THREADS, 0, s>>>(ka, va, kb, vb, total, pl.cap, shift, radix, hist,
-                                                               pl.nblk_sort, dtot);
+                k_radix_downsweep<<<pgrid, RS_THREADS, sizeof(RsSmem), s>>>(ka, va, kb, vb, total, pl.cap, shift,
+                                                                            radix, hist, pl.nblk_sort, dtot);
                 GS_CHECK_LAUNCH("k_radix_downsweep");
             }
             std::swap(ka, kb);
@@ -1403,6 +1741,14 @@ int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_sca
         ProfScope ps(PR_FIELDS_FWD, s);
         st = launch_fields_fwd(pl, workspace, s);
         if (st != GS_OK) return st;
+        if (G.skip_n > 0) {
+            long long big = 0;
+            for (int k = 0; k < G.ngroups; k++)
+                if (G.g[k].prior_off >= 0) big = std::max(big, 5LL * G.g[k].H * G.g[k].W);
+            dim3 pg((unsigned)((big + 255) / 256), (unsigned)G.ngroups, (unsigned)d->B);
+            k_add_prior<<<pg, 256, 0, s>>>(G, prior->fields, prior->fld_per_image, at<float>(workspace, pl.o_fields));
+            GS_CHECK_LAUNCH("k_add_prior");
+        }
     }
     long long Pb = (long long)(G.y1 - G.y0) * d->W;
     dim3 cg((unsigned)std::max<long long>(1, (Pb + 255) / 256), (unsigned)d->B);
@@ -1414,6 +1760,8 @@ int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_sca
     }
     return GS_OK;
 }
+
+extern "C" {
 
 int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_scale, const float *color,
                   const float *opacity, const float *bg, const float *theta, const float *grad_out, float *g_mu,
@@ -1462,9 +1810,15 @@ int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_sca
     auto acc = at<float>(workspace, pl.o_acc);
     if (d->N > 0) {
         ProfScope ps(PR_FIELDS_BWD, s);
-        if (G.tile == 8) k_fields_bwd<8, 4><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
-        else if (G.tile == 16) k_fields_bwd<16, 4><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
-        else k_fields_bwd<4, 4><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
+        if (G.odds) {
+            if (G.tile == 8) k_fields_bwd<8, 4, true><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
+            else if (G.tile == 16) k_fields_bwd<16, 4, true><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
+            else k_fields_bwd<4, 4, true><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
+        } else {
+            if (G.tile == 8) k_fields_bwd<8, 4, false><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
+            else if (G.tile == 16) k_fields_bwd<16, 4, false><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
+            else k_fields_bwd<4, 4, false><<<grid, 128, 0, s>>>(G, rec, rng, vals, Gn, gf, acc);
+        }
         GS_CHECK_LAUNCH("k_fields_bwd");
     }
     long long nfin = std::max<long long>((long long)d->B * d->N, (long long)d->B * d->C);
@@ -1544,6 +1898,79 @@ int gs_activate_scale(const float *log_scale, float *out, int64_t n, void *strea
     if (n == 0) return GS_OK;
     k_activate_scale<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(log_scale, out, n);
     GS_CHECK_LAUNCH("k_activate_scale");
+    return GS_OK;
+}
+
+size_t gs_render_points_workspace_size(const gs_render_desc *d, int32_t P, int with_backward) {
+    if (points_validate(d, P) != GS_OK) return 0;
+    PointsPlan pp;
+    points_plan(d, P, pp);
+    return with_backward ? pp.total_bytes : pp.fwd_bytes;
+}
+
+int gs_render_points_fwd(const gs_render_desc *d, int32_t P, const int64_t *px_idx, const float *mu,
+                         const float *log_scale, const float *color, const float *opacity, const float *bg,
+                         const float *theta, float *out, void *workspace, size_t workspace_bytes, void *stream) {
+    int st = points_validate(d, P);
+    if (st != GS_OK) return st;
+    if (!px_idx || !bg || !out) return GS_ERR_BAD_ARGUMENT;
+    if (d->N > 0 && (!mu || !log_scale || !color || !opacity || (d->has_theta && !theta))) return GS_ERR_BAD_ARGUMENT;
+    PointsPlan pp;
+    points_plan(d, P, pp);
+    if (!workspace || workspace_bytes < pp.fwd_bytes) return GS_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    const long long BN = (long long)d->B * d->N;
+    auto rec = at<SplatRec>(workspace, pp.o_rec);
+    auto part = at<float>(workspace, pp.o_part);
+    const long long *idx = reinterpret_cast<const long long *>(px_idx);
+    if (BN > 0) {
+        k_points_prep<<<(unsigned)((BN + 255) / 256), 256, 0, s>>>(BN, d->C, d->has_theta, mu, log_scale, color,
+                                                                  opacity, d->has_theta ? theta : nullptr, rec);
+        GS_CHECK_LAUNCH("k_points_prep");
+        dim3 grid((unsigned)((P + PT_PIX - 1) / PT_PIX), (unsigned)pp.nslices, (unsigned)d->B);
+        k_points_fwd<4><<<grid, 128, 0, s>>>(d->N, d->H, d->W, P, idx, rec, part);
+        GS_CHECK_LAUNCH("k_points_fwd");
+    } else {
+        cudaError_t e = cudaMemsetAsync(part, 0, sizeof(float) * 5 * (size_t)pp.nslices * d->B * P, s);
+        GS_COUNT(1);
+        if (e != cudaSuccess) return set_cuda_error(e, "memset");
+    }
+    const long long n = (long long)d->B * P;
+    k_points_composite<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(d->B, d->C, P, pp.nslices, part, bg,
+                                                                   at<float>(workspace, pp.o_fields), out);
+    GS_CHECK_LAUNCH("k_points_composite");
+    return GS_OK;
+}
+
+int gs_render_points_bwd(const gs_render_desc *d, int32_t P, const int64_t *px_idx, const float *log_scale,
+                         const float *bg, const float *theta, const float *grad_out, float *g_mu,
+                         float *g_log_scale, float *g_color, float *g_opacity, float *g_bg, float *g_theta,
+                         void *workspace, size_t workspace_bytes, void *stream) {
+    int st = points_validate(d, P);
+    if (st != GS_OK) return st;
+    if (!px_idx || !bg || !grad_out || !g_bg) return GS_ERR_BAD_ARGUMENT;
+    if (d->N > 0 && (!g_mu || !g_log_scale || !g_color || !g_opacity || !log_scale)) return GS_ERR_BAD_ARGUMENT;
+    PointsPlan pp;
+    points_plan(d, P, pp);
+    if (!workspace || workspace_bytes < pp.total_bytes) return GS_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t e = cudaMemsetAsync(at<char>(workspace, pp.o_acc), 0, pp.total_bytes - pp.o_acc, s);
+    GS_COUNT(1);
+    if (e != cudaSuccess) return set_cuda_error(e, "memset");
+    const long long *idx = reinterpret_cast<const long long *>(px_idx);
+    dim3 grid((unsigned)((P + PT_PIX - 1) / PT_PIX), (unsigned)pp.nslices, (unsigned)d->B);
+    k_points_bwd<4><<<grid, 128, 0, s>>>(d->N, d->C, d->H, d->W, P, idx, at<SplatRec>(workspace, pp.o_rec),
+                                         at<float>(workspace, pp.o_fields), bg, grad_out,
+                                         at<float>(workspace, pp.o_acc), at<float>(workspace, pp.o_gbg));
+    GS_CHECK_LAUNCH("k_points_bwd");
+    RenderGeom G;
+    make_geom(d, G);
+    long long nfin = std::max<long long>((long long)d->B * d->N, (long long)d->B * d->C);
+    k_finalize<<<(unsigned)((nfin + 255) / 256), 256, 0, s>>>(G, log_scale, d->has_theta ? theta : nullptr,
+                                                              at<float>(workspace, pp.o_acc),
+                                                              at<float>(workspace, pp.o_gbg), g_mu, g_log_scale,
+                                                              g_color, g_opacity, g_bg, g_theta);
+    GS_CHECK_LAUNCH("k_finalize");
     return GS_OK;
 }
 

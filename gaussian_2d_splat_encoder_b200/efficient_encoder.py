@@ -304,6 +304,16 @@ class EfficientGaussianEncoder(nn.Module):
     def forward(self, image, return_latents: bool = False):
         """image [B,3,H,W] in [0,1] (CUDA) -> dict(mu, log_scale, color, opacity, theta, bg, n_gaussians,
         n_coarse, backbone_features) in the reference's layouts (efficient_encoder.py:306-378)."""
+        return self._run(image, return_latents, render=False)[0]
+
+    def forward_and_render(self, image, return_latents: bool = False):
+        """The encode-and-render pipeline (examples/encode_and_render.py:31-38) in one library call
+        (gs_encode_render_fwd): returns (the forward's dict, render_alpha_octave(its splats, H, W,
+        odds=self.odds) with that function's defaults).  At H = W = 2 * residual_grid the render reuses the
+        octave fields of the coarse splats computed by the encoder's internal render."""
+        return self._run(image, return_latents, render=True)
+
+    def _run(self, image, return_latents, render):
         if not self._cuda_supported():
             raise NotImplementedError("the CUDA encoder implements the released 'adaptive' architecture "
                                       "(d_feature=256, stride 8, fine_stride 4, GroupNorm, gradient input)")
@@ -319,7 +329,8 @@ class EfficientGaussianEncoder(nn.Module):
             L = _lib.load()
             tens, wst = self._weights(dev)
             d = self._desc(B, H, W)
-            nbytes = int(L.gs_encoder_workspace_size(C.byref(d)))
+            size_fn = L.gs_encode_render_workspace_size if render else L.gs_encoder_workspace_size
+            nbytes = int(size_fn(C.byref(d)))
             if nbytes == 0:
                 raise ValueError("unsupported encoder configuration")
             Nc = (H // 8) * (W // 8) * self.M
@@ -332,12 +343,18 @@ class EfficientGaussianEncoder(nn.Module):
             lat = torch.empty(B, H // 4, W // 4, self.fine_decoder.out_ch, device=dev) if return_latents else None
             ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
             p = _lib.ptr
-            _lib.check(L.gs_encoder_fwd(C.byref(d), C.byref(wst), p(x), p(o["mu"]), p(o["log_scale"]), p(o["color"]),
-                                        p(o["opacity"]), p(o["theta"]), p(o["bg"]), p(feat), p(lat), p(ws), nbytes,
-                                        _lib.stream_of(dev)), "gs_encoder_fwd")
+            args = [C.byref(d), C.byref(wst), p(x), p(o["mu"]), p(o["log_scale"]), p(o["color"]), p(o["opacity"]),
+                    p(o["theta"]), p(o["bg"]), p(feat), p(lat)]
+            rec = None
+            if render:
+                rec = torch.empty(B, 3, H, W, device=dev)
+                _lib.check(L.gs_encode_render_fwd(*args, p(rec), p(ws), nbytes, _lib.stream_of(dev)),
+                           "gs_encode_render_fwd")
+            else:
+                _lib.check(L.gs_encoder_fwd(*args, p(ws), nbytes, _lib.stream_of(dev)), "gs_encoder_fwd")
         o["n_gaussians"] = N
         o["n_coarse"] = Nc
         o["backbone_features"] = feat.permute(0, 3, 1, 2)
         if return_latents:
             o["splat_features"] = lat.permute(0, 3, 1, 2)
-        return o
+        return o, rec

@@ -7,6 +7,8 @@ into a CUDA graph and replay it: the same kernels, the same numerics, one launch
 
 * ``EncodeRender`` -- ``EfficientGaussianEncoder`` forward + ``render_alpha_octave`` of its splats
   (examples/encode_and_render.py:31-38 of the reference), inference.
+* ``EncodeRenderStream`` -- the same for a stream of host images, with the PCIe copies of neighbouring
+  images overlapped with the kernels.
 * ``RenderFitStep`` -- ``render_alpha_octave`` forward + an L2 loss + the gradients of the six splat
   leaves (the fitting step of configs 1 and 4).
 
@@ -33,10 +35,8 @@ class EncodeRender:
         self.warmup = warmup
 
     def _body(self):
-        out = self.enc(self.x)
-        rec = render_alpha_octave(out["mu"], out["log_scale"], out["color"], out["opacity"], out["bg"],
-                                  self.shape[2], self.shape[3], theta=out["theta"], odds=self.enc.odds)
-        return out, rec
+        # one library call (gs_encode_render_fwd): the render reuses the encoder's coarse-render fields
+        return self.enc.forward_and_render(self.x)
 
     def capture(self, profile: bool = False):
         """Warm up eagerly, then capture one step.  profile=True captures the library's stage events
@@ -72,6 +72,69 @@ class EncodeRender:
     def replay(self):
         self.graph.replay()
         return self.rec
+
+
+class EncodeRenderStream:
+    """Throughput form of ``EncodeRender`` for a stream of host images (config 3's image batches).
+
+    ``depth`` graph instances, each with its own input and output buffers, take images in turn: the
+    host-to-device copy of the next image and the device-to-host copy of the previous reconstruction run
+    on their own streams while the current image is encoded and rendered, so PCIe traffic hides behind
+    the kernels.  ``submit(image, out)`` enqueues one image (pinned host [1,3,H,W]) and its destination
+    (pinned host [1,3,H,W]); ``synchronize()`` waits for every submitted reconstruction."""
+
+    def __init__(self, encoder, H: int, W: int, device=None, depth: int = 2):
+        self.slots = [EncodeRender(encoder, 1, H, W, device) for _ in range(depth)]
+        dev = self.slots[0].dev
+        self.dev = dev
+        self.h2d, self.comp, self.d2h = (torch.cuda.Stream(dev) for _ in range(3))
+        mk = lambda: [torch.cuda.Event() for _ in range(depth)]  # noqa: E731
+        self.ev_in, self.ev_done, self.ev_out = mk(), mk(), mk()
+        self.used = [False] * depth
+        self.n = 0
+
+    def capture(self):
+        for s in self.slots:
+            s.capture()
+        return self
+
+    def submit(self, image: torch.Tensor, out: torch.Tensor):
+        k = self.n % len(self.slots)
+        slot = self.slots[k]
+        if slot.graph is None:
+            slot.capture()
+        if self.used[k]:
+            self.h2d.wait_event(self.ev_done[k])   # the slot's input buffer was read by its last replay
+            self.comp.wait_event(self.ev_out[k])   # its output buffer was copied out
+        with torch.cuda.stream(self.h2d):
+            slot.x.copy_(image, non_blocking=True)
+            self.ev_in[k].record(self.h2d)
+        self.comp.wait_event(self.ev_in[k])
+        with torch.cuda.stream(self.comp):
+            slot.graph.replay()
+            self.ev_done[k].record(self.comp)
+        self.d2h.wait_event(self.ev_done[k])
+        with torch.cuda.stream(self.d2h):
+            out.copy_(slot.rec, non_blocking=True)
+            self.ev_out[k].record(self.d2h)
+        self.used[k] = True
+        self.n += 1
+
+    def wait_into(self, stream=None):
+        """Make `stream` (default: the current stream) wait for every submitted image."""
+        st = stream if stream is not None else torch.cuda.current_stream(self.dev)
+        for k, u in enumerate(self.used):
+            if u:
+                st.wait_event(self.ev_out[k])
+
+    def start_after(self, stream=None):
+        """Order the pipeline's streams after the work already queued on `stream` (default: current)."""
+        st = stream if stream is not None else torch.cuda.current_stream(self.dev)
+        for s in (self.h2d, self.comp, self.d2h):
+            s.wait_stream(st)
+
+    def synchronize(self):
+        self.d2h.synchronize()
 
 
 def render_l2_grads(leaves, target, H: int, W: int, odds: bool = True, row_band=None):

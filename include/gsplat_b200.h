@@ -108,6 +108,21 @@ int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_sca
                   float *g_log_scale, float *g_color, float *g_opacity, float *g_bg, float *g_theta,
                   void *workspace, size_t workspace_bytes, void *stream);
 
+/* Pixel-list render: replaces render_alpha_subsampled (render.py:68-87) and the torch autograd of its
+ * alpha_composite (render.py:30-36).  All N splats of image b are composited (alpha mode, no binning) at
+ * the P pixels px_idx[b][0..P) (flat indices y*W + x, int64, as torch.randint returns them).
+ * d->mode must be GS_MODE_EXACT and d->odds 0; tile, cutoff and the octave fields are ignored.
+ * out is [B][C][P].  The forward keeps the per-pixel sums in the workspace for the backward, which
+ * takes grad_out [B][C][P] and writes the gradients of the six leaves (g_theta may be NULL). */
+size_t gs_render_points_workspace_size(const gs_render_desc *d, int32_t P, int with_backward);
+int gs_render_points_fwd(const gs_render_desc *d, int32_t P, const int64_t *px_idx, const float *mu,
+                         const float *log_scale, const float *color, const float *opacity, const float *bg,
+                         const float *theta, float *out, void *workspace, size_t workspace_bytes, void *stream);
+int gs_render_points_bwd(const gs_render_desc *d, int32_t P, const int64_t *px_idx, const float *log_scale,
+                         const float *bg, const float *theta, const float *grad_out, float *g_mu,
+                         float *g_log_scale, float *g_color, float *g_opacity, float *g_bg, float *g_theta,
+                         void *workspace, size_t workspace_bytes, void *stream);
+
 /* Debug/parity accessors for the binning held in a forward's workspace (octave/cull/multires):
  * copies (SYNCHRONOUSLY) the total pair count, the per-group geometry and the sorted CSR so tests can
  * compare it bit-exactly with the reference's _build_tiles (render_triton.py:351-409).
@@ -120,8 +135,9 @@ int gs_render_debug_bins(const gs_render_desc *d, const void *workspace, int64_t
 
 /* One encoder convolution on the tensor cores: NHWC bf16 input [B][H][W][Cin], packed bf16 weights
  * [Cout][kh*kw*Cin] (tap-major, channel-minor), fp32 bias, NHWC bf16 output [B][Ho][Wo][Cout] with
- * bias + (optional) exact GELU applied; when gn_stats is non-NULL the GroupNorm(8) partial sums
- * (sum, sum of squares) of the output are ADDED to gn_stats[B][8][2].  kind 0: Cin a multiple of 64,
+ * bias + (optional) GELU applied (erf form, |error| < 7e-7 before the bf16 rounding); when gn_stats
+ * is non-NULL the GroupNorm(8) partial sums (sum, sum of squares) of the output are ADDED to
+ * gn_stats[B][8][2].  kind 0: Cin a multiple of 64,
  * stride 1 or 2; kind 1: the encoder's first layer expressed on its space-to-depth input (Cin = 16,
  * 4x4 taps, stride 1, pad 2, output Ho x Wo given explicitly).  Cout in {64, 128, 256}.  err_flag
  * (device int, may be NULL) receives a non-zero code if a bounded device wait gave up.
@@ -176,6 +192,19 @@ size_t gs_encoder_workspace_size(const gs_encoder_desc *e);
 int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights *w, const float *image, float *mu,
                    float *log_scale, float *color, float *opacity, float *theta, float *bg, float *features,
                    float *latents, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Encoder forward followed by render_alpha_octave of its splats at the image size, in one call: the
+ * pipeline of examples/encode_and_render.py:31-38 with render_alpha_octave's defaults (TILE 8, cutoff 3,
+ * base_texels 8, max_octaves 6, max_pairs 48e6, odds = the encoder's odds).  Outputs as gs_encoder_fwd,
+ * plus the reconstruction out [B][3][H][W].  When H = W = 2 * residual_grid the coarse splats fall on the
+ * same texel grids in both of the path's renders (octave k of the encoder's internal coarse render is
+ * octave k + 1 of the final one), so the final render adds those octaves' fields from the internal render
+ * instead of binning and compositing the coarse splats again (sums are regrouped: results agree with the
+ * two separate calls to fp32 rounding).  The workspace holds the encoder's and the render's. */
+size_t gs_encode_render_workspace_size(const gs_encoder_desc *e);
+int gs_encode_render_fwd(const gs_encoder_desc *e, const gs_encoder_weights *w, const float *image, float *mu,
+                         float *log_scale, float *color, float *opacity, float *theta, float *bg, float *features,
+                         float *latents, float *out, void *workspace, size_t workspace_bytes, void *stream);
 
 /* Reads (synchronously) the bounded-wait error flag left in an encoder workspace (0 = none). */
 int gs_encoder_error_flag(const gs_encoder_desc *e, const void *workspace, int *flag_host);

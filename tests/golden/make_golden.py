@@ -12,8 +12,8 @@ harness-level shim; the reference files are untouched).  Every fixture stores th
 from, so the tests never need the reference at run time.
 
 Cases mirror the reference's own self-tests (render_triton.py:983-1533: same seeds, shapes and cutoffs)
-plus edge cases (ragged image sizes, off-image splats, a single splat, theta=None) and the binning of
-config 1 at full size (768^2, 92,160 splats).
+plus edge cases (ragged image sizes, off-image splats, a single splat, theta=None), the binning of
+config 1 at full size (768^2, 92,160 splats) and the pixel-list render (render.py:68-87).
 """
 
 from __future__ import annotations
@@ -313,8 +313,35 @@ def make_encoder(names):
         print(f"encoder_cfg0: {time.time() - t0:.1f}s", flush=True)
 
 
+def make_points(names):
+    """render_alpha_subsampled (render.py:68-87) at seeded pixel lists (duplicates included, as
+    torch.randint draws them), with and without theta, one batch holding opacity-1 splats (the
+    alpha clamp)."""
+    if names and "points" not in names:
+        return
+    specs = {"points_theta": (31, 2, 300, 40, 56, 500, True), "points_notheta": (37, 1, 200, 33, 29, 700, False)}
+    for name, (seed, B, N, H, W, P, theta) in specs.items():
+        t0 = time.time()
+        L = leaves(seed, B, N, 3, 2.0, 0.9, theta=theta)
+        L[3][:, :5] = 1.0
+        idx = torch.randint(0, H * W, (B, P), generator=torch.Generator().manual_seed(seed + 1))
+        Lr = [t.detach().clone().requires_grad_(True) if t is not None else None for t in L]
+        out, pidx = ref_render.render_alpha_subsampled(*Lr[:5], H, W, theta=Lr[5], pixel_indices=idx)
+        gseed = 4321
+        gC = upstream_grad(out.shape, gseed)
+        (out * gC).sum().backward()
+        rec = {f"in_{n}": t.detach().numpy() for n, t in zip(NAMES, L) if t is not None}
+        rec.update({"H": H, "W": W, "gseed": gseed, "px_idx": pidx.numpy(), "out": out.detach().numpy()})
+        for n, t in zip(NAMES, Lr):
+            if t is not None:
+                rec[f"grad_{n}"] = t.grad.numpy()
+        np.savez_compressed(HERE / f"{name}.npz", **rec)
+        print(f"{name}: {time.time() - t0:.1f}s", flush=True)
+
+
 if __name__ == "__main__":
     names = set(sys.argv[1:])
     make_tiles(names)
     make_render(names)
     make_encoder(names)
+    make_points(names)

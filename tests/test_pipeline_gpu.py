@@ -30,6 +30,52 @@ def test_encode_render_graph_matches_eager(lib):
     assert pipe.launches_per_replay > 20
 
 
+@pytest.mark.parametrize("size,rg", [(256, 128), (256, 96), (768, 384)])
+def test_forward_and_render_matches_separate_calls(lib, size, rg):
+    """gs_encode_render_fwd (which, at H = W = 2 * residual_grid, takes the coarse splats' octave fields
+    from the encoder's internal render) against the encoder forward followed by render_alpha_octave."""
+    from gaussian_2d_splat_encoder_b200 import synth
+    from gaussian_2d_splat_encoder_b200.efficient_encoder import EfficientGaussianEncoder
+    from gaussian_2d_splat_encoder_b200.render_triton import render_alpha_octave
+
+    torch.manual_seed(1)
+    enc = EfficientGaussianEncoder(**{**GOLDEN_CFG, "residual_grid": rg}).cuda().eval()
+    x = synth.synth_card(size, size, 80, 30, 7).cuda()
+    with torch.inference_mode():
+        o = enc(x)
+        ref = render_alpha_octave(o["mu"], o["log_scale"], o["color"], o["opacity"], o["bg"], size, size,
+                                  theta=o["theta"], odds=True)
+        o2, rec = enc.forward_and_render(x)
+    torch.cuda.synchronize()
+    # the encoder outputs agree to the last bits the GroupNorm statistics' double-precision atomics leave
+    for k in ("mu", "log_scale", "color", "opacity", "theta", "bg"):
+        assert float((o[k] - o2[k]).abs().max()) < 1e-6, k
+    assert float((rec - ref).abs().max()) < 2e-5
+
+
+def test_encode_render_stream_matches_single(lib):
+    """The streaming pipeline (copies overlapped with the kernels of neighbouring images) returns, for
+    every image of a stream, exactly what the single-image pipeline returns."""
+    from gaussian_2d_splat_encoder_b200 import pipeline, synth
+    from gaussian_2d_splat_encoder_b200.efficient_encoder import EfficientGaussianEncoder
+
+    torch.manual_seed(0)
+    enc = EfficientGaussianEncoder(**GOLDEN_CFG).cuda().eval()
+    imgs = [synth.synth_card(256, 256, 60, 20, s).contiguous().pin_memory() for s in range(5)]
+    single = pipeline.EncodeRender(enc, 1, 256, 256)
+    refs = []
+    for x in imgs:
+        refs.append(single(x).cpu())
+    st = pipeline.EncodeRenderStream(enc, 256, 256).capture()
+    outs = [torch.empty(1, 3, 256, 256).pin_memory() for _ in imgs]
+    st.start_after()
+    for x, o in zip(imgs, outs):
+        st.submit(x, o)
+    st.synchronize()
+    for o, r in zip(outs, refs):
+        assert float((o - r).abs().max()) < 1e-6
+
+
 def test_render_fit_step_graph_matches_eager(lib):
     from gaussian_2d_splat_encoder_b200 import pipeline, synth
     from gaussian_2d_splat_encoder_b200.render_triton import render_alpha_octave
