@@ -677,7 +677,7 @@ def main():
                             "traffic": None, "units_per_launch": pp, "ops_per_unit": 40, "pairs": pairs,
                             "peak_source": f"148 SMs x 128 FP32 lanes x {f_mhz:.0f} MHz (median SM clock sampled "
                                            "during the timed region)"}
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the host baseline is an N = 1 figure
         line["cpu_baseline"] = cpu_baseline(wcls, 3)
     if rank == 0:
         print(json.dumps(line), flush=True)

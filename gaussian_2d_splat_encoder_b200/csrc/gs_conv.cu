@@ -64,15 +64,18 @@ __device__ __forceinline__ float gelu_erf(float x) {
 //   warp 0        TMA producer (one lane): A tiles of the MT M-tiles + the B slice, STAGES-deep ring
 //   warp 1        TMEM owner + MMA issuer (one lane): MT accumulators of 128 x BN fp32 per item,
 //                 double-buffered in TMEM so the epilogue of item i overlaps the K loop of item i+1
-//   warps 2..     4*MT epilogue warps: warp w drains TMEM lanes 32*(w%4).. of accumulator (w-2)/4 --
+//   warps 2..     4*MT*CS epilogue warps: warp w drains TMEM lanes 32*(w%4).. of one accumulator, one of
+//                 CS column slices --
 //                 bias, GELU (gelu_erf), GroupNorm(8) partial sums, bf16 NHWC store
 // Every wait is bounded; a wait that gives up records its stage in *err and raises a CTA-wide abort
 // flag so the other roles stop issuing, then the CTA drains its copies and MMAs and frees TMEM.
-template <int BN, int KC, int STAGES, int MT, int CPG, int MINB>
-__global__ void __launch_bounds__(64 + 128 * MT, MINB)
+template <int BN, int KC, int STAGES, int MT, int CPG, int MINB, int CS>
+__global__ void __launch_bounds__(64 + 128 * MT * CS, MINB)
     k_conv_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
               const __grid_constant__ CUtensorMap tmB, ConvArgs a) {
-    constexpr int NEPI = 4 * MT;
+    constexpr int NEPI = 4 * MT * CS;  // epilogue warps: 4 lane quarters x MT accumulators x CS column slices
+    constexpr int BNS = BN / CS;        // columns drained by one epilogue warp
+    static_assert(BNS % 16 == 0 && BNS % CPG == 0, "column slices hold whole chunks and GroupNorm groups");
     constexpr uint32_t A_BYTES = 128u * KC * 2u;
     constexpr uint32_t B_BYTES = (uint32_t)BN * KC * 2u;
     constexpr uint32_t STAGE = MT * A_BYTES + B_BYTES;
@@ -155,9 +158,9 @@ __global__ void __launch_bounds__(64 + 128 * MT, MINB)
                     for (int mt = 0; mt < MT; mt++) {
                         const int ym = y0 + mt * a.TY;
                         if (a.stride == 1) {
-                            tma_load_4d(sa + mt * A_BYTES, ma, &full[s], c0, x0 + kw - a.pad, ym + kh - a.pad, b);
+                            tma_load_4d(sa + mt * A_BYTES, ma, &full[s], c0, x0 + kw - a.padw, ym + kh - a.pad, b);
                         } else {
-                            const int xin = 2 * x0 + kw - a.pad;
+                            const int xin = 2 * x0 + kw - a.padw;
                             const int xp = xin & 1;
                             const int xh = (xin - xp) / 2;
                             for (int r = 0; r < a.TY; r++)
@@ -219,7 +222,8 @@ __global__ void __launch_bounds__(64 + 128 * MT, MINB)
         // epilogue
         const int e = warp - 2;
         const int q = warp & 3;  // TMEM lane quarter this warp may access
-        const int mt = e >> 2;
+        const int mt = (e >> 2) % MT, cs = (e >> 2) / MT;
+        const int clo = cs * BNS, chi = clo + BNS;
         const int m = q * 32 + lane;
         float *acc = sacc[e];
         int cur_b = -1, tc = 0;
@@ -249,10 +253,10 @@ __global__ void __launch_bounds__(64 + 128 * MT, MINB)
             const uint32_t taddr = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)buf * ACC + (uint32_t)(mt * BN);
             float rs = 0.f, rq = 0.f;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
+            for (int c0 = clo; c0 < chi; c0 += 16) {
                 float v[16];
                 tmem_ld16(taddr + (uint32_t)c0, v);
-                if (c0 + 16 == BN) {
+                if (c0 + 16 == chi) {
                     // the accumulator buffer is drained: hand it back to the MMA warp
                     tc_fence_before();
                     __syncwarp();
@@ -383,11 +387,11 @@ int sm_count() {
     return n[dev];
 }
 
-template <int BN, int KC, int STAGES, int MT, int CPG, int MINB>
+template <int BN, int KC, int STAGES, int MT, int CPG, int MINB, int CS>
 int launch(const CUtensorMap &tA, const CUtensorMap &tA2, const CUtensorMap &tB, const ConvArgs &a,
            cudaStream_t st) {
     constexpr size_t SMEM = (size_t)STAGES * (MT * 128 * KC * 2 + BN * KC * 2) + 1024;
-    auto kern = k_conv_tc<BN, KC, STAGES, MT, CPG, MINB>;
+    auto kern = k_conv_tc<BN, KC, STAGES, MT, CPG, MINB, CS>;
     static bool configured = false;
     if (!configured) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
@@ -396,7 +400,7 @@ int launch(const CUtensorMap &tA, const CUtensorMap &tA2, const CUtensorMap &tB,
     const long long items = (long long)a.B * a.tiles_y * a.tiles_x * (a.Co / BN);
     const long long slots = (long long)sm_count() * MINB;
     const int grid = (int)(items < slots ? items : slots);
-    kern<<<grid, 64 + 128 * MT, SMEM, st>>>(tA, tA2, tB, a);
+    kern<<<grid, 64 + 128 * MT * CS, SMEM, st>>>(tA, tA2, tB, a);
     return cudaGetLastError() == cudaSuccess ? GS_OK : GS_ERR_CUDA;
 }
 
@@ -426,7 +430,7 @@ int gs_conv_run(const gs_conv_desc *d, const void *in, const void *w, const floa
 }
 
 int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in2, const void *w, const float *bias,
-                 void *out, double *stats, int *err, cudaStream_t st) {
+                 void *out, double *stats, int *err, cudaStream_t st, int padw) {
     if (!d || !in || !w || !bias || !out) return GS_ERR_BAD_ARGUMENT;
     const int B = d->B, Hi = d->H, Wi = d->W, Ci = d->Cin, Co = d->Cout;
     const int Ci2 = Ci - Cin1;
@@ -443,9 +447,9 @@ int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in
     const int BN = Co == 256 ? 128 : Co;
     ConvArgs a;
     a.B = B; a.Hi = Hi; a.Wi = Wi; a.Ci = Ci; a.Co = Co;
-    a.KH = d->kh; a.KW = d->kw; a.stride = d->stride; a.pad = d->pad;
+    a.KH = d->kh; a.KW = d->kw; a.stride = d->stride; a.pad = d->pad; a.padw = padw >= 0 ? padw : d->pad;
     a.Ho = d->Ho > 0 ? d->Ho : (Hi + 2 * d->pad - d->kh) / d->stride + 1;
-    a.Wo = d->Wo > 0 ? d->Wo : (Wi + 2 * d->pad - d->kw) / d->stride + 1;
+    a.Wo = d->Wo > 0 ? d->Wo : (Wi + 2 * a.padw - d->kw) / d->stride + 1;
     if (a.Ho <= 0 || a.Wo <= 0) return GS_ERR_BAD_ARGUMENT;
     gs_conv_pick_tile(a.Ho, a.Wo, MT, &a.TX, &a.TY);
     a.tiles_x = (a.Wo + a.TX - 1) / a.TX;
@@ -489,10 +493,11 @@ int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in
         s = make_map(&tB, w, 2, dims, str, box, swz);
     }
     if (s != GS_OK) return s;
-    if (KC == 16) return launch<64, 16, 8, 2, 8, 2>(tA, tA2, tB, a, st);
-    if (Co == 64) return launch<64, 64, 5, 2, 8, 1>(tA, tA2, tB, a, st);
-    if (Co == 128) return launch<128, 64, 4, 2, 16, 1>(tA, tA2, tB, a, st);
-    return launch<128, 64, 6, 1, 32, 1>(tA, tA2, tB, a, st);
+    // one column slice per accumulator: doubling the epilogue warps (CS = 2) measured slower on B200
+    if (KC == 16) return launch<64, 16, 8, 2, 8, 2, 1>(tA, tA2, tB, a, st);
+    if (Co == 64) return launch<64, 64, 5, 2, 8, 1, 1>(tA, tA2, tB, a, st);
+    if (Co == 128) return launch<128, 64, 4, 2, 16, 1, 1>(tA, tA2, tB, a, st);
+    return launch<128, 64, 6, 1, 32, 1, 1>(tA, tA2, tB, a, st);
 }
 
 extern "C" int gs_conv2d(const gs_conv_desc *d, const void *in_bf16, const void *w_bf16, const float *bias,

@@ -7,7 +7,8 @@
 
 struct ConvArgs {
     int B, Hi, Wi, Ci, Co;
-    int KH, KW, stride, pad;
+    int KH, KW, stride, pad;  // pad: rows (and columns unless padw says otherwise)
+    int padw;                 // column padding
     int Ho, Wo;
     int TX, TY, tiles_x, tiles_y;
     int nchunks, nkb;
@@ -24,5 +25,6 @@ int gs_conv_run(const gs_conv_desc *d, const void *in, const void *w, const floa
                 int *err, cudaStream_t st);
 // The same convolution over the channel concatenation [in (Cin1 channels), in2 (d->Cin - Cin1 channels)],
 // both NHWC with the same B, H, W; neither is copied.
+// padw >= 0 overrides the column padding (d->pad stays the row padding).
 int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in2, const void *w, const float *bias,
-                 void *out, double *stats, int *err, cudaStream_t st);
+                 void *out, double *stats, int *err, cudaStream_t st, int padw = -1);

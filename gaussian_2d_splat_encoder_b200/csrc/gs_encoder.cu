@@ -141,14 +141,30 @@ __global__ void __launch_bounds__(256) k_pool48(const float *__restrict__ grad, 
     if (a == 0) out8[i] = s8 / 64.0f;
 }
 
+// GroupNorm(8) of channel c of image b as y * sc + sh, from the (sum, sum of squares) statistics
+__device__ __forceinline__ void gn_affine(const double *__restrict__ stats, const float *__restrict__ gamma,
+                                          const float *__restrict__ beta, int b, int c, int C, long long HW,
+                                          float &sc, float &sh) {
+    const int g = c / (C / 8);
+    const double n = (double)HW * (C / 8);
+    const double mean = stats[(b * 8 + g) * 2] / n;
+    double var = stats[(b * 8 + g) * 2 + 1] / n - mean * mean;
+    if (var < 0) var = 0;
+    const float rstd = (float)(1.0 / sqrt(var + 1e-5));
+    sc = gamma[c] * rstd;
+    sh = beta[c] - (float)mean * gamma[c] * rstd;
+}
+
 // GroupNorm(8) apply in place on NHWC bf16 [B][HW][C]; chsum (optional) receives this block's per-channel
 // sums of the normalised values, chsum[b][blockIdx.x][C] (k_bg reduces them in a fixed order, so the
 // background colour is reproducible bit for bit).  Each thread handles 8-channel vectors of one fixed
 // channel octet (the grid stride in channels, gridDim.x * 256 * 8, is a multiple of C), so its
 // scale/shift and its channel sums stay in registers.
+// With apply = 0 the tensor is only read and chsum receives the sums of the raw values.
 __global__ void __launch_bounds__(256) k_gn_apply(__nv_bfloat16 *__restrict__ x, int HW, int C,
                                                   const double *__restrict__ stats, const float *__restrict__ gamma,
-                                                  const float *__restrict__ beta, float *__restrict__ chsum) {
+                                                  const float *__restrict__ beta, float *__restrict__ chsum,
+                                                  int apply) {
     __shared__ float red[256][9];
     const int b = blockIdx.y;
     const int nvec = HW * (C / 8);
@@ -169,25 +185,27 @@ __global__ void __launch_bounds__(256) k_gn_apply(__nv_bfloat16 *__restrict__ x,
         cs[k] = 0.f;
     }
     uint4 *xb = reinterpret_cast<uint4 *>(x + (long long)b * HW * C);
-    auto apply = [&](uint4 &u) {
+    auto norm = [&](uint4 &u) {
         __nv_bfloat16 *e = reinterpret_cast<__nv_bfloat16 *>(&u);
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            e[k] = __float2bfloat16_rn(fmaf(__bfloat162float(e[k]), sc[k], sh[k]));
+            if (apply) e[k] = __float2bfloat16_rn(fmaf(__bfloat162float(e[k]), sc[k], sh[k]));
             cs[k] += __bfloat162float(e[k]);
         }
     };
     for (; v + stride < nvec; v += 2 * stride) {
         uint4 u0 = xb[v], u1 = xb[v + stride];
-        apply(u0);
-        apply(u1);
-        xb[v] = u0;
-        xb[v + stride] = u1;
+        norm(u0);
+        norm(u1);
+        if (apply) {
+            xb[v] = u0;
+            xb[v + stride] = u1;
+        }
     }
     if (v < nvec) {
         uint4 u0 = xb[v];
-        apply(u0);
-        xb[v] = u0;
+        norm(u0);
+        if (apply) xb[v] = u0;
     }
     if (chsum) {
         // threads t, t + C/8, t + 2C/8, ... share a channel octet: sum their registers in thread order
@@ -207,6 +225,8 @@ __global__ void __launch_bounds__(256) k_gn_apply(__nv_bfloat16 *__restrict__ x,
 // c sums channel c's nblk block partials in order, then the three dot products reduce over the block
 __global__ void __launch_bounds__(256) k_bg(const float *__restrict__ chsum, int nblk, int C, long long HW,
                                             const float *__restrict__ w, const float *__restrict__ bias,
+                                            const double *__restrict__ gn_stats, const float *__restrict__ gn_gamma,
+                                            const float *__restrict__ gn_beta, float2 *__restrict__ gn_table,
                                             float *__restrict__ bg) {
     __shared__ float red[3][8];
     const int b = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
@@ -214,7 +234,13 @@ __global__ void __launch_bounds__(256) k_bg(const float *__restrict__ chsum, int
     if (c < C) {
         float t = 0.f;
         for (int k = 0; k < nblk; k++) t += chsum[((long long)b * nblk + k) * C + c];
-        const float m = t / (float)HW;
+        float m = t / (float)HW;
+        if (gn_stats) {  // the sums are of the raw values: mean of the normalised = scale * mean + shift
+            float sc, sh;
+            gn_affine(gn_stats, gn_gamma, gn_beta, b, c, C, HW, sc, sh);
+            m = fmaf(m, sc, sh);
+            gn_table[b * C + c] = make_float2(sc, sh);  // for the other consumers of the raw tensor
+        }
         s0 = w[c] * m;
         s1 = w[C + c] * m;
         s2 = w[2 * C + c] * m;
@@ -260,16 +286,17 @@ struct HeadArgs {
 };
 
 // 1x1 convolution of the head + activations (efficient_encoder.py:170-197).  A block takes HEAD_CELLS
-// feature cells (lane = cell) and HEAD_PARTS warps, each warp accumulating its slice of the feature
-// channels; partial sums meet in shared memory and warp m (m < M) adds the extra channels (pooled
-// gradient, bilinear cond) and applies the activations of splat slot m.  Weights sit transposed in shared memory, [Cin][20] (18
+// feature cells (lane = cell) and PARTS warps, each warp accumulating its slice of the feature channels;
+// with PARTS > 1 the partial sums meet in shared memory; then warp w < min(PARTS, M) adds the extra
+// channels (pooled gradient, bilinear cond) and applies the activations of the splat slots m with
+// m % min(PARTS, M) == w.  PARTS = 1 (one warp per 32 cells, all channels) suits many cells; a channel
+// split (PARTS = 4) gives small grids enough warps.  Weights sit transposed in shared memory, [Cin][20] (18
 // outputs padded to 20), so one input channel is 5 broadcast 16-byte loads for 18 FMAs.
 #define HEAD_NP 20
 #define HEAD_CELLS 32
-#define HEAD_PARTS 8
-template <int M>
-__global__ void __launch_bounds__(32 * HEAD_PARTS) k_head(HeadArgs a) {
-    // wT [Cin][20], bias [20], gn scale/shift [2][Cfeat], partial sums [HEAD_PARTS][HEAD_CELLS][20]
+template <int M, int PARTS>
+__global__ void __launch_bounds__(32 * PARTS) k_head(HeadArgs a) {
+    // wT [Cin][20], bias [20], gn scale/shift [2][Cfeat], partial sums [PARTS][HEAD_CELLS][20] (PARTS > 1)
     extern __shared__ __align__(16) float shw[];
     float *wT = shw, *sb = shw + a.Cin * HEAD_NP, *gsc = sb + HEAD_NP, *gsh = gsc + a.Cfeat;
     float *red = gsh + a.Cfeat;
@@ -277,29 +304,15 @@ __global__ void __launch_bounds__(32 * HEAD_PARTS) k_head(HeadArgs a) {
     const long long cell0 = (long long)blockIdx.x * HEAD_CELLS;
     const long long ncell = (long long)a.B * a.fH * a.fW;
     const int b0 = (int)(cell0 / ((long long)a.fH * a.fW));
-    {
-        // coalesced read of w [nout][Cin], 8 independent loads in flight per thread
-        const int n = a.nout * a.Cin;
-        for (int i0 = threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {
-            float v[8];
+    // w [nout][Cin] -> wT [Cin][20]: row k, channels strided over the block (coalesced, no divisions),
+    // four rows' loads in flight per thread; outputs nout..19 are zero
+    for (int k0 = 0; k0 < HEAD_NP; k0 += 4) {
+        for (int c = threadIdx.x; c < a.Cin; c += blockDim.x) {
+            float v[4];
 #pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const int i = i0 + u * blockDim.x;
-                v[u] = i < n ? __ldg(a.w + i) : 0.f;
-            }
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const int i = i0 + u * blockDim.x;
-                if (i < n) {
-                    const int k = i / a.Cin, c = i - k * a.Cin;
-                    wT[c * HEAD_NP + k] = v[u];
-                }
-            }
+            for (int u = 0; u < 4; u++) v[u] = k0 + u < a.nout ? __ldg(a.w + (k0 + u) * a.Cin + c) : 0.f;
+            *reinterpret_cast<float4 *>(wT + c * HEAD_NP + k0) = make_float4(v[0], v[1], v[2], v[3]);
         }
-    }
-    for (int i = threadIdx.x; i < a.Cin * (HEAD_NP - a.nout); i += blockDim.x) {
-        const int c = i / (HEAD_NP - a.nout), k = a.nout + i % (HEAD_NP - a.nout);
-        wT[c * HEAD_NP + k] = 0.f;
     }
     for (int i = threadIdx.x; i < HEAD_NP; i += blockDim.x) sb[i] = i < a.nout ? a.b[i] : 0.f;
     // GroupNorm scale/shift of the block's image (blocks never straddle images: the caller requires
@@ -333,7 +346,7 @@ __global__ void __launch_bounds__(32 * HEAD_PARTS) k_head(HeadArgs a) {
             acc[4 * q + 3] = fmaf(w4.w, v, acc[4 * q + 3]);
         }
     };
-    const int per = ((a.Cfeat / 8 + HEAD_PARTS - 1) / HEAD_PARTS) * 8;
+    const int per = ((a.Cfeat / 8 + PARTS - 1) / PARTS) * 8;
     const int c_lo = warp * per, c_hi = min(a.Cfeat, c_lo + per);
     if (live) {
         // the warp's slice, up to 4 vectors of 8 channels at a time, loaded before any arithmetic
@@ -357,27 +370,32 @@ __global__ void __launch_bounds__(32 * HEAD_PARTS) k_head(HeadArgs a) {
             }
         }
     }
-    {
-        float4 *rp = reinterpret_cast<float4 *>(red + (warp * HEAD_CELLS + lane) * HEAD_NP);
+    constexpr int NFIN = PARTS < M ? PARTS : M;  // warps that finish the cells
+    if (PARTS > 1) {
+        {
+            float4 *rp = reinterpret_cast<float4 *>(red + (warp * HEAD_CELLS + lane) * HEAD_NP);
 #pragma unroll
-        for (int q = 0; q < HEAD_NP / 4; q++) rp[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
-    }
-    __syncthreads();
-    // warp m < M finishes splat slot m of the 32 cells (partials summed in a fixed order)
-    if (warp >= M || !live) return;
-#pragma unroll
-    for (int k = 0; k < HEAD_NP; k++) acc[k] = 0.f;
-#pragma unroll
-    for (int p = 0; p < HEAD_PARTS; p++) {
-        const float4 *rp = reinterpret_cast<const float4 *>(red + (p * HEAD_CELLS + lane) * HEAD_NP);
-#pragma unroll
-        for (int q = 0; q < HEAD_NP / 4; q++) {
-            const float4 t = rp[q];
-            acc[4 * q] += t.x;
-            acc[4 * q + 1] += t.y;
-            acc[4 * q + 2] += t.z;
-            acc[4 * q + 3] += t.w;
+            for (int q = 0; q < HEAD_NP / 4; q++)
+                rp[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
         }
+        __syncthreads();
+        if (warp >= NFIN || !live) return;
+#pragma unroll
+        for (int k = 0; k < HEAD_NP; k++) acc[k] = 0.f;
+#pragma unroll
+        for (int p = 0; p < PARTS; p++) {  // partials summed in a fixed order
+            const float4 *rp = reinterpret_cast<const float4 *>(red + (p * HEAD_CELLS + lane) * HEAD_NP);
+#pragma unroll
+            for (int q = 0; q < HEAD_NP / 4; q++) {
+                const float4 t = rp[q];
+                acc[4 * q] += t.x;
+                acc[4 * q + 1] += t.y;
+                acc[4 * q + 2] += t.z;
+                acc[4 * q + 3] += t.w;
+            }
+        }
+    } else if (!live) {
+        return;
     }
 #pragma unroll
     for (int k = 0; k < HEAD_NP; k++) acc[k] += sb[k];
@@ -405,7 +423,7 @@ __global__ void __launch_bounds__(32 * HEAD_PARTS) k_head(HeadArgs a) {
     const float by = lin_center(y, a.fH), bx = lin_center(x, a.fW);
 #pragma unroll
     for (int m = 0; m < M; m++) {
-        if (m != warp) continue;
+        if (m % NFIN != warp) continue;
         const long long nl = (long long)r * M + m;  // splat index inside the group (cell-major, then slot)
         const long long n = (long long)b * a.Ntot + a.n0 + nl;
         float muy = by + tanhf(acc[m * 2 + 0]) * a.off_scale;
@@ -468,7 +486,8 @@ __global__ void k_cond(const float *__restrict__ image, int B, int H, int W, con
 // efficient_encoder.py:89-91; the decoder convolution reads [up, s4] as two inputs, so the
 // concatenation is never materialised).  grid = (row blocks, H4, B); one thread per 8-channel vector.
 __global__ void __launch_bounds__(256) k_upsample(const __nv_bfloat16 *__restrict__ s8, int H8, int W8, int Cu,
-                                                  int H4, int W4, __nv_bfloat16 *__restrict__ up) {
+                                                  int H4, int W4, const float2 *__restrict__ gn_table,
+                                                  __nv_bfloat16 *__restrict__ up) {
     const int nv = Cu / 8;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= W4 * nv) return;
@@ -487,33 +506,67 @@ __global__ void __launch_bounds__(256) k_upsample(const __nv_bfloat16 *__restric
     const __nv_bfloat16 *p01 = reinterpret_cast<const __nv_bfloat16 *>(&a01);
     const __nv_bfloat16 *p10 = reinterpret_cast<const __nv_bfloat16 *>(&a10);
     const __nv_bfloat16 *p11 = reinterpret_cast<const __nv_bfloat16 *>(&a11);
+    // s8 may be the raw convolution output: GroupNorm is a per-channel affine map, so it is applied after
+    // the interpolation (the bilinear weights sum to one)
+    float sc[8], sh[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        sc[k] = 1.f;
+        sh[k] = 0.f;
+    }
+    if (gn_table) {
+        const float4 *t = reinterpret_cast<const float4 *>(gn_table + (long long)b * Cu + c0);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float4 v = t[k];
+            sc[2 * k] = v.x;
+            sh[2 * k] = v.y;
+            sc[2 * k + 1] = v.z;
+            sh[2 * k + 1] = v.w;
+        }
+    }
     uint4 res;
     __nv_bfloat16 *e = reinterpret_cast<__nv_bfloat16 *>(&res);
 #pragma unroll
     for (int k = 0; k < 8; k++) {
         float f = h0 * (w0 * __bfloat162float(p00[k]) + w1 * __bfloat162float(p01[k])) +
                   h1 * (w0 * __bfloat162float(p10[k]) + w1 * __bfloat162float(p11[k]));
-        e[k] = __float2bfloat16_rn(f);
+        e[k] = __float2bfloat16_rn(fmaf(f, sc[k], sh[k]));
     }
     *reinterpret_cast<uint4 *>(up + (((long long)b * H4 + y) * W4 + x) * Cu + c0) = res;
 }
 
-// GroupNorm(8) applied to NHWC bf16 [B][HW][C] written as NHWC fp32 (the fine decoder's normalised
-// features: splat_features of forward(return_latents=True))
-__global__ void k_gn_to_f32(const __nv_bfloat16 *__restrict__ x, int B, long long HW, int C,
-                            const double *__restrict__ stats, const float *__restrict__ gamma,
-                            const float *__restrict__ beta, float *__restrict__ out) {
-    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long long)B * HW * C) return;
-    int c = (int)(i % C);
-    int b = (int)(i / (HW * C));
-    int g = c / (C / 8);
-    const double n = (double)HW * (C / 8);
-    double mean = stats[(b * 8 + g) * 2] / n;
-    double var = stats[(b * 8 + g) * 2 + 1] / n - mean * mean;
-    if (var < 0) var = 0;
-    float rstd = (float)(1.0 / sqrt(var + 1e-5));
-    out[i] = (__bfloat162float(x[i]) - (float)mean) * rstd * gamma[c] + beta[c];
+// per-channel GroupNorm(8) scale and shift, table[b][c] = (sc, sh) with normalised = raw * sc + sh
+__global__ void __launch_bounds__(256) k_gn_table(const double *__restrict__ stats, const float *__restrict__ gamma,
+                                                  const float *__restrict__ beta, int C, long long HW,
+                                                  float2 *__restrict__ table) {
+    const int b = blockIdx.x;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float sc, sh;
+        gn_affine(stats, gamma, beta, b, c, C, HW, sc, sh);
+        table[b * C + c] = make_float2(sc, sh);
+    }
+}
+
+// GroupNorm(8) applied to NHWC bf16 [B][HW][C] written as NHWC fp32, 8 channels per thread, from a
+// scale/shift table (the fine decoder's normalised features for return_latents; the backbone features
+// when s8 stays raw)
+__global__ void __launch_bounds__(256) k_gn_to_f32(const __nv_bfloat16 *__restrict__ x, int B, long long HW, int C,
+                                                   const float2 *__restrict__ table, float *__restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // vector of 8 channels
+    if (i * 8 >= (long long)B * HW * C) return;
+    const int nv = C / 8;
+    const int c0 = (int)(i % nv) * 8;
+    const int b = (int)(i / (HW * nv));
+    const float4 *t = reinterpret_cast<const float4 *>(table + (long long)b * C + c0);
+    const float4 t0 = t[0], t1 = t[1], t2 = t[2], t3 = t[3];
+    const uint4 u = reinterpret_cast<const uint4 *>(x)[i];
+    const __nv_bfloat16 *e = reinterpret_cast<const __nv_bfloat16 *>(&u);
+    float4 *o = reinterpret_cast<float4 *>(out) + 2 * i;
+    o[0] = make_float4(fmaf(__bfloat162float(e[0]), t0.x, t0.y), fmaf(__bfloat162float(e[1]), t0.z, t0.w),
+                       fmaf(__bfloat162float(e[2]), t1.x, t1.y), fmaf(__bfloat162float(e[3]), t1.z, t1.w));
+    o[1] = make_float4(fmaf(__bfloat162float(e[4]), t2.x, t2.y), fmaf(__bfloat162float(e[5]), t2.z, t2.w),
+                       fmaf(__bfloat162float(e[6]), t3.x, t3.y), fmaf(__bfloat162float(e[7]), t3.z, t3.w));
 }
 
 // NHWC bf16 -> NHWC fp32 (backbone_features output), 8 elements per thread (n a multiple of 8)
@@ -527,19 +580,31 @@ __global__ void k_bf16_to_f32(const __nv_bfloat16 *__restrict__ in, float *__res
     o[1] = make_float4(__bfloat162float(e[4]), __bfloat162float(e[5]), __bfloat162float(e[6]), __bfloat162float(e[7]));
 }
 
-void launch_head(const HeadArgs &h, long long ncell, size_t smem, cudaStream_t s) {
+// channel split for the head: 4 warps per 32 cells for grids under ~16k cells, else one warp
+int head_parts(long long ncell) { return ncell < 16384 ? 4 : 1; }
+
+size_t head_smem(const HeadArgs &h, long long ncell) {
+    const int parts = head_parts(ncell);
+    return ((size_t)h.Cin * HEAD_NP + HEAD_NP + 2 * h.Cfeat + (parts > 1 ? parts * HEAD_CELLS * HEAD_NP : 0)) * 4;
+}
+
+void launch_head(const HeadArgs &h, long long ncell, cudaStream_t s) {
     const unsigned grid = (unsigned)((ncell + HEAD_CELLS - 1) / HEAD_CELLS);
-    if (h.M == 1)
-        k_head<1><<<grid, 32 * HEAD_PARTS, smem, s>>>(h);
-    else
-        k_head<2><<<grid, 32 * HEAD_PARTS, smem, s>>>(h);
+    const size_t smem = head_smem(h, ncell);
+    if (head_parts(ncell) == 4) {
+        if (h.M == 1) k_head<1, 4><<<grid, 128, smem, s>>>(h);
+        else k_head<2, 4><<<grid, 128, smem, s>>>(h);
+    } else {
+        if (h.M == 1) k_head<1, 1><<<grid, 32, smem, s>>>(h);
+        else k_head<2, 1><<<grid, 32, smem, s>>>(h);
+    }
 }
 
 size_t al(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct EncPlan {
     int B, H, W, H2, W2, H4, W4, H8, W8, d, Nc, Nf, N, rg;
-    size_t o_Z, o_y1, o_y2, o_y3, o_cat, o_y4, o_grad, o_g4, o_g8, o_stats, o_chsum, o_err, o_c[5], o_render,
+    size_t o_Z, o_y1, o_y2, o_y3, o_cat, o_y4, o_grad, o_g4, o_g8, o_stats, o_chsum, o_gtab, o_err, o_c[5], o_render,
         o_cond, o_rws, total;
     gs_render_desc rd;
     size_t rws;
@@ -571,6 +636,7 @@ int enc_plan(const gs_encoder_desc *e, EncPlan &p) {
     p.o_g8 = take(B * p.H8 * p.W8 * 4);
     p.o_stats = take(4 * B * 16 * sizeof(double));
     p.o_chsum = take(B * GN_BG_BLOCKS * 256 * 4);  // per-block channel sums of the normalised s8
+    p.o_gtab = take(B * (256 + 128) * 8);            // GroupNorm scale/shift tables: s8, decoder output
     p.o_err = take(64);
     const size_t nc = B * p.Nc;
     p.o_c[0] = take(nc * 2 * 4);
@@ -630,11 +696,12 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
                                                              W<float>(ws, p.o_g8));
     }
     // 2. backbone: conv -> GELU -> GroupNorm, three stages
-    auto gn = [&](void *x, long long HW, int C, double *stt, const float *gamma, const float *beta, float *chsum) {
+    auto gn = [&](void *x, long long HW, int C, const double *stt, const float *gamma, const float *beta, float *chsum,
+                  int apply) {
         // with channel sums every block ends in C global atomics: keep the grid small for that launch
         // with channel sums the grid is fixed (GN_BG_BLOCKS per image): k_bg reduces exactly that many partials
         dim3 grid((unsigned)(chsum ? GN_BG_BLOCKS : std::min<long long>(1024, (HW * C / 8 + 255) / 256)), (unsigned)B);
-        k_gn_apply<<<grid, 256, 0, s>>>((__nv_bfloat16 *)x, (int)HW, C, stt, gamma, beta, chsum);
+        k_gn_apply<<<grid, 256, 0, s>>>((__nv_bfloat16 *)x, (int)HW, C, stt, gamma, beta, chsum, apply);
     };
     gs_conv_desc cd;
     memset(&cd, 0, sizeof(cd));
@@ -644,7 +711,7 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
         ProfScope ps(PR_CONV1, s);
         if ((st = gs_conv_run(&cd, W<void>(ws, p.o_Z), w->w1, w->b1, W<void>(ws, p.o_y1), stats, err, s))) return st;
     }
-    gn(W<void>(ws, p.o_y1), (long long)p.H2 * p.W2, 64, stats, w->gn1_w, w->gn1_b, nullptr);
+    gn(W<void>(ws, p.o_y1), (long long)p.H2 * p.W2, 64, stats, w->gn1_w, w->gn1_b, nullptr, 1);
     memset(&cd, 0, sizeof(cd));
     cd.B = B; cd.H = p.H2; cd.W = p.W2; cd.Cin = 64; cd.Cout = 128; cd.kh = 3; cd.kw = 3; cd.stride = 2; cd.pad = 1;
     cd.gelu = 1;
@@ -653,7 +720,7 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
         if ((st = gs_conv_run(&cd, W<void>(ws, p.o_y1), w->w2, w->b2, W<void>(ws, p.o_y2), stats + B * 16, err, s)))
             return st;
     }
-    gn(W<void>(ws, p.o_y2), (long long)p.H4 * p.W4, 128, stats + B * 16, w->gn2_w, w->gn2_b, nullptr);
+    gn(W<void>(ws, p.o_y2), (long long)p.H4 * p.W4, 128, stats + B * 16, w->gn2_w, w->gn2_b, nullptr, 1);
     memset(&cd, 0, sizeof(cd));
     cd.B = B; cd.H = p.H4; cd.W = p.W4; cd.Cin = 128; cd.Cout = 256; cd.kh = 3; cd.kw = 3; cd.stride = 2; cd.pad = 1;
     cd.gelu = 1;
@@ -664,12 +731,21 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
             return st;
     }
     float *chsum = W<float>(ws, p.o_chsum);
-    gn(W<void>(ws, p.o_y3), (long long)p.H8 * p.W8, 256, stats + 2 * B * 16, w->gn3_w, w->gn3_b, chsum);
-    k_bg<<<B, 256, 0, s>>>(chsum, GN_BG_BLOCKS, 256, (long long)p.H8 * p.W8, w->bg_w, w->bg_b, bg);
+    // GroupNorm of s8: applied on the fly by its consumers (upsample, coarse head, features, background
+    // head) when the coarse head's 32-cell blocks cannot straddle images; else in place as for s2, s4
+    const double *gn3 = stats + 2 * B * 16;
+    const bool gn3_fly = ((long long)p.H8 * p.W8) % HEAD_CELLS == 0;
+    gn(W<void>(ws, p.o_y3), (long long)p.H8 * p.W8, 256, gn3, w->gn3_w, w->gn3_b, chsum, gn3_fly ? 0 : 1);
+    float2 *gtab = W<float2>(ws, p.o_gtab);
+    k_bg<<<B, 256, 0, s>>>(chsum, GN_BG_BLOCKS, 256, (long long)p.H8 * p.W8, w->bg_w, w->bg_b,
+                           gn3_fly ? gn3 : nullptr, w->gn3_w, w->gn3_b, gtab, bg);
     // 3. coarse head (writes the API tensors and a contiguous copy for the coarse render)
     HeadArgs h;
     memset(&h, 0, sizeof(h));
     h.B = B; h.fH = p.H8; h.fW = p.W8; h.M = e->M; h.Cfeat = 256; h.feat = W<__nv_bfloat16>(ws, p.o_y3);
+    if (gn3_fly) {
+        h.gn_stats = gn3; h.gn_gamma = w->gn3_w; h.gn_beta = w->gn3_b;
+    }
     h.gpool = W<float>(ws, p.o_g8); h.w = w->hc_w; h.b = w->hc_b; h.Cin = 257; h.nout = (e->use_rotation ? 9 : 8) * e->M;
     h.off_scale = e->coarse_offset / (float)std::max(p.H8, p.W8);
     h.ls_floor = e->coarse_ls_floor; h.min_op = e->coarse_min_opacity; h.use_rot = e->use_rotation;
@@ -679,8 +755,7 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     {
         ProfScope ps(PR_HEADS, s);
         long long ncell = (long long)B * p.H8 * p.W8;
-        size_t sm = ((size_t)h.Cin * HEAD_NP + HEAD_NP + 2 * h.Cfeat + HEAD_PARTS * HEAD_CELLS * HEAD_NP) * 4;
-        launch_head(h, ncell, sm, s);
+        launch_head(h, ncell, s);
     }
     // 4. coarse render at residual_grid^2 (odds) -> cond map
     {
@@ -698,7 +773,7 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
         ProfScope ps(PR_ENC_MISC, s);
         dim3 ug((unsigned)((p.W4 * (256 / 8) + 255) / 256), (unsigned)p.H4, (unsigned)B);
         k_upsample<<<ug, 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), p.H8, p.W8, 256, p.H4, p.W4,
-                                      W<__nv_bfloat16>(ws, p.o_cat));
+                                      gn3_fly ? gtab : nullptr, W<__nv_bfloat16>(ws, p.o_cat));
     }
     memset(&cd, 0, sizeof(cd));
     cd.B = B; cd.H = p.H4; cd.W = p.W4; cd.Cin = 384; cd.Cout = 128; cd.kh = 3; cd.kw = 3; cd.stride = 1; cd.pad = 1;
@@ -721,19 +796,23 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     {
         ProfScope ps(PR_HEADS, s);
         long long ncell = (long long)B * p.H4 * p.W4;
-        size_t sm = ((size_t)h.Cin * HEAD_NP + HEAD_NP + 2 * h.Cfeat + HEAD_PARTS * HEAD_CELLS * HEAD_NP) * 4;
-        launch_head(h, ncell, sm, s);
+        launch_head(h, ncell, s);
     }
     if (latents) {
         long long n = (long long)B * p.H4 * p.W4 * 128;
-        k_gn_to_f32<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y4), B,
-                                                                (long long)p.H4 * p.W4, 128, stats + 3 * B * 16,
-                                                                w->gn4_w, w->gn4_b, latents);
-        gs_count_launch(1);
+        float2 *gtab4 = W<float2>(ws, p.o_gtab) + B * 256;
+        k_gn_table<<<B, 128, 0, s>>>(stats + 3 * B * 16, w->gn4_w, w->gn4_b, 128, (long long)p.H4 * p.W4, gtab4);
+        k_gn_to_f32<<<(unsigned)((n / 8 + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y4), B,
+                                                                (long long)p.H4 * p.W4, 128, gtab4, latents);
+        gs_count_launch(2);
     }
     if (features) {
         long long n = (long long)B * p.H8 * p.W8 * 256;
-        k_bf16_to_f32<<<(unsigned)((n / 8 + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), features, n);
+        if (gn3_fly)
+            k_gn_to_f32<<<(unsigned)((n / 8 + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), B,
+                                                                        (long long)p.H8 * p.W8, 256, gtab, features);
+        else
+            k_bf16_to_f32<<<(unsigned)((n / 8 + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), features, n);
     }
     // memset, prep, pool, 4 convs, 3 GN applies, bg, 2 heads, cond, upsample, optional feature copy
     gs_count_launch(16 + (features ? 1 : 0));

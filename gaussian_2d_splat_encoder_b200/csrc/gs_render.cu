@@ -16,7 +16,8 @@
 //   k_composite    bilinear upsample of every present group to native resolution, sum, composite
 // Backward:
 //   k_composite_bwd  dS fields at native resolution, bg gradient
-//   k_adjoint        adjoint of the bilinear upsample -> dS fields of every coarse group
+//   k_adjoint_*      adjoint of the bilinear upsample -> dS fields of every coarse group (direct gather for
+//                    upsampling factors <= 4, separable row/column passes for deeper octaves)
 //   k_fields_bwd     one CTA per tile, one lane per (tile, splat) pair looping over the tile's
 //                    pixels; 9 per-splat sums leave through 3 vector atomics per pair
 //   k_finalize       per-splat chain rule (rotation, scale, softplus) into the leaf gradients
@@ -636,16 +637,18 @@ __global__ void __launch_bounds__(NW * 32) k_fields_fwd(RenderGeom G, const Spla
             body([](float a, float) { return a * fmaf(a, fmaf(a, fmaf(a, 1.0f, 1.0f), 1.0f), 1.0f); });
         else body([](float a, float om) { return a * gs_rcp(om); });
     };
-    // records of the next batch are fetched into registers while the current one is composited
+    // warp w takes the w-th quarter of the tile's list (even split: short lists keep all warps busy), in
+    // batches of 32 records; the next batch is fetched into registers while the current one is composited
+    const int s_lo = (int)(((long long)n * warp) / NW), s_hi = (int)(((long long)n * (warp + 1)) / NW);
     SplatRec nxt;
-    int kb = warp * 32 + lane;
-    if (kb < n) nxt = rec[dense ? b * G.N + kb : vals[p0 + kb]];
-    for (int base = warp * 32; base < n; base += NW * 32) {
-        if (base + lane < n) srec[warp][lane] = nxt;
+    int kb = s_lo + lane;
+    if (kb < s_hi) nxt = rec[dense ? b * G.N + kb : vals[p0 + kb]];
+    for (int base = s_lo; base < s_hi; base += 32) {
+        if (base + lane < s_hi) srec[warp][lane] = nxt;
         __syncwarp();
-        kb = base + NW * 32 + lane;
-        if (kb < n) nxt = rec[dense ? b * G.N + kb : vals[p0 + kb]];
-        const int nb = min(32, n - base);
+        kb = base + 32 + lane;
+        if (kb < s_hi) nxt = rec[dense ? b * G.N + kb : vals[p0 + kb]];
+        const int nb = min(32, s_hi - base);
         int i = 0;
         // (1 - a) >= 1e-4, so 8 factors stay normal in fp32: renormalise after every 8 splats
         for (; i + 8 <= nb; i += 8) {
@@ -719,20 +722,22 @@ __device__ __forceinline__ bool group_native(const RenderGeom &G, int g) { retur
 // upsampled to native resolution (torch align_corners=False), added in the reference's order
 // (render_triton.py:959-972, 914-916).
 __device__ __forceinline__ void gather_sums(const RenderGeom &G, const float *__restrict__ fields,
-                                            const int *__restrict__ gsplats, int b, long long p, int y, int x,
-                                            float S[5]) {
+                                            const int *__restrict__ gsplats, int b, int y, int x, float S[5]) {
+    // y is uniform over the block (one native row per block), so the row weights of each group are
+    // computed once in uniform registers; offsets are 32-bit inside one image's field block
 #pragma unroll
     for (int c = 0; c < 5; c++) S[c] = 0.f;
     const float *fimg = fields + (long long)b * G.fld_per_image;
 #pragma unroll
     for (int k = 0; k < GS_MAX_GROUPS; k++) {
         if (k >= G.ngroups) break;
-        int g = G.order[k];
+        const int g = G.order[k];
         if (gsplats[b * G.ngroups + g] == 0) continue;
         const float *f = fimg + G.g[g].fld_off;
-        int Hg = G.g[g].H, Wg = G.g[g].W;
-        long long plane = (long long)Hg * Wg;
+        const int Hg = G.g[g].H, Wg = G.g[g].W;
+        const int plane = Hg * Wg;
         if (Hg == G.H && Wg == G.W) {
+            const int p = y * Wg + x;
 #pragma unroll
             for (int c = 0; c < 5; c++) S[c] += f[c * plane + p];
         } else {
@@ -740,29 +745,29 @@ __device__ __forceinline__ void gather_sums(const RenderGeom &G, const float *__
             float h0, h1, w0, w1;
             lin_index_s(y, Hg, G.g[g].up_sy, y0, y1, h0, h1);
             lin_index_s(x, Wg, G.g[g].up_sx, x0, x1, w0, w1);
-            const long long a00 = (long long)y0 * Wg + x0, a01 = (long long)y0 * Wg + x1;
-            const long long a10 = (long long)y1 * Wg + x0, a11 = (long long)y1 * Wg + x1;
+            const int r0 = y0 * Wg, r1 = y1 * Wg;
 #pragma unroll
             for (int c = 0; c < 5; c++) {
                 const float *fc = f + c * plane;
-                float v = h0 * (w0 * fc[a00] + w1 * fc[a01]) + h1 * (w0 * fc[a10] + w1 * fc[a11]);
-                S[c] += v;
+                S[c] += h0 * (w0 * fc[r0 + x0] + w1 * fc[r0 + x1]) + h1 * (w0 * fc[r1 + x0] + w1 * fc[r1 + x1]);
             }
         }
     }
 }
 
-// one native pixel per thread: sum the present groups' fields and composite (render_triton.py:976-979)
-__global__ void __launch_bounds__(256) k_composite(RenderGeom G, const float *__restrict__ fields,
+// one native pixel per thread, one native row per block row (grid = (ceil(W / 128), band rows, B)): sum
+// the present groups' fields and composite (render_triton.py:976-979)
+__global__ void __launch_bounds__(128) k_composite(RenderGeom G, const float *__restrict__ fields,
                                                    const int *__restrict__ gsplats, const float *__restrict__ bg,
                                                    float *__restrict__ out) {
-    const int b = blockIdx.y;
+    const int b = blockIdx.z;
+    const int y = G.y0 + blockIdx.y;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    if (x >= G.W) return;
     const long long P = (long long)G.H * G.W;
-    long long p = (long long)G.y0 * G.W + (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (p >= (long long)G.y1 * G.W) return;
-    int y = (int)(p / G.W), x = (int)(p - (long long)y * G.W);
+    const long long p = (long long)y * G.W + x;
     float S[5];
-    gather_sums(G, fields, gsplats, b, p, y, x, S);
+    gather_sums(G, fields, gsplats, b, y, x, S);
     float asum = fmaxf(S[1], 1e-8f);
     float T = expf(S[0]);
     float *ob = out + (long long)b * G.C * P;
@@ -793,20 +798,21 @@ __global__ void __launch_bounds__(256) k_add_prior(RenderGeom G, const float *__
 
 // dS at native resolution from dL/dimage (torch autograd of render_triton.py:976-979; the cull and
 // exact paths skip the clamp_min mask, render_triton.py:644-654); bg gradient sum_p g * T.
-__global__ void __launch_bounds__(256) k_composite_bwd(RenderGeom G, const float *__restrict__ fields,
+__global__ void __launch_bounds__(128) k_composite_bwd(RenderGeom G, const float *__restrict__ fields,
                                                        const int *__restrict__ gsplats,
                                                        const float *__restrict__ bg,
                                                        const float *__restrict__ gout, float *__restrict__ Gn,
                                                        float *__restrict__ gbg, int clamp_mask) {
-    __shared__ float red[3][8];
-    const int b = blockIdx.y;
+    __shared__ float red[3][4];
+    const int b = blockIdx.z;
     const long long P = (long long)G.H * G.W;
-    long long p = (long long)G.y0 * G.W + (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int y = G.y0 + blockIdx.y;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const long long p = (long long)y * G.W + x;
     float gT[3] = {0.f, 0.f, 0.f};
-    if (p < (long long)G.y1 * G.W) {
-        const int y = (int)(p / G.W), x = (int)(p - (long long)y * G.W);
+    if (x < G.W) {
         float S[5];
-        gather_sums(G, fields, gsplats, b, p, y, x, S);
+        gather_sums(G, fields, gsplats, b, y, x, S);
         const float Sl = S[0], Sw = S[1];
         float asum = fmaxf(Sw, 1e-8f);
         float T = expf(Sl);
@@ -844,28 +850,54 @@ __global__ void __launch_bounds__(256) k_composite_bwd(RenderGeom G, const float
     __syncthreads();
     if (threadIdx.x < 3 && threadIdx.x < G.C) {
         float v = 0.f;
-        for (int w = 0; w < 8; w++) v += red[threadIdx.x][w];
+        for (int w = 0; w < 4; w++) v += red[threadIdx.x][w];
         atomicAdd(&gbg[b * 4 + threadIdx.x], v);
     }
 }
 
-// adjoint of the bilinear upsample for every present coarse group: each texel whose tile holds pairs
-// gathers, in a fixed order, the native-resolution dS values whose bilinear taps touched it
-// (deterministic; texels of empty tiles are never read by the backward and are skipped).
-__global__ void __launch_bounds__(256) k_adjoint(RenderGeom G, const int *__restrict__ gsplats,
-                                                 const int2 *__restrict__ ranges, const float *__restrict__ Gn,
-                                                 float *__restrict__ gfields) {
-    const int b = blockIdx.y;
-    const long long q0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+// Adjoint of the bilinear upsample (align_corners=False) for every coarse group, as two separable passes:
+//   X: T[g][c][y][j] = sum_x wx(x, j) * dS[c][y][x]      native rows y of the band, coarse columns j
+//   Y: dF[g][c][i][j] = sum_y wy(y, i) * T[g][c][y][j]   coarse rows i
+// Each output gathers the O(native/coarse) inputs whose taps touch it, in a fixed order; deep octaves
+// (upsampling factors past ~12) give each output a 32-lane team that splits the inputs and reduces with
+// shuffles in a fixed tree, so the result is deterministic and the work linear in the image size.
+struct AdjPlan {
+    long long uD[GS_MAX_GROUPS + 1];                          // direct-gather texel offsets per group
+    long long uX[GS_MAX_GROUPS + 1], uY[GS_MAX_GROUPS + 1];  // work-unit offsets per group (multiples of 32)
+    long long tOff[GS_MAX_GROUPS];                            // first float of the group's T block (per image)
+    long long tPerImage;
+    int teamX[GS_MAX_GROUPS], teamY[GS_MAX_GROUPS];
+};
+
+__device__ __forceinline__ int adj_group(const long long *off, long long u) {
     int g = -1;
 #pragma unroll
     for (int k = 0; k < GS_MAX_GROUPS; k++)
-        if (k < G.ngroups && G.g[k].adj_off >= 0 && q0 >= G.g[k].adj_off &&
-            q0 < G.g[k].adj_off + (long long)G.g[k].H * G.g[k].W)
-            g = k;
+        if (u >= off[k] && u < off[k + 1]) g = k;
+    return g;
+}
+
+__device__ __forceinline__ void team_reduce5(float acc[5], int team) {
+    if (team == 32) {
+#pragma unroll
+        for (int c = 0; c < 5; c++)
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], o);
+    }
+}
+
+// Shallow groups (upsampling factor <= 4, at most 11 x 11 native taps per texel) gather directly, one
+// thread per texel; texels of tiles without pairs are never read by the backward and are skipped.
+__global__ void __launch_bounds__(256) k_adjoint_direct(RenderGeom G, AdjPlan A, const int *__restrict__ gsplats,
+                                                        const int2 *__restrict__ ranges, const float *__restrict__ Gn,
+                                                        float *__restrict__ gfields) {
+    const int b = blockIdx.y;
+    const long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int g = adj_group(A.uD, u);
     if (g < 0 || gsplats[b * G.ngroups + g] == 0) return;
-    const long long q = q0 - G.g[g].adj_off;
+    const long long q = u - A.uD[g];
     const int Hg = G.g[g].H, Wg = G.g[g].W;
+    if (q >= (long long)Hg * Wg) return;
     const int i = (int)(q / Wg), j = (int)(q - (long long)i * Wg);
     const int tile = G.g[g].tile_off + (i / G.tile) * G.g[g].ntx + (j / G.tile);
     const int2 rg = ranges[(long long)b * G.tiles_per_image + tile];
@@ -877,15 +909,18 @@ __global__ void __launch_bounds__(256) k_adjoint(RenderGeom G, const int *__rest
     const int xlo = max(0, (int)ceilf((j - 0.5f) * inv_sx - 0.5f) - 1);
     const int xhi = min(G.W - 1, (int)floorf((j + 1.5f) * inv_sx - 0.5f) + 1);
     const float usy = G.g[g].up_sy, usx = G.g[g].up_sx;
-    // column weights of texel j, computed once per texel
-    constexpr int MAXW = 264;  // 2 * (W / Wg) + 3 with W / Wg <= 128 (max_octaves <= 7)
+    constexpr int MAXW = 12;  // 2 * factor + 3 <= 11 for the groups this kernel takes
     float wx[MAXW];
     const int nx = min(xhi - xlo + 1, MAXW);
-    for (int t = 0; t < nx; t++) {
-        int x0, x1;
-        float w0, w1;
-        lin_index_s(xlo + t, Wg, usx, x0, x1, w0, w1);
-        wx[t] = (x0 == j ? w0 : 0.f) + (x1 == j ? w1 : 0.f);
+#pragma unroll
+    for (int t = 0; t < MAXW; t++) {
+        wx[t] = 0.f;
+        if (t < nx) {
+            int x0, x1;
+            float w0, w1;
+            lin_index_s(xlo + t, Wg, usx, x0, x1, w0, w1);
+            wx[t] = (x0 == j ? w0 : 0.f) + (x1 == j ? w1 : 0.f);
+        }
     }
     float acc5[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
     const float *Gb = Gn + (long long)b * 5 * P;
@@ -896,9 +931,10 @@ __global__ void __launch_bounds__(256) k_adjoint(RenderGeom G, const int *__rest
         const float wy = (y0 == i ? h0 : 0.f) + (y1 == i ? h1 : 0.f);
         if (wy == 0.f) continue;
         const long long rowp = (long long)y * G.W + xlo;
-        for (int t = 0; t < nx; t++) {
+#pragma unroll
+        for (int t = 0; t < MAXW; t++) {
             const float w = wy * wx[t];
-            if (w == 0.f) continue;
+            if (t >= nx || w == 0.f) continue;
 #pragma unroll
             for (int c = 0; c < 5; c++) acc5[c] += w * Gb[c * P + rowp + t];
         }
@@ -907,6 +943,85 @@ __global__ void __launch_bounds__(256) k_adjoint(RenderGeom G, const int *__rest
     const long long plane = (long long)Hg * Wg;
 #pragma unroll
     for (int c = 0; c < 5; c++) gf[c * plane + q] = acc5[c];
+}
+
+__global__ void __launch_bounds__(256) k_adjoint_x(RenderGeom G, AdjPlan A, const int *__restrict__ gsplats,
+                                                   const float *__restrict__ Gn, float *__restrict__ T) {
+    const int b = blockIdx.y;
+    const long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int g = adj_group(A.uX, u);
+    if (g < 0 || gsplats[b * G.ngroups + g] == 0) return;  // uniform over the warp (groups padded to 32)
+    const int team = A.teamX[g];
+    const long long local = u - A.uX[g];
+    const long long out = local / team;
+    const int lt = (int)(local - out * team);
+    const int Wg = G.g[g].W;
+    const int rows = G.y1 - G.y0;
+    if (out >= (long long)rows * Wg) return;  // padding units: whole warps when team == 32
+    const int y = G.y0 + (int)(out / Wg), j = (int)(out % Wg);
+    const float inv_sx = (float)G.W / (float)Wg;
+    const int xlo = max(0, (int)ceilf((j - 0.5f) * inv_sx - 0.5f) - 1);
+    const int xhi = min(G.W - 1, (int)floorf((j + 1.5f) * inv_sx - 0.5f) + 1);
+    const float usx = G.g[g].up_sx;
+    const long long P = (long long)G.H * G.W;
+    const float *row = Gn + (long long)b * 5 * P + (long long)y * G.W;
+    float acc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int x = xlo + lt; x <= xhi; x += team) {
+        int x0, x1;
+        float w0, w1;
+        lin_index_s(x, Wg, usx, x0, x1, w0, w1);
+        const float w = (x0 == j ? w0 : 0.f) + (x1 == j ? w1 : 0.f);
+        if (w == 0.f) continue;
+#pragma unroll
+        for (int c = 0; c < 5; c++) acc[c] += w * row[c * P + x];
+    }
+    team_reduce5(acc, team);
+    if (lt == 0) {
+        float *t = T + (long long)b * A.tPerImage + A.tOff[g];
+        const long long plane = (long long)rows * Wg;
+#pragma unroll
+        for (int c = 0; c < 5; c++) t[c * plane + out] = acc[c];
+    }
+}
+
+__global__ void __launch_bounds__(256) k_adjoint_y(RenderGeom G, AdjPlan A, const int *__restrict__ gsplats,
+                                                   const float *__restrict__ T, float *__restrict__ gfields) {
+    const int b = blockIdx.y;
+    const long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int g = adj_group(A.uY, u);
+    if (g < 0 || gsplats[b * G.ngroups + g] == 0) return;
+    const int team = A.teamY[g];
+    const long long local = u - A.uY[g];
+    const long long out = local / team;
+    const int lt = (int)(local - out * team);
+    const int Hg = G.g[g].H, Wg = G.g[g].W;
+    if (out >= (long long)Hg * Wg) return;
+    const int i = (int)(out / Wg), j = (int)(out % Wg);
+    const float inv_sy = (float)G.H / (float)Hg;
+    const int ylo = max(G.y0, (int)ceilf((i - 0.5f) * inv_sy - 0.5f) - 1);
+    const int yhi = min(G.y1 - 1, (int)floorf((i + 1.5f) * inv_sy - 0.5f) + 1);
+    const float usy = G.g[g].up_sy;
+    const int rows = G.y1 - G.y0;
+    const long long tplane = (long long)rows * Wg;
+    const float *t = T + (long long)b * A.tPerImage + A.tOff[g];
+    float acc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int y = ylo + lt; y <= yhi; y += team) {
+        int y0, y1;
+        float h0, h1;
+        lin_index_s(y, Hg, usy, y0, y1, h0, h1);
+        const float w = (y0 == i ? h0 : 0.f) + (y1 == i ? h1 : 0.f);
+        if (w == 0.f) continue;
+        const long long r = (long long)(y - G.y0) * Wg + j;
+#pragma unroll
+        for (int c = 0; c < 5; c++) acc[c] += w * t[c * tplane + r];
+    }
+    team_reduce5(acc, team);
+    if (lt == 0) {
+        float *gf = gfields + (long long)b * G.fld_per_image + G.g[g].fld_off;
+        const long long plane = (long long)Hg * Wg;
+#pragma unroll
+        for (int c = 0; c < 5; c++) gf[c * plane + out] = acc[c];
+    }
 }
 
 // one CTA per tile; lane = one (tile, splat) pair looping over the tile's pixels
@@ -1320,7 +1435,8 @@ struct Plan {
     int emit_parts;  // emit blocks per preprocessing block (>= 4 blocks per SM of 148 in all)
     size_t o_rec, o_meta, o_counts, o_bsum, o_zero, o_gpairs, o_gsplats, o_misc, o_ranges, z_len;
     size_t o_keys_a, o_vals_a, o_keys_b, o_vals_b, o_hist, o_dtot, o_fields, fwd_bytes;
-    size_t o_G, o_gfields, o_bzero, o_acc, o_gbg, bz_len, total_bytes;
+    size_t o_G, o_gfields, o_adjT, o_bzero, o_acc, o_gbg, bz_len, total_bytes;
+    AdjPlan adj;
 };
 
 int validate(const gs_render_desc *d) {
@@ -1491,6 +1607,38 @@ void make_plan(const gs_render_desc *d, Plan &pl) {
     pl.fwd_bytes = o;
     pl.o_G = take(sizeof(float) * 5 * (size_t)d->B * d->H * d->W);
     pl.o_gfields = take(sizeof(float) * (size_t)d->B * pl.G.fld_per_image);
+    {
+        // separable adjoint: per coarse group, X outputs (band rows x coarse columns) and Y outputs (coarse
+        // texels), thread-per-output or a 32-lane team when an output gathers more than ~24 inputs
+        AdjPlan &A = pl.adj;
+        memset(&A, 0, sizeof(A));
+        const RenderGeom &G = pl.G;
+        const long long rows = std::max(0, G.y1 - G.y0);
+        long long ud = 0, ux = 0, uy = 0, toff = 0;
+        for (int k = 0; k < GS_MAX_GROUPS; k++) {
+            A.uD[k] = ud;
+            A.uX[k] = ux;
+            A.uY[k] = uy;
+            A.teamX[k] = A.teamY[k] = 1;
+            if (k >= G.ngroups || G.g[k].adj_off < 0) continue;
+            const long long Hg = G.g[k].H, Wg = G.g[k].W;
+            if ((d->W + Wg - 1) / Wg <= 4 && (d->H + Hg - 1) / Hg <= 4) {  // shallow: direct gather
+                ud += Hg * Wg;
+                continue;
+            }
+            A.teamX[k] = 2 * (d->W + Wg - 1) / Wg + 3 > 24 ? 32 : 1;
+            A.teamY[k] = 2 * (d->H + Hg - 1) / Hg + 3 > 24 ? 32 : 1;
+            ux += (rows * Wg * A.teamX[k] + 31) / 32 * 32;
+            uy += (Hg * Wg * A.teamY[k] + 31) / 32 * 32;
+            A.tOff[k] = toff;
+            toff += 5 * rows * Wg;
+        }
+        A.uD[GS_MAX_GROUPS] = ud;
+        A.uX[GS_MAX_GROUPS] = ux;
+        A.uY[GS_MAX_GROUPS] = uy;
+        A.tPerImage = toff;
+    }
+    pl.o_adjT = take(sizeof(float) * (size_t)std::max<long long>(1, d->B * pl.adj.tPerImage));
     pl.o_bzero = o;
     pl.o_acc = take(sizeof(float) * 12 * (size_t)std::max<long long>(BN, 1));
     pl.o_gbg = take(sizeof(float) * 4 * (size_t)d->B);
@@ -1508,6 +1656,8 @@ int launch_fields_fwd(const Plan &pl, void *ws, cudaStream_t st) {
     auto rng = at<int2>(ws, pl.o_ranges);
     const int *vals = at<int>(ws, (pl.passes % 2) ? pl.o_vals_b : pl.o_vals_a);
     auto fld = at<float>(ws, pl.o_fields);
+    // 4 warps per tile (8 measured slower: the per-warp staging and the cross-warp reduction dominate
+    // short lists)
     if (G.odds) {
         if (G.tile == 8) k_fields_fwd<8, 4, true><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
         else if (G.tile == 16) k_fields_fwd<16, 4, true><<<grid, 128, 0, st>>>(G, rec, rng, vals, fld);
@@ -1750,11 +1900,10 @@ int gs_render_fwd_prior(const gs_render_desc *d, const float *mu, const float *l
             GS_CHECK_LAUNCH("k_add_prior");
         }
     }
-    long long Pb = (long long)(G.y1 - G.y0) * d->W;
-    dim3 cg((unsigned)std::max<long long>(1, (Pb + 255) / 256), (unsigned)d->B);
-    {
+    dim3 cg((unsigned)((d->W + 127) / 128), (unsigned)std::max(1, G.y1 - G.y0), (unsigned)d->B);
+    if (G.y1 > G.y0) {
         ProfScope ps(PR_COMPOSITE, s);
-        k_composite<<<cg, 256, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,
+        k_composite<<<cg, 128, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,
                                        out);
         GS_CHECK_LAUNCH("k_composite");
     }
@@ -1780,11 +1929,10 @@ int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_sca
     cudaError_t e = cudaMemsetAsync(at<char>(workspace, pl.o_bzero), 0, pl.bz_len, s);
     GS_COUNT(1);
     if (e != cudaSuccess) return set_cuda_error(e, "memset");
-    long long Pb = (long long)(G.y1 - G.y0) * d->W;
-    dim3 cg((unsigned)std::max<long long>(1, (Pb + 255) / 256), (unsigned)d->B);
+    dim3 cg((unsigned)((d->W + 127) / 128), (unsigned)std::max(1, G.y1 - G.y0), (unsigned)d->B);
     int clamp_mask = (d->mode == GS_MODE_OCTAVE || d->mode == GS_MODE_MULTIRES) ? 1 : 0;
     std::unique_ptr<ProfScope> cb_scope(new ProfScope(PR_COMPOSITE_BWD, s));
-    k_composite_bwd<<<cg, 256, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,
+    k_composite_bwd<<<cg, 128, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,
                                        grad_out, at<float>(workspace, pl.o_G), at<float>(workspace, pl.o_gbg),
                                        clamp_mask);
     GS_CHECK_LAUNCH("k_composite_bwd");
@@ -1792,13 +1940,27 @@ int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_sca
     for (int g = 0; g < G.ngroups; g++)
         if (!(G.g[g].H == G.H && G.g[g].W == G.W)) any_coarse = true;
     if (any_coarse) {
-        long long tex = 0;
-        for (int g = 0; g < G.ngroups; g++)
-            if (G.g[g].adj_off >= 0) tex += (long long)G.g[g].H * G.g[g].W;
-        dim3 ag((unsigned)((tex + 255) / 256), (unsigned)d->B);
-        k_adjoint<<<ag, 256, 0, s>>>(G, at<int>(workspace, pl.o_gsplats), at<int2>(workspace, pl.o_ranges),
-                                     at<float>(workspace, pl.o_G), at<float>(workspace, pl.o_gfields));
-        GS_CHECK_LAUNCH("k_adjoint");
+        const AdjPlan &A = pl.adj;
+        const long long ud = A.uD[GS_MAX_GROUPS], ux = A.uX[GS_MAX_GROUPS], uy = A.uY[GS_MAX_GROUPS];
+        if (ud > 0) {
+            dim3 gd((unsigned)((ud + 255) / 256), (unsigned)d->B);
+            k_adjoint_direct<<<gd, 256, 0, s>>>(G, A, at<int>(workspace, pl.o_gsplats),
+                                                at<int2>(workspace, pl.o_ranges), at<float>(workspace, pl.o_G),
+                                                at<float>(workspace, pl.o_gfields));
+            GS_CHECK_LAUNCH("k_adjoint_direct");
+        }
+        if (ux > 0) {
+            dim3 gx((unsigned)((ux + 255) / 256), (unsigned)d->B);
+            k_adjoint_x<<<gx, 256, 0, s>>>(G, A, at<int>(workspace, pl.o_gsplats), at<float>(workspace, pl.o_G),
+                                           at<float>(workspace, pl.o_adjT));
+            GS_CHECK_LAUNCH("k_adjoint_x");
+        }
+        if (uy > 0) {
+            dim3 gy((unsigned)((uy + 255) / 256), (unsigned)d->B);
+            k_adjoint_y<<<gy, 256, 0, s>>>(G, A, at<int>(workspace, pl.o_gsplats), at<float>(workspace, pl.o_adjT),
+                                           at<float>(workspace, pl.o_gfields));
+            GS_CHECK_LAUNCH("k_adjoint_y");
+        }
     }
     cb_scope.reset();
     dim3 grid((unsigned)((long long)G.B * G.tiles_per_image));

@@ -1,6 +1,6 @@
 // Blackwell (sm_100a) tensor-core primitives used by the encoder convolutions: TMA tile loads,
 // mbarriers with bounded waits, TMEM allocation, tcgen05.mma (kind::f16, bf16 in / fp32 accumulate)
-// and tcgen05.ld.  Inline PTX only; no multicast anywhere.
+// and tcgen05.ld.  Inline PTX only; every TMA load targets its own CTA.
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -59,7 +59,7 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parit
     return false;
 }
 
-// ---- TMA (no multicast)
+// ---- TMA loads into this CTA's shared memory
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
