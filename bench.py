@@ -431,6 +431,10 @@ def cpu_baseline(workload_cls, steps: int, budget_s: float = 20.0):
     from oracle import oracle as O
 
     O.build()
+    # every host thread, whatever OMP_NUM_THREADS a launcher set (torchrun sets 1 per rank)
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    O.set_threads(n)
     s = workload_cls.cpu_inputs()
     times = []
     t_all = time.perf_counter()
@@ -639,7 +643,9 @@ def main():
         "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": tot_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 encoder / fp32 render" if wcls is EncodeRenderWorkload else "fp32", "data": "synthetic",
-        "config": {**wl.config(), "parallelism": f"dp{world} (image per GPU, no collective)"},
+        "config": {**wl.config(), "parallelism": (f"tile-row bands x{world}, one NCCL all-reduce of the splat "
+                                                  "gradients per step" if wcls is FitWorkload else
+                                                  f"dp{world} (image per GPU, no collective)")},
         "stages_ms": stages, "clocks": clocks, "gpu_launches": int(launches),
         "e2e": {"value": e2e_val, "unit": "images/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "peaks": pk,
@@ -649,9 +655,14 @@ def main():
         M, N, Kd = (wl.H // 4) * (wl.W // 4), 128, 9 * 384
         t = stages.get("conv4_decoder", {}).get("ms_per_replay", 0.0)
         ach = 2.0 * M * N * Kd / (t * 1e-3) / 1e12 if t > 0 else None
+        # traffic: dram__bytes_read.sum + dram__bytes_write.sum of one decoder launch in a full ncu capture
+        # of this workload (29.25 MB read, 0 written inside the kernel's window: its 9.4 MB output leaves
+        # L2 later); algorithmic bytes per launch = 28.3 MB input + 0.9 MB weights + 9.4 MB output
         line["roofline"] = {"bound": "tensor", "kernel": "k_conv_tc<128,64,4> (decoder 3x3 384->128 @192^2)",
                             "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                            "frac": (ach / pk["bf16_tflops"]) if ach else None, "traffic": None,
+                            "frac": (ach / pk["bf16_tflops"]) if ach else None, "traffic": 29.25e6,
+                            "traffic_source": "ncu --set full capture of this workload (decoder launch)",
+                            "algorithmic_bytes": 2 * M * (256 + 128) + 2 * N * Kd + 2 * M * N,
                             "flops_per_launch": 2.0 * M * N * Kd,
                             "peak_source": f"MEASURED_PEAKS.json bf16_tflops (burst, {pk['source']})"}
         line["render_fwd_bwd_ms_per_image"] = sec["render_fwd_bwd_ms_per_image"] if sec else None

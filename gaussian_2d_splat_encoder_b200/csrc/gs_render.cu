@@ -17,7 +17,7 @@
 // Backward:
 //   k_composite_bwd  dS fields at native resolution, bg gradient
 //   k_adjoint_*      adjoint of the bilinear upsample -> dS fields of every coarse group (direct gather for
-//                    upsampling factors <= 4, separable row/column passes for deeper octaves)
+//                    upsampling factors <= 8, separable row/column passes for deeper octaves)
 //   k_fields_bwd     one CTA per tile, one lane per (tile, splat) pair looping over the tile's
 //                    pixels; 9 per-splat sums leave through 3 vector atomics per pair
 //   k_finalize       per-splat chain rule (rotation, scale, softplus) into the leaf gradients
@@ -858,9 +858,9 @@ __global__ void __launch_bounds__(128) k_composite_bwd(RenderGeom G, const float
 // Adjoint of the bilinear upsample (align_corners=False) for every coarse group, as two separable passes:
 //   X: T[g][c][y][j] = sum_x wx(x, j) * dS[c][y][x]      native rows y of the band, coarse columns j
 //   Y: dF[g][c][i][j] = sum_y wy(y, i) * T[g][c][y][j]   coarse rows i
-// Each output gathers the O(native/coarse) inputs whose taps touch it, in a fixed order; deep octaves
-// (upsampling factors past ~12) give each output a 32-lane team that splits the inputs and reduces with
-// shuffles in a fixed tree, so the result is deterministic and the work linear in the image size.
+// Each output gathers the O(native/coarse) inputs whose taps touch it, in a fixed order; the deepest
+// octaves (upsampling factor 64 and up) give each output a 32-lane team that splits the inputs and reduces
+// with shuffles in a fixed tree, so the result is deterministic and the work linear in the image size.
 struct AdjPlan {
     long long uD[GS_MAX_GROUPS + 1];                          // direct-gather texel offsets per group
     long long uX[GS_MAX_GROUPS + 1], uY[GS_MAX_GROUPS + 1];  // work-unit offsets per group (multiples of 32)
@@ -886,8 +886,9 @@ __device__ __forceinline__ void team_reduce5(float acc[5], int team) {
     }
 }
 
-// Shallow groups (upsampling factor <= 4, at most 11 x 11 native taps per texel) gather directly, one
-// thread per texel; texels of tiles without pairs are never read by the backward and are skipped.
+// Shallow groups (upsampling factor <= 8, at most 19 x 19 native taps per texel) gather directly, one
+// thread per texel; texels of tiles without pairs are never read by the backward and are skipped, which
+// keeps sparsely populated octaves cheap.
 __global__ void __launch_bounds__(256) k_adjoint_direct(RenderGeom G, AdjPlan A, const int *__restrict__ gsplats,
                                                         const int2 *__restrict__ ranges, const float *__restrict__ Gn,
                                                         float *__restrict__ gfields) {
@@ -909,7 +910,7 @@ __global__ void __launch_bounds__(256) k_adjoint_direct(RenderGeom G, AdjPlan A,
     const int xlo = max(0, (int)ceilf((j - 0.5f) * inv_sx - 0.5f) - 1);
     const int xhi = min(G.W - 1, (int)floorf((j + 1.5f) * inv_sx - 0.5f) + 1);
     const float usy = G.g[g].up_sy, usx = G.g[g].up_sx;
-    constexpr int MAXW = 12;  // 2 * factor + 3 <= 11 for the groups this kernel takes
+    constexpr int MAXW = 20;  // 2 * factor + 3 <= 19 for the groups this kernel takes
     float wx[MAXW];
     const int nx = min(xhi - xlo + 1, MAXW);
 #pragma unroll
@@ -1179,7 +1180,7 @@ __global__ void __launch_bounds__(256) k_finalize(RenderGeom G, const float *__r
 // ----------------------------------------------------------------------------------------------------
 // pixel-list render (render.py:68-87, render_alpha_subsampled): alpha compositing of all N splats of an
 // image at P listed pixels (flat indices y*W + x), dense (no binning), alpha mode, autograd of
-// render.py:30-36 including the clamp_min(1e-8) mask.  CTA = PT_PIX pixels x one slice of the splats.
+// render.py:47-65 including the clamp_min(1e-8) mask.  CTA = PT_PIX pixels x one slice of the splats.
 
 #define PT_PIX 64
 #define PT_SLICE 2048
@@ -1261,7 +1262,7 @@ __global__ void __launch_bounds__(NW * 32) k_points_fwd(int N, int H, int W, int
     }
 }
 
-// fields[b][5][p] = sum over slices (fixed order), then the composite of render.py:30-36:
+// fields[b][5][p] = sum over slices (fixed order), then the composite of render.py:47-65:
 // out[b][c][p] = (1 - T) * S_c / max(S_w, 1e-8) + T * bg[b][c]
 __global__ void __launch_bounds__(256) k_points_composite(int B, int C, int P, int nslices,
                                                           const float *__restrict__ part,
@@ -1622,12 +1623,14 @@ void make_plan(const gs_render_desc *d, Plan &pl) {
             A.teamX[k] = A.teamY[k] = 1;
             if (k >= G.ngroups || G.g[k].adj_off < 0) continue;
             const long long Hg = G.g[k].H, Wg = G.g[k].W;
-            if ((d->W + Wg - 1) / Wg <= 4 && (d->H + Hg - 1) / Hg <= 4) {  // shallow: direct gather
+            if ((d->W + Wg - 1) / Wg <= 8 && (d->H + Hg - 1) / Hg <= 8) {  // shallow: direct gather
                 ud += Hg * Wg;
                 continue;
             }
-            A.teamX[k] = 2 * (d->W + Wg - 1) / Wg + 3 > 24 ? 32 : 1;
-            A.teamY[k] = 2 * (d->H + Hg - 1) / Hg + 3 > 24 ? 32 : 1;
+            // a 32-lane team only where one output gathers more than ~100 taps (factor >= 64): a team
+            // multiplies the launch 32-fold, which costs even when the group turns out empty on the device
+            A.teamX[k] = 2 * (d->W + Wg - 1) / Wg + 3 > 100 ? 32 : 1;
+            A.teamY[k] = 2 * (d->H + Hg - 1) / Hg + 3 > 100 ? 32 : 1;
             ux += (rows * Wg * A.teamX[k] + 31) / 32 * 32;
             uy += (Hg * Wg * A.teamY[k] + 31) / 32 * 32;
             A.tOff[k] = toff;

@@ -109,7 +109,7 @@ int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_sca
                   void *workspace, size_t workspace_bytes, void *stream);
 
 /* Pixel-list render: replaces render_alpha_subsampled (render.py:68-87) and the torch autograd of its
- * alpha_composite (render.py:30-36).  All N splats of image b are composited (alpha mode, no binning) at
+ * alpha_composite (render.py:47-65).  All N splats of image b are composited (alpha mode, no binning) at
  * the P pixels px_idx[b][0..P) (flat indices y*W + x, int64, as torch.randint returns them).
  * d->mode must be GS_MODE_EXACT and d->odds 0; tile, cutoff and the octave fields are ignored.
  * out is [B][C][P].  The forward keeps the per-pixel sums in the workspace for the backward, which

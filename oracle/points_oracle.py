@@ -1,6 +1,6 @@
 """TEST INFRASTRUCTURE ONLY: CPU restatement of the reference's pixel-list render
 (bigwolfeman/gaussian-2d-splat-encoder, gaussian_splat_encoder/render.py:68-87, render_alpha_subsampled,
-with gaussian_falloff render.py:17-27, alpha_composite render.py:30-36 and activate_scale
+with gaussian_falloff render.py:34-44, alpha_composite render.py:47-65 and activate_scale
 params.py:18-28), in float64 torch on the CPU, gradients by torch autograd of the same expressions.
 
 Used as the checker of the CUDA point kernels (gs_render_points_fwd / _bwd) by the parity tests; the
