@@ -1,7 +1,7 @@
 """Generate the golden fixtures under tests/golden/ by running the REFERENCE implementation.
 
-Run once in a container that has the reference checkout (default ``/root/reference``, or set
-``GSPLAT_REFERENCE``):
+Run once in a container that has the reference checkout, next to this repository (``../reference``)
+or wherever ``GSPLAT_REFERENCE`` points:
 
     python tests/golden/make_golden.py [case ...]
 
@@ -34,7 +34,7 @@ import triton.language.core as tlc  # noqa: E402
 tlc.tensor.cos = lambda self: tl.cos(self)
 tlc.tensor.sin = lambda self: tl.sin(self)
 
-REF = Path(os.environ.get("GSPLAT_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("GSPLAT_REFERENCE", Path(__file__).resolve().parents[3] / "reference"))
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(HERE.parents[1]))

@@ -74,3 +74,38 @@ def test_no_cpu_fallback():
     t = torch.zeros(1, 4, 2)
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         rt.render_alpha_octave(t, t, torch.zeros(1, 4, 3), torch.zeros(1, 4), torch.zeros(1, 3), 16, 16)
+
+
+def test_points_workspace_host_only(lib):
+    """gs_render_points_workspace_size: positive for the pixel-list render's exact mode, with backward
+    larger than forward; 0 for the octave/odds modes it does not serve and for an empty pixel list."""
+    from gaussian_2d_splat_encoder_b200 import _lib
+
+    d = _desc(mode=_lib.MODE_EXACT, B=2, N=4096, C=3, H=256, W=256, TILE=8, odds=False, has_theta=True,
+              cutoff=3.0)
+    f = lib.gs_render_points_workspace_size(C.byref(d), 10000, 0)
+    b = lib.gs_render_points_workspace_size(C.byref(d), 10000, 1)
+    # splat records + per-slice partial sums of 5 fields for every (image, pixel)
+    assert 2 * 10000 * 5 * 4 * 2 < f < b < (1 << 28)
+    assert lib.gs_render_points_workspace_size(C.byref(d), 0, 0) == 0
+    d.odds = 1
+    assert lib.gs_render_points_workspace_size(C.byref(d), 10000, 0) == 0
+    d.odds, d.mode = 0, _lib.MODE_OCTAVE
+    assert lib.gs_render_points_workspace_size(C.byref(d), 10000, 0) == 0
+
+
+def test_encode_render_workspace_host_only(lib):
+    """The fused encode+render workspace is the encoder's plus a render's; unsupported image sizes give 0."""
+    import torch
+    from enc_util import GOLDEN_CFG
+    from gaussian_2d_splat_encoder_b200.efficient_encoder import EfficientGaussianEncoder
+
+    torch.manual_seed(0)
+    m = EfficientGaussianEncoder(**GOLDEN_CFG)
+    d = m._desc(1, 256, 256)
+    enc = lib.gs_encoder_workspace_size(C.byref(d))
+    both = lib.gs_encode_render_workspace_size(C.byref(d))
+    assert 0 < enc < both < (1 << 32)
+    d.H = 250
+    assert lib.gs_encoder_workspace_size(C.byref(d)) == 0
+    assert lib.gs_encode_render_workspace_size(C.byref(d)) == 0
