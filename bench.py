@@ -36,6 +36,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "768² encode+render images/s at 1/2/4/8 B200; render fwd+bwd ms/image"
+FIT_METRIC = "config 4: 2048^2 fitting step (render fwd+bwd + NCCL all-reduce + Adam) steps/s"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 STAGE_NAMES = {0: "binning", 1: "fields_fwd", 2: "composite", 3: "composite_bwd+adjoint", 4: "fields_bwd",
                5: "finalize", 8: "enc_prep", 9: "conv1", 10: "conv2", 11: "conv3", 12: "conv4_decoder",
@@ -52,25 +53,103 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed region.
+
+    Primary source: NVML (the library nvidia-smi reads) polled every 2 ms from a host thread, so even a
+    timed region of a few tens of milliseconds carries many samples; only samples taken inside
+    `window()` count.  Fallback when NVML cannot be opened: an `nvidia-smi --query-gpu ... -lms 50` process
+    started (and waited on until its first row) before the region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits that the run reports (hardware power brake is a form of hw_slowdown)
+    REASON_BITS = (("hw_slowdown", 0x8), ("hw_slowdown", 0x80), ("hw_thermal_slowdown", 0x40),
+                   ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
+    PERIOD_S = 0.002
 
-    def __init__(self, gpu_index: int):
-        self.idx, self.proc, self.f = gpu_index, None, None
+    def __init__(self, gpu_index: int, uuid: str | None = None, nvml=None):
+        self.idx, self.uuid, self.nvml = gpu_index, uuid, nvml
+        self.proc, self.f, self.thread, self.handle = None, None, None, None
+        self.samples, self.win, self.max_mhz = [], None, None
+        self._stop = None
+
+    # ---- NVML path
+    def _open_nvml(self):
+        import threading
+
+        nv = self.nvml
+        if nv is None:
+            import pynvml as nv
+        nv.nvmlInit()
+        h = None
+        if self.uuid:  # the CUDA device's own UUID: immune to CUDA_VISIBLE_DEVICES / ordering differences
+            try:
+                h = nv.nvmlDeviceGetHandleByUUID("GPU-" + self.uuid)
+            except Exception:
+                h = None
+        if h is None:
+            h = nv.nvmlDeviceGetHandleByIndex(self.idx)
+        self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        self.nvml, self.handle = nv, h
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    t = time.perf_counter()
+                    mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((t, float(mhz), int(rs)))
+                except Exception:
+                    break
+                self._stop.wait(self.PERIOD_S)
+
+        self.thread = threading.Thread(target=run, name="clock-sampler", daemon=True)
+        self.thread.start()
+
+    # ---- nvidia-smi fallback
+    def _open_smi(self):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                      "-i", str(self.idx), "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and self.proc.poll() is None:  # first row written before timing starts
+            if Path(self.f.name).stat().st_size > 0:
+                break
+            time.sleep(0.02)
 
     def __enter__(self):
         try:
-            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.idx), "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+            self._open_nvml()
         except Exception:
-            self.proc = None
+            self.thread = None
+            try:
+                self._open_smi()
+            except Exception:
+                self.proc = None
         return self
 
+    def window(self):
+        sampler = self
+
+        class _Win:
+            def __enter__(self):
+                sampler.win = [time.perf_counter(), None]
+
+            def __exit__(self, *a):
+                sampler.win[1] = time.perf_counter()
+
+        return _Win()
+
     def __exit__(self, *a):
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
         if self.proc is not None:
             time.sleep(0.06)
             self.proc.terminate()
@@ -80,6 +159,15 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        if self.thread is not None:
+            rows = list(self.samples)
+            if self.win and self.win[1] is not None:
+                inside = [r for r in rows if self.win[0] <= r[0] <= self.win[1]]
+                rows = inside or [r for r in rows if r[0] >= self.win[0]][:1]
+            reasons = {n for _, _, rs in rows for n, bit in self.REASON_BITS if rs & bit}
+            sm = [mhz for _, mhz, _ in rows]
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "nvml, 2 ms, inside the timed region"}
         if self.proc is None or self.f is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
         self.f.flush()
@@ -100,7 +188,7 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi -lms 50"}
 
 
 # ------------------------------------------------------------------------------------------ workloads
@@ -127,6 +215,7 @@ def _load_encoder(dev=None):
 
 class EncodeRenderWorkload:
     name = "encode_render"
+    metric, unit, scaling = METRIC, "images/s", "weak"
     H = W = 768
     SEEDS = list(range(100, 164))
 
@@ -180,11 +269,17 @@ class EncodeRenderWorkload:
     def io_bytes(self):
         return 3 * self.H * self.W * 4, 3 * self.H * self.W * 4
 
+    @classmethod
+    def describe(cls, wdesc):
+        """The workload both arms run (the reference arm's line carries the same keys)."""
+        return {"workload": "configs 2/3: 768x768 test cards (seeds 100-163), EfficientGaussianEncoder forward + "
+                            "render_alpha_octave(odds) of its splats, inference",
+                "images_per_step_per_gpu": 1, "encoder_weights": wdesc, "H": cls.H, "W": cls.W,
+                "splats_per_image": (cls.H // 8) ** 2 * 2 + (cls.H // 4) ** 2 * 2}
+
     def config(self):
-        return {"workload": "configs 2/3: 768x768 test cards (seeds 100-163), EfficientGaussianEncoder (bf16, "
-                            "tcgen05) + render_alpha_octave(odds) fp32, inference, one CUDA graph per step",
-                "images_per_step_per_gpu": 1, "encoder_weights": self.wdesc, "H": self.H, "W": self.W,
-                "splats_per_image": (self.H // 8) ** 2 * 2 + (self.H // 4) ** 2 * 2,
+        return {**self.describe(self.wdesc),
+                "implementation": "bf16 tcgen05 encoder + fp32 render, one CUDA graph per step",
                 "e2e_api": "pipeline.EncodeRenderStream: pinned host image -> H2D -> encode+render graph -> D2H "
                            "of the reconstruction, per image; two graph instances so the copies of "
                            "neighbouring images overlap the kernels",
@@ -217,6 +312,7 @@ class RenderWorkload:
     """Config 1: render_alpha_octave(odds) forward + L2 backward of one 768^2 image, 92,160 splats."""
 
     name = "render"
+    metric, unit, scaling = METRIC, "images/s", "weak"
     H = W = 768
     N = 92160
 
@@ -261,10 +357,13 @@ class RenderWorkload:
         d2h = sum(self.host[k].numel() * 4 for k in self.keys) + 4
         return h2d, d2h
 
-    def config(self):
+    @classmethod
+    def describe(cls, wdesc=None):
         return {"workload": "config 1: render_alpha_octave(odds=True) fwd + L2 bwd, 768x768, 92,160 splats (seed 1)",
-                "images_per_step_per_gpu": 1, "H": self.H, "W": self.W, "splats": self.N,
-                "l2": "flushed between timed steps (256 MB write, outside the timed events)"}
+                "images_per_step_per_gpu": 1, "H": cls.H, "W": cls.W, "splats": cls.N}
+
+    def config(self):
+        return {**self.describe(), "l2": "flushed between timed steps (256 MB write, outside the timed events)"}
 
     @classmethod
     def cpu_inputs(cls):
@@ -274,12 +373,9 @@ class RenderWorkload:
 
     @classmethod
     def cpu_step(cls, O, s):
-        """One step of the reference's algorithm on the host: forward, then backward of the L2 loss."""
-        out = O.render_alpha_octave(s["mu"], s["log_scale"], s["color"], s["opacity"], s["bg"], cls.H, cls.W,
-                                    theta=s["theta"], odds=True)
-        g = (2.0 / out.size) * (out - s["target"])
-        O.render_alpha_octave(s["mu"], s["log_scale"], s["color"], s["opacity"], s["bg"], cls.H, cls.W,
-                              theta=s["theta"], odds=True, grad_out=g)
+        """One step of the reference's algorithm on the host: forward, L2 loss, backward (forward run once)."""
+        O.render_alpha_octave_l2(s["mu"], s["log_scale"], s["color"], s["opacity"], s["bg"], cls.H, cls.W,
+                                 s["target"], theta=s["theta"], odds=True)
 
 
 def time_points(torch, dev, N=92160, P=3000, H=768, W=768, reps=20):
@@ -319,7 +415,9 @@ class FitWorkload:
     one CUDA graph replay (render fwd + bwd + all-reduce + Adam)."""
 
     name = "fit"
+    metric, unit, scaling = FIT_METRIC, "steps/s", "strong"
     H = W = 2048
+    KEYS = ("mu", "log_scale", "color", "opacity", "bg", "theta")
 
     def __init__(self, dev, rank=0, world=1):
         import torch
@@ -407,12 +505,56 @@ class FitWorkload:
     def io_bytes(self):
         return 0, 4
 
+    @classmethod
+    def describe(cls, wdesc, N=655360):
+        return {"workload": "config 4: 2048x2048 card (seed 4), 655,360 encoder-initialised splats, "
+                            "render_alpha_octave(odds) fwd + L2 bwd + Adam lr 1e-2 per step",
+                "splats": N, "H": cls.H, "W": cls.W, "encoder_weights": wdesc}
+
     def config(self):
-        return {"workload": "config 4: 2048x2048 card (seed 4), 655,360 encoder-initialised splats, render_alpha_octave"
-                            "(odds) fwd+bwd on a native-row band per rank, NCCL all-reduce of the splat gradients, "
-                            "fused Adam lr 1e-2; one CUDA graph per step", "splats": self.N, "H": self.H,
-                "W": self.W, "band_rows": list(self.band), "encoder_weights": self.wdesc,
+        return {**self.describe(self.wdesc, self.N),
+                "implementation": "render fwd+bwd on a native-row band per rank, NCCL all-reduce of the splat "
+                                  "gradients, fused Adam; one CUDA graph per step",
+                "band_rows": list(self.band),
                 "l2": "flushed between timed steps (256 MB write, outside the timed events)"}
+
+    @classmethod
+    def cpu_inputs(cls):
+        """Splats from the fp32 encoder oracle on the config-4 card, zeroed Adam moments."""
+        import numpy as np
+
+        from gaussian_2d_splat_encoder_b200 import synth
+        from oracle import encoder_oracle as E
+
+        sys.path.insert(0, str(ROOT / "tests"))
+        from enc_util import GOLDEN_CFG
+
+        m, desc = _load_encoder()
+        img = synth.card_for_config(4)
+        o = E.encode(m.state_dict(), GOLDEN_CFG, img)
+        p = {k: np.ascontiguousarray(o[k].detach().numpy(), dtype=np.float32) for k in cls.KEYS}
+        return dict(p=p, m={k: np.zeros_like(v) for k, v in p.items()}, v={k: np.zeros_like(v) for k, v in p.items()},
+                    t=0, target=np.ascontiguousarray(img.numpy(), dtype=np.float32), desc=desc)
+
+    @classmethod
+    def cpu_step(cls, O, s):
+        """One fitting step on the host: render forward, mse loss, backward, Adam (lr 1e-2, betas
+        (0.9, 0.999), eps 1e-8: torch.optim.Adam's update) on every render input."""
+        import numpy as np
+
+        p = s["p"]
+        _, _, _, g = O.render_alpha_octave_l2(p["mu"], p["log_scale"], p["color"], p["opacity"], p["bg"], cls.H,
+                                              cls.W, s["target"], theta=p["theta"], odds=True)
+        s["t"] += 1
+        b1, b2, lr, eps = 0.9, 0.999, 1e-2, 1e-8
+        c1, c2 = 1.0 - b1 ** s["t"], 1.0 - b2 ** s["t"]
+        for k in cls.KEYS:
+            m, v = s["m"][k], s["v"][k]
+            m *= b1
+            m += (1.0 - b1) * g[k]
+            v *= b2
+            v += (1.0 - b2) * g[k] * g[k]
+            p[k] -= (lr / c1) * m / (np.sqrt(v / c2) + eps)
 
     def release(self):
         self.graph = None
@@ -423,9 +565,10 @@ WORKLOADS = {"encode_render": EncodeRenderWorkload, "render": RenderWorkload, "f
 
 
 # ------------------------------------------------------------------------------------------ CPU side
-def cpu_baseline(workload_cls, steps: int, budget_s: float = 20.0):
+def cpu_baseline(workload_cls, steps: int, budget_s: float = 20.0, warmup: int = 1, warmup_budget_s: float = 60.0):
     """The reference's algorithm on the host cores (torch-CPU fp32 encoder + C oracle renderer, all
-    threads): images/s over a bounded sample of whole steps."""
+    threads): `warmup` untimed steps, then up to `steps` timed whole steps while the timed total stays
+    under `budget_s` (at least one).  Returns (the cpu_baseline dict, the inputs' weight description)."""
     import torch
 
     from oracle import oracle as O
@@ -436,6 +579,11 @@ def cpu_baseline(workload_cls, steps: int, budget_s: float = 20.0):
     torch.set_num_threads(n)
     O.set_threads(n)
     s = workload_cls.cpu_inputs()
+    t_w = time.perf_counter()
+    nw = 0
+    while nw < warmup and (nw == 0 or time.perf_counter() - t_w < warmup_budget_s):
+        workload_cls.cpu_step(O, s)
+        nw += 1
     times = []
     t_all = time.perf_counter()
     for _ in range(max(1, steps)):
@@ -445,10 +593,17 @@ def cpu_baseline(workload_cls, steps: int, budget_s: float = 20.0):
         if time.perf_counter() - t_all > budget_s:
             break
     per = statistics.mean(times)
-    return {"value": 1.0 / per, "unit": "images/s", "cores": O.num_threads(), "kind": "port",
-            "sample": f"{len(times)} whole {workload_cls.name} steps at 768x768 on the host: torch-CPU fp32 encoder "
-                      f"({torch.get_num_threads()} threads) + C oracle renderer ({O.num_threads()} OpenMP threads); "
-                      f"os.cpu_count()={os.cpu_count()}"}
+    res = workload_cls.H
+    what = {"encode_render": "encode + render steps (one image each)", "render": "render fwd+bwd steps (one image each)",
+            "fit": "fitting steps (render fwd + L2 bwd + Adam)"}[workload_cls.name]
+    parts = (f"torch-CPU fp32 encoder ({torch.get_num_threads()} threads) + " if workload_cls.name == "encode_render"
+             else "") + f"C oracle renderer ({O.num_threads()} OpenMP threads)"
+    r = {"value": 1.0 / per, "unit": workload_cls.unit, "cores": O.num_threads(), "kind": "port",
+         "sample": f"{len(times)} timed {what} at {res}x{res} after {nw} untimed, on the host: {parts}; "
+                   f"os.cpu_count()={os.cpu_count()}"}
+    if len(times) < steps:
+        r["sample"] += f"; {len(times)} of the {steps} requested steps fitted the {budget_s:.0f} s bound"
+    return r, s.get("desc") if isinstance(s, dict) else None
 
 
 # ------------------------------------------------------------------------------------------ GPU timing
@@ -535,12 +690,14 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        r = cpu_baseline(wcls, K, budget_s=150.0)
-        line = {"metric": METRIC, "value": r["value"], "unit": "images/s", "n_gpus": args.gpus, "steps": K,
-                "warmup": W, "ms_per_step": 1000.0 / r["value"], "higher_is_better": True, "scaling": "weak",
+        r, wdesc = cpu_baseline(wcls, K, budget_s=150.0, warmup=W)
+        line = {"metric": wcls.metric, "value": r["value"], "unit": wcls.unit, "n_gpus": args.gpus, "steps": K,
+                "warmup": W, "ms_per_step": 1000.0 / r["value"], "higher_is_better": True, "scaling": wcls.scaling,
                 "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
-                "config": {"workload": wcls.name}, "cpu_baseline": r,
-                "e2e": {"value": r["value"], "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                "config": {**wcls.describe(wdesc), "implementation": "host CPU: the reference's algorithm restated "
+                           "(oracle/), all host threads", "parallelism": "rank 0 only (host cores)"},
+                "cpu_baseline": r,
+                "e2e": {"value": r["value"], "unit": wcls.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
 
@@ -588,8 +745,15 @@ def main():
         return
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     idx = int(vis.split(",")[local]) if vis else local
-    with ClockSampler(idx) as clk:
-        step_ms = time_steps(torch, wl, K, flush)
+    try:
+        import uuid as _uuid
+
+        uuid = str(_uuid.UUID(bytes=bytes(torch.cuda.get_device_properties(dev).uuid.bytes)))
+    except Exception:
+        uuid = None
+    with ClockSampler(idx, uuid) as clk:
+        with clk.window():
+            step_ms = time_steps(torch, wl, K, flush)
     launches = per_replay * K
     tot_ms = max_over_ranks(sum(step_ms))
     barrier()
@@ -673,8 +837,7 @@ def main():
             line["render_fwd_bwd_ms_per_image"] = tot_ms / K
             pairs = count_pairs(torch, lib, dev, wl.dev_in, wl.H, wl.W)
         else:
-            line.update(unit="steps/s", scaling="strong", dtype="fp32",
-                        metric="config 4: 2048^2 fitting step (render fwd+bwd + NCCL all-reduce + Adam) steps/s")
+            line.update(unit=wcls.unit, scaling=wcls.scaling, dtype="fp32", metric=wcls.metric)
             line["value"] = K / (tot_ms / 1000.0)
             line["e2e"]["value"] = Ke / (e2e_ms / 1000.0)
             line["e2e"]["unit"] = "steps/s"
@@ -689,7 +852,7 @@ def main():
                             "peak_source": f"148 SMs x 128 FP32 lanes x {f_mhz:.0f} MHz (median SM clock sampled "
                                            "during the timed region)"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the host baseline is an N = 1 figure
-        line["cpu_baseline"] = cpu_baseline(wcls, 3)
+        line["cpu_baseline"] = cpu_baseline(wcls, 3)[0]
     if rank == 0:
         print(json.dumps(line), flush=True)
     if hasattr(wl, "release"):

@@ -33,6 +33,13 @@ def synth_card(H: int, W: int, n_shapes: int = 40, n_strokes: int = 20, seed: in
         t = (t - t.min()) / max(t.max() - t.min(), 1e-12)
         img += (1.0 - t)[..., None] * c0 + t[..., None] * c1
     img /= 3.0
+    def box(ylo, yhi, xlo, xhi):
+        # pixel-centre window that holds every pixel a shape can cover (2 px margin); the per-pixel
+        # tests below run on that window only and give the same mask as over the whole image
+        r0, r1 = max(0, int(math.floor(ylo)) - 2), min(H, int(math.ceil(yhi)) + 2)
+        c0, c1 = max(0, int(math.floor(xlo)) - 2), min(W, int(math.ceil(xhi)) + 2)
+        return (slice(r0, max(r0, r1)), slice(c0, max(c0, c1)))
+
     for _ in range(n_shapes):
         kind = int(rng.integers(2))
         hh = rng.uniform(0.02, 0.25) * H
@@ -40,11 +47,13 @@ def synth_card(H: int, W: int, n_shapes: int = 40, n_strokes: int = 20, seed: in
         cy = rng.uniform(0.0, H)
         cx = rng.uniform(0.0, W)
         col = rng.uniform(size=3)
+        win = box(cy - hh / 2, cy + hh / 2, cx - ww / 2, cx + ww / 2)
+        y, x = yy[win], xx[win]
         if kind == 0:
-            m = (np.abs(yy - cy) <= hh / 2) & (np.abs(xx - cx) <= ww / 2)
+            m = (np.abs(y - cy) <= hh / 2) & (np.abs(x - cx) <= ww / 2)
         else:
-            m = ((yy - cy) / (hh / 2)) ** 2 + ((xx - cx) / (ww / 2)) ** 2 <= 1.0
-        img[m] = col
+            m = ((y - cy) / (hh / 2)) ** 2 + ((x - cx) / (ww / 2)) ** 2 <= 1.0
+        img[win][m] = col
     for _ in range(n_strokes):
         y0, y1 = rng.uniform(0.0, H, size=2)
         x0, x1 = rng.uniform(0.0, W, size=2)
@@ -52,9 +61,21 @@ def synth_card(H: int, W: int, n_shapes: int = 40, n_strokes: int = 20, seed: in
         col = rng.uniform(size=3)
         dy, dx = y1 - y0, x1 - x0
         L2 = max(dy * dy + dx * dx, 1e-12)
-        t = np.clip(((yy - y0) * dy + (xx - x0) * dx) / L2, 0.0, 1.0)
-        d2 = (yy - (y0 + t * dy)) ** 2 + (xx - (x0 + t * dx)) ** 2
-        img[d2 <= (width / 2.0) ** 2] = col
+        r = width / 2.0
+        # bands of 32 rows, each narrowed to the columns the segment (widened by r) can reach there
+        for ya in range(max(0, int(min(y0, y1) - r) - 2), min(H, int(max(y0, y1) + r) + 3), 32):
+            yb = ya + 32
+            if abs(dy) > 1e-9:
+                ta = min(max((ya - r - 2 - y0) / dy, 0.0), 1.0)
+                tb = min(max((yb + r + 2 - y0) / dy, 0.0), 1.0)
+                xa, xb = x0 + ta * dx, x0 + tb * dx
+            else:
+                xa, xb = x0, x1
+            win = box(ya + 2, yb - 2, min(xa, xb) - r, max(xa, xb) + r)
+            y, x = yy[win], xx[win]
+            t = np.clip(((y - y0) * dy + (x - x0) * dx) / L2, 0.0, 1.0)
+            d2 = (y - (y0 + t * dy)) ** 2 + (x - (x0 + t * dx)) ** 2
+            img[win][d2 <= r ** 2] = col
     img = np.clip(img, 0.0, 1.0).astype(np.float32)
     return torch.from_numpy(np.ascontiguousarray(img.transpose(2, 0, 1)))[None]
 

@@ -466,8 +466,10 @@ static int render_groups(int mode, int B, int N, int C, const float *mu, const f
                          const float *op, const float *bg, const float *th, int H, int W, float cutoff, int TILE,
                          float base_texels, int max_octaves, int n_coarse, int coarse_factor, long max_pairs,
                          int odds, float *out, const float *gC, float *gmu, float *gls, float *gcol, float *gop,
-                         float *gbg, float *gth) {
+                         float *gbg, float *gth, const float *l2_target, float l2_scale, float *l2_grad,
+                         double *l2_loss) {
     int P = H * W, has_th = th != NULL;
+    if (l2_target) gC = l2_grad;
     float *sc = (float *)malloc(sizeof(float) * (size_t)B * N * 2);
     orc_activate_scale(ls, sc, (long)B * N * 2);
     if (gC) {
@@ -537,6 +539,17 @@ static int render_groups(int mode, int B, int N, int C, const float *mu, const f
         }
         if (!status) {
             composite_fwd(P, C, slog, sa, sac, bg + (size_t)b * C, out + (size_t)b * C * P);
+            if (l2_target) { /* the fitting loss l2_scale * sum (out - target)^2 and its gradient */
+                const float *ob = out + (size_t)b * C * P, *tb = l2_target + (size_t)b * C * P;
+                float *gb = l2_grad + (size_t)b * C * P;
+                double acc = 0.0;
+                for (long i = 0; i < (long)C * P; i++) {
+                    float d = ob[i] - tb[i];
+                    gb[i] = 2.0f * l2_scale * d;
+                    acc += (double)d * d;
+                }
+                *l2_loss += (double)l2_scale * acc;
+            }
             if (gC) {
                 float *dslog = (float *)malloc(sizeof(float) * P), *dsa = (float *)malloc(sizeof(float) * P);
                 float *dsac = (float *)malloc(sizeof(float) * (size_t)P * C);
@@ -580,7 +593,20 @@ int orc_render_octave(int B, int N, int C, const float *mu, const float *ls, con
                       int max_octaves, long max_pairs, int odds, float *out, const float *gC, float *gmu, float *gls,
                       float *gcol, float *gop, float *gbg, float *gth) {
     return render_groups(0, B, N, C, mu, ls, col, op, bg, th, H, W, cutoff, TILE, base_texels, max_octaves, 0, 0,
-                         max_pairs, odds, out, gC, gmu, gls, gcol, gop, gbg, gth);
+                         max_pairs, odds, out, gC, gmu, gls, gcol, gop, gbg, gth, NULL, 0.0f, NULL, NULL);
+}
+
+/* One fitting step's render: forward, loss = scale * sum (out - target)^2 (scale = 1/out.numel() is
+ * mse_loss), its gradient into gC_out, and the backward of that gradient -- the forward runs once, as
+ * in the reference's autograd (render_triton.py:935-980 forward, its Function's backward). */
+int orc_render_octave_l2(int B, int N, int C, const float *mu, const float *ls, const float *col, const float *op,
+                         const float *bg, const float *th, int H, int W, float cutoff, int TILE, float base_texels,
+                         int max_octaves, long max_pairs, int odds, const float *target, float scale, float *out,
+                         float *gC_out, double *loss, float *gmu, float *gls, float *gcol, float *gop, float *gbg,
+                         float *gth) {
+    *loss = 0.0;
+    return render_groups(0, B, N, C, mu, ls, col, op, bg, th, H, W, cutoff, TILE, base_texels, max_octaves, 0, 0,
+                         max_pairs, odds, out, NULL, gmu, gls, gcol, gop, gbg, gth, target, scale, gC_out, loss);
 }
 
 int orc_render_multires(int B, int N, int C, const float *mu, const float *ls, const float *col, const float *op,
@@ -588,7 +614,7 @@ int orc_render_multires(int B, int N, int C, const float *mu, const float *ls, c
                         int TILE, long max_pairs, int odds, float *out, const float *gC, float *gmu, float *gls,
                         float *gcol, float *gop, float *gbg, float *gth) {
     return render_groups(1, B, N, C, mu, ls, col, op, bg, th, H, W, cutoff, TILE, 0.0f, 0, n_coarse, coarse_factor,
-                         max_pairs, odds, out, gC, gmu, gls, gcol, gop, gbg, gth);
+                         max_pairs, odds, out, gC, gmu, gls, gcol, gop, gbg, gth, NULL, 0.0f, NULL, NULL);
 }
 
 /* render_alpha_full_triton(cull=True): one group at (H,W), composite inside the kernel; the backward

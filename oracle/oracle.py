@@ -46,6 +46,8 @@ def lib():
         p = C.c_void_p
         L = C.c_long
         _lib.orc_render_octave.argtypes = [i, i, i, p, p, p, p, p, p, i, i, f, i, f, i, L, i, p, p, p, p, p, p, p, p]
+        _lib.orc_render_octave_l2.argtypes = [i, i, i, p, p, p, p, p, p, i, i, f, i, f, i, L, i, p, f, p, p, p,
+                                              p, p, p, p, p, p]
         _lib.orc_render_multires.argtypes = [i, i, i, p, p, p, p, p, p, i, i, i, i, f, i, L, i, p, p, p, p, p, p, p, p]
         _lib.orc_render_cull.argtypes = [i, i, i, p, p, p, p, p, p, i, i, i, f, i, p, p, p, p, p, p, p, p]
         _lib.orc_render_exact.argtypes = [i, i, i, p, p, p, p, p, p, i, i, p, p, p, p, p, p, p, p]
@@ -109,6 +111,31 @@ def render_alpha_octave(mu, log_scale, color, opacity, bg, H, W, theta=None, cut
     mp = -1 if max_pairs is None else int(max_pairs)
     return _run("octave", mu, log_scale, color, opacity, bg, H, W, theta, grad_out,
                 [float(cutoff), int(TILE), float(base_texels), int(max_octaves), mp, int(bool(odds))])
+
+
+def render_alpha_octave_l2(mu, log_scale, color, opacity, bg, H, W, target, theta=None, scale=None, cutoff=3.0,
+                           TILE=8, base_texels=8.0, max_octaves=6, max_pairs=48_000_000, odds=False):
+    """One fitting step's render: render_alpha_octave forward (render_triton.py:935-980), the loss
+    scale * sum (out - target)^2 (scale defaults to 1/out.size: mse_loss) and the backward of that loss,
+    with the forward run once.  Returns (out, loss, grad_out, grads)."""
+    mu, ls, col, op, bg, th, tg = map(_f32, (mu, log_scale, color, opacity, bg, theta, target))
+    B, N, Cc = col.shape
+    out = np.empty((B, Cc, H, W), np.float32)
+    if tg.shape != out.shape:
+        raise ValueError(f"target shape {tg.shape} != {out.shape}")
+    g = np.empty_like(out)
+    sc = np.float32(1.0 / out.size if scale is None else scale)
+    grads = dict(mu=np.empty_like(mu), log_scale=np.empty_like(ls), color=np.empty_like(col),
+                 opacity=np.empty_like(op), bg=np.empty_like(bg), theta=np.empty_like(th) if th is not None else None)
+    loss = C.c_double(0.0)
+    mp = -1 if max_pairs is None else int(max_pairs)
+    st = lib().orc_render_octave_l2(B, N, Cc, _ptr(mu), _ptr(ls), _ptr(col), _ptr(op), _ptr(bg), _ptr(th), H, W,
+                                    float(cutoff), int(TILE), float(base_texels), int(max_octaves), mp,
+                                    int(bool(odds)), _ptr(tg), float(sc), _ptr(out), _ptr(g), C.byref(loss),
+                                    *[_ptr(grads[k]) for k in ("mu", "log_scale", "color", "opacity", "bg", "theta")])
+    if st == 1:
+        raise OracleBudgetExceeded(f"oracle: a (tile, splat) pair count exceeds max_pairs @ {H}x{W}")
+    return out, float(loss.value), g, grads
 
 
 def render_alpha_multires(mu, log_scale, color, opacity, bg, H, W, theta=None, n_coarse=None,

@@ -1,0 +1,84 @@
+"""Host-side pieces of bench.py that need no GPU: the clock sampler's windowing and reason decoding
+(against a fake NVML), and the JSON contract keys of the reference arm's line."""
+
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+
+class FakeNVML:
+    NVML_CLOCK_SM = 1
+
+    def __init__(self, reasons_after=None):
+        self.t0 = None
+        self.reasons_after = reasons_after
+        self.closed = False
+
+    def nvmlInit(self):
+        self.t0 = time.perf_counter()
+
+    def nvmlShutdown(self):
+        self.closed = True
+
+    def nvmlDeviceGetHandleByUUID(self, u):
+        assert u.startswith("GPU-")
+        return "h"
+
+    def nvmlDeviceGetHandleByIndex(self, i):
+        return "h"
+
+    def nvmlDeviceGetMaxClockInfo(self, h, kind):
+        return 1965
+
+    def nvmlDeviceGetClockInfo(self, h, kind):
+        return 1965 if self.reasons_after is None else 1800
+
+    def nvmlDeviceGetCurrentClocksEventReasons(self, h):
+        return 0x4 | 0x40 if self.reasons_after is not None else 0
+
+
+def test_clock_sampler_window_and_reasons():
+    import bench
+
+    nv = FakeNVML()
+    with bench.ClockSampler(0, "0123", nvml=nv) as clk:
+        time.sleep(0.02)  # idle samples before the region are not counted
+        with clk.window():
+            time.sleep(0.05)
+        time.sleep(0.02)
+    s = clk.summary()
+    assert nv.closed
+    assert s["sm_mhz"] == 1965 and s["sm_max_mhz"] == 1965 and s["reasons"] == []
+    assert 3 <= s["samples"] < len(clk.samples)
+    assert all(clk.win[0] <= t <= clk.win[1] for t, _, _ in clk.samples[:0])
+
+    nv = FakeNVML(reasons_after=0)
+    with bench.ClockSampler(0, None, nvml=nv) as clk:
+        with clk.window():
+            time.sleep(0.03)
+    s = clk.summary()
+    assert s["sm_mhz"] == 1800 and s["reasons"] == ["hw_thermal_slowdown", "sw_power_cap"]
+
+
+def test_clock_sampler_without_nvml_or_smi(monkeypatch):
+    """No NVML and no nvidia-smi: the summary says so instead of raising."""
+    import subprocess
+
+    import bench
+
+    class Broken(FakeNVML):
+        def nvmlInit(self):
+            raise RuntimeError("no driver")
+
+    def no_smi(*a, **k):
+        raise FileNotFoundError("nvidia-smi")
+
+    monkeypatch.setattr(subprocess, "Popen", no_smi)
+    with bench.ClockSampler(0, None, nvml=Broken()) as clk:
+        with clk.window():
+            pass
+    s = clk.summary()
+    assert s["samples"] == 0 and s["sm_mhz"] is None

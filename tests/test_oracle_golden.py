@@ -78,3 +78,25 @@ def test_oracle_upsample_adjoint_is_transpose(oracle):
         L.orc_upsample_adjoint_add(y.ctypes.data, ho, wo, 1, aty.ctypes.data, hi, wi)
         a, b = float((ux * y).sum(dtype=np.float64)), float((x * aty).sum(dtype=np.float64))
         assert abs(a - b) <= 1e-4 * max(1.0, abs(a))
+
+
+def test_oracle_l2_step_matches_two_calls(oracle):
+    """render_alpha_octave_l2 (forward once, mse gradient, backward) gives the same image and loss gradient,
+    bit for bit, and the same splat gradients (up to the order of the oracle's threaded accumulation) as a
+    forward followed by a backward call with that gradient."""
+    from gaussian_2d_splat_encoder_b200 import synth
+
+    s = {k: v.numpy() for k, v in synth.synth_splats_cfg1(600, 64, 96, seed=3).items()}
+    tgt = np.random.default_rng(5).random((1, 3, 64, 96), dtype=np.float32)
+    out, loss, g, grads = oracle.render_alpha_octave_l2(s["mu"], s["log_scale"], s["color"], s["opacity"],
+                                                         s["bg"], 64, 96, tgt, theta=s["theta"], odds=True)
+    ref = oracle.render_alpha_octave(s["mu"], s["log_scale"], s["color"], s["opacity"], s["bg"], 64, 96,
+                                     theta=s["theta"], odds=True)
+    assert np.array_equal(out, ref)
+    g_ref = (2.0 / ref.size) * (ref - tgt)
+    assert np.array_equal(g, g_ref)
+    assert abs(loss - float(np.mean((ref.astype(np.float64) - tgt) ** 2))) < 1e-9
+    _, grads_ref = oracle.render_alpha_octave(s["mu"], s["log_scale"], s["color"], s["opacity"], s["bg"], 64, 96,
+                                              theta=s["theta"], odds=True, grad_out=g_ref)
+    for k in grads_ref:
+        np.testing.assert_allclose(grads[k], grads_ref[k], rtol=1e-5, atol=1e-9, err_msg=k)
