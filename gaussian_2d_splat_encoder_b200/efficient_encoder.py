@@ -191,6 +191,92 @@ def pack_conv(w: torch.Tensor) -> torch.Tensor:
     return w.permute(0, 2, 3, 1).reshape(w.shape[0], -1)
 
 
+def make_desc(fields: dict, B: int, H: int, W: int) -> _GsEncoderDesc:
+    d = _GsEncoderDesc()
+    d.B, d.H, d.W = B, H, W
+    for k, v in fields.items():
+        setattr(d, k, v)
+    return d
+
+
+def _weight_struct(t: dict) -> _GsEncoderWeights:
+    return _GsEncoderWeights(**{k: t[k].data_ptr() for k in _WEIGHT_FIELDS})
+
+
+def pack_weights(enc, device) -> dict:
+    """The encoder's parameters in the layouts gs_encoder_fwd reads: bf16 implicit-GEMM weights
+    ([Co, taps*Ci], tap-major; the first layer as its 4x4 space-to-depth equivalent), fp32 biases,
+    GroupNorm affines, the background linear layer and the two heads' packed 1x1 weights."""
+    bb = enc.backbone
+    blk = enc.fine_decoder.blocks[0].fuse
+
+    def f32(t):
+        return t.detach().to(device, torch.float32).contiguous()
+
+    def b16(t):
+        return t.detach().to(device, torch.float32).to(torch.bfloat16).contiguous()
+
+    hc_w, hc_b = enc.coarse_head.packed()
+    hf_w, hf_b = enc.fine_head.packed()
+    return dict(
+        w1=b16(pack_first_layer(bb.stage_s2[0].weight.float())), w2=b16(pack_conv(bb.stage_s4[0].weight)),
+        w3=b16(pack_conv(bb.stage_s8[0].weight)), w4=b16(pack_conv(blk[0].weight)),
+        b1=f32(bb.stage_s2[0].bias), b2=f32(bb.stage_s4[0].bias), b3=f32(bb.stage_s8[0].bias), b4=f32(blk[0].bias),
+        gn1_w=f32(bb.stage_s2[2].weight), gn1_b=f32(bb.stage_s2[2].bias),
+        gn2_w=f32(bb.stage_s4[2].weight), gn2_b=f32(bb.stage_s4[2].bias),
+        gn3_w=f32(bb.stage_s8[2].weight), gn3_b=f32(bb.stage_s8[2].bias),
+        gn4_w=f32(blk[2].weight), gn4_b=f32(blk[2].bias),
+        bg_w=f32(enc.bg_head.weight), bg_b=f32(enc.bg_head.bias),
+        hc_w=f32(hc_w), hc_b=f32(hc_b), hf_w=f32(hf_w), hf_b=f32(hf_b))
+
+
+def cuda_forward(enc, image, return_latents, render):
+    """gs_encoder_fwd / gs_encode_render_fwd for any object that provides the packed weights
+    (`_weights(device)` -> (tensors, _GsEncoderWeights)), `_desc(B, H, W)` and the attributes M, Mf,
+    d_feature, use_rotation and latent_ch: the nn.Module and the pre-packed checkpoint share it."""
+    dev = _lib.require_cuda(image)
+    if image.dim() != 4 or image.shape[1] != 3:
+        raise ValueError("image must be [B,3,H,W]")
+    B, _, H, W = image.shape
+    if H % 8 or W % 8 or ((H // 4) * (W // 4)) % 64:
+        raise NotImplementedError(f"image size {H}x{W}: the CUDA encoder needs H, W multiples of 8 and "
+                                  "(H/4)(W/4) a multiple of 64")
+    x = image.detach().contiguous().float()
+    with torch.cuda.device(dev):
+        L = _lib.load()
+        tens, wst = enc._weights(dev)
+        d = enc._desc(B, H, W)
+        size_fn = L.gs_encode_render_workspace_size if render else L.gs_encoder_workspace_size
+        nbytes = int(size_fn(C.byref(d)))
+        if nbytes == 0:
+            raise ValueError("unsupported encoder configuration")
+        Nc = (H // 8) * (W // 8) * enc.M
+        N = Nc + (H // 4) * (W // 4) * enc.Mf
+        o = dict(mu=torch.empty(B, N, 2, device=dev), log_scale=torch.empty(B, N, 2, device=dev),
+                 color=torch.empty(B, N, 3, device=dev), opacity=torch.empty(B, N, device=dev),
+                 theta=torch.empty(B, N, device=dev) if enc.use_rotation else None,
+                 bg=torch.empty(B, 3, device=dev))
+        feat = torch.empty(B, H // 8, W // 8, enc.d_feature, device=dev)
+        lat = torch.empty(B, H // 4, W // 4, enc.latent_ch, device=dev) if return_latents else None
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        p = _lib.ptr
+        args = [C.byref(d), C.byref(wst), p(x), p(o["mu"]), p(o["log_scale"]), p(o["color"]), p(o["opacity"]),
+                p(o["theta"]), p(o["bg"]), p(feat), p(lat)]
+        rec = None
+        if render:
+            rec = torch.empty(B, 3, H, W, device=dev)
+            _lib.check(L.gs_encode_render_fwd(*args, p(rec), p(ws), nbytes, _lib.stream_of(dev)),
+                       "gs_encode_render_fwd")
+        else:
+            _lib.check(L.gs_encoder_fwd(*args, p(ws), nbytes, _lib.stream_of(dev)), "gs_encoder_fwd")
+    o["n_gaussians"] = N
+    o["n_coarse"] = Nc
+    o["backbone_features"] = feat.permute(0, 3, 1, 2)
+    if return_latents:
+        o["splat_features"] = lat.permute(0, 3, 1, 2)
+    return o, rec
+
+
 class EfficientGaussianEncoder(nn.Module):
     def __init__(self, d_feature=128, stride=8, variant="free", norm_type="group",
                  use_rotation=True, use_grad_input=True,
@@ -244,42 +330,25 @@ class EfficientGaussianEncoder(nn.Module):
         key = (device, tuple((p.data_ptr(), p._version) for p in self.parameters()))
         if self._packed is not None and self._packed_key == key:
             return self._packed
-        bb = self.backbone
-        blk = self.fine_decoder.blocks[0].fuse
-        dev = device
-
-        def f32(t):
-            return t.detach().to(dev, torch.float32).contiguous()
-
-        def b16(t):
-            return t.detach().to(dev, torch.float32).to(torch.bfloat16).contiguous()
-
-        hc_w, hc_b = self.coarse_head.packed()
-        hf_w, hf_b = self.fine_head.packed()
-        t = dict(
-            w1=b16(pack_first_layer(bb.stage_s2[0].weight.float())), w2=b16(pack_conv(bb.stage_s4[0].weight)),
-            w3=b16(pack_conv(bb.stage_s8[0].weight)), w4=b16(pack_conv(blk[0].weight)),
-            b1=f32(bb.stage_s2[0].bias), b2=f32(bb.stage_s4[0].bias), b3=f32(bb.stage_s8[0].bias), b4=f32(blk[0].bias),
-            gn1_w=f32(bb.stage_s2[2].weight), gn1_b=f32(bb.stage_s2[2].bias),
-            gn2_w=f32(bb.stage_s4[2].weight), gn2_b=f32(bb.stage_s4[2].bias),
-            gn3_w=f32(bb.stage_s8[2].weight), gn3_b=f32(bb.stage_s8[2].bias),
-            gn4_w=f32(blk[2].weight), gn4_b=f32(blk[2].bias),
-            bg_w=f32(self.bg_head.weight), bg_b=f32(self.bg_head.bias),
-            hc_w=f32(hc_w), hc_b=f32(hc_b), hf_w=f32(hf_w), hf_b=f32(hf_b))
-        st = _GsEncoderWeights(**{k: t[k].data_ptr() for k in _WEIGHT_FIELDS})
-        self._packed = (t, st)
+        t = pack_weights(self, device)
+        self._packed = (t, _weight_struct(t))
         self._packed_key = key
         return self._packed
 
+    @property
+    def latent_ch(self):
+        return self.fine_decoder.out_ch
+
+    def desc_fields(self):
+        """The architecture fields of gs_encoder_desc (everything but the batch and image size)."""
+        return dict(d=int(self.d_feature), M=int(self.M), Mf=int(self.Mf), residual_grid=int(self.residual_grid),
+                    odds=int(bool(self.odds)), use_rotation=int(self.use_rotation),
+                    coarse_ls_floor=self.coarse_ls_floor if self.coarse_ls_floor is not None else -float("inf"),
+                    coarse_offset=float(self.coarse_head.offset_cells), fine_offset=float(self.fine_head.offset_cells),
+                    coarse_min_opacity=float(self.coarse_head.min_opacity))
+
     def _desc(self, B, H, W):
-        d = _GsEncoderDesc()
-        d.B, d.H, d.W, d.d, d.M, d.Mf = B, H, W, self.d_feature, self.M, self.Mf
-        d.residual_grid, d.odds, d.use_rotation = int(self.residual_grid), int(bool(self.odds)), int(self.use_rotation)
-        d.coarse_ls_floor = self.coarse_ls_floor if self.coarse_ls_floor is not None else -float("inf")
-        d.coarse_offset = float(self.coarse_head.offset_cells)
-        d.fine_offset = float(self.fine_head.offset_cells)
-        d.coarse_min_opacity = float(self.coarse_head.min_opacity)
-        return d
+        return make_desc(self.desc_fields(), B, H, W)
 
     def _bg(self, feat):
         return torch.sigmoid(self.bg_head(feat.mean(dim=(2, 3))))
@@ -317,44 +386,4 @@ class EfficientGaussianEncoder(nn.Module):
         if not self._cuda_supported():
             raise NotImplementedError("the CUDA encoder implements the released 'adaptive' architecture "
                                       "(d_feature=256, stride 8, fine_stride 4, GroupNorm, gradient input)")
-        dev = _lib.require_cuda(image)
-        if image.dim() != 4 or image.shape[1] != 3:
-            raise ValueError("image must be [B,3,H,W]")
-        B, _, H, W = image.shape
-        if H % 8 or W % 8 or ((H // 4) * (W // 4)) % 64:
-            raise NotImplementedError(f"image size {H}x{W}: the CUDA encoder needs H, W multiples of 8 and "
-                                      "(H/4)(W/4) a multiple of 64")
-        x = image.detach().contiguous().float()
-        with torch.cuda.device(dev):
-            L = _lib.load()
-            tens, wst = self._weights(dev)
-            d = self._desc(B, H, W)
-            size_fn = L.gs_encode_render_workspace_size if render else L.gs_encoder_workspace_size
-            nbytes = int(size_fn(C.byref(d)))
-            if nbytes == 0:
-                raise ValueError("unsupported encoder configuration")
-            Nc = (H // 8) * (W // 8) * self.M
-            N = Nc + (H // 4) * (W // 4) * self.Mf
-            o = dict(mu=torch.empty(B, N, 2, device=dev), log_scale=torch.empty(B, N, 2, device=dev),
-                     color=torch.empty(B, N, 3, device=dev), opacity=torch.empty(B, N, device=dev),
-                     theta=torch.empty(B, N, device=dev) if self.use_rotation else None,
-                     bg=torch.empty(B, 3, device=dev))
-            feat = torch.empty(B, H // 8, W // 8, self.d_feature, device=dev)
-            lat = torch.empty(B, H // 4, W // 4, self.fine_decoder.out_ch, device=dev) if return_latents else None
-            ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-            p = _lib.ptr
-            args = [C.byref(d), C.byref(wst), p(x), p(o["mu"]), p(o["log_scale"]), p(o["color"]), p(o["opacity"]),
-                    p(o["theta"]), p(o["bg"]), p(feat), p(lat)]
-            rec = None
-            if render:
-                rec = torch.empty(B, 3, H, W, device=dev)
-                _lib.check(L.gs_encode_render_fwd(*args, p(rec), p(ws), nbytes, _lib.stream_of(dev)),
-                           "gs_encode_render_fwd")
-            else:
-                _lib.check(L.gs_encoder_fwd(*args, p(ws), nbytes, _lib.stream_of(dev)), "gs_encoder_fwd")
-        o["n_gaussians"] = N
-        o["n_coarse"] = Nc
-        o["backbone_features"] = feat.permute(0, 3, 1, 2)
-        if return_latents:
-            o["splat_features"] = lat.permute(0, 3, 1, 2)
-        return o, rec
+        return cuda_forward(self, image, return_latents, render)

@@ -114,3 +114,30 @@ def test_return_latents_and_gather(lib):
     lat = m.gather_splat_latents(o)
     assert lat.shape == (1, o["n_gaussians"], 128)
     assert float(lat[:, :o["n_coarse"]].abs().max()) == 0.0
+
+
+def test_packed_checkpoint_matches_module(lib, tmp_path):
+    """load_packed(save_packed(module)) runs the same kernels on the same packed weights: forward (with
+    latents) and forward_and_render agree with the module's to the run-to-run spread of the GroupNorm
+    statistics' atomics (1e-6)."""
+    from gaussian_2d_splat_encoder_b200 import checkpoint as ck
+    from gaussian_2d_splat_encoder_b200.efficient_encoder import EfficientGaussianEncoder
+
+    torch.manual_seed(0)
+    m = EfficientGaussianEncoder(**GOLDEN_CFG).eval()
+    ck.save_packed(m, tmp_path / "enc.packed")
+    pe = ck.load_packed(tmp_path / "enc.packed")
+    m = m.cuda()
+    x = torch.from_numpy(np.load(GOLDEN / "encoder_cfg0.npz")["image"]).cuda()
+    with torch.no_grad():
+        a = m(x, return_latents=True)
+        b = pe(x, return_latents=True)
+        ar, rr = m.forward_and_render(x)
+        br, pr = pe.forward_and_render(x)
+    torch.cuda.synchronize()
+    for k in ("mu", "log_scale", "color", "opacity", "theta", "bg", "backbone_features", "splat_features"):
+        assert float((a[k] - b[k]).abs().max()) <= 1e-6, k
+        assert float((ar[k] - br[k]).abs().max()) <= 1e-6 if k in ar else True, k
+    assert (a["n_gaussians"], a["n_coarse"]) == (b["n_gaussians"], b["n_coarse"])
+    assert float((rr - pr).abs().max()) <= 1e-6
+    assert pe.gather_splat_latents(b).shape == m.gather_splat_latents(a).shape
