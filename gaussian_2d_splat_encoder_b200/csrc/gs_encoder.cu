@@ -23,6 +23,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "../../include/gsplat_b200.h"
 #include "gs_conv.cuh"
@@ -661,6 +662,58 @@ int enc_plan(const gs_encoder_desc *e, EncPlan &p) {
 template <typename T>
 T *W(void *ws, size_t off) { return reinterpret_cast<T *>(reinterpret_cast<char *>(ws) + off); }
 
+// A second stream per (host thread, device) for the fine decoder, which needs only the backbone: it runs
+// while the internal coarse render -- a latency-bound chain that keeps a fraction of the SMs busy --
+// proceeds on the caller's stream.  Fork and join are event edges, so a CUDA graph capture of the
+// caller's stream records the two branches as parallel graph nodes.  Per thread, so concurrent callers
+// never re-record each other's events.
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+// *out stays NULL (the caller runs both branches on its own stream) when the side stream does not exist
+// yet and `main` is being captured: the stream and events are only ever created outside a capture.
+int side_stream(cudaStream_t main, SideStream **out) {
+    static thread_local std::vector<SideStream> per_dev;  // index: device ordinal (never destroyed)
+    *out = nullptr;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return GS_ERR_CUDA;
+    if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1);
+    SideStream &ss = per_dev[dev];
+    if (!ss.s) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(main, &cs) != cudaSuccess) return GS_ERR_CUDA;
+        if (cs != cudaStreamCaptureStatusNone) return GS_OK;
+        if (cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking) != cudaSuccess) return GS_ERR_CUDA;
+        if (cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess) return GS_ERR_CUDA;
+        if (cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess) return GS_ERR_CUDA;
+    }
+    *out = &ss;
+    return GS_OK;
+}
+
+// Forks `side` from `main` on construction; joins it back (once) on join() or on scope exit, so an early
+// error return never leaves a capture with an unjoined branch.
+struct Fork {
+    SideStream *ss;
+    cudaStream_t main;
+    bool joined = false;
+    Fork(SideStream *x, cudaStream_t m) : ss(x), main(m) {
+        if (!ss) return;
+        cudaEventRecord(ss->fork, main);
+        cudaStreamWaitEvent(ss->s, ss->fork, 0);
+    }
+    cudaStream_t side() const { return ss ? ss->s : main; }
+    void join() {
+        if (joined || !ss) return;
+        cudaEventRecord(ss->join, ss->s);
+        cudaStreamWaitEvent(main, ss->join, 0);
+        joined = true;
+    }
+    ~Fork() { join(); }
+};
+
 }  // namespace
 
 extern "C" size_t gs_encoder_workspace_size(const gs_encoder_desc *e) {
@@ -739,6 +792,28 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     float2 *gtab = W<float2>(ws, p.o_gtab);
     k_bg<<<B, 256, 0, s>>>(chsum, GN_BG_BLOCKS, 256, (long long)p.H8 * p.W8, w->bg_w, w->bg_b,
                            gn3_fly ? gn3 : nullptr, w->gn3_w, w->gn3_b, gtab, bg);
+    // fork: the fine decoder (5.) on the side stream, the coarse head and render (3., 4.) on the caller's.
+    // With stage profiling on, both run on the caller's stream so each stage's events time its own kernels.
+    SideStream *side = nullptr;
+    if (!gs_prof_on() && (st = side_stream(s, &side))) return st;
+    Fork fork(side, s);
+    const cudaStream_t s2 = fork.side();
+    // 5. fine decoder: bilinear(s8) || s4 -> 3x3 conv 384->128 (+GELU, GN stats)
+    {
+        ProfScope ps(PR_ENC_MISC, s2);
+        dim3 ug((unsigned)((p.W4 * (256 / 8) + 255) / 256), (unsigned)p.H4, (unsigned)B);
+        k_upsample<<<ug, 256, 0, s2>>>(W<__nv_bfloat16>(ws, p.o_y3), p.H8, p.W8, 256, p.H4, p.W4,
+                                       gn3_fly ? gtab : nullptr, W<__nv_bfloat16>(ws, p.o_cat));
+    }
+    memset(&cd, 0, sizeof(cd));
+    cd.B = B; cd.H = p.H4; cd.W = p.W4; cd.Cin = 384; cd.Cout = 128; cd.kh = 3; cd.kw = 3; cd.stride = 1; cd.pad = 1;
+    cd.gelu = 1;
+    {
+        ProfScope ps(PR_CONV4, s2);
+        if ((st = gs_conv_run2(&cd, W<void>(ws, p.o_cat), 256, W<void>(ws, p.o_y2), w->w4, w->b4,
+                               W<void>(ws, p.o_y4), stats + 3 * B * 16, err, s2)))
+            return st;
+    }
     // 3. coarse head (writes the API tensors and a contiguous copy for the coarse render)
     HeadArgs h;
     memset(&h, 0, sizeof(h));
@@ -768,22 +843,8 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
         k_cond<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(image, B, p.H, p.W, W<float>(ws, p.o_render), p.rg,
                                                           W<float>(ws, p.o_cond));
     }
-    // 5. fine decoder: bilinear(s8) || s4 -> 3x3 conv 384->128 (+GELU, GN stats)
-    {
-        ProfScope ps(PR_ENC_MISC, s);
-        dim3 ug((unsigned)((p.W4 * (256 / 8) + 255) / 256), (unsigned)p.H4, (unsigned)B);
-        k_upsample<<<ug, 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), p.H8, p.W8, 256, p.H4, p.W4,
-                                      gn3_fly ? gtab : nullptr, W<__nv_bfloat16>(ws, p.o_cat));
-    }
-    memset(&cd, 0, sizeof(cd));
-    cd.B = B; cd.H = p.H4; cd.W = p.W4; cd.Cin = 384; cd.Cout = 128; cd.kh = 3; cd.kw = 3; cd.stride = 1; cd.pad = 1;
-    cd.gelu = 1;
-    {
-        ProfScope ps(PR_CONV4, s);
-        if ((st = gs_conv_run2(&cd, W<void>(ws, p.o_cat), 256, W<void>(ws, p.o_y2), w->w4, w->b4,
-                               W<void>(ws, p.o_y4), stats + 3 * B * 16, err, s)))
-            return st;
-    }
+    // join: the fine head needs the decoder's output and statistics and the coarse render's cond map
+    fork.join();
     // 6. fine head: GN on the fly, + pooled gradient + bilinear(cond)
     memset(&h, 0, sizeof(h));
     h.B = B; h.fH = p.H4; h.fW = p.W4; h.M = e->Mf; h.Cfeat = 128; h.feat = W<__nv_bfloat16>(ws, p.o_y4);
