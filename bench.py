@@ -643,6 +643,29 @@ def count_pairs(torch, lib, dev, ins, H, W, row_band=None):
     return int(tot.value)
 
 
+def compositing_rooflines(stages, pairs, f_mhz):
+    """Config-1 compositing against its rooflines, by fixed per-pixel-pair counts (pixel-pairs = pairs x
+    64): forward 3 SFU (exp, log, rcp) + 17 FP32 ops, backward 2 SFU + 40 FP32 ops; peaks 148 SMs x 16
+    MUFU and x 128 FP32 lanes per clock at the SM clock sampled in the timed region.  frac = roofline
+    time / measured time of the kernel (stage events, one launch per replay)."""
+    pp = pairs * 64
+    sfu = 148 * 16 * f_mhz * 1e6  # ops/s
+    fp32 = 148 * 128 * f_mhz * 1e6
+    out = {"workload": "config 1 (92,160 splats, 768^2, odds)", "pairs": pairs, "pixel_pairs": pp,
+           "peak_sfu_ops_per_s": sfu, "peak_fp32_ops_per_s": fp32,
+           "peak_source": f"148 SMs x 16 MUFU / 128 FP32 lanes x {f_mhz:.0f} MHz (sampled SM clock)"}
+    for key, kern, n_sfu, n_fp32 in (("fields_fwd", "k_fields_fwd<8,4,odds>", 3, 17),
+                                     ("fields_bwd", "k_fields_bwd<8,4,odds>", 2, 40)):
+        t = stages.get(key, {}).get("ms_per_replay", 0.0) * 1e-3
+        if t <= 0:
+            continue
+        t_sfu, t_fp32 = pp * n_sfu / sfu, pp * n_fp32 / fp32
+        out[key] = {"kernel": kern, "bound": "sfu" if t_sfu >= t_fp32 else "fp32", "ms": t * 1e3,
+                    "roofline_ms": max(t_sfu, t_fp32) * 1e3, "frac": max(t_sfu, t_fp32) / t,
+                    "achieved_sfu_ops_per_s": pp * n_sfu / t, "achieved_fp32_ops_per_s": pp * n_fp32 / t}
+    return out
+
+
 def profile_stages(torch, lib, wl_cls, dev, flush, reps=20, rank=0, world=1):
     """Per-stage device time from CUDA events the library records on its own stream around each stage,
     captured as event nodes into a separate graph of the same step and read after every replay."""
@@ -790,6 +813,11 @@ def main():
         rms = time_steps(torch, rw, 50, flush)
         sec = {"render_fwd_bwd_ms_per_image": statistics.mean(rms),
                "stages_ms": profile_stages(torch, lib, RenderWorkload, dev, flush)}
+        try:  # (tile, splat) pairs of the config-1 render, for its compositing rooflines
+            sec["pairs"] = count_pairs(torch, lib, dev, rw.dev_in, rw.H, rw.W)
+        except Exception as ex:
+            sec["pairs"] = None
+            sec["pairs_error"] = f"{type(ex).__name__}: {ex}"
         pms, ppairs = time_points(torch, dev)
         sec["points"] = {"workload": "render_alpha_subsampled fwd+bwd, 92,160 config-1 splats x 3,000 pixels",
                          "ms_per_step": pms, "pixel_pairs": ppairs,
@@ -831,6 +859,9 @@ def main():
                             "peak_source": f"MEASURED_PEAKS.json bf16_tflops (burst, {pk['source']})"}
         line["render_fwd_bwd_ms_per_image"] = sec["render_fwd_bwd_ms_per_image"] if sec else None
         line["render_stages_ms"] = sec["stages_ms"] if sec else None
+        if sec:
+            line["render_roofline"] = (compositing_rooflines(sec["stages_ms"], sec["pairs"], f_mhz) if sec["pairs"]
+                                       else {"unavailable": sec.get("pairs_error", "no pair count")})
         line["points_fwd_bwd"] = sec["points"] if sec else None
     else:
         if wcls is RenderWorkload:

@@ -82,3 +82,19 @@ def test_clock_sampler_without_nvml_or_smi(monkeypatch):
             pass
     s = clk.summary()
     assert s["samples"] == 0 and s["sm_mhz"] is None
+
+
+def test_compositing_rooflines_arithmetic():
+    """Forward: 3 SFU ops per pixel-pair against 148 x 16 MUFU per clock; backward: 40 FP32 ops against
+    148 x 128 lanes; frac = roofline time / measured time."""
+    import bench
+
+    r = bench.compositing_rooflines({"fields_fwd": {"ms_per_replay": 0.05}, "fields_bwd": {"ms_per_replay": 0.1}},
+                                    pairs=1000, f_mhz=1000.0)
+    pp = 64000
+    assert r["pixel_pairs"] == pp
+    f, b = r["fields_fwd"], r["fields_bwd"]
+    assert f["bound"] == "sfu" and abs(f["roofline_ms"] - pp * 3 / (148 * 16 * 1e9) * 1e3) < 1e-15
+    assert abs(f["frac"] - f["roofline_ms"] / 0.05) < 1e-12
+    assert b["bound"] == "fp32" and abs(b["roofline_ms"] - pp * 40 / (148 * 128 * 1e9) * 1e3) < 1e-15
+    assert "fields_fwd" not in bench.compositing_rooflines({}, pairs=10, f_mhz=1965.0)
