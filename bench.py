@@ -643,6 +643,30 @@ def count_pairs(torch, lib, dev, ins, H, W, row_band=None):
     return int(tot.value)
 
 
+def octave_tiles(H, W, tile=8, max_octaves=6):
+    """Tiles of an octave render: sum over octaves o of the TILE grid of max(8, H>>o) x max(8, W>>o)."""
+    n = 0
+    for o in range(max_octaves + 1):
+        h, w = max(8, H >> o), max(8, W >> o)
+        n += -(-h // tile) * -(-w // tile)
+    return n
+
+
+def binning_roofline(stages, pairs, N, H, W, hbm_gbs):
+    """Binning of one render against HBM: algorithmic bytes N*36 (splat parameters read) + N*4 (per-splat
+    pair counts) + pairs*8 (sorted (tile, splat) written once) + (tiles+1)*4 (tile ranges), over the
+    measured time of the binning stage (preprocess .. ranges, one render)."""
+    t = stages.get("binning", {}).get("ms_per_replay", 0.0) * 1e-3
+    if t <= 0 or not pairs:
+        return None
+    nt = octave_tiles(H, W)
+    nbytes = N * 36 + N * 4 + pairs * 8 + (nt + 1) * 4
+    gbs = nbytes / t / 1e9
+    return {"bound": "hbm", "kernels": "k_preprocess .. k_ranges (10 launches incl. a memset)", "ms": t * 1e3,
+            "algorithmic_bytes": nbytes, "tiles": nt, "achieved_gbs": gbs, "peak_gbs": hbm_gbs,
+            "frac": gbs / hbm_gbs}
+
+
 def compositing_rooflines(stages, pairs, f_mhz):
     """Config-1 compositing against its rooflines, by fixed per-pixel-pair counts (pixel-pairs = pairs x
     64): forward 3 SFU (exp, log, rcp) + 17 FP32 ops, backward 2 SFU + 40 FP32 ops; peaks 148 SMs x 16
@@ -862,6 +886,10 @@ def main():
         if sec:
             line["render_roofline"] = (compositing_rooflines(sec["stages_ms"], sec["pairs"], f_mhz) if sec["pairs"]
                                        else {"unavailable": sec.get("pairs_error", "no pair count")})
+            if sec["pairs"]:
+                line["render_roofline"]["binning"] = binning_roofline(sec["stages_ms"], sec["pairs"],
+                                                                      RenderWorkload.N, RenderWorkload.H,
+                                                                      RenderWorkload.W, pk["hbm_gbs"])
         line["points_fwd_bwd"] = sec["points"] if sec else None
     else:
         if wcls is RenderWorkload:

@@ -98,3 +98,16 @@ def test_compositing_rooflines_arithmetic():
     assert abs(f["frac"] - f["roofline_ms"] / 0.05) < 1e-12
     assert b["bound"] == "fp32" and abs(b["roofline_ms"] - pp * 40 / (148 * 128 * 1e9) * 1e3) < 1e-15
     assert "fields_fwd" not in bench.compositing_rooflines({}, pairs=10, f_mhz=1965.0)
+
+
+def test_binning_roofline_arithmetic():
+    """Octave tile counts (768^2 -> 12,289 tiles; 384^2 -> 3,074, the grids of the two renders) and the
+    algorithmic bytes N*36 + N*4 + pairs*8 + (tiles+1)*4 over the binning stage time."""
+    import bench
+
+    assert bench.octave_tiles(768, 768) == 12289 and bench.octave_tiles(384, 384) == 3074
+    r = bench.binning_roofline({"binning": {"ms_per_replay": 0.1}}, pairs=1000, N=100, H=768, W=768, hbm_gbs=1000.0)
+    nbytes = 100 * 40 + 1000 * 8 + 12290 * 4
+    assert r["algorithmic_bytes"] == nbytes
+    assert abs(r["achieved_gbs"] - nbytes / 1e-4 / 1e9) < 1e-9 and abs(r["frac"] - r["achieved_gbs"] / 1000.0) < 1e-12
+    assert bench.binning_roofline({}, 1000, 100, 768, 768, 1000.0) is None
