@@ -109,3 +109,27 @@ def test_encode_render_workspace_host_only(lib):
     d.H = 250
     assert lib.gs_encoder_workspace_size(C.byref(d)) == 0
     assert lib.gs_encode_render_workspace_size(C.byref(d)) == 0
+
+
+def test_plain_c_consumer(lib, tmp_path):
+    """A C99 program that includes only include/gsplat_b200.h and links libgsplat_b200.so gets the same
+    host-side answers as the Python binding (the boundary needs no torch and no C++)."""
+    import shutil
+
+    from gaussian_2d_splat_encoder_b200 import _lib
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        import pytest
+
+        pytest.skip("no C compiler")
+    exe = tmp_path / "consumer"
+    libdir = str(_lib.LIB_PATH.parent)
+    subprocess.run([cc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", str(ROOT / "include"),
+                    str(ROOT / "tests" / "c_abi_consumer.c"), "-o", str(exe), "-L", libdir,
+                    f"-l:{_lib.LIB_PATH.name}", f"-Wl,-rpath,{libdir}"], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
+    got = dict(kv.split("=") for kv in out.split())
+    assert got["arch"] == "100" and int(got["bound"]) == 64 * 92160
+    assert 0 < int(got["ws_fwd"]) < int(got["ws_bwd"])
+    assert int(got["bad_args"]) == _lib.GS_ERR_BAD_ARGUMENT and got["ws_bad_tile"] == "0"
