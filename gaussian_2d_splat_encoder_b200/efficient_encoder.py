@@ -248,6 +248,14 @@ def cuda_forward(enc, image, return_latents, render):
         d = enc._desc(B, H, W)
         size_fn = L.gs_encode_render_workspace_size if render else L.gs_encoder_workspace_size
         nbytes = int(size_fn(C.byref(d)))
+        if nbytes == 0 and render and int(L.gs_encoder_workspace_size(C.byref(d))) > 0:
+            # the fused call sizes its final render from the host pair bound; where that bound passes the
+            # reference's per-image budget, the encoder runs alone and render_alpha_octave (which counts
+            # the pairs exactly before it refuses, render_triton.py:378-385) renders its splats
+            o, _ = cuda_forward(enc, image, return_latents, render=False)
+            rec = render_alpha_octave(o["mu"], o["log_scale"], o["color"], o["opacity"], o["bg"], H, W,
+                                      theta=o["theta"], odds=bool(enc.odds))
+            return o, rec
         if nbytes == 0:
             raise ValueError("unsupported encoder configuration")
         Nc = (H // 8) * (W // 8) * enc.M
