@@ -190,6 +190,14 @@ def case_render():
     th = (torch.rand(1, N) - 0.5) * 3.14
     L = [mu, ls, col, op, bgv, th]
     cases["octave_coarse384"] = (rt.render_alpha_octave, L, 384, 384, dict(odds=True))
+    # colour-channel counts other than 3 (the reference takes any C; the encoder uses 3) and TILE 16 on
+    # the octave path
+    L = leaves(31, 2, 400, 1, 2.0, 0.9)
+    cases["octave_c1_odds"] = (rt.render_alpha_octave, L, 64, 48, dict(odds=True))
+    L = leaves(37, 1, 300, 2, 2.2)
+    cases["cull_c2_alpha_noth"] = (rt.render_alpha_full_triton, L[:5] + [None], 40, 56, dict(cull=True))
+    L = leaves(41, 2, 500, C, 2.0, 0.9)
+    cases["octave_tile16_odds"] = (rt.render_alpha_octave, L, 96, 80, dict(odds=True, TILE=16))
     return cases
 
 
