@@ -68,7 +68,7 @@ class _PointsRender(torch.autograd.Function):
         if px_idx.dim() != 2 or px_idx.shape[0] != B:
             raise ValueError("pixel indices must be [B, n_px]")
         if not 1 <= Cc <= 3:
-            raise ValueError(f"colour channels must be 1..3, got {Cc}")
+            raise ValueError(f"colour channels of one render call must be 1..3, got {Cc}")
         f = [None if t is None else t.detach().contiguous().float() for t in (mu, log_scale, color, opacity, bg, theta)]
         idx = px_idx.detach().contiguous().to(torch.int64)
         P = int(idx.shape[1])
@@ -120,5 +120,10 @@ def render_alpha_subsampled(mu, log_scale, color, opacity, bg, H, W, theta=None,
         px_idx = pixel_indices
     else:
         px_idx = torch.randint(0, total, (B, min(int(n_pixels), total)), device=mu.device)
-    rendered = _PointsRender.apply(mu, log_scale, color, opacity, bg, theta, px_idx, int(H), int(W))
+    C = color.shape[-1]
+    if C <= 3:
+        rendered = _PointsRender.apply(mu, log_scale, color, opacity, bg, theta, px_idx, int(H), int(W))
+    else:  # groups of at most three channels composite independently (see render_triton._render)
+        rendered = torch.cat([_PointsRender.apply(mu, log_scale, color[..., c:c + 3], opacity, bg[:, c:c + 3], theta,
+                                                  px_idx, int(H), int(W)) for c in range(0, C, 3)], dim=1)
     return rendered, px_idx

@@ -100,7 +100,7 @@ class _Render(torch.autograd.Function):
         if mu.shape != (B, N, 2) or log_scale.shape != (B, N, 2) or opacity.shape != (B, N) or bg.shape[0] != B:
             raise ValueError("shape mismatch: mu/log_scale [B,N,2], color [B,N,C], opacity [B,N], bg [B,C]")
         if not 1 <= Cc <= 3:
-            raise ValueError(f"colour channels must be 1..3, got {Cc}")
+            raise ValueError(f"colour channels of one render call must be 1..3, got {Cc}")
         f = [_f32(t) for t in (mu, log_scale, color, opacity, bg, theta)]
         has_th = theta is not None
         with torch.cuda.device(dev):
@@ -141,7 +141,15 @@ class _Render(torch.autograd.Function):
 
 
 def _render(mode, mu, log_scale, color, opacity, bg, H, W, theta, kw):
-    return _Render.apply(mu, log_scale, color, opacity, bg, theta, (mode, int(H), int(W), kw))
+    cfg = (mode, int(H), int(W), kw)
+    C = color.shape[-1]
+    if C <= 3:
+        return _Render.apply(mu, log_scale, color, opacity, bg, theta, cfg)
+    # More than three channels (the reference's kernels take any C): the transmittance and the weight sum
+    # do not depend on colour and every output channel composites on its own, so groups of at most three
+    # channels render independently and concatenate exactly; autograd sums the shared leaves' gradients.
+    return torch.cat([_Render.apply(mu, log_scale, color[..., c:c + 3], opacity, bg[:, c:c + 3], theta, cfg)
+                      for c in range(0, C, 3)], dim=1)
 
 
 def render_alpha_octave(mu, log_scale, color, opacity, bg, H, W, theta=None, cutoff=3.0, TILE=8,

@@ -20,6 +20,35 @@ def _activate_scale(ls):
     return F.softplus(ls) + 1e-4
 
 
+def composite_points(mu, ls, col, op, bg, theta, idx, H, W, chunk: int = 1 << 22):
+    """The composite on torch tensors (autograd-capable, any dtype and channel count): every splat at
+    every pixel of idx [B,P] (flat y*W + x); returns out [B,C,P]."""
+    B, N, C = col.shape
+    P = idx.shape[1]
+    scale = _activate_scale(ls)
+    py = ((idx // W).to(mu.dtype) + 0.5) / H
+    px = ((idx % W).to(mu.dtype) + 0.5) / W
+    pix = torch.stack([py, px], dim=-1)  # [B,P,2]
+    # the [B,P,N] reductions of alpha_composite, chunked over pixels to bound memory
+    step = max(1, chunk // max(N, 1))
+    logT, asum, acol = [], [], []
+    for p0 in range(0, P, step):
+        d = pix[:, p0:p0 + step].unsqueeze(2) - mu.unsqueeze(1)  # [B,p,N,2]
+        dy, dx = d[..., 0], d[..., 1]
+        if theta is not None:
+            c, s = torch.cos(theta).unsqueeze(1), torch.sin(theta).unsqueeze(1)
+            dy, dx = c * dy + s * dx, -s * dy + c * dx
+        maha = (dy / scale[..., 0].unsqueeze(1)) ** 2 + (dx / scale[..., 1].unsqueeze(1)) ** 2
+        alpha = (torch.exp(-0.5 * maha) * op.unsqueeze(1)).clamp(max=1.0 - 1e-4)
+        logT.append(torch.log1p(-alpha).sum(-1))
+        asum.append(alpha.sum(-1))
+        acol.append(torch.bmm(alpha, col))
+    T = torch.exp(torch.cat(logT, 1))
+    a = torch.cat(asum, 1).clamp_min(1e-8)
+    fg = torch.cat(acol, 1) / a.unsqueeze(-1)
+    return ((1.0 - T).unsqueeze(-1) * fg + T.unsqueeze(-1) * bg.unsqueeze(1)).permute(0, 2, 1)  # [B,C,P]
+
+
 def render_points(mu, log_scale, color, opacity, bg, H, W, px_idx, theta=None, grad_out=None,
                   chunk: int = 1 << 22):
     """Every splat at every listed pixel.  Arrays in the reference layouts (mu [B,N,2] (y,x),
@@ -35,30 +64,7 @@ def render_points(mu, log_scale, color, opacity, bg, H, W, px_idx, theta=None, g
                 x.requires_grad_(True)
     mu_, ls_, col_, op_, bg_, th_ = leaves
     idx = torch.as_tensor(np.asarray(px_idx), dtype=torch.int64)
-    B, N, C = col_.shape
-    P = idx.shape[1]
-    scale = _activate_scale(ls_)
-    py = ((idx // W).to(torch.float64) + 0.5) / H
-    px = ((idx % W).to(torch.float64) + 0.5) / W
-    pix = torch.stack([py, px], dim=-1)  # [B,P,2]
-    # the [B,P,N] reductions of alpha_composite, chunked over pixels to bound memory
-    step = max(1, chunk // max(N, 1))
-    logT, asum, acol = [], [], []
-    for p0 in range(0, P, step):
-        d = pix[:, p0:p0 + step].unsqueeze(2) - mu_.unsqueeze(1)  # [B,p,N,2]
-        dy, dx = d[..., 0], d[..., 1]
-        if th_ is not None:
-            c, s = torch.cos(th_).unsqueeze(1), torch.sin(th_).unsqueeze(1)
-            dy, dx = c * dy + s * dx, -s * dy + c * dx
-        maha = (dy / scale[..., 0].unsqueeze(1)) ** 2 + (dx / scale[..., 1].unsqueeze(1)) ** 2
-        alpha = (torch.exp(-0.5 * maha) * op_.unsqueeze(1)).clamp(max=1.0 - 1e-4)
-        logT.append(torch.log1p(-alpha).sum(-1))
-        asum.append(alpha.sum(-1))
-        acol.append(torch.bmm(alpha, col_))
-    T = torch.exp(torch.cat(logT, 1))
-    a = torch.cat(asum, 1).clamp_min(1e-8)
-    fg = torch.cat(acol, 1) / a.unsqueeze(-1)
-    out = ((1.0 - T).unsqueeze(-1) * fg + T.unsqueeze(-1) * bg_.unsqueeze(1)).permute(0, 2, 1)  # [B,C,P]
+    out = composite_points(mu_, ls_, col_, op_, bg_, th_, idx, H, W, chunk)
     if not need:
         return out.detach().numpy()
     g = torch.as_tensor(np.asarray(grad_out), dtype=torch.float64)

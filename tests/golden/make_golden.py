@@ -198,6 +198,8 @@ def case_render():
     cases["cull_c2_alpha_noth"] = (rt.render_alpha_full_triton, L[:5] + [None], 40, 56, dict(cull=True))
     L = leaves(41, 2, 500, C, 2.0, 0.9)
     cases["octave_tile16_odds"] = (rt.render_alpha_octave, L, 96, 80, dict(odds=True, TILE=16))
+    L = leaves(43, 1, 400, 5, 2.0, 0.9)
+    cases["octave_c5_odds"] = (rt.render_alpha_octave, L, 48, 64, dict(odds=True))
     return cases
 
 

@@ -18,7 +18,7 @@ def render_cases():
 
 # Fixtures (made by the reference, pinned against the oracle on the CPU) whose CUDA parity has not been run
 # on a GPU yet: the GPU parity test skips them until it has.
-GPU_PENDING = {"octave_c1_odds", "cull_c2_alpha_noth", "octave_tile16_odds"}
+GPU_PENDING = {"octave_c1_odds", "cull_c2_alpha_noth", "octave_tile16_odds", "octave_c5_odds"}
 
 
 def load_render(name):
