@@ -1741,10 +1741,14 @@ int64_t gs_render_pair_bound(const gs_render_desc *d) {
     return pair_bound(d, G);
 }
 
+// Pair positions and tile ranges are 32-bit: one call holds fewer than 2^31 (tile, splat) pairs.
+static bool pairs_fit(const Plan &pl) { return pl.cap < (1LL << 31); }
+
 size_t gs_render_workspace_size(const gs_render_desc *d, int with_backward) {
     if (validate(d) != GS_OK) return 0;
     Plan pl;
     make_plan(d, pl);
+    if (!pairs_fit(pl)) return 0;
     return with_backward ? pl.total_bytes : pl.fwd_bytes;
 }
 
@@ -1833,6 +1837,7 @@ int gs_render_fwd_prior(const gs_render_desc *d, const float *mu, const float *l
     if (d->N > 0 && (!mu || !log_scale || !color || !opacity || (d->has_theta && !theta))) return GS_ERR_BAD_ARGUMENT;
     Plan pl;
     make_plan(d, pl);
+    if (!pairs_fit(pl)) return GS_ERR_BAD_ARGUMENT;
     if (!workspace || workspace_bytes < pl.fwd_bytes) return GS_ERR_WORKSPACE;
     cudaStream_t s = (cudaStream_t)stream;
     if (prior && prior->fields) {

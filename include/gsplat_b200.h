@@ -69,7 +69,8 @@ typedef struct {
  * (render_triton.py:378-391) whenever the bound is within budget. */
 int64_t gs_render_pair_bound(const gs_render_desc *d);
 
-/* Workspace bytes for a forward (with_backward = 0) or a forward + backward (with_backward = 1). */
+/* Workspace bytes for a forward (with_backward = 0) or a forward + backward (with_backward = 1); 0 for
+ * an invalid descriptor or a pair capacity of 2^31 or more (pair positions are 32-bit; split the batch). */
 size_t gs_render_workspace_size(const gs_render_desc *d, int with_backward);
 
 /* Forward render without any caller-provided workspace (no counterpart in the reference).  For callers

@@ -51,6 +51,11 @@ def test_pair_bound_and_workspace_host_only(lib):
     ws_f = lib.gs_render_workspace_size(C.byref(d), 0)
     ws_b = lib.gs_render_workspace_size(C.byref(d), 1)
     assert 0 < ws_f < ws_b < (1 << 31)
+    d.pair_capacity = (1 << 31) - 1  # the largest capacity 32-bit pair positions address
+    assert lib.gs_render_workspace_size(C.byref(d), 0) > 0
+    d.pair_capacity = 1 << 31
+    assert lib.gs_render_workspace_size(C.byref(d), 0) == 0
+    d.pair_capacity = 0
     d.tile = 5
     assert lib.gs_render_workspace_size(C.byref(d), 0) == 0
     assert lib.gs_render_pair_bound(C.byref(d)) == -1
