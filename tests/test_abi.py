@@ -138,3 +138,33 @@ def test_plain_c_consumer(lib, tmp_path):
     assert got["arch"] == "100" and int(got["bound"]) == 64 * 92160
     assert 0 < int(got["ws_fwd"]) < int(got["ws_bwd"])
     assert int(got["bad_args"]) == _lib.GS_ERR_BAD_ARGUMENT and got["ws_bad_tile"] == "0"
+
+
+def test_host_queries_fuzz(lib):
+    """Random descriptors (valid and invalid): the host-only queries never fault, a valid descriptor gets a
+    forward workspace no larger than the forward+backward one, and an invalid one gets 0 / -1."""
+    import numpy as np
+
+    from gaussian_2d_splat_encoder_b200 import _lib
+
+    rng = np.random.default_rng(0)
+    for _ in range(400):
+        mode = int(rng.integers(-1, 5))
+        kw = dict(mode=mode, B=int(rng.integers(0, 5)), N=int(rng.integers(-2, 5000)), C=int(rng.integers(0, 5)),
+                  H=int(rng.integers(0, 700)), W=int(rng.integers(0, 700)), TILE=int(rng.choice([3, 4, 8, 16, 32])),
+                  odds=bool(rng.integers(0, 2)), has_theta=bool(rng.integers(0, 2)),
+                  cutoff=float(rng.choice([0.0, 3.0, 5.0])))
+        d = _desc(**kw)
+        d.max_octaves = int(rng.integers(-1, 9))
+        valid = (0 <= mode <= 3 and kw["B"] >= 1 and kw["N"] >= 0 and 1 <= kw["C"] <= 3 and kw["H"] >= 1
+                 and kw["W"] >= 1 and kw["TILE"] in (4, 8, 16) and kw["cutoff"] > 0
+                 and not (mode == _lib.MODE_EXACT and kw["odds"])
+                 and not (mode == _lib.MODE_OCTAVE and not 0 <= d.max_octaves <= 7))
+        f = lib.gs_render_workspace_size(C.byref(d), 0)
+        b = lib.gs_render_workspace_size(C.byref(d), 1)
+        bound = lib.gs_render_pair_bound(C.byref(d))
+        if valid:
+            assert 0 < f <= b, kw
+            assert bound >= 0, kw
+        else:
+            assert f == 0 and b == 0, kw
