@@ -26,7 +26,9 @@ from .render_triton import render_alpha_octave
 class EncodeRender:
     def __init__(self, encoder, batch: int, H: int, W: int, device=None, warmup: int = 2):
         self.enc = encoder
-        self.dev = torch.device(device) if device is not None else next(encoder.parameters()).device
+        if device is None:  # the module's parameters, or a PackedEncoder's device
+            device = next(encoder.parameters()).device if hasattr(encoder, "parameters") else encoder.device
+        self.dev = torch.device(device)
         self.shape = (batch, 3, H, W)
         self.x = torch.zeros(self.shape, device=self.dev)
         self.graph = None

@@ -80,3 +80,14 @@ def test_packed_forward_needs_cuda(tmp_path):
     pe = ck.load_packed(tmp_path / "enc.packed", device="cpu")
     with pytest.raises(RuntimeError, match="CUDA"):
         pe(torch.zeros(1, 3, 64, 64))
+
+
+def test_pipeline_takes_a_packed_encoder(tmp_path):
+    """pipeline.EncodeRender finds a PackedEncoder's device (it has no parameters)."""
+    from gaussian_2d_splat_encoder_b200 import checkpoint as ck
+    from gaussian_2d_splat_encoder_b200 import pipeline
+
+    ck.save_packed(_module(), tmp_path / "enc.packed")
+    pe = ck.load_packed(tmp_path / "enc.packed", device="cpu")
+    er = pipeline.EncodeRender(pe, 1, 64, 64)
+    assert er.dev == torch.device("cpu") and er.x.shape == (1, 3, 64, 64)
