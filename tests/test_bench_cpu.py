@@ -111,3 +111,26 @@ def test_binning_roofline_arithmetic():
     assert r["algorithmic_bytes"] == nbytes
     assert abs(r["achieved_gbs"] - nbytes / 1e-4 / 1e9) < 1e-9 and abs(r["frac"] - r["achieved_gbs"] / 1000.0) < 1e-12
     assert bench.binning_roofline({}, 1000, 100, 768, 768, 1000.0) is None
+
+
+def test_reference_arm_line():
+    """`bench.py --impl reference` (host CPU, no GPU): one JSON line with the contract's keys, the same
+    metric/unit/scaling as our arm's line for the workload, and an e2e entry with no host-device bytes."""
+    import json
+    import subprocess
+
+    import bench
+
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", "render",
+                        "--steps", "1", "--warmup", "1"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+              "vs_baseline", "dtype", "data", "config", "impl", "cpu_baseline", "e2e"):
+        assert k in line, k
+    assert line["impl"] == "reference" and line["value"] > 0 and line["warmup"] >= 3
+    assert (line["metric"], line["unit"], line["scaling"]) == (bench.RenderWorkload.metric, "images/s", "weak")
+    assert line["config"]["splats"] == 92160 and line["config"]["H"] == 768
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    cb = line["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and "render fwd+bwd" in cb["sample"]
