@@ -38,8 +38,12 @@ sys.path.insert(0, str(ROOT))
 METRIC = "768² encode+render images/s at 1/2/4/8 B200; render fwd+bwd ms/image"
 FIT_METRIC = "config 4: 2048^2 fitting step (render fwd+bwd + NCCL all-reduce + Adam) steps/s"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+# dram__bytes_read.sum + dram__bytes_write.sum of the two k_fields_fwd launches of one encode+render step
+# (ncu, profiles/fields_fwd_encode_render_768.md): 3.84 MB (coarse render) + 7.93 MB (final render) read,
+# nothing written back inside the launches (the field planes stay in L2)
+FIELDS_FWD_TRAFFIC = 11.77e6
 STAGE_NAMES = {0: "binning", 1: "fields_fwd", 2: "composite", 3: "composite_bwd+adjoint", 4: "fields_bwd",
-               5: "finalize", 8: "enc_prep", 9: "conv1", 10: "conv2", 11: "conv3", 12: "conv4_decoder",
+               5: "finalize", 6: "enc_binning", 7: "enc_fields_fwd", 8: "enc_prep", 9: "conv1", 10: "conv2", 11: "conv3", 12: "conv4_decoder",
                13: "heads", 14: "enc_gn_concat_cond", 15: "enc_coarse_render"}
 
 
@@ -716,6 +720,151 @@ def profile_stages(torch, lib, wl_cls, dev, flush, reps=20, rank=0, world=1):
     return {n: {"ms_per_replay": v[0] / reps, "calls_per_replay": v[1]} for n, v in acc.items()}
 
 
+def encode_render_pairs(torch, lib, enc, x):
+    """(tile, splat) pairs of one encode+render call: [encoder's internal 384^2 coarse render, final 768^2
+    render], read back from a workspace this function owns (gs_encode_render_debug_pairs)."""
+    from gaussian_2d_splat_encoder_b200 import _lib
+    from gaussian_2d_splat_encoder_b200.efficient_encoder import cuda_forward
+
+    B, _, H, W = x.shape
+    d = enc._desc(B, H, W)
+    nb = int(lib.gs_encode_render_workspace_size(C.byref(d)))
+    ws = torch.empty(nb, dtype=torch.uint8, device=x.device)
+    with torch.inference_mode():
+        cuda_forward(enc, x, False, True, workspace=ws)
+    torch.cuda.synchronize()
+    pairs = (C.c_int64 * 2)()
+    _lib.check(lib.gs_encode_render_debug_pairs(C.byref(d), _lib.ptr(ws), pairs), "gs_encode_render_debug_pairs")
+    return int(pairs[0]), int(pairs[1])
+
+
+def fields_fwd_roofline(stages, pairs_coarse, pairs_final, f_mhz, traffic=None):
+    """k_fields_fwd of one encode+render step (the internal 384^2 coarse render + the final 768^2 render)
+    against the SFU roofline: 3 SFU ops (exp, log, rcp) per pixel-pair in odds mode, pixel-pairs = pairs x
+    64 (TILE 8), over the two launches' device time (stage events).  Peak: 148 SMs x 16 MUFU results per
+    clock at the SM clock sampled during the timed region."""
+    tc = stages.get("enc_fields_fwd", {}).get("ms_per_replay", 0.0)
+    tf = stages.get("fields_fwd", {}).get("ms_per_replay", 0.0)
+    if tc <= 0 or tf <= 0:
+        return {"unavailable": "no stage times for the field kernels"}
+    sfu = 148 * 16 * f_mhz * 1e6
+    pp = (pairs_coarse + pairs_final) * 64
+    t = (tc + tf) * 1e-3
+    ach = 3.0 * pp / t
+    per = {}
+    for name, pr, tm in (("coarse_384", pairs_coarse, tc), ("final_768", pairs_final, tf)):
+        ppr = pr * 64
+        per[name] = {"pairs": pr, "pixel_pairs": ppr, "ms": tm, "roofline_ms": 3.0 * ppr / sfu * 1e3,
+                     "frac": (3.0 * ppr / sfu) / (tm * 1e-3)}
+    return {"bound": "sfu", "kernel": "k_fields_fwd<8,4,odds> (2 launches per step: coarse 384^2 + final 768^2)",
+            "achieved": ach / 1e12, "peak": sfu / 1e12, "unit": "T SFU-op/s", "frac": ach / sfu,
+            "traffic": traffic, "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, both launches of "
+                                                   "one step (profiles/fields_fwd_encode_render_768.md)"
+                                                   if traffic else None),
+            "units_per_step": pp, "unit_name": "pixel-pair", "ops_per_unit": 3, "launches_per_step": 2,
+            "ms_per_step": tc + tf, "per_render": per,
+            "peak_source": f"148 SMs x 16 MUFU x {f_mhz:.0f} MHz (median SM clock sampled in the timed region)"}
+
+
+def reference_triton_leg(torch, dev, H=768, W=768, warmup=5, runs=30):
+    """The reference's own GPU path on this B200 (the denominator of the target's >= 50x): the unmodified
+    reference package from baseline/_ref, EfficientGaussianEncoder forward + render_alpha_octave(odds) of
+    its splats, timed with CUDA events per call after `warmup` calls (examples/encode_and_render.py:75-89
+    of the reference, with the final render included), one config-3 card (seed 100), inference."""
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "gaussian_splat_encoder" / "render_triton.py").exists():
+        return {"unavailable": "reference package not present under baseline/_ref"}
+    sys.path.insert(0, str(ref_root))
+    try:
+        import triton
+
+        from gaussian_splat_encoder.efficient_encoder import EfficientGaussianEncoder as RefEnc
+        from gaussian_splat_encoder.render_triton import render_alpha_octave as ref_render
+    except Exception as ex:  # noqa: BLE001
+        return {"unavailable": f"reference import failed: {type(ex).__name__}: {ex}"}
+    finally:
+        sys.path.remove(str(ref_root))
+    from gaussian_2d_splat_encoder_b200 import synth
+
+    sys.path.insert(0, str(ROOT / "tests"))
+    from enc_util import GOLDEN_CFG, load_golden
+
+    enc = load_golden(RefEnc)
+    desc = "released checkpoint encoder_golden_d256.pt"
+    if enc is None:
+        torch.manual_seed(0)
+        enc = RefEnc(**GOLDEN_CFG).eval()
+        desc = "reference architecture, random init (torch.manual_seed(0))"
+    enc = enc.to(dev)
+    x = synth.synth_card(H, W, 500, 150, EncodeRenderWorkload.SEEDS[0]).to(dev)
+
+    def one():
+        with torch.no_grad():
+            o = enc(x)
+            return ref_render(o["mu"], o["log_scale"], o["color"], o["opacity"], o["bg"], H, W, theta=o["theta"],
+                              odds=bool(getattr(enc, "odds", True)))
+
+    t0 = time.perf_counter()
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    t_warm = time.perf_counter() - t0
+    ms = []
+    for _ in range(runs):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        one()
+        b.record()
+        torch.cuda.synchronize()
+        ms.append(a.elapsed_time(b))
+    ms.sort()
+    med = statistics.median(ms)
+    return {"images_per_s": 1000.0 / med, "ms_median": med, "ms_p10": ms[len(ms) // 10],
+            "ms_p90": ms[(9 * len(ms)) // 10], "warmup": warmup, "runs": runs, "warmup_s_incl_jit": t_warm,
+            "what": "unmodified reference (baseline/_ref/gaussian_splat_encoder): EfficientGaussianEncoder forward "
+                    "(fp32 torch convs + its Triton 384^2 coarse render) + render_alpha_octave(odds=True) at 768^2, "
+                    "torch.no_grad, CUDA events per image, no L2 flush",
+            "encoder_weights": desc, "torch": torch.__version__, "triton": triton.__version__}
+
+
+def fit_leg(torch, lib, dev, flush, rank, world, K=20, warmup=3, max_over_ranks=None, barrier=None):
+    """Config 4 at this N (tile-row bands, one NCCL all-reduce of the splat gradients per step): steps/s as
+    the max over ranks of K graph replays, the field backward's roofline, and the all-reduce alone."""
+    wl = FitWorkload(dev, rank, world)
+    wl.capture()
+    for _ in range(warmup):
+        wl.step()
+    barrier()
+    ms = time_steps(torch, wl, K, flush)
+    tot = max_over_ranks(sum(ms))
+    launches = wl.pipe.launches_per_replay
+    band = list(wl.band)
+    pairs = count_pairs(torch, lib, dev, {k: wl.init[k] for k in wl.keys}, wl.H, wl.W, wl.band)
+    ar = None
+    if world > 1:
+        import torch.distributed as dist
+
+        buf = wl.flat
+        for _ in range(3):
+            dist.all_reduce(buf)
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(K):
+            dist.all_reduce(buf)
+        b.record()
+        torch.cuda.synchronize()
+        ar = {"ms": max_over_ranks(a.elapsed_time(b) / K), "bytes": buf.numel() * 4,
+              "what": "NCCL all-reduce (sum) of the flattened splat gradients alone, eager, max over ranks"}
+    wl.release()
+    barrier()
+    stages = profile_stages(torch, lib, FitWorkload, dev, flush, rank=rank, world=world)
+    return {"metric": FIT_METRIC, "value": K / (tot / 1000.0), "unit": "steps/s", "ms_per_step": tot / K,
+            "steps": K, "warmup": warmup, "band_rows_rank0": band, "pairs_rank0_band": pairs,
+            "gpu_launches_per_step": launches, "stages_ms": stages, "allreduce": ar,
+            "workload": FitWorkload.describe(wl.wdesc, wl.N)["workload"], "scaling": "strong"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -724,6 +873,9 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="encode_render")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-fit", action="store_true", help="skip the config-4 sub-object of the default line")
+    ap.add_argument("--no-reference-triton", action="store_true",
+                    help="skip timing the reference's own GPU path (default line, N = 1)")
     ap.add_argument("--kernels-only", action="store_true",
                     help="warm-up + K graph replays and nothing else (for ncu launch lists)")
     args = ap.parse_args()
@@ -867,20 +1019,22 @@ def main():
         "peaks": pk,
     }
     if wcls is EncodeRenderWorkload:
-        # dominant kernel: the decoder convolution (tensor-bound): 2*M*N*K flops per launch
+        # dominant kernel of the step: k_fields_fwd (both renders), SFU-bound
+        try:
+            pc, pf = encode_render_pairs(torch, lib, wl.enc, wl.dev_imgs[0])
+            line["roofline"] = fields_fwd_roofline(stages, pc, pf, f_mhz, traffic=FIELDS_FWD_TRAFFIC)
+        except Exception as ex:  # noqa: BLE001
+            line["roofline"] = {"unavailable": f"{type(ex).__name__}: {ex}"}
+        # secondary: the decoder convolution (tensor-bound, off the critical path): 2*M*N*K flops per launch
         M, N, Kd = (wl.H // 4) * (wl.W // 4), 128, 9 * 384
         t = stages.get("conv4_decoder", {}).get("ms_per_replay", 0.0)
         ach = 2.0 * M * N * Kd / (t * 1e-3) / 1e12 if t > 0 else None
-        # traffic: dram__bytes_read.sum + dram__bytes_write.sum of one decoder launch in a full ncu capture
-        # of this workload (29.25 MB read, 0 written inside the kernel's window: its 9.4 MB output leaves
-        # L2 later); algorithmic bytes per launch = 28.3 MB input + 0.9 MB weights + 9.4 MB output
-        line["roofline"] = {"bound": "tensor", "kernel": "k_conv_tc<128,64,4> (decoder 3x3 384->128 @192^2)",
-                            "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                            "frac": (ach / pk["bf16_tflops"]) if ach else None, "traffic": 29.25e6,
-                            "traffic_source": "ncu --set full capture of this workload (decoder launch)",
-                            "algorithmic_bytes": 2 * M * (256 + 128) + 2 * N * Kd + 2 * M * N,
-                            "flops_per_launch": 2.0 * M * N * Kd,
-                            "peak_source": f"MEASURED_PEAKS.json bf16_tflops (burst, {pk['source']})"}
+        line["roofline_decoder"] = {"bound": "tensor", "kernel": "k_conv_tc (decoder 3x3 384->128 @192^2)",
+                                    "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                                    "frac": (ach / pk["bf16_tflops"]) if ach else None,
+                                    "algorithmic_bytes": 2 * M * (256 + 128) + 2 * N * Kd + 2 * M * N,
+                                    "flops_per_launch": 2.0 * M * N * Kd,
+                                    "peak_source": f"MEASURED_PEAKS.json bf16_tflops (burst, {pk['source']})"}
         line["render_fwd_bwd_ms_per_image"] = sec["render_fwd_bwd_ms_per_image"] if sec else None
         line["render_stages_ms"] = sec["stages_ms"] if sec else None
         if sec:
@@ -910,6 +1064,26 @@ def main():
                             "traffic": None, "units_per_launch": pp, "ops_per_unit": 40, "pairs": pairs,
                             "peak_source": f"148 SMs x 128 FP32 lanes x {f_mhz:.0f} MHz (median SM clock sampled "
                                            "during the timed region)"}
+    if wcls is EncodeRenderWorkload and not args.no_fit:
+        # config 4 at this N: the one path with a collective (every rank takes part)
+        fit = fit_leg(torch, lib, dev, flush, rank, world, max_over_ranks=max_over_ranks, barrier=barrier)
+        fb = fit["stages_ms"].get("fields_bwd", {}).get("ms_per_replay", 0.0)
+        fp32_peak = 148 * 128 * f_mhz * 1e6
+        if fb > 0:
+            fit["fields_bwd_roofline"] = {"bound": "fp32", "ops_per_pixel_pair": 40,
+                                          "pixel_pairs_rank0": fit["pairs_rank0_band"] * 64,
+                                          "frac": 40.0 * fit["pairs_rank0_band"] * 64 / fp32_peak / (fb * 1e-3)}
+        line["fit"] = fit
+    if wcls is EncodeRenderWorkload and world == 1 and not args.no_reference_triton:
+        try:
+            rt = reference_triton_leg(torch, dev)
+        except Exception as ex:  # noqa: BLE001
+            rt = {"unavailable": f"reference run failed: {type(ex).__name__}: {ex}"}
+        if "images_per_s" in rt:
+            rt["ours_over_reference"] = value / rt["images_per_s"]
+            rt["ours_e2e_over_reference"] = e2e_val / rt["images_per_s"]
+            rt["target"] = ">= 50x (north_star)"
+        line["reference_triton"] = rt
     if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the host baseline is an N = 1 figure
         line["cpu_baseline"] = cpu_baseline(wcls, 3)[0]
     if rank == 0:

@@ -58,6 +58,7 @@ SIGNATURES = {
     "gs_encoder_workspace_size": (C.c_size_t, [_P]),
     "gs_encoder_fwd": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "gs_encoder_error_flag": (C.c_int, [_P, _P, _P]),
+    "gs_encode_render_debug_pairs": (C.c_int, [_P, _P, _P]),
     "gs_encode_render_workspace_size": (C.c_size_t, [_P]),
     "gs_encode_render_fwd": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, _P]),
     "gs_last_error": (C.c_char_p, []),

@@ -836,8 +836,10 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     {
         ProfScope ps(PR_ENC_RENDER, s);
         float *bgws = bg;
+        gs_prof_set_internal(1);
         st = gs_render_fwd(&p.rd, h.cmu, h.cls, h.ccol, h.cop, bgws, h.cth, W<float>(ws, p.o_render),
                            W<void>(ws, p.o_rws), p.rws, stream);
+        gs_prof_set_internal(0);
         if (st != GS_OK) return st;
         long long n = (long long)B * p.rg * p.rg;
         k_cond<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(image, B, p.H, p.W, W<float>(ws, p.o_render), p.rg,
@@ -928,6 +930,24 @@ extern "C" int gs_encode_render_fwd(const gs_encoder_desc *e, const gs_encoder_w
     const int mapped = gs_render_prior_map(&p.rd, W<void>(workspace, p.o_rws), &fd, p.Nc, &prior);
     return gs_render_fwd_prior(&fd, mu, log_scale, color, opacity, bg, theta, out, mapped ? &prior : nullptr,
                                W<void>(workspace, al(p.total)), rws, stream);
+}
+
+extern "C" int gs_encode_render_debug_pairs(const gs_encoder_desc *e, const void *workspace, int64_t *pairs) {
+    EncPlan p;
+    int st = enc_plan(e, p);
+    if (st != GS_OK) return st;
+    gs_render_desc fd;
+    if ((st = final_render_desc(e, p, fd)) != GS_OK) return st;
+    if (!workspace || !pairs) return GS_ERR_BAD_ARGUMENT;
+    int64_t a = 0, b = 0;
+    st = gs_render_debug_bins(&p.rd, W<void>(const_cast<void *>(workspace), p.o_rws), &a, nullptr, nullptr, nullptr,
+                              nullptr, nullptr);
+    if (st != GS_OK) return st;
+    st = gs_render_debug_bins(&fd, W<void>(const_cast<void *>(workspace), al(p.total)), &b, nullptr, nullptr, nullptr,
+                              nullptr, nullptr);
+    pairs[0] = a;
+    pairs[1] = b;
+    return st;
 }
 
 extern "C" int gs_encoder_error_flag(const gs_encoder_desc *e, const void *workspace, int *flag_host) {

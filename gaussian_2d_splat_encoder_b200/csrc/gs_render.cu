@@ -55,6 +55,9 @@ size_t g_prof_used = 0;
 }  // namespace
 
 bool gs_prof_on() { return g_prof_on; }
+static thread_local int g_prof_internal = 0;
+void gs_prof_set_internal(int on) { g_prof_internal = on; }
+int gs_prof_internal() { return g_prof_internal; }
 void gs_prof_take(int region, cudaEvent_t *a, cudaEvent_t *b) {
     std::lock_guard<std::mutex> lk(g_prof_mu);
     if (g_prof_used >= g_prof_pool.size()) {
@@ -67,6 +70,8 @@ void gs_prof_take(int region, cudaEvent_t *a, cudaEvent_t *b) {
     *b = e.b;
 }
 void gs_count_launch(unsigned long long n) { GS_COUNT(n); }
+
+void gs_set_last_error(const char *msg) { snprintf(g_last_error, sizeof(g_last_error), "%s", msg ? msg : ""); }
 
 static int set_cuda_error(cudaError_t e, const char *where) {
     snprintf(g_last_error, sizeof(g_last_error), "%s: %s", where, cudaGetErrorString(e));
@@ -83,31 +88,31 @@ static int set_cuda_error(cudaError_t e, const char *where) {
 // ----------------------------------------------------------------------------------------------------
 // block-wide helpers
 
-template <int NT>
-__device__ __forceinline__ int block_excl_scan(int v, int *warp_sums, int *total) {
+template <int NT, typename T = int>
+__device__ __forceinline__ T block_excl_scan(T v, T *warp_sums, T *total) {
     constexpr int NWARP = NT / 32;
     int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int x = v;
+    T x = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        int y = __shfl_up_sync(0xffffffffu, x, o);
+        T y = __shfl_up_sync(0xffffffffu, x, o);
         if (lane >= o) x += y;
     }
     if (lane == 31) warp_sums[warp] = x;
     __syncthreads();
     if (warp == 0) {
-        int s = lane < NWARP ? warp_sums[lane] : 0;
+        T s = lane < NWARP ? warp_sums[lane] : (T)0;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            int y = __shfl_up_sync(0xffffffffu, s, o);
+            T y = __shfl_up_sync(0xffffffffu, s, o);
             if (lane >= o) s += y;
         }
         if (lane < NWARP) warp_sums[lane] = s;  // inclusive
     }
     __syncthreads();
-    int warp_prefix = warp > 0 ? warp_sums[warp - 1] : 0;
+    T warp_prefix = warp > 0 ? warp_sums[warp - 1] : (T)0;
     if (total) *total = warp_sums[NWARP - 1];
-    int r = warp_prefix + x - v;
+    T r = warp_prefix + x - v;
     __syncthreads();
     return r;
 }
@@ -183,10 +188,10 @@ __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *_
                                                     const float *__restrict__ ls, const float *__restrict__ col,
                                                     const float *__restrict__ op, const float *__restrict__ th,
                                                     SplatRec *__restrict__ rec, int4 *__restrict__ meta,
-                                                    int *__restrict__ counts, int *__restrict__ bsum,
+                                                    int *__restrict__ counts, long long *__restrict__ bsum,
                                                     unsigned long long *__restrict__ gpairs,
                                                     int *__restrict__ gsplats) {
-    __shared__ int wsum[8];
+    __shared__ long long wsum[8];
     __shared__ unsigned long long s_pairs[4 * GS_MAX_GROUPS];
     __shared__ int s_spl[4 * GS_MAX_GROUPS];
     if (threadIdx.x < 4 * GS_MAX_GROUPS) {
@@ -248,34 +253,46 @@ __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *_
         atomicAdd(&gpairs[bb * G.ngroups + gg], s_pairs[threadIdx.x]);
         atomicAdd(&gsplats[bb * G.ngroups + gg], s_spl[threadIdx.x]);
     }
-    // per-block pair total
-    int v = count;
+    // per-block pair total (64-bit: 256 splats of up to 2^31 tiles each)
+    long long v = count;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = v;
     __syncthreads();
     if (threadIdx.x == 0) {
-        int t = 0;
+        long long t = 0;
         for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += wsum[w];
         bsum[blockIdx.x] = t;
     }
 }
 
-// single-block exclusive scan of n ints in place; total -> *total (as long long)
-__global__ void __launch_bounds__(1024) k_scan_blocks(int *__restrict__ data, int n, long long *__restrict__ total) {
-    __shared__ int wsum[32];
+// Layout of the 64-byte status block of a render workspace (zeroed before every forward).
+#define MISC_TOTAL 0   // long long: pairs of the whole call
+#define MISC_STATUS 8  // int: bit 0 set when the pairs exceed the workspace's pair capacity
+#define MISC_NEFF 16   // long long: pairs the sort and the field kernels process (0 after an overflow)
+
+// single-block exclusive scan of the n per-block pair totals in place (64-bit); the call's pair total ->
+// misc.  When the total exceeds the pair capacity nothing is emitted or sorted (the effective count stays
+// 0 and the status bit is set), so no kernel writes past the pair buffers; the host reports the overflow.
+__global__ void __launch_bounds__(1024) k_scan_blocks(long long *__restrict__ data, int n, long long cap,
+                                                      unsigned char *__restrict__ misc) {
+    __shared__ long long wsum[32];
     int per = (n + 1023) / 1024;
     int lo = threadIdx.x * per, hi = min(n, lo + per);
-    int s = 0;
+    long long s = 0;
     for (int i = lo; i < hi; i++) s += data[i];
-    int tot;
-    int pre = block_excl_scan<1024>(s, wsum, &tot);
+    long long tot;
+    long long pre = block_excl_scan<1024, long long>(s, wsum, &tot);
     for (int i = lo; i < hi; i++) {
-        int v = data[i];
+        long long v = data[i];
         data[i] = pre;
         pre += v;
     }
-    if (threadIdx.x == 0) *total = tot;
+    if (threadIdx.x == 0) {
+        *reinterpret_cast<long long *>(misc + MISC_TOTAL) = tot;
+        if (tot > cap) *reinterpret_cast<int *>(misc + MISC_STATUS) |= 1;
+        *reinterpret_cast<long long *>(misc + MISC_NEFF) = tot > cap ? 0 : tot;
+    }
 }
 
 // pairs in splat order: key = global tile id, value = global splat id.  Splat block j (256 splats, the
@@ -284,14 +301,17 @@ __global__ void __launch_bounds__(1024) k_scan_blocks(int *__restrict__ data, in
 // c = ceil(tot_j / parts).  Each emit block also writes the digit-0 histogram of its sub-segment
 // (hist0 column = emit block), so the first radix pass needs no separate counting sweep.
 __global__ void __launch_bounds__(256) k_emit(RenderGeom G, const int4 *__restrict__ meta,
-                                              const int *__restrict__ counts, const int *__restrict__ bpre,
+                                              const int *__restrict__ counts, const long long *__restrict__ bpre,
                                               int parts, unsigned *__restrict__ keys, int *__restrict__ vals,
-                                              int *__restrict__ status, int *__restrict__ hist0, int hist_stride,
-                                              int radix0) {
+                                              const unsigned char *__restrict__ misc, int *__restrict__ hist0,
+                                              int hist_stride, int radix0) {
     __shared__ int wsum[8];
     __shared__ int soff[257];
     __shared__ int4 smeta[256];
     __shared__ int shist[256];
+    // after a capacity overflow (k_scan_blocks) nothing is emitted; otherwise every position below is
+    // < total <= cap < 2^31, so the block-local offsets fit in 32 bits
+    if (*reinterpret_cast<const int *>(misc + MISC_STATUS) != 0) return;
     if (hist0)
         for (int d = threadIdx.x; d < radix0; d += 256) shist[d] = 0;
     const int j = blockIdx.x / parts, part = blockIdx.x - j * parts;
@@ -309,7 +329,7 @@ __global__ void __launch_bounds__(256) k_emit(RenderGeom G, const int4 *__restri
     smeta[threadIdx.x] = mt;
     if (threadIdx.x == 0) soff[256] = tot;
     __syncthreads();
-    long long base = bpre[j];
+    const long long base = bpre[j];
     const int chunk = (tot + parts - 1) / parts;
     const int e_lo = min(part * chunk, tot), e_hi = min(e_lo + chunk, tot);
     for (int e = e_lo + threadIdx.x; e < e_hi; e += 256) {
@@ -324,13 +344,11 @@ __global__ void __launch_bounds__(256) k_emit(RenderGeom G, const int4 *__restri
         int w = m.y & 0xffffff;
         int q = r / w;
         unsigned tile = (unsigned)(m.x + q * m.z + (r - q * w));
-        long long pos = base + e;
-        if (pos < G.cap) {
+        const long long pos = base + e;
+        if (pos >= 0 && pos < G.cap) {  // always true when the status is clear (total <= cap)
             keys[pos] = tile;
             vals[pos] = (int)(s0 + lo);
             if (hist0) atomicAdd(&shist[tile & (unsigned)(radix0 - 1)], 1);
-        } else {
-            atomicOr(status, 1);
         }
     }
     if (hist0) {
@@ -347,6 +365,7 @@ __global__ void __launch_bounds__(256) k_emit(RenderGeom G, const int4 *__restri
 #define RS_ROUNDS 8
 #define RS_ITEMS (RS_THREADS * RS_ROUNDS)
 
+// n_ptr points at the effective pair count (MISC_NEFF: 0 after a capacity overflow)
 __device__ __forceinline__ long long clamp_n(const long long *n_ptr, long long cap) {
     long long n = *n_ptr;
     return n < cap ? n : cap;
@@ -452,7 +471,7 @@ __device__ __forceinline__ void rs_chunk(RsSmem &sm, const unsigned *__restrict_
             tot += c;
         }
     }
-    const int lb = block_excl_scan<RS_THREADS>(tot, sm.wsum, nullptr);  // ends with a block barrier
+    const int lb = block_excl_scan<RS_THREADS, int>(tot, sm.wsum, nullptr);  // ends with a block barrier
     if (tid < radix) sm.lbase[tid] = lb;
     __syncthreads();
 #pragma unroll
@@ -492,7 +511,7 @@ __global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep(const unsigned *
     const int nblk = (int)((n + RS_ITEMS - 1) / RS_ITEMS);
     const int tid = threadIdx.x;
     const int dv = tid < radix ? dtot[tid] : 0;
-    const int dpre = block_excl_scan<RS_THREADS>(dv, sm.wsum, nullptr);
+    const int dpre = block_excl_scan<RS_THREADS, int>(dv, sm.wsum, nullptr);
     if (tid < radix) dbase[tid] = dpre;
     for (int vb = blockIdx.x; vb < nblk; vb += gridDim.x) {
         if (tid < radix) sm.gbase[tid] = dbase[tid] + hist[tid * nblk_cap + vb];
@@ -509,7 +528,7 @@ __global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep_seg(const unsign
                                                                     const int *__restrict__ vin,
                                                                     unsigned *__restrict__ kout,
                                                                     int *__restrict__ vout,
-                                                                    const int *__restrict__ bpre, int nblk_pre,
+                                                                    const long long *__restrict__ bpre, int nblk_pre,
                                                                     int parts, const long long *__restrict__ n_ptr,
                                                                     long long cap, int shift, int radix,
                                                                     const int *__restrict__ hist, int hist_stride,
@@ -520,13 +539,13 @@ __global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep_seg(const unsign
     const long long n = clamp_n(n_ptr, cap);
     const int tid = threadIdx.x;
     const int dv = tid < radix ? dtot[tid] : 0;
-    const int dpre = block_excl_scan<RS_THREADS>(dv, sm.wsum, nullptr);
+    const int dpre = block_excl_scan<RS_THREADS, int>(dv, sm.wsum, nullptr);
     if (tid < radix) dbase[tid] = dpre;
     const int nseg = nblk_pre * parts;
     for (int j = blockIdx.x; j < nseg; j += gridDim.x) {
         const int sb = j / parts, part = j - sb * parts;
         const long long beg = bpre[sb];
-        const long long end = sb + 1 < nblk_pre ? (long long)bpre[sb + 1] : n;
+        const long long end = sb + 1 < nblk_pre ? bpre[sb + 1] : n;
         const long long tot = end - beg;
         const long long chunk = (tot + parts - 1) / parts;
         const long long b0 = min(beg + min(part * chunk, tot), n);
@@ -1568,6 +1587,13 @@ long long pair_bound(const gs_render_desc *d, const RenderGeom &G) {
     return worst * (long long)d->N * d->B;
 }
 
+// Splats of one image that group g may hold: every splat in octave mode (routing is by scale), the
+// head split in multires mode.
+long long group_splats(const gs_render_desc *d, int g) {
+    if (d->mode == GS_MODE_MULTIRES && d->n_coarse > 0 && d->n_coarse < d->N) return g == 0 ? d->n_coarse : d->N - d->n_coarse;
+    return d->N;
+}
+
 void make_plan(const gs_render_desc *d, Plan &pl) {
     memset(&pl, 0, sizeof(pl));
     make_geom(d, pl.G);
@@ -1590,7 +1616,7 @@ void make_plan(const gs_render_desc *d, Plan &pl) {
     pl.o_rec = take(sizeof(SplatRec) * (size_t)std::max<long long>(BN, 1));
     pl.o_meta = take(sizeof(int4) * (size_t)std::max<long long>(BN, 1));
     pl.o_counts = take(sizeof(int) * (size_t)std::max<long long>(BN, 1));
-    pl.o_bsum = take(sizeof(int) * (size_t)pl.nblk_pre);
+    pl.o_bsum = take(sizeof(long long) * (size_t)pl.nblk_pre);
     // zeroed block: group stats, misc (total pairs as int64 + status), tile ranges
     pl.o_zero = o;
     pl.o_gpairs = take(sizeof(unsigned long long) * (size_t)d->B * pl.ngroups);
@@ -1649,6 +1675,19 @@ void make_plan(const gs_render_desc *d, Plan &pl) {
     pl.total_bytes = o;
 }
 
+// The pair counts must be read back (one stream sync) before the pairs are emitted when the host bound
+// cannot rule out (a) a (image, group) pair count above the budget max_pairs -- the reference's
+// _build_tiles refusal, render_triton.py:378-385 -- or (b) more pairs than the workspace's pair capacity
+// (a capacity set below gs_render_pair_bound).
+bool needs_exact_check(const gs_render_desc *d, const Plan &pl) {
+    if (d->mode == GS_MODE_EXACT || d->N <= 0) return false;
+    if (pl.cap < pair_bound(d, pl.G)) return true;
+    if (d->max_pairs < 0) return false;
+    for (int g = 0; g < pl.G.ngroups; g++)
+        if (group_tile_bound(d, pl.G, g) * group_splats(d, g) > d->max_pairs) return true;
+    return false;
+}
+
 template <typename T>
 T *at(void *ws, size_t off) { return reinterpret_cast<T *>(reinterpret_cast<char *>(ws) + off); }
 
@@ -1682,9 +1721,48 @@ int run_preprocess(const Plan &pl, const float *mu, const float *ls, const float
     if (e != cudaSuccess) return set_cuda_error(e, "memset");
     k_preprocess<<<pl.nblk_pre, 256, 0, st>>>(G, mu, ls, col, op, G.has_theta ? th : nullptr, at<SplatRec>(ws, pl.o_rec),
                                               at<int4>(ws, pl.o_meta), at<int>(ws, pl.o_counts),
-                                              at<int>(ws, pl.o_bsum), at<unsigned long long>(ws, pl.o_gpairs),
+                                              at<long long>(ws, pl.o_bsum), at<unsigned long long>(ws, pl.o_gpairs),
                                               at<int>(ws, pl.o_gsplats));
     GS_CHECK_LAUNCH("k_preprocess");
+    return GS_OK;
+}
+
+// Exact check after k_preprocess (its per-(image, group) pair counts are in the workspace): copies them to
+// the host, synchronising the stream.  GS_ERR_PAIR_BUDGET when one (image, group) exceeds d->max_pairs,
+// GS_ERR_WORKSPACE when the call's pairs exceed the pair capacity; refused during stream capture, where a
+// synchronisation is not possible (size the capacity from gs_render_pair_bound or gs_render_count then).
+int exact_check(const gs_render_desc *d, const Plan &pl, void *ws, cudaStream_t s) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone) {
+        snprintf(g_last_error, sizeof(g_last_error),
+                 "gs_render_fwd: the pair budget / pair capacity check needs the exact pair counts (a stream "
+                 "synchronisation), which stream capture does not allow; capture with pair_capacity = 0 and a "
+                 "budget the host bound satisfies");
+        return GS_ERR_BAD_ARGUMENT;
+    }
+    const int n = d->B * pl.ngroups;
+    std::vector<unsigned long long> cnt((size_t)n);
+    cudaError_t e = cudaMemcpyAsync(cnt.data(), at<unsigned long long>(ws, pl.o_gpairs),
+                                    sizeof(unsigned long long) * (size_t)n, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return set_cuda_error(e, "gs_render_fwd (pair check)");
+    unsigned long long worst = 0, total = 0;
+    for (int i = 0; i < n; i++) {
+        worst = std::max(worst, cnt[(size_t)i]);
+        total += cnt[(size_t)i];
+    }
+    if (d->max_pairs >= 0 && worst > (unsigned long long)d->max_pairs) {
+        snprintf(g_last_error, sizeof(g_last_error),
+                 "%llu (tile, splat) pairs in one (image, group) exceed the %lld budget @ %dx%d TILE=%d cutoff=%g "
+                 "N=%d; refusing to render", worst, (long long)d->max_pairs, d->H, d->W, d->tile, (double)d->cutoff,
+                 d->N);
+        return GS_ERR_PAIR_BUDGET;
+    }
+    if (total > (unsigned long long)pl.cap) {
+        snprintf(g_last_error, sizeof(g_last_error),
+                 "%llu (tile, splat) pairs exceed the workspace's pair capacity %lld", total, (long long)pl.cap);
+        return GS_ERR_WORKSPACE;
+    }
     return GS_OK;
 }
 
@@ -1849,21 +1927,25 @@ int gs_render_fwd_prior(const gs_render_desc *d, const float *mu, const float *l
         }
     }
     const RenderGeom &G = pl.G;
-    std::unique_ptr<ProfScope> bin_scope(new ProfScope(PR_BIN, s));
+    std::unique_ptr<ProfScope> bin_scope(new ProfScope(gs_prof_internal() ? PR_ENC_BIN : PR_BIN, s));
     st = run_preprocess(pl, mu, log_scale, color, opacity, theta, workspace, s);
     if (st != GS_OK) return st;
-    long long *total = at<long long>(workspace, pl.o_misc);
-    int *status = at<int>(workspace, pl.o_misc + 8);
+    unsigned char *misc = at<unsigned char>(workspace, pl.o_misc);
+    const long long *n_eff = reinterpret_cast<const long long *>(misc + MISC_NEFF);
     if (d->mode != GS_MODE_EXACT && d->N > 0) {
-        k_scan_blocks<<<1, 1024, 0, s>>>(at<int>(workspace, pl.o_bsum), pl.nblk_pre, total);
+        if (needs_exact_check(d, pl)) {
+            st = exact_check(d, pl, workspace, s);
+            if (st != GS_OK) return st;
+        }
+        k_scan_blocks<<<1, 1024, 0, s>>>(at<long long>(workspace, pl.o_bsum), pl.nblk_pre, pl.cap, misc);
         GS_CHECK_LAUNCH("k_scan_blocks");
         int radix = 1 << pl.radix_bits;
         int *hist = at<int>(workspace, pl.o_hist), *dtot = at<int>(workspace, pl.o_dtot);
         const int nemit = pl.nblk_pre * pl.emit_parts;
         k_emit<<<nemit, 256, 0, s>>>(G, at<int4>(workspace, pl.o_meta), at<int>(workspace, pl.o_counts),
-                                     at<int>(workspace, pl.o_bsum), pl.emit_parts, at<unsigned>(workspace, pl.o_keys_a),
-                                     at<int>(workspace, pl.o_vals_a), status, pl.passes > 0 ? hist : nullptr, nemit,
-                                     radix);
+                                     at<long long>(workspace, pl.o_bsum), pl.emit_parts,
+                                     at<unsigned>(workspace, pl.o_keys_a), at<int>(workspace, pl.o_vals_a), misc,
+                                     pl.passes > 0 ? hist : nullptr, nemit, radix);
         GS_CHECK_LAUNCH("k_emit");
         unsigned *ka = at<unsigned>(workspace, pl.o_keys_a), *kb = at<unsigned>(workspace, pl.o_keys_b);
         int *va = at<int>(workspace, pl.o_vals_a), *vb = at<int>(workspace, pl.o_vals_b);
@@ -1872,18 +1954,18 @@ int gs_render_fwd_prior(const gs_render_desc *d, const float *mu, const float *l
             int shift = p * pl.radix_bits;
             if (p == 0) {
                 // digit-0 histograms per emit segment come from k_emit
-                k_radix_scan<<<radix, 256, 0, s>>>(hist, total, pl.cap, nemit, dtot, nemit);
+                k_radix_scan<<<radix, 256, 0, s>>>(hist, n_eff, pl.cap, nemit, dtot, nemit);
                 GS_CHECK_LAUNCH("k_radix_scan");
                 k_radix_downsweep_seg<<<std::min(nemit, 148 * 8), RS_THREADS, sizeof(RsSmem), s>>>(
-                    ka, va, kb, vb, at<int>(workspace, pl.o_bsum), pl.nblk_pre, pl.emit_parts, total, pl.cap, shift,
-                    radix, hist, nemit, dtot);
+                    ka, va, kb, vb, at<long long>(workspace, pl.o_bsum), pl.nblk_pre, pl.emit_parts, n_eff, pl.cap,
+                    shift, radix, hist, nemit, dtot);
                 GS_CHECK_LAUNCH("k_radix_downsweep_seg");
             } else {
-                k_radix_upsweep<<<pgrid, RS_THREADS, 0, s>>>(ka, total, pl.cap, shift, radix, hist, pl.nblk_sort);
+                k_radix_upsweep<<<pgrid, RS_THREADS, 0, s>>>(ka, n_eff, pl.cap, shift, radix, hist, pl.nblk_sort);
                 GS_CHECK_LAUNCH("k_radix_upsweep");
-                k_radix_scan<<<radix, 256, 0, s>>>(hist, total, pl.cap, pl.nblk_sort, dtot, 0);
+                k_radix_scan<<<radix, 256, 0, s>>>(hist, n_eff, pl.cap, pl.nblk_sort, dtot, 0);
                 GS_CHECK_LAUNCH("k_radix_scan");
-                k_radix_downsweep<<<pgrid, RS_THREADS, sizeof(RsSmem), s>>>(ka, va, kb, vb, total, pl.cap, shift,
+                k_radix_downsweep<<<pgrid, RS_THREADS, sizeof(RsSmem), s>>>(ka, va, kb, vb, n_eff, pl.cap, shift,
                                                                             radix, hist, pl.nblk_sort, dtot);
                 GS_CHECK_LAUNCH("k_radix_downsweep");
             }
@@ -1891,12 +1973,12 @@ int gs_render_fwd_prior(const gs_render_desc *d, const float *mu, const float *l
             std::swap(va, vb);
         }
         unsigned nrb = (unsigned)std::min<long long>(std::max<long long>(1, (pl.cap + 255) / 256), 148 * 8);
-        k_ranges<<<nrb, 256, 0, s>>>(ka, total, pl.cap, at<int2>(workspace, pl.o_ranges));
+        k_ranges<<<nrb, 256, 0, s>>>(ka, n_eff, pl.cap, at<int2>(workspace, pl.o_ranges));
         GS_CHECK_LAUNCH("k_ranges");
     }
     bin_scope.reset();
     {
-        ProfScope ps(PR_FIELDS_FWD, s);
+        ProfScope ps(gs_prof_internal() ? PR_ENC_FIELDS_FWD : PR_FIELDS_FWD, s);
         st = launch_fields_fwd(pl, workspace, s);
         if (st != GS_OK) return st;
         if (G.skip_n > 0) {

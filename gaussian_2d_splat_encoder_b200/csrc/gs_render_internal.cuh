@@ -27,3 +27,6 @@ int gs_render_prior_map(const gs_render_desc *prior_d, const void *prior_ws, con
 int gs_render_fwd_prior(const gs_render_desc *d, const float *mu, const float *log_scale, const float *color,
                         const float *opacity, const float *bg, const float *theta, float *out, const GsPrior *prior,
                         void *workspace, size_t workspace_bytes, void *stream);
+
+// Sets the text gs_last_error returns to the calling thread.
+void gs_set_last_error(const char *msg);

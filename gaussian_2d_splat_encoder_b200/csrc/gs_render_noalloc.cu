@@ -15,13 +15,18 @@
 //     clears the parts it needs zeroed), so calls whose work overlaps on the GPU -- different streams,
 //     or other host threads -- race and must be serialised by the caller;
 //   * the first call on each device looks up the array's device address (cudaGetSymbolAddress) with
-//     that device current; make that first call before any stream capture.
+//     that device current; make that first call before any stream capture.  The address is kept for the
+//     life of the process: after a cudaDeviceReset the library has to be reloaded;
+//   * the render's own checks apply as in gs_render_fwd: a pair_capacity below gs_render_pair_bound, or a
+//     max_pairs the host bound cannot rule out, makes the call count the pairs first (one stream
+//     synchronisation) and refuse with GS_ERR_WORKSPACE / GS_ERR_PAIR_BUDGET instead of truncating.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <mutex>
 
 #include "../../include/gsplat_b200.h"
+#include "gs_render_internal.cuh"
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[GS_NOALLOC_SCRATCH_BYTES];
 
@@ -34,12 +39,23 @@ void *g_noalloc_ptr[kMaxDevices] = {nullptr};
 // host-side stand-in, so the address has to come from cudaGetSymbolAddress, once per device.
 int scratch_address(void **out) {
     int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GS_ERR_CUDA;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        gs_set_last_error(cudaGetErrorString(e));
+        return GS_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= kMaxDevices) {
+        gs_set_last_error("gs_render_fwd_noalloc: device index beyond the 64 this library tracks");
+        return GS_ERR_CUDA;
+    }
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     if (!g_noalloc_ptr[dev]) {
         void *p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p) return GS_ERR_CUDA;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            gs_set_last_error(e != cudaSuccess ? cudaGetErrorString(e) : "cudaGetSymbolAddress returned NULL");
+            return GS_ERR_CUDA;
+        }
         g_noalloc_ptr[dev] = p;
     }
     *out = g_noalloc_ptr[dev];

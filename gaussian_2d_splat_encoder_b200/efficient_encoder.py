@@ -230,10 +230,12 @@ def pack_weights(enc, device) -> dict:
         hc_w=f32(hc_w), hc_b=f32(hc_b), hf_w=f32(hf_w), hf_b=f32(hf_b))
 
 
-def cuda_forward(enc, image, return_latents, render):
+def cuda_forward(enc, image, return_latents, render, workspace=None):
     """gs_encoder_fwd / gs_encode_render_fwd for any object that provides the packed weights
     (`_weights(device)` -> (tensors, _GsEncoderWeights)), `_desc(B, H, W)` and the attributes M, Mf,
-    d_feature, use_rotation and latent_ch: the nn.Module and the pre-packed checkpoint share it."""
+    d_feature, use_rotation and latent_ch: the nn.Module and the pre-packed checkpoint share it.
+    `workspace` (optional): a caller-owned uint8 CUDA tensor of at least the size the library asks for,
+    used instead of a fresh allocation (it then holds the call's binning for the debug accessors)."""
     dev = _lib.require_cuda(image)
     if image.dim() != 4 or image.shape[1] != 3:
         raise ValueError("image must be [B,3,H,W]")
@@ -266,7 +268,12 @@ def cuda_forward(enc, image, return_latents, render):
                  bg=torch.empty(B, 3, device=dev))
         feat = torch.empty(B, H // 8, W // 8, enc.d_feature, device=dev)
         lat = torch.empty(B, H // 4, W // 4, enc.latent_ch, device=dev) if return_latents else None
-        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        if workspace is not None:
+            if workspace.dtype != torch.uint8 or workspace.device != dev or workspace.numel() < nbytes:
+                raise ValueError(f"workspace must be a uint8 tensor on {dev} of at least {nbytes} bytes")
+            ws = workspace
+        else:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         p = _lib.ptr
         args = [C.byref(d), C.byref(wst), p(x), p(o["mu"]), p(o["log_scale"]), p(o["color"]), p(o["opacity"]),
                 p(o["theta"]), p(o["bg"]), p(feat), p(lat)]

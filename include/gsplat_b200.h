@@ -57,8 +57,12 @@ typedef struct {
     int32_t coarse_factor; /* multires mode (reference default 8) */
     float cutoff;          /* bbox radius in sigmas (reference default 3.0) */
     float base_texels;     /* octave mode (reference default 8.0) */
-    int64_t max_pairs;     /* per (image, group) pair budget; < 0 disables the check */
-    int64_t pair_capacity; /* pairs the workspace holds for the whole batch; 0 -> gs_render_pair_bound */
+    int64_t max_pairs;     /* per (image, group) pair budget; < 0 disables the check.  gs_render_fwd refuses a
+                              render with more pairs in one (image, group) (GS_ERR_PAIR_BUDGET), as the
+                              reference's _build_tiles does (render_triton.py:378-385) */
+    int64_t pair_capacity; /* pairs the workspace holds for the whole batch; 0 -> gs_render_pair_bound.  A
+                              capacity below the bound makes gs_render_fwd count first and refuse a render
+                              that would not fit (GS_ERR_WORKSPACE); pairs are never silently dropped */
     int32_t row_begin;     /* native row band [row_begin, row_end) this call renders (tile-row sharding); */
     int32_t row_end;       /* row_end <= 0 -> all rows.  Output rows outside the band are not written and
                               the backward reads grad_out only inside it. */
@@ -82,7 +86,9 @@ size_t gs_render_workspace_size(const gs_render_desc *d, int with_backward);
  * GS_ERR_WORKSPACE before any launch; every GPU that loads the library holds the array until exit;
  * all calls on a device share it, so calls that overlap on the GPU (other streams or threads) race and
  * must be serialised by the caller; the first call on a device looks up the array's address and
- * should come before any stream capture.  There is no backward variant. */
+ * should come before any stream capture (the address is cached for the process's life, so a
+ * cudaDeviceReset needs a reload of the library).  The pair checks of gs_render_fwd apply unchanged.
+ * There is no backward variant. */
 #define GS_NOALLOC_SCRATCH_BYTES (32u << 20)
 int gs_render_fwd_noalloc(const gs_render_desc *d, const float *mu, const float *log_scale, const float *color,
                           const float *opacity, const float *bg, const float *theta, float *out, void *stream);
@@ -96,7 +102,13 @@ int gs_render_count(const gs_render_desc *d, const float *mu, const float *log_s
 
 /* Forward render: out [B][C][H][W].  Replaces _forward_cull / _forward_cull_fields + the octave loop
  * of render_alpha_octave / render_alpha_multires + the exact _forward (render_triton.py:128-157,
- * 538-600, 879-980).  Keeps the state its backward needs in the workspace. */
+ * 538-600, 879-980).  Keeps the state its backward needs in the workspace.
+ * Pair checks: when the host bound (gs_render_pair_bound, per group) cannot rule out a (image, group)
+ * count above max_pairs, or pair_capacity is below the bound, the call reads the exact counts back first
+ * (one synchronisation of `stream`, like the reference's .item()) and returns GS_ERR_PAIR_BUDGET
+ * (budget) or GS_ERR_WORKSPACE (capacity) without rendering.  That read-back is not possible while
+ * `stream` is being captured: such a call returns GS_ERR_BAD_ARGUMENT (capture with pair_capacity = 0
+ * and a budget the bound satisfies).  The kernels themselves never write past the pair capacity. */
 int gs_render_fwd(const gs_render_desc *d, const float *mu, const float *log_scale, const float *color,
                   const float *opacity, const float *bg, const float *theta, float *out, void *workspace,
                   size_t workspace_bytes, void *stream);
@@ -207,6 +219,11 @@ int gs_encode_render_fwd(const gs_encoder_desc *e, const gs_encoder_weights *w, 
                          float *log_scale, float *color, float *opacity, float *theta, float *bg, float *features,
                          float *latents, float *out, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Debug accessor of a gs_encode_render_fwd workspace (SYNCHRONOUS, like gs_render_debug_bins): pairs[0] =
+ * (tile, splat) pairs of the encoder's internal coarse render, pairs[1] = pairs the final render binned
+ * (the coarse splats whose fields it reused from the internal render are not binned again). */
+int gs_encode_render_debug_pairs(const gs_encoder_desc *e, const void *workspace, int64_t *pairs);
+
 /* Reads (synchronously) the bounded-wait error flag left in an encoder workspace (0 = none). */
 int gs_encoder_error_flag(const gs_encoder_desc *e, const void *workspace, int *flag_host);
 
@@ -231,7 +248,8 @@ uint64_t gs_kernel_launches(void);
 /* Device-time profiling of library stages.  While enabled, the entry points record CUDA events on
  * their stream around each stage; gs_profile_collect waits for them and returns per-stage totals (ms)
  * and call counts (arrays of 16): 0 binning (preprocess..tile ranges), 1 fields forward, 2 composite,
- * 3 composite backward + upsample adjoint, 4 fields backward, 5 finalize, 8 encoder input preparation,
+ * 3 composite backward + upsample adjoint, 4 fields backward, 5 finalize, 6 binning and 7 fields forward
+ * of the encoder's internal coarse render, 8 encoder input preparation,
  * 9..12 encoder convolutions 1..4, 13 encoder heads, 14 encoder GroupNorm/concat/cond, 15 the
  * encoder's internal coarse render. */
 void gs_profile_enable(int on);

@@ -16,11 +16,6 @@ def render_cases():
     return sorted(p.stem[len("render_"):] for p in GOLDEN.glob("render_*.npz"))
 
 
-# Fixtures (made by the reference, pinned against the oracle on the CPU) whose CUDA parity has not been run
-# on a GPU yet: the GPU parity test skips them until it has.
-GPU_PENDING = {"octave_c1_odds", "cull_c2_alpha_noth", "octave_tile16_odds", "octave_c5_odds"}
-
-
 def load_render(name):
     d = np.load(GOLDEN / f"render_{name}.npz", allow_pickle=False)
     kw = {k[3:]: d[k].item() for k in d.files if k.startswith("kw_")}

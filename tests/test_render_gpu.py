@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden_util import GOLDEN, GPU_PENDING, fnv_tile_hash, grad_rel, load_render, render_cases
+from golden_util import GOLDEN, fnv_tile_hash, grad_rel, load_render, render_cases
 
 pytestmark = pytest.mark.gpu
 
@@ -34,8 +34,6 @@ def _run_api(fn, ins, H, W, gC, kw, dev="cuda"):
 
 @pytest.mark.parametrize("name", render_cases())
 def test_render_matches_reference(lib, name):
-    if name in GPU_PENDING:
-        pytest.skip("fixture added after the last GPU run; its CUDA parity is still to be measured")
     c = load_render(name)
     fn = getattr(_api(), c["fn"])
     out, g = _run_api(fn, c["ins"], c["H"], c["W"], c["gC"], c["kw"])

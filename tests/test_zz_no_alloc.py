@@ -23,12 +23,12 @@ def _inputs(N, H, W, seed):
     return [s[k].cuda().contiguous() for k in KEYS]
 
 
-def _desc(N, H, W):
+def _desc(N, H, W, capacity=0):
     from gaussian_2d_splat_encoder_b200 import _lib
     from gaussian_2d_splat_encoder_b200.render_triton import _desc as mk
 
     return mk(mode=_lib.MODE_OCTAVE, B=1, N=N, C=3, H=H, W=W, TILE=8, odds=True, has_theta=True, cutoff=3.0,
-              base_texels=8.0, max_octaves=6, max_pairs=48_000_000)
+              base_texels=8.0, max_octaves=6, max_pairs=48_000_000, capacity=capacity)
 
 
 def _with_workspace(lib, d, ins, H, W):
@@ -64,6 +64,41 @@ def test_no_alloc_forward_matches_workspace_forward(lib):
         torch.cuda.synchronize()
         assert st == 0
         assert torch.allclose(got, ref, atol=1e-6, rtol=0), (got - ref).abs().max().item()
+
+
+def test_no_alloc_smaller_render_after_larger(lib):
+    """A smaller render (other size, fewer splats) right after a 256^2 one: the previous call's tile ranges
+    and fields left in the shared array must not leak into it."""
+    big = _desc(6000, 256, 256)
+    ins = _inputs(6000, 256, 256, 23)
+    st, _ = _no_alloc(lib, big, ins, 256, 256)
+    assert st == 0
+    H, W, N = 96, 160, 700
+    d = _desc(N, H, W)
+    ins = _inputs(N, H, W, 24)
+    ref = _with_workspace(lib, d, ins, H, W)
+    st, got = _no_alloc(lib, d, ins, H, W)
+    torch.cuda.synchronize()
+    assert st == 0
+    assert torch.allclose(got, ref, atol=1e-6, rtol=0), (got - ref).abs().max().item()
+
+
+def test_no_alloc_explicit_pair_capacity(lib):
+    """An explicit pair capacity below the real pair count is refused (GS_ERR_WORKSPACE), never rendered
+    with pairs dropped; a capacity that holds every pair renders like the default."""
+    from gaussian_2d_splat_encoder_b200 import _lib
+
+    H = W = 256
+    N = 6000
+    ins = _inputs(N, H, W, 25)
+    ref = _with_workspace(lib, _desc(N, H, W), ins, H, W)
+    st, _ = _no_alloc(lib, _desc(N, H, W, capacity=500), ins, H, W)
+    torch.cuda.synchronize()
+    assert st == _lib.GS_ERR_WORKSPACE
+    st, got = _no_alloc(lib, _desc(N, H, W, capacity=64 * N), ins, H, W)
+    torch.cuda.synchronize()
+    assert st == 0
+    assert torch.allclose(got, ref, atol=1e-6, rtol=0), (got - ref).abs().max().item()
 
 
 def test_no_alloc_refuses_oversized_render(lib):
