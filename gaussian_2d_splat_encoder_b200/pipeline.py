@@ -7,8 +7,8 @@ into a CUDA graph and replay it: the same kernels, the same numerics, one launch
 
 * ``EncodeRender`` -- ``EfficientGaussianEncoder`` forward + ``render_alpha_octave`` of its splats
   (examples/encode_and_render.py:31-38 of the reference), inference.
-* ``EncodeRenderStream`` -- the same for a stream of host images, with the PCIe copies of neighbouring
-  images overlapped with the kernels.
+* ``EncodeRenderStream`` -- the same for a stream of images, several in flight at once on their own
+  streams, with the PCIe copies of neighbouring images overlapped with the kernels.
 * ``RenderFitStep`` -- ``render_alpha_octave`` forward + an L2 loss + the gradients of the six splat
   leaves (the fitting step of configs 1 and 4).
 
@@ -79,17 +79,20 @@ class EncodeRender:
 class EncodeRenderStream:
     """Throughput form of ``EncodeRender`` for a stream of host images (config 3's image batches).
 
-    ``depth`` graph instances, each with its own input and output buffers, take images in turn: the
-    host-to-device copy of the next image and the device-to-host copy of the previous reconstruction run
-    on their own streams while the current image is encoded and rendered, so PCIe traffic hides behind
-    the kernels.  ``submit(image, out)`` enqueues one image (pinned host [1,3,H,W]) and its destination
-    (pinned host [1,3,H,W]); ``synchronize()`` waits for every submitted reconstruction."""
+    ``depth`` graph instances, each with its own input, workspace and output buffers and its own compute
+    stream, take images in turn: up to ``depth`` images are encoded and rendered at once (one image's
+    latency-bound kernel chains -- binning, the small convolutions -- leave most SMs idle, which the
+    neighbouring images fill), and the host-to-device copy of the next image and the device-to-host copy
+    of a finished reconstruction run on their own streams, so PCIe traffic hides behind the kernels.
+    ``submit(image, out)`` enqueues one image (pinned host or device [1,3,H,W]) and optionally its
+    destination (pinned host [1,3,H,W]); ``synchronize()`` waits for every submitted reconstruction."""
 
-    def __init__(self, encoder, H: int, W: int, device=None, depth: int = 2):
+    def __init__(self, encoder, H: int, W: int, device=None, depth: int = 4):
         self.slots = [EncodeRender(encoder, 1, H, W, device) for _ in range(depth)]
         dev = self.slots[0].dev
         self.dev = dev
-        self.h2d, self.comp, self.d2h = (torch.cuda.Stream(dev) for _ in range(3))
+        self.h2d, self.d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        self.comps = [torch.cuda.Stream(dev) for _ in range(depth)]
         mk = lambda: [torch.cuda.Event() for _ in range(depth)]  # noqa: E731
         self.ev_in, self.ev_done, self.ev_out = mk(), mk(), mk()
         self.used = [False] * depth
@@ -100,27 +103,41 @@ class EncodeRenderStream:
             s.capture()
         return self
 
-    def submit(self, image: torch.Tensor, out: torch.Tensor):
+    def submit(self, image: torch.Tensor, out: torch.Tensor | None = None):
+        """Enqueue one image.  A host image (pinned) is copied in on the H2D stream; a device image is
+        copied into the slot's input buffer on the slot's own stream.  With `out` (pinned host) the
+        reconstruction is copied out on the D2H stream; without it, it stays in the slot's static buffer,
+        which is returned and stays valid until that slot's next image (``depth`` submits later)."""
         k = self.n % len(self.slots)
         slot = self.slots[k]
         if slot.graph is None:
             slot.capture()
+        comp = self.comps[k]
         if self.used[k]:
-            self.h2d.wait_event(self.ev_done[k])   # the slot's input buffer was read by its last replay
-            self.comp.wait_event(self.ev_out[k])   # its output buffer was copied out
-        with torch.cuda.stream(self.h2d):
-            slot.x.copy_(image, non_blocking=True)
-            self.ev_in[k].record(self.h2d)
-        self.comp.wait_event(self.ev_in[k])
-        with torch.cuda.stream(self.comp):
+            comp.wait_event(self.ev_out[k])        # the slot's output buffer was copied out
+        if image.is_cuda:
+            with torch.cuda.stream(comp):
+                slot.x.copy_(image, non_blocking=True)
+        else:
+            if self.used[k]:
+                self.h2d.wait_event(self.ev_done[k])   # the slot's input buffer was read by its last replay
+            with torch.cuda.stream(self.h2d):
+                slot.x.copy_(image, non_blocking=True)
+                self.ev_in[k].record(self.h2d)
+            comp.wait_event(self.ev_in[k])
+        with torch.cuda.stream(comp):
             slot.graph.replay()
-            self.ev_done[k].record(self.comp)
-        self.d2h.wait_event(self.ev_done[k])
-        with torch.cuda.stream(self.d2h):
-            out.copy_(slot.rec, non_blocking=True)
-            self.ev_out[k].record(self.d2h)
+            self.ev_done[k].record(comp)
+        if out is not None:
+            self.d2h.wait_event(self.ev_done[k])
+            with torch.cuda.stream(self.d2h):
+                out.copy_(slot.rec, non_blocking=True)
+                self.ev_out[k].record(self.d2h)
+        else:
+            self.ev_out[k].record(comp)
         self.used[k] = True
         self.n += 1
+        return slot.rec
 
     def wait_into(self, stream=None):
         """Make `stream` (default: the current stream) wait for every submitted image."""
@@ -132,11 +149,12 @@ class EncodeRenderStream:
     def start_after(self, stream=None):
         """Order the pipeline's streams after the work already queued on `stream` (default: current)."""
         st = stream if stream is not None else torch.cuda.current_stream(self.dev)
-        for s in (self.h2d, self.comp, self.d2h):
+        for s in (self.h2d, self.d2h, *self.comps):
             s.wait_stream(st)
 
     def synchronize(self):
-        self.d2h.synchronize()
+        for s in (self.h2d, self.d2h, *self.comps):
+            s.synchronize()
 
 
 def render_l2_grads(leaves, target, H: int, W: int, odds: bool = True, row_band=None):

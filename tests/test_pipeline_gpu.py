@@ -74,6 +74,13 @@ def test_encode_render_stream_matches_single(lib):
     st.synchronize()
     for o, r in zip(outs, refs):
         assert float((o - r).abs().max()) < 1e-6
+    # device-resident images, several in flight on their own streams, results left in the slots
+    dev_imgs = [x.cuda() for x in imgs[:len(st.slots)]]
+    st.start_after()
+    recs = [st.submit(x) for x in dev_imgs]
+    st.synchronize()
+    for rec, r in zip(recs, refs):
+        assert float((rec.cpu() - r).abs().max()) < 1e-6
 
 
 def test_render_fit_step_graph_matches_eager(lib):
