@@ -692,14 +692,14 @@ def octave_tiles(H, W, tile=8, max_octaves=6):
 def binning_roofline(stages, pairs, N, H, W, hbm_gbs):
     """Binning of one render against HBM: algorithmic bytes N*36 (splat parameters read) + N*4 (per-splat
     pair counts) + pairs*8 (sorted (tile, splat) written once) + (tiles+1)*4 (tile ranges), over the
-    measured time of the binning stage (preprocess .. ranges, one render)."""
+    measured time of the binning stage (memset, k_preprocess, k_tile_scan, k_scatter of one render)."""
     t = stages.get("binning", {}).get("ms_per_replay", 0.0) * 1e-3
     if t <= 0 or not pairs:
         return None
     nt = octave_tiles(H, W)
     nbytes = N * 36 + N * 4 + pairs * 8 + (nt + 1) * 4
     gbs = nbytes / t / 1e9
-    return {"bound": "hbm", "kernels": "k_preprocess .. k_ranges (10 launches incl. a memset)", "ms": t * 1e3,
+    return {"bound": "hbm", "kernels": "memset + k_preprocess + k_tile_scan + k_scatter", "ms": t * 1e3,
             "algorithmic_bytes": nbytes, "tiles": nt, "achieved_gbs": gbs, "peak_gbs": hbm_gbs,
             "frac": gbs / hbm_gbs}
 

@@ -6,11 +6,10 @@
 // _render_bwd_cull_kernel + index_add_ + the autograd of the upsample/composite (backward).
 //
 // Forward, one launch sequence for the whole batch and all octaves (no host sync):
-//   k_preprocess   per splat: softplus scale, octave, clamped tile rectangle, 48-byte render record
-//   k_scan_blocks  exclusive scan of per-block pair counts
-//   k_emit         (global tile id, splat id) pairs in splat order, load-balanced per block
-//   k_radix_*      stable LSD radix sort of the pairs by global tile id (2 passes for <= 16 bits)
-//   k_ranges       [begin, end) of every tile in the sorted pair list
+//   k_preprocess   per splat: softplus scale, octave, clamped tile rectangle, 48-byte render record; the
+//                  rectangle rows into a difference array of per-tile pair counts
+//   k_tile_scan    tile counts -> every tile's [begin, end) in the pair list, a cursor per tile, the total
+//   k_scatter      every (tile, splat) pair placed at its tile's cursor (load-balanced per 256 splats)
 //   k_fields_fwd   one CTA per tile: raw sums S_log, S_w, S_wc of every group (octave) at its own
 //                  resolution; splat records staged per warp in shared memory
 //   k_composite    bilinear upsample of every present group to native resolution, sum, composite
@@ -183,15 +182,42 @@ __device__ __forceinline__ SplatRec make_rec(long long s, int C, int has_theta, 
     return r;
 }
 
+// ----------------------------------------------------------------------------------------------------
+// binning: per tile, the list of splats whose tile rectangle covers it (render_triton.py:351-409), as a
+// counting sort of the (tile, splat) pairs by global tile id:
+//
+//   k_preprocess  per splat as above; each rectangle row [a, a + w) of global tile ids adds +1 at a and
+//                 -1 at a + w of a difference array over all tiles (equal addresses of a warp summed
+//                 first; the pairs themselves are not enumerated)
+//   k_tile_scan   one block: tile counts = prefix of the differences, tile starts = exclusive prefix of
+//                 the counts -> every tile's [begin, end), a cursor at its begin, the pair total, and the
+//                 list of deep tiles (more than FW_DEEP pairs) for the 16-warp field kernel
+//   k_scatter     the pairs enumerated in splat order, load-balanced per block of 256 splats, counted per
+//                 tile in a shared-memory hash table and placed with one cursor atomic per (chunk, tile)
+//
+// Within a tile the splats therefore come in the order their groups reach the cursor, not by splat id:
+// the forward fields are sums (alpha compositing of the octave/odds path is a commutative monoid), so the
+// order only changes floating-point rounding, as the reference's own unstable argsort does.
+
+// Layout of the 64-byte status block of a render workspace (zeroed before every forward).
+#define MISC_TOTAL 0   // long long: pairs of the whole call
+#define MISC_STATUS 8  // int: bit 0 set when the pairs exceed the workspace's pair capacity
+#define MISC_NEFF 16   // long long: pairs the field kernels process (0 after an overflow)
+#define MISC_NDEEP 24  // int: tiles in the deep-tile list
+#define FW_DEEP 256    // pairs above which a TILE 8 tile is composited by 16 warps
+
+__device__ __forceinline__ void red_add_i32(int *p, int v) {
+    asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // meta = {global tile id of the rectangle's top-left, width | group << 24, ntx of the group, count}
+// tdiff: tile difference array (zeroed beforehand; nullptr when only the counts are wanted).
 __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *__restrict__ mu,
                                                     const float *__restrict__ ls, const float *__restrict__ col,
                                                     const float *__restrict__ op, const float *__restrict__ th,
                                                     SplatRec *__restrict__ rec, int4 *__restrict__ meta,
-                                                    int *__restrict__ counts, long long *__restrict__ bsum,
-                                                    unsigned long long *__restrict__ gpairs,
-                                                    int *__restrict__ gsplats) {
-    __shared__ long long wsum[8];
+                                                    int *__restrict__ counts, unsigned long long *__restrict__ gpairs,
+                                                    int *__restrict__ gsplats, int *__restrict__ tdiff) {
     __shared__ unsigned long long s_pairs[4 * GS_MAX_GROUPS];
     __shared__ int s_spl[4 * GS_MAX_GROUPS];
     if (threadIdx.x < 4 * GS_MAX_GROUPS) {
@@ -203,6 +229,7 @@ __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *_
     long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     int count = 0;
     int skey = -1;
+    int row0 = 0, rstep = 0, rw = 1, nrows = 0;  // the rectangle's rows in global tile ids
     if (s < (long long)G.B * G.N) {
         int b = (int)(s / G.N), i = (int)(s - (long long)b * G.N);
         float2 m = reinterpret_cast<const float2 *>(mu)[s];  // (y, x)
@@ -229,6 +256,28 @@ __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *_
         meta[s] = mt;
         counts[s] = count;
         skey = b * GS_MAX_GROUPS + g;
+        row0 = mt.x;
+        rstep = mt.z;
+        rw = mt.y & 0xffffff;
+        nrows = count > 0 ? count / rw : 0;
+    }
+    if (tdiff) {
+        // rectangle rows into the difference array; neighbouring splats (the encoder emits them cell by
+        // cell) often share a row's first or past-the-end tile, so equal addresses of a warp are summed
+        // before one reduction each
+        int rmax = nrows;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) rmax = max(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
+        const unsigned lt = (1u << (threadIdx.x & 31)) - 1u;
+        for (int q = 0; q < rmax; q++) {
+            const bool on = q < nrows;
+            const int a = on ? row0 + q * rstep : -1;
+            unsigned peers = __match_any_sync(0xffffffffu, a);
+            if (on && (peers & lt) == 0u) red_add_i32(tdiff + a, __popc(peers));
+            const int e = on ? a + rw : -1;
+            peers = __match_any_sync(0xffffffffu, e);
+            if (on && (peers & lt) == 0u) red_add_i32(tdiff + e, -(int)__popc(peers));
+        }
     }
     {
         // aggregate per warp over lanes with the same (image, group), then per block in shared memory
@@ -253,317 +302,182 @@ __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *_
         atomicAdd(&gpairs[bb * G.ngroups + gg], s_pairs[threadIdx.x]);
         atomicAdd(&gsplats[bb * G.ngroups + gg], s_spl[threadIdx.x]);
     }
-    // per-block pair total (64-bit: 256 splats of up to 2^31 tiles each)
-    long long v = count;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = v;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        long long t = 0;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += wsum[w];
-        bsum[blockIdx.x] = t;
-    }
 }
 
-// Layout of the 64-byte status block of a render workspace (zeroed before every forward).
-#define MISC_TOTAL 0   // long long: pairs of the whole call
-#define MISC_STATUS 8  // int: bit 0 set when the pairs exceed the workspace's pair capacity
-#define MISC_NEFF 16   // long long: pairs the sort and the field kernels process (0 after an overflow)
-
-// single-block exclusive scan of the n per-block pair totals in place (64-bit); the call's pair total ->
-// misc.  When the total exceeds the pair capacity nothing is emitted or sorted (the effective count stays
-// 0 and the status bit is set), so no kernel writes past the pair buffers; the host reports the overflow.
-__global__ void __launch_bounds__(1024) k_scan_blocks(long long *__restrict__ data, int n, long long cap,
-                                                      unsigned char *__restrict__ misc) {
+// One block of 1024 threads over the nt = B * tiles_per_image tiles, TS_PER consecutive tiles per thread
+// per round: count = prefix of tdiff, begin = exclusive prefix of count (64-bit), ranges = [begin, begin +
+// count), cursor = begin; tiles with more than FW_DEEP pairs go to dlist (order of arrival; at most
+// cap / (FW_DEEP + 1) of them); misc gets the total, the overflow status, the effective pair count and
+// the deep-tile count.  After an overflow (total > cap: rare, the ranges then point past the pair
+// buffer) a second sweep empties every range and the lists, and k_scatter places nothing.
+#define TS_THREADS 1024
+#define TS_PER 16
+__global__ void __launch_bounds__(TS_THREADS) k_tile_scan(const int *__restrict__ tdiff, long long nt, long long cap,
+                                                          int2 *__restrict__ ranges, int *__restrict__ cursor,
+                                                          int *__restrict__ dlist, int dcap,
+                                                          unsigned char *__restrict__ misc) {
     __shared__ long long wsum[32];
-    int per = (n + 1023) / 1024;
-    int lo = threadIdx.x * per, hi = min(n, lo + per);
-    long long s = 0;
-    for (int i = lo; i < hi; i++) s += data[i];
-    long long tot;
-    long long pre = block_excl_scan<1024, long long>(s, wsum, &tot);
-    for (int i = lo; i < hi; i++) {
-        long long v = data[i];
-        data[i] = pre;
-        pre += v;
+    const int tid = threadIdx.x;
+    long long carry_d = 0, carry_c = 0;
+    for (long long base = 0; base < nt; base += (long long)TS_THREADS * TS_PER) {
+        const long long lo = base + (long long)tid * TS_PER;
+        // 16-byte loads: the difference array is zeroed and allocated in whole 256-byte blocks
+        int dl[TS_PER];
+#pragma unroll
+        for (int k = 0; k < TS_PER; k += 4) {
+            const int4 v = lo + k < nt ? *reinterpret_cast<const int4 *>(tdiff + lo + k) : make_int4(0, 0, 0, 0);
+            dl[k] = v.x;
+            dl[k + 1] = v.y;
+            dl[k + 2] = v.z;
+            dl[k + 3] = v.w;
+        }
+        long long sd = 0;
+#pragma unroll
+        for (int k = 0; k < TS_PER; k++) {
+            if (lo + k >= nt) dl[k] = 0;
+            sd += dl[k];
+        }
+        long long td;
+        const long long pd = carry_d + block_excl_scan<TS_THREADS, long long>(sd, wsum, &td);
+        // counts of this thread's tiles (past the last tile the running prefix is not a count)
+        long long run = pd, sc = 0;
+        int cnt[TS_PER];
+#pragma unroll
+        for (int k = 0; k < TS_PER; k++) {
+            run += dl[k];
+            cnt[k] = lo + k < nt ? (int)run : 0;
+            sc += cnt[k];
+        }
+        long long tc;
+        long long beg = carry_c + block_excl_scan<TS_THREADS, long long>(sc, wsum, &tc);
+        int bg[TS_PER];
+#pragma unroll
+        for (int k = 0; k < TS_PER; k++) {
+            bg[k] = (int)beg;
+            beg += cnt[k];
+            if (cnt[k] > FW_DEEP) {
+                const int i = atomicAdd(reinterpret_cast<int *>(misc + MISC_NDEEP), 1);
+                if (i < dcap) dlist[i] = (int)(lo + k);
+            }
+        }
+        if (lo + TS_PER <= nt) {  // a whole run of 16 tiles: 16-byte stores
+#pragma unroll
+            for (int k = 0; k < TS_PER; k += 2)
+                *reinterpret_cast<int4 *>(ranges + lo + k) =
+                    make_int4(bg[k], bg[k] + cnt[k], bg[k + 1], bg[k + 1] + cnt[k + 1]);
+#pragma unroll
+            for (int k = 0; k < TS_PER; k += 4)
+                *reinterpret_cast<int4 *>(cursor + lo + k) = make_int4(bg[k], bg[k + 1], bg[k + 2], bg[k + 3]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < TS_PER; k++)
+                if (lo + k < nt) {
+                    ranges[lo + k] = make_int2(bg[k], bg[k] + cnt[k]);
+                    cursor[lo + k] = bg[k];
+                }
+        }
+        carry_d += td;
+        carry_c += tc;
     }
-    if (threadIdx.x == 0) {
-        *reinterpret_cast<long long *>(misc + MISC_TOTAL) = tot;
-        if (tot > cap) *reinterpret_cast<int *>(misc + MISC_STATUS) |= 1;
-        *reinterpret_cast<long long *>(misc + MISC_NEFF) = tot > cap ? 0 : tot;
+    const long long total = carry_c;
+    const bool ok = total <= cap;
+    if (tid == 0) {
+        *reinterpret_cast<long long *>(misc + MISC_TOTAL) = total;
+        if (!ok) *reinterpret_cast<int *>(misc + MISC_STATUS) |= 1;
+        *reinterpret_cast<long long *>(misc + MISC_NEFF) = ok ? total : 0;
+    }
+    if (!ok) {
+        __syncthreads();  // (after every thread's writes above)
+        for (long long i = tid; i < nt; i += TS_THREADS) ranges[i] = make_int2(0, 0);
+        if (tid == 0) *reinterpret_cast<int *>(misc + MISC_NDEEP) = 0;
     }
 }
 
-// pairs in splat order: key = global tile id, value = global splat id.  Splat block j (256 splats, the
-// preprocessing block) owns the output segment [bpre[j], bpre[j] + tot_j); `parts` emit blocks share it,
-// part p writing the sub-segment [bpre[j] + min(p*c, tot_j), bpre[j] + min((p+1)*c, tot_j)) with
-// c = ceil(tot_j / parts).  Each emit block also writes the digit-0 histogram of its sub-segment
-// (hist0 column = emit block), so the first radix pass needs no separate counting sweep.
-__global__ void __launch_bounds__(256) k_emit(RenderGeom G, const int4 *__restrict__ meta,
-                                              const int *__restrict__ counts, const long long *__restrict__ bpre,
-                                              int parts, unsigned *__restrict__ keys, int *__restrict__ vals,
-                                              const unsigned char *__restrict__ misc, int *__restrict__ hist0,
-                                              int hist_stride, int radix0) {
+// Every pair of the call placed at its tile's cursor.  Splat block j (256 splats, the preprocessing block)
+// is shared by `parts` scatter blocks, part p taking pairs [min(p*c, tot_j), min((p+1)*c, tot_j)) of the
+// block's pairs in splat order, c = ceil(tot_j / parts).  A block works in chunks of SC_CHUNK pairs: it
+// counts the chunk's pairs per tile in a shared-memory hash table (the rank of each pair inside its
+// tile's group), reserves each tile's group with ONE global atomic, then writes the pairs.  Deep tiles (a
+// coarse octave tile under a thousand splats of neighbouring encoder cells) otherwise serialise on their
+// cursor.
+#define SC_CHUNK 2048
+#define SC_HASH 4096  // >= 2 * SC_CHUNK: a probe sequence always ends
+__global__ void __launch_bounds__(256) k_scatter(RenderGeom G, const int4 *__restrict__ meta,
+                                                 const int *__restrict__ counts, int parts,
+                                                 int *__restrict__ cursor, int *__restrict__ vals,
+                                                 const unsigned char *__restrict__ misc) {
     __shared__ int wsum[8];
     __shared__ int soff[257];
     __shared__ int4 smeta[256];
-    __shared__ int shist[256];
-    // after a capacity overflow (k_scan_blocks) nothing is emitted; otherwise every position below is
-    // < total <= cap < 2^31, so the block-local offsets fit in 32 bits
+    __shared__ int hkey[SC_HASH];
+    __shared__ int hval[SC_HASH];               // per tile: pairs in the chunk, then their global start
+    __shared__ unsigned short pslot[SC_CHUNK];  // per pair: hash slot of its tile
+    __shared__ unsigned short prank[SC_CHUNK];  // per pair: rank among the chunk's pairs of that tile
+    __shared__ unsigned char psplat[SC_CHUNK];  // per pair: splat of the block
+    // after a capacity overflow (k_tile_scan) nothing is scattered
     if (*reinterpret_cast<const int *>(misc + MISC_STATUS) != 0) return;
-    if (hist0)
-        for (int d = threadIdx.x; d < radix0; d += 256) shist[d] = 0;
+    const int tid = threadIdx.x;
     const int j = blockIdx.x / parts, part = blockIdx.x - j * parts;
-    long long s0 = (long long)j * 256;
-    long long s = s0 + threadIdx.x;
+    const long long s0 = (long long)j * 256;
+    const long long s = s0 + tid;
     int c = 0;
-    int4 mt = make_int4(0, 0, 1, 0);
+    int4 mt = make_int4(0, 1, 1, 0);
     if (s < (long long)G.B * G.N) {
         c = counts[s];
         mt = meta[s];
     }
     int tot;
-    int off = block_excl_scan<256>(c, wsum, &tot);
-    soff[threadIdx.x] = off;
-    smeta[threadIdx.x] = mt;
-    if (threadIdx.x == 0) soff[256] = tot;
+    const int off = block_excl_scan<256>(c, wsum, &tot);
+    soff[tid] = off;
+    smeta[tid] = mt;
+    if (tid == 0) soff[256] = tot;
     __syncthreads();
-    const long long base = bpre[j];
     const int chunk = (tot + parts - 1) / parts;
     const int e_lo = min(part * chunk, tot), e_hi = min(e_lo + chunk, tot);
-    for (int e = e_lo + threadIdx.x; e < e_hi; e += 256) {
-        // splat k of this block with soff[k] <= e < soff[k+1]
-        int lo = 0, hi = 255;
-        while (lo < hi) {
-            int mid = (lo + hi + 1) >> 1;
-            if (soff[mid] <= e) lo = mid; else hi = mid - 1;
-        }
-        int4 m = smeta[lo];
-        int r = e - soff[lo];
-        int w = m.y & 0xffffff;
-        int q = r / w;
-        unsigned tile = (unsigned)(m.x + q * m.z + (r - q * w));
-        const long long pos = base + e;
-        if (pos >= 0 && pos < G.cap) {  // always true when the status is clear (total <= cap)
-            keys[pos] = tile;
-            vals[pos] = (int)(s0 + lo);
-            if (hist0) atomicAdd(&shist[tile & (unsigned)(radix0 - 1)], 1);
-        }
-    }
-    if (hist0) {
-        // digit-0 histogram of this block's output segment (the first radix pass scatters per segment)
-        __syncthreads();
-        for (int d = threadIdx.x; d < radix0; d += 256) hist0[d * hist_stride + blockIdx.x] = shist[d];
-    }
-}
-
-// ----------------------------------------------------------------------------------------------------
-// stable LSD radix sort of (key, value) pairs; n read from the device, grids sized for the capacity.
-
-#define RS_THREADS 256
-#define RS_ROUNDS 8
-#define RS_ITEMS (RS_THREADS * RS_ROUNDS)
-
-// n_ptr points at the effective pair count (MISC_NEFF: 0 after a capacity overflow)
-__device__ __forceinline__ long long clamp_n(const long long *n_ptr, long long cap) {
-    long long n = *n_ptr;
-    return n < cap ? n : cap;
-}
-
-// grid-stride over "virtual blocks" of RS_ITEMS keys; n is read from the device
-__global__ void __launch_bounds__(RS_THREADS) k_radix_upsweep(const unsigned *__restrict__ keys,
-                                                              const long long *__restrict__ n_ptr, long long cap,
-                                                              int shift, int radix, int *__restrict__ hist,
-                                                              int nblk_cap) {
-    __shared__ int h[256];
-    const long long n = clamp_n(n_ptr, cap);
-    const int nblk = (int)((n + RS_ITEMS - 1) / RS_ITEMS);
-    const unsigned mask = (unsigned)radix - 1u;
-    for (int vb = blockIdx.x; vb < nblk; vb += gridDim.x) {
-        const long long base = (long long)vb * RS_ITEMS;
-        for (int d = threadIdx.x; d < radix; d += RS_THREADS) h[d] = 0;
-        __syncthreads();
-        for (int r = 0; r < RS_ROUNDS; r++) {
-            long long i = base + r * RS_THREADS + threadIdx.x;
-            if (i < n) atomicAdd(&h[(keys[i] >> shift) & mask], 1);
+    const long long cap = G.cap;
+    for (int c0 = e_lo; c0 < e_hi; c0 += SC_CHUNK) {  // block-uniform
+        const int n = min(SC_CHUNK, e_hi - c0);
+        // a table of the next power of two >= 2n slots (at least 64): short chunks clear a short table
+        const int hbits = max(6, 32 - __clz(2 * n - 1));  // <= 12 (n <= SC_CHUNK)
+        const int hsize = 1 << hbits;
+        for (int i = tid; i < hsize; i += 256) {
+            hkey[i] = -1;
+            hval[i] = 0;
         }
         __syncthreads();
-        for (int d = threadIdx.x; d < radix; d += RS_THREADS) hist[d * nblk_cap + vb] = h[d];
-        __syncthreads();
-    }
-}
-
-// grid = radix blocks: exclusive scan of one digit's per-block counts; digit total -> dtot[d]
-__global__ void __launch_bounds__(256) k_radix_scan(int *__restrict__ hist, const long long *__restrict__ n_ptr,
-                                                    long long cap, int nblk_cap, int *__restrict__ dtot,
-                                                    int nblk_fixed) {
-    __shared__ int wsum[8];
-    long long n = clamp_n(n_ptr, cap);
-    int nblk = nblk_fixed > 0 ? nblk_fixed : (int)((n + RS_ITEMS - 1) / RS_ITEMS);
-    int *h = hist + (long long)blockIdx.x * nblk_cap;
-    int carry = 0;
-    for (int c0 = 0; c0 < nblk; c0 += 256) {
-        int i = c0 + threadIdx.x;
-        int v = i < nblk ? h[i] : 0;
-        int tot;
-        int pre = block_excl_scan<256>(v, wsum, &tot);
-        if (i < nblk) h[i] = carry + pre;
-        carry += tot;
-    }
-    if (threadIdx.x == 0) dtot[blockIdx.x] = carry;
-}
-
-// Shared memory of one radix scatter block.
-struct RsSmem {
-    int wsum[RS_THREADS / 32];
-    int wcnt[RS_THREADS / 32][256];  // per warp and digit: count, then the warp's start inside the chunk
-    int lbase[256];                  // start of each digit inside the chunk's digit-sorted order
-    int gbase[256];                  // global output position of each digit's first key of the chunk
-    unsigned skey[RS_ITEMS];         // the chunk, stably sorted by digit
-    int sval[RS_ITEMS];
-};
-
-// One chunk [c0, c1) (at most RS_ITEMS keys) of a stable LSD pass.  Warp w ranks its own 256 consecutive
-// keys in 8 sequential rounds (match_any within the round + a running per-warp digit count); a block-wide
-// scan over digits turns the counts into chunk-local positions, the chunk is staged in shared memory in
-// digit order, and each digit's run is then written to gbase[d] onwards with consecutive threads on
-// consecutive positions (coalesced).  gbase[d] advances by the chunk's digit-d count.
-__device__ __forceinline__ void rs_chunk(RsSmem &sm, const unsigned *__restrict__ kin, const int *__restrict__ vin,
-                                         unsigned *__restrict__ kout, int *__restrict__ vout, long long c0,
-                                         long long c1, int shift, int radix) {
-    constexpr int NWARP = RS_THREADS / 32;
-    constexpr int PER_WARP = RS_ITEMS / NWARP;  // 256
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const unsigned mask = (unsigned)radix - 1u;
-    const unsigned lt_mask = (1u << lane) - 1u;
-    const long long base = c0 + warp * PER_WARP;
-    for (int d = lane; d < radix; d += 32) sm.wcnt[warp][d] = 0;
-    __syncwarp();
-    unsigned key[RS_ROUNDS];
-    int val[RS_ROUNDS], dig[RS_ROUNDS], rank[RS_ROUNDS];
-#pragma unroll
-    for (int r = 0; r < RS_ROUNDS; r++) {
-        const long long i = base + r * 32 + lane;
-        key[r] = i < c1 ? __ldg(kin + i) : 0u;
-        val[r] = i < c1 ? __ldg(vin + i) : 0;
-    }
-#pragma unroll
-    for (int r = 0; r < RS_ROUNDS; r++) {
-        const long long i = base + r * 32 + lane;
-        const bool valid = i < c1;
-        const int d = valid ? (int)((key[r] >> shift) & mask) : -1;
-        dig[r] = d;
-        const unsigned peers = __match_any_sync(0xffffffffu, d);
-        const int pre = valid ? sm.wcnt[warp][d] : 0;
-        rank[r] = pre + __popc(peers & lt_mask);
-        __syncwarp();
-        if (valid && (peers & lt_mask) == 0u) sm.wcnt[warp][d] = pre + __popc(peers);
-        __syncwarp();
-    }
-    __syncthreads();
-    int tot = 0;
-    if (tid < radix) {
-#pragma unroll
-        for (int w = 0; w < NWARP; w++) {
-            const int c = sm.wcnt[w][tid];
-            sm.wcnt[w][tid] = tot;
-            tot += c;
+        for (int jj = tid; jj < n; jj += 256) {
+            const int e = c0 + jj;
+            int lo = 0, hi = 255;  // splat k of this block with soff[k] <= e < soff[k+1]
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (soff[mid] <= e) lo = mid; else hi = mid - 1;
+            }
+            const int4 m = smeta[lo];
+            const int r = e - soff[lo];
+            const int w = m.y & 0xffffff;
+            const int q = r / w;
+            const int tile = m.x + q * m.z + (r - q * w);
+            unsigned h = ((unsigned)tile * 2654435761u) >> (32 - hbits);
+            for (int probe = 0; probe < hsize; probe++) {
+                const int k = atomicCAS(&hkey[h], -1, tile);
+                if (k == -1 || k == tile) break;
+                h = (h + 1) & (unsigned)(hsize - 1);
+            }
+            pslot[jj] = (unsigned short)h;
+            prank[jj] = (unsigned short)atomicAdd(&hval[h], 1);
+            psplat[jj] = (unsigned char)lo;
         }
-    }
-    const int lb = block_excl_scan<RS_THREADS, int>(tot, sm.wsum, nullptr);  // ends with a block barrier
-    if (tid < radix) sm.lbase[tid] = lb;
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < RS_ROUNDS; r++) {
-        if (dig[r] >= 0) {
-            const int local = sm.lbase[dig[r]] + sm.wcnt[warp][dig[r]] + rank[r];
-            sm.skey[local] = key[r];
-            sm.sval[local] = val[r];
-        }
-    }
-    __syncthreads();
-    const int n = (int)(c1 - c0);
-    for (int t = tid; t < n; t += RS_THREADS) {
-        const unsigned k = sm.skey[t];
-        const int d = (int)((k >> shift) & mask);
-        const long long pos = (long long)sm.gbase[d] + (t - sm.lbase[d]);
-        kout[pos] = k;
-        vout[pos] = sm.sval[t];
-    }
-    __syncthreads();
-    if (tid < radix) sm.gbase[tid] += tot;
-    __syncthreads();
-}
-
-// Stable scatter of one digit over "virtual blocks" of RS_ITEMS keys (grid-stride); the per-block digit
-// counts come from k_radix_upsweep, scanned by k_radix_scan.
-__global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep(const unsigned *__restrict__ kin,
-                                                                const int *__restrict__ vin,
-                                                                unsigned *__restrict__ kout, int *__restrict__ vout,
-                                                                const long long *__restrict__ n_ptr, long long cap,
-                                                                int shift, int radix, const int *__restrict__ hist,
-                                                                int nblk_cap, const int *__restrict__ dtot) {
-    extern __shared__ __align__(16) unsigned char rs_dsmem[];
-    RsSmem &sm = *reinterpret_cast<RsSmem *>(rs_dsmem);
-    __shared__ int dbase[256];
-    const long long n = clamp_n(n_ptr, cap);
-    const int nblk = (int)((n + RS_ITEMS - 1) / RS_ITEMS);
-    const int tid = threadIdx.x;
-    const int dv = tid < radix ? dtot[tid] : 0;
-    const int dpre = block_excl_scan<RS_THREADS, int>(dv, sm.wsum, nullptr);
-    if (tid < radix) dbase[tid] = dpre;
-    for (int vb = blockIdx.x; vb < nblk; vb += gridDim.x) {
-        if (tid < radix) sm.gbase[tid] = dbase[tid] + hist[tid * nblk_cap + vb];
-        // (rs_chunk reads gbase only after several block barriers)
-        const long long c0 = (long long)vb * RS_ITEMS;
-        rs_chunk(sm, kin, vin, kout, vout, c0, min(c0 + RS_ITEMS, n), shift, radix);
-    }
-}
-
-// First radix pass over the emit kernel's output sub-segments (one per emit block: part p of splat block
-// j, bounds as in k_emit), whose digit histograms k_emit already wrote.  Each sub-segment is scattered
-// in chunks of RS_ITEMS keys, the per-digit output position carried across its chunks.
-__global__ void __launch_bounds__(RS_THREADS) k_radix_downsweep_seg(const unsigned *__restrict__ kin,
-                                                                    const int *__restrict__ vin,
-                                                                    unsigned *__restrict__ kout,
-                                                                    int *__restrict__ vout,
-                                                                    const long long *__restrict__ bpre, int nblk_pre,
-                                                                    int parts, const long long *__restrict__ n_ptr,
-                                                                    long long cap, int shift, int radix,
-                                                                    const int *__restrict__ hist, int hist_stride,
-                                                                    const int *__restrict__ dtot) {
-    extern __shared__ __align__(16) unsigned char rs_dsmem[];
-    RsSmem &sm = *reinterpret_cast<RsSmem *>(rs_dsmem);
-    __shared__ int dbase[256];
-    const long long n = clamp_n(n_ptr, cap);
-    const int tid = threadIdx.x;
-    const int dv = tid < radix ? dtot[tid] : 0;
-    const int dpre = block_excl_scan<RS_THREADS, int>(dv, sm.wsum, nullptr);
-    if (tid < radix) dbase[tid] = dpre;
-    const int nseg = nblk_pre * parts;
-    for (int j = blockIdx.x; j < nseg; j += gridDim.x) {
-        const int sb = j / parts, part = j - sb * parts;
-        const long long beg = bpre[sb];
-        const long long end = sb + 1 < nblk_pre ? bpre[sb + 1] : n;
-        const long long tot = end - beg;
-        const long long chunk = (tot + parts - 1) / parts;
-        const long long b0 = min(beg + min(part * chunk, tot), n);
-        const long long b1 = min(beg + min((part + 1) * chunk, tot), n);
-        if (tid < radix) sm.gbase[tid] = dbase[tid] + hist[tid * hist_stride + j];
-        for (long long c0 = b0; c0 < b1; c0 += RS_ITEMS) rs_chunk(sm, kin, vin, kout, vout, c0, min(c0 + RS_ITEMS, b1), shift, radix);
         __syncthreads();
-    }
-}
-
-// [begin, end) of every tile present in the sorted key list (ranges zeroed beforehand); grid-stride
-__global__ void __launch_bounds__(256) k_ranges(const unsigned *__restrict__ keys, const long long *__restrict__ n_ptr,
-                                                long long cap, int2 *__restrict__ ranges) {
-    const long long n = clamp_n(n_ptr, cap);
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-        unsigned k = keys[i];
-        if (i == 0 || keys[i - 1] != k) ranges[k].x = (int)i;
-        if (i == n - 1 || keys[i + 1] != k) ranges[k].y = (int)(i + 1);
+        for (int i = tid; i < hsize; i += 256) {
+            const int k = hkey[i];
+            if (k >= 0) hval[i] = atomicAdd(cursor + k, hval[i]);
+        }
+        __syncthreads();
+        for (int jj = tid; jj < n; jj += 256) {
+            const int pos = hval[pslot[jj]] + prank[jj];
+            if (pos >= 0 && pos < cap) vals[pos] = (int)(s0 + psplat[jj]);  // (always: the counts bound the cursors)
+        }
+        __syncthreads();
     }
 }
 
@@ -605,9 +519,9 @@ __global__ void __launch_bounds__(NW * 32) k_fields_fwd(RenderGeom G, const Spla
         p0 = 0;
         p1 = G.N;
     } else {
-        int2 rg = ranges[gt];
-        p0 = rg.x;
-        p1 = rg.y;
+        const int2 rg = ranges[gt];  // empty tile: begin == end
+        p0 = rg.y > rg.x ? rg.x : 0;
+        p1 = rg.y > rg.x ? rg.y : 0;
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     // the PPL pixels of a lane share one column (32 is a multiple of TILE), so the x terms of the
@@ -1070,9 +984,9 @@ __global__ void __launch_bounds__(NW * 32) k_fields_bwd(RenderGeom G, const Spla
         p0 = 0;
         p1 = G.N;
     } else {
-        int2 rg = ranges[gt];
-        p0 = rg.x;
-        p1 = rg.y;
+        const int2 rg = ranges[gt];  // empty tile: begin == end
+        p0 = rg.y > rg.x ? rg.x : 0;
+        p1 = rg.y > rg.x ? rg.y : 0;
     }
     if (p1 <= p0) return;
     const float *src;
@@ -1451,10 +1365,11 @@ struct Plan {
     RenderGeom G;
     int ngroups;
     long long cap;
-    int nblk_pre, nblk_sort, passes, radix_bits;
-    int emit_parts;  // emit blocks per preprocessing block (>= 4 blocks per SM of 148 in all)
-    size_t o_rec, o_meta, o_counts, o_bsum, o_zero, o_gpairs, o_gsplats, o_misc, o_ranges, z_len;
-    size_t o_keys_a, o_vals_a, o_keys_b, o_vals_b, o_hist, o_dtot, o_fields, fwd_bytes;
+    int nblk_pre;
+    int scatter_parts;  // scatter blocks per preprocessing block (>= 4 blocks per SM of 148 in all)
+    int dcap;           // deep-tile list capacity
+    size_t o_rec, o_meta, o_counts, o_zero, o_gpairs, o_gsplats, o_misc, o_tdiff, z_len;
+    size_t o_ranges, o_cursor, o_dlist, o_vals, o_fields, fwd_bytes;
     size_t o_G, o_gfields, o_adjT, o_bzero, o_acc, o_gbg, bz_len, total_bytes;
     AdjPlan adj;
 };
@@ -1604,32 +1519,25 @@ void make_plan(const gs_render_desc *d, Plan &pl) {
     pl.G.cap = cap;
     long long BN = (long long)d->B * d->N;
     pl.nblk_pre = (int)std::max<long long>(1, (BN + 255) / 256);
-    pl.nblk_sort = (int)std::max<long long>(1, (cap + RS_ITEMS - 1) / RS_ITEMS);
-    pl.emit_parts = std::min(8, std::max(1, (4 * 148 + pl.nblk_pre - 1) / pl.nblk_pre));
-    long long ntiles = (long long)d->B * pl.G.tiles_per_image;
-    int bits = 0;
-    while ((1LL << bits) < ntiles) bits++;
-    pl.passes = (bits + 7) / 8;
-    pl.radix_bits = pl.passes ? (bits + pl.passes - 1) / pl.passes : 0;
+    pl.scatter_parts = std::min(8, std::max(1, (4 * 148 + pl.nblk_pre - 1) / pl.nblk_pre));
+    const long long ntiles = (long long)d->B * pl.G.tiles_per_image;
     size_t o = 0;
     auto take = [&](size_t bytes) { size_t r = o; o = align256(o + bytes); return r; };
     pl.o_rec = take(sizeof(SplatRec) * (size_t)std::max<long long>(BN, 1));
     pl.o_meta = take(sizeof(int4) * (size_t)std::max<long long>(BN, 1));
     pl.o_counts = take(sizeof(int) * (size_t)std::max<long long>(BN, 1));
-    pl.o_bsum = take(sizeof(long long) * (size_t)pl.nblk_pre);
-    // zeroed block: group stats, misc (total pairs as int64 + status), tile ranges
+    // zeroed block (memset): group stats, misc (total pairs as int64 + status), the tile difference array
     pl.o_zero = o;
     pl.o_gpairs = take(sizeof(unsigned long long) * (size_t)d->B * pl.ngroups);
     pl.o_gsplats = take(sizeof(int) * (size_t)d->B * pl.ngroups);
     pl.o_misc = take(64);
-    pl.o_ranges = take(sizeof(int2) * (size_t)ntiles);
+    pl.o_tdiff = take(sizeof(int) * (size_t)(ntiles + 1));
     pl.z_len = o - pl.o_zero;
-    pl.o_keys_a = take(sizeof(unsigned) * (size_t)std::max<long long>(cap, 1));
-    pl.o_vals_a = take(sizeof(int) * (size_t)std::max<long long>(cap, 1));
-    pl.o_keys_b = take(sizeof(unsigned) * (size_t)std::max<long long>(cap, 1));
-    pl.o_vals_b = take(sizeof(int) * (size_t)std::max<long long>(cap, 1));
-    pl.o_hist = take(sizeof(int) * 256 * (size_t)std::max(pl.nblk_sort, pl.nblk_pre * pl.emit_parts));
-    pl.o_dtot = take(sizeof(int) * 256);
+    pl.o_ranges = take(sizeof(int2) * (size_t)ntiles);  // written whole by k_tile_scan
+    pl.o_cursor = take(sizeof(int) * (size_t)ntiles);
+    pl.dcap = (int)std::min<long long>(ntiles, cap / (FW_DEEP + 1) + 1);
+    pl.o_dlist = take(sizeof(int) * (size_t)std::max(pl.dcap, 1));
+    pl.o_vals = take(sizeof(int) * (size_t)std::max<long long>(cap, 1));
     pl.o_fields = take(sizeof(float) * (size_t)d->B * pl.G.fld_per_image);
     pl.fwd_bytes = o;
     pl.o_G = take(sizeof(float) * 5 * (size_t)d->B * d->H * d->W);
@@ -1696,7 +1604,7 @@ int launch_fields_fwd(const Plan &pl, void *ws, cudaStream_t st) {
     dim3 grid((unsigned)((long long)G.B * G.tiles_per_image));
     auto rec = at<SplatRec>(ws, pl.o_rec);
     auto rng = at<int2>(ws, pl.o_ranges);
-    const int *vals = at<int>(ws, (pl.passes % 2) ? pl.o_vals_b : pl.o_vals_a);
+    const int *vals = at<int>(ws, pl.o_vals);
     auto fld = at<float>(ws, pl.o_fields);
     // 4 warps per tile (8 measured slower: the per-warp staging and the cross-warp reduction dominate
     // short lists)
@@ -1713,16 +1621,18 @@ int launch_fields_fwd(const Plan &pl, void *ws, cudaStream_t st) {
     return GS_OK;
 }
 
+// with_bins: the workspace holds the binning buffers (not so for gs_render_count's short one)
 int run_preprocess(const Plan &pl, const float *mu, const float *ls, const float *col, const float *op,
-                   const float *th, void *ws, cudaStream_t st) {
+                   const float *th, void *ws, cudaStream_t st, bool with_bins = true) {
     const RenderGeom &G = pl.G;
     cudaError_t e = cudaMemsetAsync(at<char>(ws, pl.o_zero), 0, pl.z_len, st);
     GS_COUNT(1);
     if (e != cudaSuccess) return set_cuda_error(e, "memset");
+    const bool bins = with_bins && G.mode != GS_MODE_EXACT;
     k_preprocess<<<pl.nblk_pre, 256, 0, st>>>(G, mu, ls, col, op, G.has_theta ? th : nullptr, at<SplatRec>(ws, pl.o_rec),
                                               at<int4>(ws, pl.o_meta), at<int>(ws, pl.o_counts),
-                                              at<long long>(ws, pl.o_bsum), at<unsigned long long>(ws, pl.o_gpairs),
-                                              at<int>(ws, pl.o_gsplats));
+                                              at<unsigned long long>(ws, pl.o_gpairs), at<int>(ws, pl.o_gsplats),
+                                              bins ? at<int>(ws, pl.o_tdiff) : nullptr);
     GS_CHECK_LAUNCH("k_preprocess");
     return GS_OK;
 }
@@ -1839,13 +1749,13 @@ int gs_render_count(const gs_render_desc *d, const float *mu, const float *log_s
     dd.pair_capacity = 1;
     Plan pl;
     make_plan(&dd, pl);
-    if (workspace_bytes < pl.o_keys_a) return GS_ERR_WORKSPACE;
+    if (workspace_bytes < pl.o_ranges) return GS_ERR_WORKSPACE;
     cudaStream_t s = (cudaStream_t)stream;
     // colour/opacity are not needed for counting: point them at the positions (any readable floats)
     const float *dummy = mu;
     pl.G.C = 1;
     pl.G.has_theta = 0;
-    st = run_preprocess(pl, mu, log_scale, dummy, dummy, nullptr, workspace, s);
+    st = run_preprocess(pl, mu, log_scale, dummy, dummy, nullptr, workspace, s, false);
     if (st != GS_OK) return st;
     int n = d->B * pl.ngroups;
     unsigned long long *tmp = new unsigned long long[n];
@@ -1931,50 +1841,24 @@ int gs_render_fwd_prior(const gs_render_desc *d, const float *mu, const float *l
     st = run_preprocess(pl, mu, log_scale, color, opacity, theta, workspace, s);
     if (st != GS_OK) return st;
     unsigned char *misc = at<unsigned char>(workspace, pl.o_misc);
-    const long long *n_eff = reinterpret_cast<const long long *>(misc + MISC_NEFF);
-    if (d->mode != GS_MODE_EXACT && d->N > 0) {
-        if (needs_exact_check(d, pl)) {
+    if (d->mode != GS_MODE_EXACT) {
+        if (d->N > 0 && needs_exact_check(d, pl)) {
             st = exact_check(d, pl, workspace, s);
             if (st != GS_OK) return st;
         }
-        k_scan_blocks<<<1, 1024, 0, s>>>(at<long long>(workspace, pl.o_bsum), pl.nblk_pre, pl.cap, misc);
-        GS_CHECK_LAUNCH("k_scan_blocks");
-        int radix = 1 << pl.radix_bits;
-        int *hist = at<int>(workspace, pl.o_hist), *dtot = at<int>(workspace, pl.o_dtot);
-        const int nemit = pl.nblk_pre * pl.emit_parts;
-        k_emit<<<nemit, 256, 0, s>>>(G, at<int4>(workspace, pl.o_meta), at<int>(workspace, pl.o_counts),
-                                     at<long long>(workspace, pl.o_bsum), pl.emit_parts,
-                                     at<unsigned>(workspace, pl.o_keys_a), at<int>(workspace, pl.o_vals_a), misc,
-                                     pl.passes > 0 ? hist : nullptr, nemit, radix);
-        GS_CHECK_LAUNCH("k_emit");
-        unsigned *ka = at<unsigned>(workspace, pl.o_keys_a), *kb = at<unsigned>(workspace, pl.o_keys_b);
-        int *va = at<int>(workspace, pl.o_vals_a), *vb = at<int>(workspace, pl.o_vals_b);
-        const int pgrid = std::min(pl.nblk_sort, 148 * 8);
-        for (int p = 0; p < pl.passes; p++) {
-            int shift = p * pl.radix_bits;
-            if (p == 0) {
-                // digit-0 histograms per emit segment come from k_emit
-                k_radix_scan<<<radix, 256, 0, s>>>(hist, n_eff, pl.cap, nemit, dtot, nemit);
-                GS_CHECK_LAUNCH("k_radix_scan");
-                k_radix_downsweep_seg<<<std::min(nemit, 148 * 8), RS_THREADS, sizeof(RsSmem), s>>>(
-                    ka, va, kb, vb, at<long long>(workspace, pl.o_bsum), pl.nblk_pre, pl.emit_parts, n_eff, pl.cap,
-                    shift, radix, hist, nemit, dtot);
-                GS_CHECK_LAUNCH("k_radix_downsweep_seg");
-            } else {
-                k_radix_upsweep<<<pgrid, RS_THREADS, 0, s>>>(ka, n_eff, pl.cap, shift, radix, hist, pl.nblk_sort);
-                GS_CHECK_LAUNCH("k_radix_upsweep");
-                k_radix_scan<<<radix, 256, 0, s>>>(hist, n_eff, pl.cap, pl.nblk_sort, dtot, 0);
-                GS_CHECK_LAUNCH("k_radix_scan");
-                k_radix_downsweep<<<pgrid, RS_THREADS, sizeof(RsSmem), s>>>(ka, va, kb, vb, n_eff, pl.cap, shift,
-                                                                            radix, hist, pl.nblk_sort, dtot);
-                GS_CHECK_LAUNCH("k_radix_downsweep");
-            }
-            std::swap(ka, kb);
-            std::swap(va, vb);
+        // (with no splats the scan still runs: it writes every tile's range empty)
+        const long long nt = (long long)d->B * G.tiles_per_image;
+        int *cursor = at<int>(workspace, pl.o_cursor);
+        k_tile_scan<<<1, TS_THREADS, 0, s>>>(at<int>(workspace, pl.o_tdiff), nt, pl.cap, at<int2>(workspace, pl.o_ranges),
+                                             cursor, at<int>(workspace, pl.o_dlist), pl.dcap, misc);
+        GS_CHECK_LAUNCH("k_tile_scan");
+        if (d->N > 0) {
+            k_scatter<<<pl.nblk_pre * pl.scatter_parts, 256, 0, s>>>(G, at<int4>(workspace, pl.o_meta),
+                                                                     at<int>(workspace, pl.o_counts),
+                                                                     pl.scatter_parts, cursor,
+                                                                     at<int>(workspace, pl.o_vals), misc);
+            GS_CHECK_LAUNCH("k_scatter");
         }
-        unsigned nrb = (unsigned)std::min<long long>(std::max<long long>(1, (pl.cap + 255) / 256), 148 * 8);
-        k_ranges<<<nrb, 256, 0, s>>>(ka, n_eff, pl.cap, at<int2>(workspace, pl.o_ranges));
-        GS_CHECK_LAUNCH("k_ranges");
     }
     bin_scope.reset();
     {
@@ -2056,7 +1940,7 @@ int gs_render_bwd(const gs_render_desc *d, const float *mu, const float *log_sca
     dim3 grid((unsigned)((long long)G.B * G.tiles_per_image));
     auto rec = at<SplatRec>(workspace, pl.o_rec);
     auto rng = at<int2>(workspace, pl.o_ranges);
-    const int *vals = at<int>(workspace, (pl.passes % 2) ? pl.o_vals_b : pl.o_vals_a);
+    const int *vals = at<int>(workspace, pl.o_vals);
     auto Gn = at<float>(workspace, pl.o_G);
     auto gf = at<float>(workspace, pl.o_gfields);
     auto acc = at<float>(workspace, pl.o_acc);
@@ -2109,7 +1993,7 @@ int gs_render_debug_bins(const gs_render_desc *d, const void *workspace, int64_t
         if (e != cudaSuccess) return set_cuda_error(e, "debug_bins");
     }
     if (splat_ids_host && tot > 0) {
-        const int *vals = at<int>(ws, (pl.passes % 2) ? pl.o_vals_b : pl.o_vals_a);
+        const int *vals = at<int>(ws, pl.o_vals);
         e = cudaMemcpy(splat_ids_host, vals, sizeof(int) * (size_t)std::min<long long>(tot, pl.cap),
                        cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) return set_cuda_error(e, "debug_bins");

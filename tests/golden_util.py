@@ -9,6 +9,11 @@ import numpy as np
 import torch
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
+# A tile's splats enter its list in the order its atomic cursor hands out slots, so two renders of the same
+# inputs agree only to the float rounding of the per-tile sums (the fields are order-independent sums, and
+# the reference's own per-tile order comes from an unstable argsort): the absolute tolerance of
+# render-against-render checks.
+REORDER_TOL = 1e-5
 LEAVES = ("mu", "log_scale", "color", "opacity", "bg", "theta")
 
 

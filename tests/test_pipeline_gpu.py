@@ -5,6 +5,7 @@ import pytest
 import torch
 
 from enc_util import GOLDEN_CFG
+from golden_util import REORDER_TOL
 
 pytestmark = pytest.mark.gpu
 
@@ -73,14 +74,14 @@ def test_encode_render_stream_matches_single(lib):
         st.submit(x, o)
     st.synchronize()
     for o, r in zip(outs, refs):
-        assert float((o - r).abs().max()) < 1e-6
+        assert float((o - r).abs().max()) < REORDER_TOL
     # device-resident images, several in flight on their own streams, results left in the slots
     dev_imgs = [x.cuda() for x in imgs[:len(st.slots)]]
     st.start_after()
     recs = [st.submit(x) for x in dev_imgs]
     st.synchronize()
     for rec, r in zip(recs, refs):
-        assert float((rec.cpu() - r).abs().max()) < 1e-6
+        assert float((rec.cpu() - r).abs().max()) < REORDER_TOL
 
 
 def test_render_fit_step_graph_matches_eager(lib):

