@@ -498,6 +498,183 @@ __device__ __forceinline__ void renorm(float &P, int &E) {
     P = __int_as_float((bits & 0x807fffff) | 0x3f000000);
 }
 
+// One splat record of opacity 0: composites to nothing (pads a batch to a multiple of 8).
+__device__ __forceinline__ SplatRec null_rec() {
+    SplatRec z;
+    z.a = make_float4(0.f, 0.f, 0.f, 0.f);
+    z.b = make_float4(0.f, 0.f, 0.f, -INFINITY);  // log2 opacity: alpha = 2^-inf = 0
+    z.c = make_float4(0.f, 0.f, 0.f, 0.f);
+    return z;
+}
+
+// Composite the staged records sr[0, nb8) (nb8 a multiple of 8) into the lane's PPL pixels, all in one
+// column (x terms once per splat): alpha = min(2^(log2 op - u^2 - v^2), 1 - 1e-4), the running product
+// of (1 - alpha) renormalised every 8 splats, and the weight sums (w = alpha / (1 - alpha) for odds).
+template <int PPL, bool ODDS>
+__device__ __forceinline__ void fields_sweep8(const SplatRec *__restrict__ sr, int nb8, const float (&py)[PPL],
+                                              float pxl, float (&P)[PPL], int (&E)[PPL], float (&Sw)[PPL],
+                                              float (&S0)[PPL], float (&S1)[PPL], float (&S2)[PPL]) {
+    for (int i = 0; i < nb8; i += 8) {
+#pragma unroll
+        for (int ii = 0; ii < 8; ii++) {
+            const SplatRec &r = sr[i + ii];
+            const float4 A = r.a, Bv = r.b, Cv = r.c;
+            const float dx = pxl - A.y;
+            const float ux = A.w * dx, vx = Bv.y * dx;
+#pragma unroll
+            for (int j = 0; j < PPL; j++) {
+                const float dy = py[j] - A.x;
+                const float u = fmaf(A.z, dy, ux);
+                const float v = fmaf(Bv.x, dy, vx);
+                const float arg = fmaf(-u, u, fmaf(-v, v, Bv.w));
+                const float a = fminf(gs_ex2(arg), GS_ALPHA_MAX);
+                const float om = 1.0f - a;
+                P[j] *= om;
+                const float w = ODDS ? a * gs_rcp(om) : a;
+                Sw[j] += w;
+                S0[j] = fmaf(w, Cv.x, S0[j]);
+                S1[j] = fmaf(w, Cv.y, S1[j]);
+                S2[j] = fmaf(w, Cv.z, S2[j]);
+            }
+        }
+        // (1 - a) >= 1e-4, so 8 factors stay normal in fp32
+#pragma unroll
+        for (int j = 0; j < PPL; j++) renorm(P[j], E[j]);
+    }
+}
+
+// Stage the records [base, base + 32) of a warp's list (splat ids ids[0, n)) in sr, padded with null
+// records to a multiple of 8; the next batch is fetched into `nxt` meanwhile.  Returns the padded count.
+__device__ __forceinline__ int stage_batch(SplatRec *__restrict__ sr, SplatRec &nxt, const SplatRec *__restrict__ rec,
+                                           const int *__restrict__ ids, int base, int n, int lane) {
+    const int nb = min(32, n - base), nb8 = (nb + 7) & ~7;
+    if (lane < nb) sr[lane] = nxt;
+    else if (lane < nb8) sr[lane] = null_rec();
+    __syncwarp();
+    const int kb = base + 32 + lane;
+    if (kb < n) nxt = rec[ids[kb]];
+    return nb8;
+}
+
+// TILE 8, binned modes: one WARP per tile (four tiles per CTA), 2 pixels per lane in one column, so there
+// is no cross-warp reduction and one set-up per tile and lane; each lane writes its pixels' five sums.
+// Tiles with more than FW_DEEP pairs are left to k_fields_deep8.
+template <bool ODDS>
+__global__ void __launch_bounds__(128) k_fields_w8(RenderGeom G, const SplatRec *__restrict__ rec,
+                                                   const int2 *__restrict__ ranges, const int *__restrict__ vals,
+                                                   float *__restrict__ fields, int nt) {
+    __shared__ SplatRec srec[4][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gt = blockIdx.x * 4 + warp;
+    if (gt >= nt) return;  // (warp-uniform; the kernel synchronises warps only)
+    const int2 rg = ranges[gt];  // empty tile: begin == end
+    const int p0 = rg.y > rg.x ? rg.x : 0;
+    const int n = rg.y > rg.x ? rg.y - rg.x : 0;
+    if (n > FW_DEEP) return;
+    const int b = gt / G.tiles_per_image;
+    const int lt = gt - b * G.tiles_per_image;
+    const int g = group_of_tile(G, lt);
+    const int Hg = G.g[g].H, Wg = G.g[g].W, ntx = G.g[g].ntx;
+    const int t = lt - G.g[g].tile_off;
+    const int tx = t % ntx, ty = t / ntx;
+    float py[2];
+#pragma unroll
+    for (int j = 0; j < 2; j++) py[j] = __fdiv_rn((float)(ty * 8 + (lane >> 3) + 4 * j) + 0.5f, (float)Hg);
+    const float pxl = __fdiv_rn((float)(tx * 8 + (lane & 7)) + 0.5f, (float)Wg);
+    float P[2] = {1.f, 1.f}, Sw[2] = {0.f, 0.f}, S0[2] = {0.f, 0.f}, S1[2] = {0.f, 0.f}, S2[2] = {0.f, 0.f};
+    int E[2] = {0, 0};
+    const int *ids = vals + p0;
+    SplatRec nxt;
+    if (lane < n) nxt = rec[ids[lane]];
+    for (int base = 0; base < n; base += 32) {
+        const int nb8 = stage_batch(srec[warp], nxt, rec, ids, base, n, lane);
+        fields_sweep8<2, ODDS>(srec[warp], nb8, py, pxl, P, E, Sw, S0, S1, S2);
+        __syncwarp();
+    }
+    float *fb = fields + (long long)b * G.fld_per_image + G.g[g].fld_off;
+    const long long plane = (long long)Hg * Wg;
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int yp = ty * 8 + (lane >> 3) + 4 * j, xp = tx * 8 + (lane & 7);
+        if (yp < Hg && xp < Wg) {
+            float *f = fb + (long long)yp * Wg + xp;
+            renorm(P[j], E[j]);
+            f[0] = __logf(P[j]) + (float)E[j] * GS_LN2;
+            f[plane] = Sw[j];
+            f[2 * plane] = S0[j];
+            f[3 * plane] = S1[j];
+            f[4 * plane] = S2[j];
+        }
+    }
+}
+
+// TILE 8 deep tiles (more than FW_DEEP pairs, listed by k_tile_scan): a persistent grid over the list,
+// 16 warps per tile splitting its list, combined in shared memory in fixed warp order.  The encoder's
+// internal coarse render puts ~1,250 splats on each of its busy tiles.
+template <bool ODDS>
+__global__ void __launch_bounds__(512) k_fields_deep8(RenderGeom G, const SplatRec *__restrict__ rec,
+                                                      const int2 *__restrict__ ranges, const int *__restrict__ vals,
+                                                      const int *__restrict__ dlist,
+                                                      const unsigned char *__restrict__ misc,
+                                                      float *__restrict__ fields) {
+    constexpr int NW = 16;
+    __shared__ SplatRec srec[NW][32];
+    __shared__ float red[NW][5][64];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwork = *reinterpret_cast<const volatile int *>(misc + MISC_NDEEP);
+    for (int wi = blockIdx.x; wi < nwork; wi += gridDim.x) {
+        const int gt = dlist[wi];
+        const int2 rg = ranges[gt];
+        const int p0 = rg.x, n = rg.y - rg.x;  // (> FW_DEEP: listed tiles are not empty)
+        const int b = gt / G.tiles_per_image;
+        const int lt = gt - b * G.tiles_per_image;
+        const int g = group_of_tile(G, lt);
+        const int Hg = G.g[g].H, Wg = G.g[g].W, ntx = G.g[g].ntx;
+        const int t = lt - G.g[g].tile_off;
+        const int tx = t % ntx, ty = t / ntx;
+        float py[2];
+#pragma unroll
+        for (int j = 0; j < 2; j++) py[j] = __fdiv_rn((float)(ty * 8 + (lane >> 3) + 4 * j) + 0.5f, (float)Hg);
+        const float pxl = __fdiv_rn((float)(tx * 8 + (lane & 7)) + 0.5f, (float)Wg);
+        float P[2] = {1.f, 1.f}, Sw[2] = {0.f, 0.f}, S0[2] = {0.f, 0.f}, S1[2] = {0.f, 0.f}, S2[2] = {0.f, 0.f};
+        int E[2] = {0, 0};
+        const int s_lo = (int)(((long long)n * warp) / NW), s_hi = (int)(((long long)n * (warp + 1)) / NW);
+        const int *ids = vals + p0 + s_lo;
+        const int m = s_hi - s_lo;
+        SplatRec nxt;
+        if (lane < m) nxt = rec[ids[lane]];
+        for (int base = 0; base < m; base += 32) {
+            const int nb8 = stage_batch(srec[warp], nxt, rec, ids, base, m, lane);
+            fields_sweep8<2, ODDS>(srec[warp], nb8, py, pxl, P, E, Sw, S0, S1, S2);
+            __syncwarp();
+        }
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const int q = lane + 32 * j;
+            renorm(P[j], E[j]);
+            red[warp][0][q] = __logf(P[j]) + (float)E[j] * GS_LN2;
+            red[warp][1][q] = Sw[j];
+            red[warp][2][q] = S0[j];
+            red[warp][3][q] = S1[j];
+            red[warp][4][q] = S2[j];
+        }
+        __syncthreads();
+        float *fb = fields + (long long)b * G.fld_per_image + G.g[g].fld_off;
+        const long long plane = (long long)Hg * Wg;
+        if (threadIdx.x < 5 * 64) {
+            const int c = threadIdx.x >> 6, pq = threadIdx.x & 63;
+            const int yp = ty * 8 + (pq >> 3), xp = tx * 8 + (pq & 7);
+            float sacc = 0.f;
+#pragma unroll
+            for (int w = 0; w < NW; w++) sacc += red[w][c][pq];
+            if (yp < Hg && xp < Wg) fb[c * plane + (long long)yp * Wg + xp] = sacc;
+        }
+        __syncthreads();  // (srec and red are reused by the next listed tile)
+    }
+}
+
+// Generic form (TILE 4 and 16, and the dense EXACT mode): one CTA of NW warps per tile, the warps
+// splitting the tile's list.
 template <int TILE, int NW, bool ODDS>
 __global__ void __launch_bounds__(NW * 32) k_fields_fwd(RenderGeom G, const SplatRec *__restrict__ rec,
                                                         const int2 *__restrict__ ranges,
@@ -1606,6 +1783,25 @@ int launch_fields_fwd(const Plan &pl, void *ws, cudaStream_t st) {
     auto rng = at<int2>(ws, pl.o_ranges);
     const int *vals = at<int>(ws, pl.o_vals);
     auto fld = at<float>(ws, pl.o_fields);
+    if (G.tile == 8 && G.mode != GS_MODE_EXACT) {
+        // deep tiles (more than FW_DEEP pairs) first, 16 warps each on a persistent grid (two 512-thread
+        // CTAs per SM); then one warp per remaining tile
+        const int *dl = at<int>(ws, pl.o_dlist);
+        const unsigned char *misc = at<unsigned char>(ws, pl.o_misc);
+        const unsigned dgrid = (unsigned)std::max(1, std::min(pl.dcap, 148 * 2));
+        const int nt = (int)((long long)G.B * G.tiles_per_image);
+        const unsigned wgrid = (unsigned)((nt + 3) / 4);
+        if (G.odds) {
+            k_fields_deep8<true><<<dgrid, 512, 0, st>>>(G, rec, rng, vals, dl, misc, fld);
+            k_fields_w8<true><<<wgrid, 128, 0, st>>>(G, rec, rng, vals, fld, nt);
+        } else {
+            k_fields_deep8<false><<<dgrid, 512, 0, st>>>(G, rec, rng, vals, dl, misc, fld);
+            k_fields_w8<false><<<wgrid, 128, 0, st>>>(G, rec, rng, vals, fld, nt);
+        }
+        GS_COUNT(1);
+        GS_CHECK_LAUNCH("k_fields_w8");
+        return GS_OK;
+    }
     // 4 warps per tile (8 measured slower: the per-warp staging and the cross-warp reduction dominate
     // short lists)
     if (G.odds) {
