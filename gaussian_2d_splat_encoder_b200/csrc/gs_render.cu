@@ -543,11 +543,46 @@ __device__ __forceinline__ void fields_sweep8(const SplatRec *__restrict__ sr, i
     }
 }
 
+// The same with the two half-warps on alternate records: half h composites sr[h], sr[h + 2], ... (nb16 a
+// multiple of 16, so each half renormalises after every 8 of its splats).
+template <int PPL, bool ODDS>
+__device__ __forceinline__ void fields_sweep16h(const SplatRec *__restrict__ sr, int nb16, int h, const float (&py)[PPL],
+                                                float pxl, float (&P)[PPL], int (&E)[PPL], float (&Sw)[PPL],
+                                                float (&S0)[PPL], float (&S1)[PPL], float (&S2)[PPL]) {
+    for (int i = 0; i < nb16; i += 16) {
+#pragma unroll
+        for (int ii = 0; ii < 8; ii++) {
+            const SplatRec &r = sr[i + 2 * ii + h];
+            const float4 A = r.a, Bv = r.b, Cv = r.c;
+            const float dx = pxl - A.y;
+            const float ux = A.w * dx, vx = Bv.y * dx;
+#pragma unroll
+            for (int j = 0; j < PPL; j++) {
+                const float dy = py[j] - A.x;
+                const float u = fmaf(A.z, dy, ux);
+                const float v = fmaf(Bv.x, dy, vx);
+                const float arg = fmaf(-u, u, fmaf(-v, v, Bv.w));
+                const float a = fminf(gs_ex2(arg), GS_ALPHA_MAX);
+                const float om = 1.0f - a;
+                P[j] *= om;
+                const float w = ODDS ? a * gs_rcp(om) : a;
+                Sw[j] += w;
+                S0[j] = fmaf(w, Cv.x, S0[j]);
+                S1[j] = fmaf(w, Cv.y, S1[j]);
+                S2[j] = fmaf(w, Cv.z, S2[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < PPL; j++) renorm(P[j], E[j]);
+    }
+}
+
 // Stage the records [base, base + 32) of a warp's list (splat ids ids[0, n)) in sr, padded with null
 // records to a multiple of 8; the next batch is fetched into `nxt` meanwhile.  Returns the padded count.
+template <int PAD = 8>
 __device__ __forceinline__ int stage_batch(SplatRec *__restrict__ sr, SplatRec &nxt, const SplatRec *__restrict__ rec,
                                            const int *__restrict__ ids, int base, int n, int lane) {
-    const int nb = min(32, n - base), nb8 = (nb + 7) & ~7;
+    const int nb = min(32, n - base), nb8 = (nb + PAD - 1) & ~(PAD - 1);
     if (lane < nb) sr[lane] = nxt;
     else if (lane < nb8) sr[lane] = null_rec();
     __syncwarp();
@@ -565,6 +600,7 @@ __global__ void __launch_bounds__(128) k_fields_w8(RenderGeom G, const SplatRec 
                                                    float *__restrict__ fields, int nt) {
     __shared__ SplatRec srec[4][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int h = lane >> 4, hl = lane & 15;  // half-warp; pixels (column hl & 7, rows (hl >> 3) + 2j)
     const int gt = blockIdx.x * 4 + warp;
     if (gt >= nt) return;  // (warp-uniform; the kernel synchronises warps only)
     const int2 rg = ranges[gt];  // empty tile: begin == end
@@ -577,33 +613,41 @@ __global__ void __launch_bounds__(128) k_fields_w8(RenderGeom G, const SplatRec 
     const int Hg = G.g[g].H, Wg = G.g[g].W, ntx = G.g[g].ntx;
     const int t = lt - G.g[g].tile_off;
     const int tx = t % ntx, ty = t / ntx;
-    float py[2];
+    float py[4];
 #pragma unroll
-    for (int j = 0; j < 2; j++) py[j] = __fdiv_rn((float)(ty * 8 + (lane >> 3) + 4 * j) + 0.5f, (float)Hg);
-    const float pxl = __fdiv_rn((float)(tx * 8 + (lane & 7)) + 0.5f, (float)Wg);
-    float P[2] = {1.f, 1.f}, Sw[2] = {0.f, 0.f}, S0[2] = {0.f, 0.f}, S1[2] = {0.f, 0.f}, S2[2] = {0.f, 0.f};
-    int E[2] = {0, 0};
+    for (int j = 0; j < 4; j++) py[j] = __fdiv_rn((float)(ty * 8 + (hl >> 3) + 2 * j) + 0.5f, (float)Hg);
+    const float pxl = __fdiv_rn((float)(tx * 8 + (hl & 7)) + 0.5f, (float)Wg);
+    float P[4] = {1.f, 1.f, 1.f, 1.f}, Sw[4] = {0.f, 0.f, 0.f, 0.f}, S0[4] = {0.f, 0.f, 0.f, 0.f},
+          S1[4] = {0.f, 0.f, 0.f, 0.f}, S2[4] = {0.f, 0.f, 0.f, 0.f};
+    int E[4] = {0, 0, 0, 0};
     const int *ids = vals + p0;
     SplatRec nxt;
     if (lane < n) nxt = rec[ids[lane]];
     for (int base = 0; base < n; base += 32) {
-        const int nb8 = stage_batch(srec[warp], nxt, rec, ids, base, n, lane);
-        fields_sweep8<2, ODDS>(srec[warp], nb8, py, pxl, P, E, Sw, S0, S1, S2);
+        const int nb16 = stage_batch<16>(srec[warp], nxt, rec, ids, base, n, lane);
+        fields_sweep16h<4, ODDS>(srec[warp], nb16, h, py, pxl, P, E, Sw, S0, S1, S2);
         __syncwarp();
     }
+    // lanes l and l + 16 hold the same pixels: the halves' sums combine (log form for the transmittance)
     float *fb = fields + (long long)b * G.fld_per_image + G.g[g].fld_off;
     const long long plane = (long long)Hg * Wg;
 #pragma unroll
-    for (int j = 0; j < 2; j++) {
-        const int yp = ty * 8 + (lane >> 3) + 4 * j, xp = tx * 8 + (lane & 7);
-        if (yp < Hg && xp < Wg) {
+    for (int j = 0; j < 4; j++) {
+        renorm(P[j], E[j]);
+        float sl = __logf(P[j]) + (float)E[j] * GS_LN2;
+        sl += __shfl_xor_sync(0xffffffffu, sl, 16);
+        const float sw = Sw[j] + __shfl_xor_sync(0xffffffffu, Sw[j], 16);
+        const float s0 = S0[j] + __shfl_xor_sync(0xffffffffu, S0[j], 16);
+        const float s1 = S1[j] + __shfl_xor_sync(0xffffffffu, S1[j], 16);
+        const float s2 = S2[j] + __shfl_xor_sync(0xffffffffu, S2[j], 16);
+        const int yp = ty * 8 + (hl >> 3) + 2 * j, xp = tx * 8 + (hl & 7);
+        if (h == 0 && yp < Hg && xp < Wg) {
             float *f = fb + (long long)yp * Wg + xp;
-            renorm(P[j], E[j]);
-            f[0] = __logf(P[j]) + (float)E[j] * GS_LN2;
-            f[plane] = Sw[j];
-            f[2 * plane] = S0[j];
-            f[3 * plane] = S1[j];
-            f[4 * plane] = S2[j];
+            f[0] = sl;
+            f[plane] = sw;
+            f[2 * plane] = s0;
+            f[3 * plane] = s1;
+            f[4 * plane] = s2;
         }
     }
 }
