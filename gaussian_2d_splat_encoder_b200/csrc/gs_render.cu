@@ -312,13 +312,49 @@ __global__ void __launch_bounds__(256) k_preprocess(RenderGeom G, const float *_
 // buffer) a second sweep empties every range and the lists, and k_scatter places nothing.
 #define TS_THREADS 1024
 #define TS_PER 16
+// Exclusive block scan of non-negative values with the sum saturating at TS_SAT (associative for
+// non-negative inputs, so the saturation only marks an overflowing total).
+#define TS_SAT 0x7fffffffu
+template <int NT>
+__device__ __forceinline__ unsigned block_excl_scan_sat(unsigned v, unsigned *warp_sums, unsigned *total) {
+    constexpr int NWARP = NT / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x = min(x + y, TS_SAT);
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        unsigned s = lane < NWARP ? warp_sums[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s = min(s + y, TS_SAT);
+        }
+        if (lane < NWARP) warp_sums[lane] = s;  // inclusive
+    }
+    __syncthreads();
+    const unsigned wp = warp > 0 ? warp_sums[warp - 1] : 0u;
+    if (total) *total = warp_sums[NWARP - 1];
+    const unsigned r = min(wp + x, TS_SAT) - v;  // (exact whenever the inclusive sum did not saturate)
+    __syncthreads();
+    return r;
+}
+
 __global__ void __launch_bounds__(TS_THREADS) k_tile_scan(const int *__restrict__ tdiff, long long nt, long long cap,
                                                           int2 *__restrict__ ranges, int *__restrict__ cursor,
                                                           int *__restrict__ dlist, int dcap,
                                                           unsigned char *__restrict__ misc) {
-    __shared__ long long wsum[32];
+    __shared__ int wsum_d[32];
+    __shared__ unsigned wsum_c[32];
     const int tid = threadIdx.x;
-    long long carry_d = 0, carry_c = 0;
+    // 32-bit throughout: a tile's count (a prefix of the differences) is at most the splats of one image,
+    // and the begin offsets saturate at 2^31 - 1 > cap, which then reads as an overflow
+    int carry_d = 0;
+    unsigned carry_c = 0u;
     for (long long base = 0; base < nt; base += (long long)TS_THREADS * TS_PER) {
         const long long lo = base + (long long)tid * TS_PER;
         // 16-byte loads: the difference array is zeroed and allocated in whole 256-byte blocks
@@ -331,30 +367,31 @@ __global__ void __launch_bounds__(TS_THREADS) k_tile_scan(const int *__restrict_
             dl[k + 2] = v.z;
             dl[k + 3] = v.w;
         }
-        long long sd = 0;
+        int sd = 0;
 #pragma unroll
         for (int k = 0; k < TS_PER; k++) {
             if (lo + k >= nt) dl[k] = 0;
             sd += dl[k];
         }
-        long long td;
-        const long long pd = carry_d + block_excl_scan<TS_THREADS, long long>(sd, wsum, &td);
+        int td;
+        const int pd = carry_d + block_excl_scan<TS_THREADS, int>(sd, wsum_d, &td);
         // counts of this thread's tiles (past the last tile the running prefix is not a count)
-        long long run = pd, sc = 0;
+        int run = pd;
+        unsigned sc = 0u;
         int cnt[TS_PER];
 #pragma unroll
         for (int k = 0; k < TS_PER; k++) {
             run += dl[k];
-            cnt[k] = lo + k < nt ? (int)run : 0;
-            sc += cnt[k];
+            cnt[k] = lo + k < nt ? run : 0;
+            sc = min(sc + (unsigned)cnt[k], TS_SAT);
         }
-        long long tc;
-        long long beg = carry_c + block_excl_scan<TS_THREADS, long long>(sc, wsum, &tc);
+        unsigned tc;
+        unsigned beg = min(carry_c + block_excl_scan_sat<TS_THREADS>(sc, wsum_c, &tc), TS_SAT);
         int bg[TS_PER];
 #pragma unroll
         for (int k = 0; k < TS_PER; k++) {
             bg[k] = (int)beg;
-            beg += cnt[k];
+            beg = min(beg + (unsigned)cnt[k], TS_SAT);
             if (cnt[k] > FW_DEEP) {
                 const int i = atomicAdd(reinterpret_cast<int *>(misc + MISC_NDEEP), 1);
                 if (i < dcap) dlist[i] = (int)(lo + k);
@@ -377,10 +414,10 @@ __global__ void __launch_bounds__(TS_THREADS) k_tile_scan(const int *__restrict_
                 }
         }
         carry_d += td;
-        carry_c += tc;
+        carry_c = min(carry_c + tc, TS_SAT);
     }
-    const long long total = carry_c;
-    const bool ok = total <= cap;
+    const long long total = (long long)carry_c;  // (TS_SAT: at least 2^31 - 1 pairs, more than any capacity)
+    const bool ok = total <= cap && carry_c < TS_SAT;
     if (tid == 0) {
         *reinterpret_cast<long long *>(misc + MISC_TOTAL) = total;
         if (!ok) *reinterpret_cast<int *>(misc + MISC_STATUS) |= 1;
@@ -653,18 +690,22 @@ __global__ void __launch_bounds__(128) k_fields_w8(RenderGeom G, const SplatRec 
 }
 
 // TILE 8 deep tiles (more than FW_DEEP pairs, listed by k_tile_scan): a persistent grid over the list,
-// 16 warps per tile splitting its list, combined in shared memory in fixed warp order.  The encoder's
-// internal coarse render puts ~1,250 splats on each of its busy tiles.
+// FW_DEEP_NW warps per tile splitting its list (half-warps on alternate splats, 4 pixels per lane as in
+// k_fields_w8), combined in shared memory in fixed warp order.  The encoder's internal coarse render puts
+// ~1,250 splats on each of its busy tiles.
+#define FW_DEEP_NW 8
 template <bool ODDS>
-__global__ void __launch_bounds__(512) k_fields_deep8(RenderGeom G, const SplatRec *__restrict__ rec,
-                                                      const int2 *__restrict__ ranges, const int *__restrict__ vals,
-                                                      const int *__restrict__ dlist,
-                                                      const unsigned char *__restrict__ misc,
-                                                      float *__restrict__ fields) {
-    constexpr int NW = 16;
+__global__ void __launch_bounds__(FW_DEEP_NW * 32) k_fields_deep8(RenderGeom G, const SplatRec *__restrict__ rec,
+                                                                 const int2 *__restrict__ ranges,
+                                                                 const int *__restrict__ vals,
+                                                                 const int *__restrict__ dlist,
+                                                                 const unsigned char *__restrict__ misc,
+                                                                 float *__restrict__ fields) {
+    constexpr int NW = FW_DEEP_NW;
     __shared__ SplatRec srec[NW][32];
     __shared__ float red[NW][5][64];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int h = lane >> 4, hl = lane & 15;
     const int nwork = *reinterpret_cast<const volatile int *>(misc + MISC_NDEEP);
     for (int wi = blockIdx.x; wi < nwork; wi += gridDim.x) {
         const int gt = dlist[wi];
@@ -676,37 +717,46 @@ __global__ void __launch_bounds__(512) k_fields_deep8(RenderGeom G, const SplatR
         const int Hg = G.g[g].H, Wg = G.g[g].W, ntx = G.g[g].ntx;
         const int t = lt - G.g[g].tile_off;
         const int tx = t % ntx, ty = t / ntx;
-        float py[2];
+        float py[4];
 #pragma unroll
-        for (int j = 0; j < 2; j++) py[j] = __fdiv_rn((float)(ty * 8 + (lane >> 3) + 4 * j) + 0.5f, (float)Hg);
-        const float pxl = __fdiv_rn((float)(tx * 8 + (lane & 7)) + 0.5f, (float)Wg);
-        float P[2] = {1.f, 1.f}, Sw[2] = {0.f, 0.f}, S0[2] = {0.f, 0.f}, S1[2] = {0.f, 0.f}, S2[2] = {0.f, 0.f};
-        int E[2] = {0, 0};
+        for (int j = 0; j < 4; j++) py[j] = __fdiv_rn((float)(ty * 8 + (hl >> 3) + 2 * j) + 0.5f, (float)Hg);
+        const float pxl = __fdiv_rn((float)(tx * 8 + (hl & 7)) + 0.5f, (float)Wg);
+        float P[4] = {1.f, 1.f, 1.f, 1.f}, Sw[4] = {0.f, 0.f, 0.f, 0.f}, S0[4] = {0.f, 0.f, 0.f, 0.f},
+              S1[4] = {0.f, 0.f, 0.f, 0.f}, S2[4] = {0.f, 0.f, 0.f, 0.f};
+        int E[4] = {0, 0, 0, 0};
         const int s_lo = (int)(((long long)n * warp) / NW), s_hi = (int)(((long long)n * (warp + 1)) / NW);
         const int *ids = vals + p0 + s_lo;
         const int m = s_hi - s_lo;
         SplatRec nxt;
         if (lane < m) nxt = rec[ids[lane]];
         for (int base = 0; base < m; base += 32) {
-            const int nb8 = stage_batch(srec[warp], nxt, rec, ids, base, m, lane);
-            fields_sweep8<2, ODDS>(srec[warp], nb8, py, pxl, P, E, Sw, S0, S1, S2);
+            const int nb16 = stage_batch<16>(srec[warp], nxt, rec, ids, base, m, lane);
+            fields_sweep16h<4, ODDS>(srec[warp], nb16, h, py, pxl, P, E, Sw, S0, S1, S2);
             __syncwarp();
         }
 #pragma unroll
-        for (int j = 0; j < 2; j++) {
-            const int q = lane + 32 * j;
+        for (int j = 0; j < 4; j++) {
             renorm(P[j], E[j]);
-            red[warp][0][q] = __logf(P[j]) + (float)E[j] * GS_LN2;
-            red[warp][1][q] = Sw[j];
-            red[warp][2][q] = S0[j];
-            red[warp][3][q] = S1[j];
-            red[warp][4][q] = S2[j];
+            float sl = __logf(P[j]) + (float)E[j] * GS_LN2;
+            sl += __shfl_xor_sync(0xffffffffu, sl, 16);
+            const float sw = Sw[j] + __shfl_xor_sync(0xffffffffu, Sw[j], 16);
+            const float s0 = S0[j] + __shfl_xor_sync(0xffffffffu, S0[j], 16);
+            const float s1 = S1[j] + __shfl_xor_sync(0xffffffffu, S1[j], 16);
+            const float s2 = S2[j] + __shfl_xor_sync(0xffffffffu, S2[j], 16);
+            if (h == 0) {
+                const int q = ((hl >> 3) + 2 * j) * 8 + (hl & 7);
+                red[warp][0][q] = sl;
+                red[warp][1][q] = sw;
+                red[warp][2][q] = s0;
+                red[warp][3][q] = s1;
+                red[warp][4][q] = s2;
+            }
         }
         __syncthreads();
         float *fb = fields + (long long)b * G.fld_per_image + G.g[g].fld_off;
         const long long plane = (long long)Hg * Wg;
-        if (threadIdx.x < 5 * 64) {
-            const int c = threadIdx.x >> 6, pq = threadIdx.x & 63;
+        for (int i = threadIdx.x; i < 5 * 64; i += NW * 32) {
+            const int c = i >> 6, pq = i & 63;
             const int yp = ty * 8 + (pq >> 3), xp = tx * 8 + (pq & 7);
             float sacc = 0.f;
 #pragma unroll
@@ -1828,18 +1878,18 @@ int launch_fields_fwd(const Plan &pl, void *ws, cudaStream_t st) {
     const int *vals = at<int>(ws, pl.o_vals);
     auto fld = at<float>(ws, pl.o_fields);
     if (G.tile == 8 && G.mode != GS_MODE_EXACT) {
-        // deep tiles (more than FW_DEEP pairs) first, 16 warps each on a persistent grid (two 512-thread
+        // deep tiles (more than FW_DEEP pairs) first, FW_DEEP_NW warps each on a persistent grid (three
         // CTAs per SM); then one warp per remaining tile
         const int *dl = at<int>(ws, pl.o_dlist);
         const unsigned char *misc = at<unsigned char>(ws, pl.o_misc);
-        const unsigned dgrid = (unsigned)std::max(1, std::min(pl.dcap, 148 * 2));
+        const unsigned dgrid = (unsigned)std::max(1, std::min(pl.dcap, 148 * 3));
         const int nt = (int)((long long)G.B * G.tiles_per_image);
         const unsigned wgrid = (unsigned)((nt + 3) / 4);
         if (G.odds) {
-            k_fields_deep8<true><<<dgrid, 512, 0, st>>>(G, rec, rng, vals, dl, misc, fld);
+            k_fields_deep8<true><<<dgrid, FW_DEEP_NW * 32, 0, st>>>(G, rec, rng, vals, dl, misc, fld);
             k_fields_w8<true><<<wgrid, 128, 0, st>>>(G, rec, rng, vals, fld, nt);
         } else {
-            k_fields_deep8<false><<<dgrid, 512, 0, st>>>(G, rec, rng, vals, dl, misc, fld);
+            k_fields_deep8<false><<<dgrid, FW_DEEP_NW * 32, 0, st>>>(G, rec, rng, vals, dl, misc, fld);
             k_fields_w8<false><<<wgrid, 128, 0, st>>>(G, rec, rng, vals, fld, nt);
         }
         GS_COUNT(1);
