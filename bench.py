@@ -38,10 +38,10 @@ sys.path.insert(0, str(ROOT))
 METRIC = "768² encode+render images/s at 1/2/4/8 B200; render fwd+bwd ms/image"
 FIT_METRIC = "config 4: 2048^2 fitting step (render fwd+bwd + NCCL all-reduce + Adam) steps/s"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
-# dram__bytes_read.sum + dram__bytes_write.sum of the two k_fields_fwd launches of one encode+render step
-# (ncu, profiles/fields_fwd_encode_render_768.md): 3.84 MB (coarse render) + 7.93 MB (final render) read,
-# nothing written back inside the launches (the field planes stay in L2)
-FIELDS_FWD_TRAFFIC = 11.77e6
+# dram__bytes_read.sum + dram__bytes_write.sum of the forward field kernels of one encode+render step
+# (ncu, profiles/fields_fwd_encode_render_768.md): 3.81 MB (coarse render, k_fields_deep8) + 7.93 MB (final
+# render, k_fields_w8) read, nothing written back inside the launches (the field planes stay in L2)
+FIELDS_FWD_TRAFFIC = 11.74e6
 STAGE_NAMES = {0: "binning", 1: "fields_fwd", 2: "composite", 3: "composite_bwd+adjoint", 4: "fields_bwd",
                5: "finalize", 6: "enc_binning", 7: "enc_fields_fwd", 8: "enc_prep", 9: "conv1", 10: "conv2", 11: "conv3", 12: "conv4_decoder",
                13: "heads", 14: "enc_gn_concat_cond", 15: "enc_coarse_render"}
@@ -715,7 +715,7 @@ def compositing_rooflines(stages, pairs, f_mhz):
     out = {"workload": "config 1 (92,160 splats, 768^2, odds)", "pairs": pairs, "pixel_pairs": pp,
            "peak_sfu_ops_per_s": sfu, "peak_fp32_ops_per_s": fp32,
            "peak_source": f"148 SMs x 16 MUFU / 128 FP32 lanes x {f_mhz:.0f} MHz (sampled SM clock)"}
-    for key, kern, n_sfu, n_fp32 in (("fields_fwd", "k_fields_fwd<8,4,odds>", 3, 17),
+    for key, kern, n_sfu, n_fp32 in (("fields_fwd", "k_fields_w8 + k_fields_deep8 (odds)", 3, 17),
                                      ("fields_bwd", "k_fields_bwd<8,4,odds>", 2, 40)):
         t = stages.get(key, {}).get("ms_per_replay", 0.0) * 1e-3
         if t <= 0:
@@ -789,7 +789,7 @@ def fields_fwd_roofline(stages, pairs_coarse, pairs_final, f_mhz, traffic=None):
         ppr = pr * 64
         per[name] = {"pairs": pr, "pixel_pairs": ppr, "ms": tm, "roofline_ms": 3.0 * ppr / sfu * 1e3,
                      "frac": (3.0 * ppr / sfu) / (tm * 1e-3)}
-    return {"bound": "sfu", "kernel": "k_fields_fwd<8,4,odds> (2 launches per step: coarse 384^2 + final 768^2)",
+    return {"bound": "sfu", "kernel": "k_fields_deep8 + k_fields_w8 (odds; coarse 384^2 render + final 768^2 render)",
             "achieved": ach / 1e12, "peak": sfu / 1e12, "unit": "T SFU-op/s", "frac": ach / sfu,
             "traffic": traffic, "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, both launches of "
                                                    "one step (profiles/fields_fwd_encode_render_768.md)"

@@ -290,19 +290,23 @@ struct HeadArgs {
 // feature cells (lane = cell) and PARTS warps, each warp accumulating its slice of the feature channels;
 // with PARTS > 1 the partial sums meet in shared memory; then warp w < min(PARTS, M) adds the extra
 // channels (pooled gradient, bilinear cond) and applies the activations of the splat slots m with
-// m % min(PARTS, M) == w.  PARTS = 1 (one warp per 32 cells, all channels) suits many cells; a channel
-// split (PARTS = 4) gives small grids enough warps.  Weights sit transposed in shared memory, [Cin][20] (18
-// outputs padded to 20), so one input channel is 5 broadcast 16-byte loads for 18 FMAs.
+// m % min(PARTS, M) == w.  PARTS = 1 (each warp 32 cells, all channels; WPB such warps per block share
+// one staging of the weights and GroupNorm table) suits many cells; a channel split (PARTS = 4) gives
+// small grids enough warps.  Weights sit transposed in shared memory, [Cin][20] (18 outputs padded to
+// 20), so one input channel is 5 broadcast 16-byte loads for 18 FMAs.
 #define HEAD_NP 20
 #define HEAD_CELLS 32
-template <int M, int PARTS>
-__global__ void __launch_bounds__(32 * PARTS) k_head(HeadArgs a) {
+template <int M, int PARTS, int WPB = 1>
+__global__ void __launch_bounds__(32 * PARTS * WPB) k_head(HeadArgs a) {
+    static_assert(PARTS == 1 || WPB == 1, "a channel split works on one group of 32 cells");
     // wT [Cin][20], bias [20], gn scale/shift [2][Cfeat], partial sums [PARTS][HEAD_CELLS][20] (PARTS > 1)
     extern __shared__ __align__(16) float shw[];
     float *wT = shw, *sb = shw + a.Cin * HEAD_NP, *gsc = sb + HEAD_NP, *gsh = gsc + a.Cfeat;
     float *red = gsh + a.Cfeat;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long cell0 = (long long)blockIdx.x * HEAD_CELLS;
+    const int part = PARTS > 1 ? warp : 0;  // channel slice of this warp
+    const int cw = PARTS > 1 ? 0 : warp;    // group of 32 cells of this warp inside the block
+    const long long cell0 = (long long)blockIdx.x * (HEAD_CELLS * WPB);
     const long long ncell = (long long)a.B * a.fH * a.fW;
     const int b0 = (int)(cell0 / ((long long)a.fH * a.fW));
     // w [nout][Cin] -> wT [Cin][20]: row k, channels strided over the block (coalesced, no divisions),
@@ -317,7 +321,8 @@ __global__ void __launch_bounds__(32 * PARTS) k_head(HeadArgs a) {
     }
     for (int i = threadIdx.x; i < HEAD_NP; i += blockDim.x) sb[i] = i < a.nout ? a.b[i] : 0.f;
     // GroupNorm scale/shift of the block's image (blocks never straddle images: the caller requires
-    // fH*fW to be a multiple of HEAD_CELLS when gn_stats is used)
+    // fH*fW to be a multiple of HEAD_CELLS when gn_stats is used, and launch_head takes WPB > 1 only when
+    // fH*fW is a multiple of the block's HEAD_CELLS * WPB cells)
     if (a.gn_stats) {
         const double n = (double)a.fH * a.fW * (a.Cfeat / 8);
         for (int c = threadIdx.x; c < a.Cfeat; c += blockDim.x) {
@@ -331,7 +336,7 @@ __global__ void __launch_bounds__(32 * PARTS) k_head(HeadArgs a) {
         }
     }
     __syncthreads();
-    const long long cell = cell0 + lane;
+    const long long cell = cell0 + cw * HEAD_CELLS + lane;
     const bool live = cell < ncell;
     float acc[HEAD_NP];
 #pragma unroll
@@ -348,7 +353,7 @@ __global__ void __launch_bounds__(32 * PARTS) k_head(HeadArgs a) {
         }
     };
     const int per = ((a.Cfeat / 8 + PARTS - 1) / PARTS) * 8;
-    const int c_lo = warp * per, c_hi = min(a.Cfeat, c_lo + per);
+    const int c_lo = part * per, c_hi = min(a.Cfeat, c_lo + per);
     if (live) {
         // the warp's slice, up to 4 vectors of 8 channels at a time, loaded before any arithmetic
         const __nv_bfloat16 *fp = a.feat + cell * a.Cfeat;
@@ -424,7 +429,7 @@ __global__ void __launch_bounds__(32 * PARTS) k_head(HeadArgs a) {
     const float by = lin_center(y, a.fH), bx = lin_center(x, a.fW);
 #pragma unroll
     for (int m = 0; m < M; m++) {
-        if (m % NFIN != warp) continue;
+        if (m % NFIN != part) continue;
         const long long nl = (long long)r * M + m;  // splat index inside the group (cell-major, then slot)
         const long long n = (long long)b * a.Ntot + a.n0 + nl;
         float muy = by + tanhf(acc[m * 2 + 0]) * a.off_scale;
@@ -590,12 +595,18 @@ size_t head_smem(const HeadArgs &h, long long ncell) {
 }
 
 void launch_head(const HeadArgs &h, long long ncell, cudaStream_t s) {
-    const unsigned grid = (unsigned)((ncell + HEAD_CELLS - 1) / HEAD_CELLS);
     const size_t smem = head_smem(h, ncell);
     if (head_parts(ncell) == 4) {
+        const unsigned grid = (unsigned)((ncell + HEAD_CELLS - 1) / HEAD_CELLS);
         if (h.M == 1) k_head<1, 4><<<grid, 128, smem, s>>>(h);
         else k_head<2, 4><<<grid, 128, smem, s>>>(h);
+    } else if (((long long)h.fH * h.fW) % (HEAD_CELLS * 8) == 0) {
+        // 8 warps of 32 cells per block: one weight staging for 256 cells
+        const unsigned grid = (unsigned)((ncell + HEAD_CELLS * 8 - 1) / (HEAD_CELLS * 8));
+        if (h.M == 1) k_head<1, 1, 8><<<grid, 256, smem, s>>>(h);
+        else k_head<2, 1, 8><<<grid, 256, smem, s>>>(h);
     } else {
+        const unsigned grid = (unsigned)((ncell + HEAD_CELLS - 1) / HEAD_CELLS);
         if (h.M == 1) k_head<1, 1><<<grid, 32, smem, s>>>(h);
         else k_head<2, 1><<<grid, 32, smem, s>>>(h);
     }
