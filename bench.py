@@ -36,7 +36,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "768² encode+render images/s at 1/2/4/8 B200; render fwd+bwd ms/image"
-FIT_METRIC = "config 4: 2048^2 fitting step (render fwd+bwd + NCCL all-reduce + Adam) steps/s"
+FIT_METRIC = "config 4: 2048^2 fitting step (render fwd+bwd + NCCL reduce-scatter + sharded Adam + all-gather) steps/s"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 # dram__bytes_read.sum + dram__bytes_write.sum of the forward field kernels of one encode+render step
 # (ncu, profiles/fields_fwd_encode_render_768.md): 3.81 MB (coarse render, k_fields_deep8) + 7.93 MB (final
@@ -447,9 +447,10 @@ def time_points(torch, dev, N=92160, P=3000, H=768, W=768, reps=20):
 class FitWorkload:
     """Config 4: fitting loop on one 2048x2048 card (seed 4) with 655,360 splats initialised by the encoder.
     Rank r renders native rows [r*H/R, (r+1)*H/R) (render_alpha_octave row_band), the L2 loss is normalised
-    by the global pixel count, the splat-parameter gradients (9 floats per splat + bg) are summed across
-    ranks with one NCCL all-reduce, and every rank applies the same fused Adam step (lr 1e-2).  One step =
-    one CUDA graph replay (render fwd + bwd + all-reduce + Adam)."""
+    by the global pixel count, the splat-parameter gradients (9 floats per splat + bg) are summed and split
+    across ranks with one NCCL reduce-scatter, each rank runs the fused Adam step (lr 1e-2) on its 1/R of
+    the parameters, and one all-gather returns the full parameters (shard.ShardedAdam).  One step = one CUDA
+    graph replay (render fwd + bwd + reduce-scatter + Adam + all-gather)."""
 
     name = "fit"
     metric, unit, scaling = FIT_METRIC, "steps/s", "strong"
@@ -476,8 +477,7 @@ class FitWorkload:
         from gaussian_2d_splat_encoder_b200 import shard
 
         self.band = shard.row_bands(self.H, world)[rank]
-        self.opt = torch.optim.Adam(self.leaves, lr=1e-2, fused=True, capturable=True)
-        self.flat = torch.zeros(sum(t.numel() for t in self.leaves), device=dev)
+        self.opt = shard.ShardedAdam(self.leaves, lr=1e-2)
         self.graph = None
 
         class _P:  # launches_per_replay holder, like the pipelines
@@ -486,13 +486,11 @@ class FitWorkload:
         self.pipe = _P()
 
     def _body(self):
-        from gaussian_2d_splat_encoder_b200 import pipeline, shard
+        from gaussian_2d_splat_encoder_b200 import pipeline
 
         L = self.leaves
         loss, grads = pipeline.render_l2_grads(L, self.target, self.H, self.W, True, self.band)
-        for t, g in zip(L, shard.allreduce_grads(grads, self.flat)):
-            t.grad = g
-        self.opt.step()
+        self.opt.step(grads)
         return loss
 
     def capture(self, profile=False):
@@ -527,11 +525,6 @@ class FitWorkload:
         self.graph.replay()
         return self.loss
 
-    def reset(self):
-        with self.torch.no_grad():
-            for t, k in zip(self.leaves, self.keys):
-                t.copy_(self.init[k])
-
     def e2e_buffers(self):
         return self.torch.empty(1).pin_memory()
 
@@ -550,7 +543,7 @@ class FitWorkload:
 
     def config(self):
         return {**self.describe(self.wdesc, self.N),
-                "implementation": "render fwd+bwd on a native-row band per rank, NCCL all-reduce of the splat "
+                "implementation": "render fwd+bwd on a native-row band per rank, NCCL reduce-scatter of the splat "
                                   "gradients, fused Adam; one CUDA graph per step",
                 "band_rows": list(self.band),
                 "l2": "flushed between timed steps (256 MB write, outside the timed events)"}
@@ -872,8 +865,9 @@ def reference_triton_leg(torch, dev, H=768, W=768, warmup=5, runs=30):
 
 
 def fit_leg(torch, lib, dev, flush, rank, world, K=20, warmup=3, max_over_ranks=None, barrier=None):
-    """Config 4 at this N (tile-row bands, one NCCL all-reduce of the splat gradients per step): steps/s as
-    the max over ranks of K graph replays, the field backward's roofline, and the all-reduce alone."""
+    """Config 4 at this N (tile-row bands, NCCL reduce-scatter + all-gather around a sharded Adam per step):
+    steps/s as the max over ranks of K graph replays, the field backward's roofline, and the two
+    collectives alone."""
     wl = FitWorkload(dev, rank, world)
     wl.capture()
     for _ in range(warmup):
@@ -888,18 +882,24 @@ def fit_leg(torch, lib, dev, flush, rank, world, K=20, warmup=3, max_over_ranks=
     if world > 1:
         import torch.distributed as dist
 
-        buf = wl.flat
+        o = wl.opt
+
+        def coll():
+            dist.reduce_scatter_tensor(o.gshard, o.flat_g)
+            dist.all_gather_into_tensor(o.flat_p, o.param.data)
+
         for _ in range(3):
-            dist.all_reduce(buf)
+            coll()
         barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(K):
-            dist.all_reduce(buf)
+            coll()
         b.record()
         torch.cuda.synchronize()
-        ar = {"ms": max_over_ranks(a.elapsed_time(b) / K), "bytes": buf.numel() * 4,
-              "what": "NCCL all-reduce (sum) of the flattened splat gradients alone, eager, max over ranks"}
+        ar = {"ms": max_over_ranks(a.elapsed_time(b) / K), "bytes": o.flat_g.numel() * 4,
+              "what": "NCCL reduce-scatter of the flattened splat gradients + all-gather of the updated "
+                      "parameter shards, alone, eager, max over ranks"}
     wl.release()
     barrier()
     stages = profile_stages(torch, lib, FitWorkload, dev, flush, rank=rank, world=world)
@@ -1061,7 +1061,7 @@ def main():
         "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": tot_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 encoder / fp32 render" if wcls is EncodeRenderWorkload else "fp32", "data": "synthetic",
-        "config": {**wl.config(), "parallelism": (f"tile-row bands x{world}, one NCCL all-reduce of the splat "
+        "config": {**wl.config(), "parallelism": (f"tile-row bands x{world}, NCCL reduce-scatter / all-gather of the splat "
                                                   "gradients per step" if wcls is FitWorkload else
                                                   f"dp{world} (image per GPU, no collective)")},
         "stages_ms": stages, "clocks": clocks, "gpu_launches": int(launches),

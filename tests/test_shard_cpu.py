@@ -1,6 +1,7 @@
 """Multi-process host logic on CPU (gloo, world size 2): row bands partition the image, per-band partial
 gradients (the oracle's gradients of the band's share of the loss) all-reduce to the full gradient, and
-the replicated Adam steps stay identical across ranks; image dealing covers every image once."""
+the replicated Adam steps stay identical across ranks; the sharded Adam (reduce-scatter, Adam on 1/R of
+the parameters, all-gather) gives the same parameters; image dealing covers every image once."""
 
 import os
 import socket
@@ -19,7 +20,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, sharded=False):
     import torch.distributed as dist
 
     from gaussian_2d_splat_encoder_b200 import shard
@@ -37,7 +38,8 @@ def _worker(rank, world, port, q):
     keys = ("mu", "log_scale", "color", "opacity", "bg", "theta")
     band = shard.row_bands(H, world)[rank]
     leaves = [ins[k].clone() for k in keys]
-    opt = torch.optim.Adam([t.requires_grad_(True) for t in leaves], lr=1e-2)
+    opt = (shard.ShardedAdam(leaves, lr=1e-2) if sharded
+           else torch.optim.Adam([t.requires_grad_(True) for t in leaves], lr=1e-2))
     flat = torch.zeros(sum(t.numel() for t in leaves))
     for _ in range(2):
         npi = [t.detach().numpy() for t in leaves]
@@ -46,6 +48,9 @@ def _worker(rank, world, port, q):
         y0, y1 = band
         gout[:, :, y0:y1] = 2.0 * (out - target.numpy())[:, :, y0:y1] / out.size    # d band_mse / d out
         _, og = O.render_alpha_octave(*npi[:5], H, W, theta=npi[5], odds=True, grad_out=gout)
+        if sharded:
+            opt.step([torch.from_numpy(og[k]) for k in keys])
+            continue
         grads = shard.allreduce_grads([torch.from_numpy(og[k]) for k in keys], flat)
         for t, gr in zip(leaves, grads):
             t.grad = gr.clone()
@@ -94,3 +99,27 @@ def test_sharded_fit_matches_single_process():
     p.join(timeout=60)
     for a, b in zip(res[0], single):
         assert np.allclose(a, b, atol=1e-6, rtol=1e-5)
+
+
+def test_sharded_adam_matches_replicated():
+    """ShardedAdam over 2 gloo ranks: both ranks end with identical parameters, equal to the replicated
+    all-reduce + Adam run of the same steps."""
+    from oracle import oracle as O
+
+    O.build()
+    ctx = mp.get_context("spawn")
+    runs = {}
+    for sharded in (False, True):
+        q = ctx.Queue()
+        port = _free_port()
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, q, sharded)) for r in range(2)]
+        for p in procs:
+            p.start()
+        runs[sharded] = dict(q.get(timeout=300) for _ in procs)
+        for p in procs:
+            p.join(timeout=60)
+            assert p.exitcode == 0
+    for a, b in zip(runs[True][0], runs[True][1]):
+        assert np.array_equal(a, b)
+    for a, b in zip(runs[True][0], runs[False][0]):
+        assert np.allclose(a, b, atol=1e-6, rtol=1e-6)
