@@ -442,9 +442,12 @@ int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in
     if (d->kind == 1 && Co != 64) return GS_ERR_BAD_ARGUMENT;
     if (d->stride == 2 && (Wi % 2 != 0)) return GS_ERR_BAD_ARGUMENT;
     if (d->stride != 1 && d->stride != 2) return GS_ERR_BAD_ARGUMENT;
-    // kernel shape per layer: MT stacked M-tiles per work item, BN output channels per item
-    const int MT = Co == 256 ? 1 : 2;
-    const int BN = Co == 256 ? 128 : Co;
+    // kernel shape per layer: MT stacked M-tiles per work item, BN output channels per item.  The 3x3
+    // layers at Cout 128 / 256 take single 128-pixel tiles (and 64-channel slices at 256) with 3 stages, so
+    // two or three CTAs share an SM: a layer at 768^2 has only ~150 items of MT = 2, one per SM, whose TMA +
+    // MMA latency chain and epilogue then ran back to back with nothing to overlap them
+    const int MT = (KC == 64 && Co >= 128) ? 1 : 2;
+    const int BN = Co == 256 ? 64 : Co;
     ConvArgs a;
     a.B = B; a.Hi = Hi; a.Wi = Wi; a.Ci = Ci; a.Co = Co;
     a.KH = d->kh; a.KW = d->kw; a.stride = d->stride; a.pad = d->pad; a.padw = padw >= 0 ? padw : d->pad;
@@ -496,8 +499,8 @@ int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in
     // one column slice per accumulator: doubling the epilogue warps (CS = 2) measured slower on B200
     if (KC == 16) return launch<64, 16, 8, 2, 8, 2, 1>(tA, tA2, tB, a, st);
     if (Co == 64) return launch<64, 64, 5, 2, 8, 1, 1>(tA, tA2, tB, a, st);
-    if (Co == 128) return launch<128, 64, 4, 2, 16, 1, 1>(tA, tA2, tB, a, st);
-    return launch<128, 64, 6, 1, 32, 1, 1>(tA, tA2, tB, a, st);
+    if (Co == 128) return launch<128, 64, 3, 1, 16, 2, 1>(tA, tA2, tB, a, st);
+    return launch<64, 64, 3, 1, 32, 3, 1>(tA, tA2, tB, a, st);
 }
 
 extern "C" int gs_conv2d(const gs_conv_desc *d, const void *in_bf16, const void *w_bf16, const float *bias,

@@ -505,9 +505,24 @@ __global__ void __launch_bounds__(256) k_scatter(RenderGeom G, const int4 *__res
             psplat[jj] = (unsigned char)lo;
         }
         __syncthreads();
-        for (int i = tid; i < hsize; i += 256) {
-            const int k = hkey[i];
-            if (k >= 0) hval[i] = atomicAdd(cursor + k, hval[i]);
+        {
+            // every slot's cursor atomic issued before any result is used (up to 16 in flight per thread)
+            constexpr int HJ = SC_HASH / 256;
+            int res[HJ];
+#pragma unroll
+            for (int jj = 0; jj < HJ; jj++) {
+                const int i = tid + jj * 256;
+                res[jj] = 0;
+                if (i < hsize) {
+                    const int k = hkey[i];
+                    if (k >= 0) res[jj] = atomicAdd(cursor + k, hval[i]);
+                }
+            }
+#pragma unroll
+            for (int jj = 0; jj < HJ; jj++) {
+                const int i = tid + jj * 256;
+                if (i < hsize && hkey[i] >= 0) hval[i] = res[jj];
+            }
         }
         __syncthreads();
         for (int jj = tid; jj < n; jj += 256) {
