@@ -920,11 +920,14 @@ def main():
     ap.add_argument("--no-fit", action="store_true", help="skip the config-4 sub-object of the default line")
     ap.add_argument("--no-reference-triton", action="store_true",
                     help="skip timing the reference's own GPU path (default line, N = 1)")
+    ap.add_argument("--depth", type=int, default=EncodeRenderWorkload.DEPTH,
+                    help="images in flight in the throughput (value) and e2e measurements of encode_render")
     ap.add_argument("--kernels-only", action="store_true",
                     help="warm-up + K graph replays and nothing else (for ncu launch lists)")
     args = ap.parse_args()
     W = max(3, args.warmup)
     K = max(1, args.steps)
+    EncodeRenderWorkload.DEPTH = max(1, args.depth)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -224,17 +224,36 @@ __global__ void __launch_bounds__(256) k_gn_apply(__nv_bfloat16 *__restrict__ x,
 
 // bg = sigmoid(W * mean_hw(s8) + b) (efficient_encoder.py:308-309); one block of C threads per image: thread
 // c sums channel c's nblk block partials in order, then the three dot products reduce over the block
-__global__ void __launch_bounds__(256) k_bg(const float *__restrict__ chsum, int nblk, int C, long long HW,
-                                            const float *__restrict__ w, const float *__restrict__ bias,
-                                            const double *__restrict__ gn_stats, const float *__restrict__ gn_gamma,
-                                            const float *__restrict__ gn_beta, float2 *__restrict__ gn_table,
-                                            float *__restrict__ bg) {
+__global__ void __launch_bounds__(1024) k_bg(const float *__restrict__ chsum, int nblk, int C, long long HW,
+                                             const float *__restrict__ w, const float *__restrict__ bias,
+                                             const double *__restrict__ gn_stats, const float *__restrict__ gn_gamma,
+                                             const float *__restrict__ gn_beta, float2 *__restrict__ gn_table,
+                                             float *__restrict__ bg) {
+    // 4 threads per channel (C <= 256), each a quarter of the nblk partials with 4 independent running
+    // sums (loads in flight together), combined in a fixed order: reproducible
+    __shared__ float part[4][256];
     __shared__ float red[3][8];
-    const int b = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
+    const int b = blockIdx.x, c = threadIdx.x & 255, pq = threadIdx.x >> 8;
+    if (c < C) {
+        const int k0 = pq * nblk / 4, k1 = (pq + 1) * nblk / 4;
+        const float *src = chsum + (long long)b * nblk * C + c;
+        float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+        int k = k0;
+        for (; k + 4 <= k1; k += 4) {
+            t0 += src[(long long)k * C];
+            t1 += src[(long long)(k + 1) * C];
+            t2 += src[(long long)(k + 2) * C];
+            t3 += src[(long long)(k + 3) * C];
+        }
+        for (; k < k1; k++) t0 += src[(long long)k * C];
+        part[pq][c] = (t0 + t1) + (t2 + t3);
+    }
+    __syncthreads();
+    if (threadIdx.x >= 256) return;
+    const int lane = c & 31, warp = c >> 5;
     float s0 = 0.f, s1 = 0.f, s2 = 0.f;
     if (c < C) {
-        float t = 0.f;
-        for (int k = 0; k < nblk; k++) t += chsum[((long long)b * nblk + k) * C + c];
+        float t = (part[0][c] + part[1][c]) + (part[2][c] + part[3][c]);
         float m = t / (float)HW;
         if (gn_stats) {  // the sums are of the raw values: mean of the normalised = scale * mean + shift
             float sc, sh;
@@ -257,10 +276,10 @@ __global__ void __launch_bounds__(256) k_bg(const float *__restrict__ chsum, int
         red[1][warp] = s1;
         red[2][warp] = s2;
     }
-    __syncthreads();
+    asm volatile("bar.sync 1, 256;" ::: "memory");  // the first 256 threads only
     if (c < 3) {
         float s = bias[c];
-        for (int k = 0; k < (int)(blockDim.x >> 5); k++) s += red[c][k];
+        for (int k = 0; k < 8; k++) s += red[c][k];
         bg[b * 3 + c] = 1.0f / (1.0f + expf(-s));
     }
 }
@@ -801,7 +820,7 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     const bool gn3_fly = ((long long)p.H8 * p.W8) % HEAD_CELLS == 0;
     gn(W<void>(ws, p.o_y3), (long long)p.H8 * p.W8, 256, gn3, w->gn3_w, w->gn3_b, chsum, gn3_fly ? 0 : 1);
     float2 *gtab = W<float2>(ws, p.o_gtab);
-    k_bg<<<B, 256, 0, s>>>(chsum, GN_BG_BLOCKS, 256, (long long)p.H8 * p.W8, w->bg_w, w->bg_b,
+    k_bg<<<B, 1024, 0, s>>>(chsum, GN_BG_BLOCKS, 256, (long long)p.H8 * p.W8, w->bg_w, w->bg_b,
                            gn3_fly ? gn3 : nullptr, w->gn3_w, w->gn3_b, gtab, bg);
     // fork: the fine decoder (5.) on the side stream, the coarse head and render (3., 4.) on the caller's.
     // With stage profiling on, both run on the caller's stream so each stage's events time its own kernels.
