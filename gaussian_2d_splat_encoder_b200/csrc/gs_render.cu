@@ -26,6 +26,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "../../include/gsplat_b200.h"
 #include "gs_common.cuh"
@@ -1313,46 +1314,53 @@ __global__ void __launch_bounds__(NW * 32) k_fields_bwd(RenderGeom G, const Spla
             vx[lx] = D * dx;
         }
         float Su = 0.f, Sv = 0.f, Suu = 0.f, Svv = 0.f, Suv = 0.f, Sf = 0.f, Sc0 = 0.f, Sc1 = 0.f, Sc2 = 0.f;
-        // rows rolled, columns unrolled: the loop body stays small enough for the instruction cache
+        // alpha = min(op f, 1 - 1e-4) with f <= 1: when every splat of the warp has op below the clamp, no
+        // pixel clamps and the clamp's compare / select drop out of the loop (CLAMP = false)
+        auto sweep = [&](auto clamp_tag) {
+            constexpr bool CLAMP = decltype(clamp_tag)::value;
+            // rows rolled, columns unrolled: the loop body stays small enough for the instruction cache
 #pragma unroll 1
-        for (int ly = 0; ly < TILE; ly++) {
-            const float dy = spy[ly] - muy;
-            const float uy = A * dy, vy = Cc * dy;
+            for (int ly = 0; ly < TILE; ly++) {
+                const float dy = spy[ly] - muy;
+                const float uy = A * dy, vy = Cc * dy;
 #pragma unroll
-            for (int lx = 0; lx < TILE; lx++) {
-                const int q = ly * TILE + lx;
-                const float4 d4 = dsa[q];
-                const float dS2 = dsb[q];
-                const float u = uy + ux[lx];
-                const float v = vy + vx[lx];
-                const float f = gs_ex2(-fmaf(u, u, v * v));
-                const float fo = op * f;
-                const float a = fminf(fo, GS_ALPHA_MAX);
-                const float om = 1.0f - a;
-                const float rr = gs_rcp(om);
-                const float col_term = fmaf(d4.z, c0, fmaf(d4.w, c1, dS2 * c2));
-                float da, cw;
-                if (ODDS) {
-                    da = fmaf(d4.y + col_term, rr, -d4.x) * rr;
-                    cw = a * rr;
-                } else {
-                    da = fmaf(-d4.x, rr, d4.y + col_term);
-                    cw = a;
+                for (int lx = 0; lx < TILE; lx++) {
+                    const int q = ly * TILE + lx;
+                    const float4 d4 = dsa[q];
+                    const float dS2 = dsb[q];
+                    const float u = uy + ux[lx];
+                    const float v = vy + vx[lx];
+                    const float f = gs_ex2(-fmaf(u, u, v * v));
+                    const float fo = op * f;
+                    const float a = CLAMP ? fminf(fo, GS_ALPHA_MAX) : fo;
+                    const float om = 1.0f - a;
+                    const float rr = gs_rcp(om);
+                    const float col_term = fmaf(d4.z, c0, fmaf(d4.w, c1, dS2 * c2));
+                    float da, cw;
+                    if (ODDS) {
+                        da = fmaf(d4.y + col_term, rr, -d4.x) * rr;
+                        cw = a * rr;
+                    } else {
+                        da = fmaf(-d4.x, rr, d4.y + col_term);
+                        cw = a;
+                    }
+                    Sc0 = fmaf(cw, d4.z, Sc0);
+                    Sc1 = fmaf(cw, d4.w, Sc1);
+                    Sc2 = fmaf(cw, dS2, Sc2);
+                    const float dafo = (!CLAMP || fo < GS_ALPHA_MAX) ? da : 0.0f;
+                    Sf = fmaf(dafo, f, Sf);
+                    const float Gm = dafo * fo;
+                    const float Gu = Gm * u, Gv = Gm * v;
+                    Su += Gu;
+                    Sv += Gv;
+                    Suu = fmaf(Gu, u, Suu);
+                    Svv = fmaf(Gv, v, Svv);
+                    Suv = fmaf(Gu, v, Suv);
                 }
-                Sc0 = fmaf(cw, d4.z, Sc0);
-                Sc1 = fmaf(cw, d4.w, Sc1);
-                Sc2 = fmaf(cw, dS2, Sc2);
-                const float dafo = fo < GS_ALPHA_MAX ? da : 0.0f;
-                Sf = fmaf(dafo, f, Sf);
-                const float Gm = dafo * fo;
-                const float Gu = Gm * u, Gv = Gm * v;
-                Su += Gu;
-                Sv += Gv;
-                Suu = fmaf(Gu, u, Suu);
-                Svv = fmaf(Gv, v, Svv);
-                Suv = fmaf(Gu, v, Suv);
             }
-        }
+        };
+        if (__all_sync(__activemask(), op < GS_ALPHA_MAX)) sweep(std::false_type());
+        else sweep(std::true_type());
         float *ap = acc + (long long)sid * 12;
         gs_red_add_v4(ap, Su, Sv, Suu, Svv);
         gs_red_add_v4(ap + 4, Suv, Sf, Sc0, Sc1);
