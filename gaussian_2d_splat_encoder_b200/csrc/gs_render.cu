@@ -560,44 +560,11 @@ __device__ __forceinline__ SplatRec null_rec() {
     return z;
 }
 
-// Composite the staged records sr[0, nb8) (nb8 a multiple of 8) into the lane's PPL pixels, all in one
-// column (x terms once per splat): alpha = min(2^(log2 op - u^2 - v^2), 1 - 1e-4), the running product
-// of (1 - alpha) renormalised every 8 splats, and the weight sums (w = alpha / (1 - alpha) for odds).
-template <int PPL, bool ODDS>
-__device__ __forceinline__ void fields_sweep8(const SplatRec *__restrict__ sr, int nb8, const float (&py)[PPL],
-                                              float pxl, float (&P)[PPL], int (&E)[PPL], float (&Sw)[PPL],
-                                              float (&S0)[PPL], float (&S1)[PPL], float (&S2)[PPL]) {
-    for (int i = 0; i < nb8; i += 8) {
-#pragma unroll
-        for (int ii = 0; ii < 8; ii++) {
-            const SplatRec &r = sr[i + ii];
-            const float4 A = r.a, Bv = r.b, Cv = r.c;
-            const float dx = pxl - A.y;
-            const float ux = A.w * dx, vx = Bv.y * dx;
-#pragma unroll
-            for (int j = 0; j < PPL; j++) {
-                const float dy = py[j] - A.x;
-                const float u = fmaf(A.z, dy, ux);
-                const float v = fmaf(Bv.x, dy, vx);
-                const float arg = fmaf(-u, u, fmaf(-v, v, Bv.w));
-                const float a = fminf(gs_ex2(arg), GS_ALPHA_MAX);
-                const float om = 1.0f - a;
-                P[j] *= om;
-                const float w = ODDS ? a * gs_rcp(om) : a;
-                Sw[j] += w;
-                S0[j] = fmaf(w, Cv.x, S0[j]);
-                S1[j] = fmaf(w, Cv.y, S1[j]);
-                S2[j] = fmaf(w, Cv.z, S2[j]);
-            }
-        }
-        // (1 - a) >= 1e-4, so 8 factors stay normal in fp32
-#pragma unroll
-        for (int j = 0; j < PPL; j++) renorm(P[j], E[j]);
-    }
-}
-
-// The same with the two half-warps on alternate records: half h composites sr[h], sr[h + 2], ... (nb16 a
-// multiple of 16, so each half renormalises after every 8 of its splats).
+// Composite the staged records into the lane's PPL pixels, all in one column (x terms once per splat), the
+// two half-warps on alternate records: half h takes sr[h], sr[h + 2], ... (nb16 a multiple of 16, so each
+// half renormalises after every 8 of its splats).  alpha = min(2^(log2 op - u^2 - v^2), 1 - 1e-4), the
+// running product of (1 - alpha) renormalised every 8 splats, and the weight sums (w = alpha / (1 - alpha)
+// for odds).
 template <int PPL, bool ODDS>
 __device__ __forceinline__ void fields_sweep16h(const SplatRec *__restrict__ sr, int nb16, int h, const float (&py)[PPL],
                                                 float pxl, float (&P)[PPL], int (&E)[PPL], float (&Sw)[PPL],
