@@ -234,46 +234,62 @@ class EncodeRenderWorkload:
         imgs = [synth.synth_card(self.H, self.W, 500, 150, s) for s in mine]
         self.host = [x.contiguous().pin_memory() for x in imgs]
         self.dev_imgs = [x.to(dev) for x in imgs]
-        self.pipe = pipeline.EncodeRender(self.enc, 1, self.H, self.W, dev)
+        # the single-image graph of the latency figure; PIPE_BATCH > 1 (--kernels-only --batch-graph) makes
+        # it the throughput form's batch graph, for launch lists of that form
+        self.pipe = pipeline.EncodeRender(self.enc, self.PIPE_BATCH, self.H, self.W, dev)
+        self.stage_src = self.dev_imgs if self.PIPE_BATCH == 1 else self._batches(self.dev_imgs, n=self.PIPE_BATCH)
         self.i = 0
 
     def capture(self, profile=False):
-        self.pipe.x.copy_(self.dev_imgs[0])
+        self.pipe.x.copy_(self.stage_src[0])
         self.pipe.capture(profile)
 
     def stage(self):
         """Put the next image into the pipeline's input buffer (outside the timed events)."""
-        self.pipe.x.copy_(self.dev_imgs[self.i % len(self.dev_imgs)], non_blocking=True)
+        self.pipe.x.copy_(self.stage_src[self.i % len(self.stage_src)], non_blocking=True)
         self.i += 1
 
     def step(self):
         return self.pipe.replay()
 
-    DEPTH = 4  # images in flight (graph instances on their own streams)
+    DEPTH = 3  # batches in flight (graph instances on their own streams)
+    BATCH = 4  # images per graph replay in the throughput and e2e forms (one step = one batch)
+    PIPE_BATCH = 1
+
+    def _batches(self, cards, pin=False, n=None):
+        """This rank's cards stacked into [n,3,H,W] batches (n = BATCH by default), every card used (cycled
+        when a rank holds fewer than n)."""
+        torch, B = self.torch, n or self.BATCH
+        nb = max(1, len(cards) // B)
+        out = [torch.stack([cards[(j * B + t) % len(cards)][0] for t in range(B)]) for j in range(nb)]
+        return [x.contiguous().pin_memory() for x in out] if pin else out
 
     def _stream(self):
         from gaussian_2d_splat_encoder_b200 import pipeline
 
         if not hasattr(self, "stream"):
-            self.stream = pipeline.EncodeRenderStream(self.enc, self.H, self.W, self.dev, depth=self.DEPTH).capture()
+            self.stream = pipeline.EncodeRenderStream(self.enc, self.H, self.W, self.dev, depth=self.DEPTH,
+                                                      batch=self.BATCH).capture()
+            self.dev_batches = self._batches(self.dev_imgs)
         return self.stream
 
     def time_pipelined(self, K, warmup):
-        """Whole-job throughput: K device-resident cards (cycling through all of this rank's cards, 453 MB
-        for 64, more than L2) through EncodeRenderStream with DEPTH images in flight; CUDA events on the
-        current stream around the K submits.  Returns the elapsed ms."""
+        """Whole-job throughput: K device-resident batches of BATCH cards (cycling through all of this
+        rank's cards, 453 MB for 64, more than L2) through EncodeRenderStream with DEPTH batches in
+        flight; CUDA events on the current stream around the K submits.  Returns the elapsed ms."""
         torch = self.torch
         st = self._stream()
+        nb = len(self.dev_batches)
         st.start_after()
         for i in range(warmup):
-            st.submit(self.dev_imgs[i % len(self.dev_imgs)])
+            st.submit(self.dev_batches[i % nb])
         st.wait_into()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         st.start_after()
         for i in range(K):
-            st.submit(self.dev_imgs[(self.i + i) % len(self.dev_imgs)])
+            st.submit(self.dev_batches[(self.i + i) % nb])
         st.wait_into()
         b.record()
         torch.cuda.synchronize()
@@ -281,25 +297,26 @@ class EncodeRenderWorkload:
         return a.elapsed_time(b)
 
     def e2e_buffers(self):
-        """The streaming form of the public pipeline (EncodeRenderStream, DEPTH graph instances) and DEPTH
-        pinned output images."""
+        """The streaming form of the public pipeline (EncodeRenderStream, DEPTH graph instances of BATCH
+        images), pinned input batches and DEPTH pinned output batches."""
         self._stream()
-        return [self.torch.empty(1, 3, self.H, self.W).pin_memory() for _ in range(self.DEPTH)]
+        self.host_batches = self._batches(self.host, pin=True)
+        return [self.torch.empty(self.BATCH, 3, self.H, self.W).pin_memory() for _ in range(self.DEPTH)]
 
     def e2e_begin(self):
         self.stream.start_after()
 
     def e2e_step(self, bufs):
-        # H2D of this image from pinned memory, encode + render, D2H of its reconstruction; the copies of
-        # neighbouring images overlap the kernels, up to DEPTH images are in flight
-        self.stream.submit(self.host[self.i % len(self.host)], bufs[self.i % len(bufs)])
+        # H2D of this batch from pinned memory, encode + render, D2H of its reconstructions; the copies of
+        # neighbouring batches overlap the kernels, up to DEPTH batches are in flight
+        self.stream.submit(self.host_batches[self.i % len(self.host_batches)], bufs[self.i % len(bufs)])
         self.i += 1
 
     def e2e_end(self):
         self.stream.wait_into()
 
     def io_bytes(self):
-        return 3 * self.H * self.W * 4, 3 * self.H * self.W * 4
+        return self.BATCH * 3 * self.H * self.W * 4, self.BATCH * 3 * self.H * self.W * 4
 
     @classmethod
     def describe(cls, wdesc):
@@ -311,14 +328,16 @@ class EncodeRenderWorkload:
 
     def config(self):
         return {**self.describe(self.wdesc),
-                "implementation": "bf16 tcgen05 encoder + fp32 render, one CUDA graph per image",
-                "images_in_flight": self.DEPTH,
-                "value_api": "pipeline.EncodeRenderStream.submit(device image): one graph replay per image, "
-                             f"{self.DEPTH} graph instances on their own streams; every card of this rank "
-                             "(64 x 7.1 MB at N=1) cycled, device-resident",
-                "e2e_api": "pipeline.EncodeRenderStream.submit(pinned host image, pinned host output): H2D -> "
-                           "encode+render graph -> D2H of the reconstruction, per image, "
-                           f"{self.DEPTH} images in flight, copies overlapped with the kernels",
+                "implementation": "bf16 tcgen05 encoder + fp32 render, one CUDA graph per batch",
+                "images_per_step_per_gpu": self.BATCH,
+                "images_in_flight": self.DEPTH * self.BATCH,
+                "value_api": f"pipeline.EncodeRenderStream.submit(device batch of {self.BATCH}): one graph replay "
+                             f"per batch, {self.DEPTH} graph instances on their own streams; every card of this "
+                             "rank (64 x 7.1 MB at N=1) cycled, device-resident",
+                "e2e_api": "pipeline.EncodeRenderStream.submit(pinned host batch, pinned host output): H2D -> "
+                           f"encode+render graph -> D2H of the reconstructions, per batch of {self.BATCH}, "
+                           f"{self.DEPTH} batches in flight, copies overlapped with the kernels",
+                "latency_api": "pipeline.EncodeRender (batch 1): one graph replay per image",
                 "l2": "inputs larger than L2 (the cycled cards, 453 MB at N=1) for value; the single-image "
                       "latency figure flushes L2 (256 MB write) between its timed steps"}
 
@@ -854,13 +873,38 @@ def reference_triton_leg(torch, dev, H=768, W=768, warmup=5, runs=30):
     b.record()
     torch.cuda.synchronize()
     b2b = a.elapsed_time(b) / runs
-    return {"images_per_s": 1000.0 / min(med, b2b), "images_per_s_per_image_events": 1000.0 / med,
-            "images_per_s_back_to_back": 1000.0 / b2b, "ms_median": med, "ms_p10": ms[len(ms) // 10],
+    # the same path on batches of EncodeRenderWorkload.BATCH cards (our throughput form's batch), back to
+    # back: its per-image cost when it, too, is given several images per call
+    nb = EncodeRenderWorkload.BATCH
+    xb = torch.stack([synth.synth_card(H, W, 500, 150, s)[0] for s in EncodeRenderWorkload.SEEDS[:nb]]).to(dev)
+
+    def batch():
+        with torch.no_grad():
+            o = enc(xb)
+            return ref_render(o["mu"], o["log_scale"], o["color"], o["opacity"], o["bg"], H, W, theta=o["theta"],
+                              odds=bool(getattr(enc, "odds", True)))
+
+    try:
+        for _ in range(2):
+            batch()
+        a.record()
+        for _ in range(max(1, runs // nb)):
+            batch()
+        b.record()
+        torch.cuda.synchronize()
+        bat = a.elapsed_time(b) / (max(1, runs // nb) * nb)
+    except Exception:  # noqa: BLE001  (a batch the reference does not take: single images only)
+        bat = float("inf")
+    return {"images_per_s": 1000.0 / min(med, b2b, bat), "images_per_s_per_image_events": 1000.0 / med,
+            "images_per_s_back_to_back": 1000.0 / b2b,
+            f"images_per_s_batch{nb}": (1000.0 / bat) if bat != float("inf") else None,
+            "ms_median": med, "ms_p10": ms[len(ms) // 10],
             "ms_p90": ms[(9 * len(ms)) // 10], "warmup": warmup, "runs": runs, "warmup_s_incl_jit": t_warm,
             "what": "unmodified reference (baseline/_ref/gaussian_splat_encoder): EfficientGaussianEncoder forward "
                     "(fp32 torch convs + its Triton 384^2 coarse render) + render_alpha_octave(odds=True) at 768^2, "
-                    "torch.no_grad, no L2 flush; images_per_s = the better of CUDA events per image (median) and "
-                    "the same calls back to back (its host synchronisations inside _build_tiles stay)",
+                    "torch.no_grad, no L2 flush; images_per_s = the best of CUDA events per image (median), the same "
+                    "calls back to back (its host synchronisations inside _build_tiles stay) and batches of "
+                    f"{nb} cards back to back",
             "encoder_weights": desc, "torch": torch.__version__, "triton": triton.__version__}
 
 
@@ -920,14 +964,21 @@ def main():
     ap.add_argument("--no-fit", action="store_true", help="skip the config-4 sub-object of the default line")
     ap.add_argument("--no-reference-triton", action="store_true",
                     help="skip timing the reference's own GPU path (default line, N = 1)")
+    ap.add_argument("--batch", type=int, default=EncodeRenderWorkload.BATCH,
+                    help="images per graph replay in the throughput and e2e forms")
     ap.add_argument("--depth", type=int, default=EncodeRenderWorkload.DEPTH,
-                    help="images in flight in the throughput (value) and e2e measurements of encode_render")
+                    help="batches in flight in the throughput (value) and e2e measurements of encode_render")
+    ap.add_argument("--batch-graph", action="store_true",
+                    help="with --kernels-only: replay the throughput form's batch graph (--batch images)")
     ap.add_argument("--kernels-only", action="store_true",
                     help="warm-up + K graph replays and nothing else (for ncu launch lists)")
     args = ap.parse_args()
     W = max(3, args.warmup)
     K = max(1, args.steps)
     EncodeRenderWorkload.DEPTH = max(1, args.depth)
+    EncodeRenderWorkload.BATCH = max(1, args.batch)
+    if args.kernels_only and args.batch_graph:
+        EncodeRenderWorkload.PIPE_BATCH = EncodeRenderWorkload.BATCH
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -1004,7 +1055,8 @@ def main():
             if pipelined:
                 barrier()
                 thr_ms = wl.time_pipelined(K, W)
-    launches = per_replay * K
+    # our kernels in the value's timed region (one replay per step of the pipelined graphs)
+    launches = (wl.stream.slots[0].launches_per_replay if pipelined else per_replay) * K
     lat_ms = max_over_ranks(sum(step_ms))
     # value: whole-job throughput (images in flight where the workload pipelines them), max over ranks
     tot_ms = max_over_ranks(thr_ms) if pipelined else lat_ms
@@ -1053,9 +1105,10 @@ def main():
                          "gpixel_pairs_per_s": ppairs / (pms * 1e-3) / 1e9}
     barrier()
 
-    images = K * world
+    ips = getattr(wl, "BATCH", 1)  # images per step of the throughput and e2e forms
+    images = K * world * (ips if pipelined else 1)
     value = images / (tot_ms / 1000.0)
-    e2e_val = Ke * world / (e2e_ms / 1000.0)
+    e2e_val = Ke * world * ips / (e2e_ms / 1000.0)
     h2d, d2h = wl.io_bytes()
     clocks = clk.summary()
     f_mhz = clocks["sm_mhz"] or 1965.0

@@ -561,6 +561,86 @@ __global__ void __launch_bounds__(256) k_upsample(const __nv_bfloat16 *__restric
     *reinterpret_cast<uint4 *>(up + (((long long)b * H4 + y) * W4 + x) * Cu + c0) = res;
 }
 
+// k_upsample for an exact 2x upsample (H4 = 2 H8, W4 = 2 W8), one thread per 2x2 output block of one
+// 8-channel vector: output rows 2p and 2p+1 read source rows p-1, p, p+1 (clamped) and likewise the
+// columns, so 9 vector loads serve 4 outputs and the horizontal blends of the middle source row serve both
+// output rows.  Even outputs take source slots (0, 1), odd ones (1, 2); at a border the clamped slot holds
+// the same row or column as its neighbour and the weight from lin_idx is 1/0 there, so every output is
+// the same torch bilinear (align_corners=False) value as k_upsample's.
+__global__ void __launch_bounds__(256) k_upsample2x(const __nv_bfloat16 *__restrict__ s8, int H8, int W8, int Cu,
+                                                    const float2 *__restrict__ gn_table,
+                                                    __nv_bfloat16 *__restrict__ up) {
+    const int nv = Cu / 8;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= W8 * nv) return;
+    const int p = blockIdx.y, b = blockIdx.z;
+    const int q = i / nv, c0 = (i - q * nv) * 8;
+    const int H4 = 2 * H8, W4 = 2 * W8;
+    // weights of output rows 2p, 2p+1 and columns 2q, 2q+1 (slots as above)
+    float hy[2][2], wx[2][2];
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        int i0, i1;
+        lin_idx(2 * p + t, H8, H4, i0, i1, hy[t][0], hy[t][1]);
+        lin_idx(2 * q + t, W8, W4, i0, i1, wx[t][0], wx[t][1]);
+    }
+    const __nv_bfloat16 *sb = s8 + (long long)b * H8 * W8 * Cu + c0;
+    uint4 v[3][3];
+#pragma unroll
+    for (int r = 0; r < 3; r++) {
+        const int yy = min(max(p - 1 + r, 0), H8 - 1);
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+            const int xx = min(max(q - 1 + c, 0), W8 - 1);
+            v[r][c] = __ldg(reinterpret_cast<const uint4 *>(sb + ((long long)yy * W8 + xx) * Cu));
+        }
+    }
+    float sc[8], sh[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        sc[k] = 1.f;
+        sh[k] = 0.f;
+    }
+    if (gn_table) {
+        const float4 *t = reinterpret_cast<const float4 *>(gn_table + (long long)b * Cu + c0);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float4 g = t[k];
+            sc[2 * k] = g.x;
+            sh[2 * k] = g.y;
+            sc[2 * k + 1] = g.z;
+            sh[2 * k + 1] = g.w;
+        }
+    }
+    uint4 res[2][2];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        float f[3][3];
+#pragma unroll
+        for (int r = 0; r < 3; r++)
+#pragma unroll
+            for (int c = 0; c < 3; c++) f[r][c] = __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(&v[r][c])[k]);
+        // horizontal blends of the three source rows at the two output columns
+        float hb[3][2];
+#pragma unroll
+        for (int r = 0; r < 3; r++)
+#pragma unroll
+            for (int t = 0; t < 2; t++) hb[r][t] = wx[t][0] * f[r][t] + wx[t][1] * f[r][t + 1];
+#pragma unroll
+        for (int ty = 0; ty < 2; ty++)
+#pragma unroll
+            for (int tx = 0; tx < 2; tx++) {
+                const float o = hy[ty][0] * hb[ty][tx] + hy[ty][1] * hb[ty + 1][tx];
+                reinterpret_cast<__nv_bfloat16 *>(&res[ty][tx])[k] = __float2bfloat16_rn(fmaf(o, sc[k], sh[k]));
+            }
+    }
+#pragma unroll
+    for (int ty = 0; ty < 2; ty++)
+#pragma unroll
+        for (int tx = 0; tx < 2; tx++)
+            *reinterpret_cast<uint4 *>(up + (((long long)b * H4 + 2 * p + ty) * W4 + 2 * q + tx) * Cu + c0) = res[ty][tx];
+}
+
 // per-channel GroupNorm(8) scale and shift, table[b][c] = (sc, sh) with normalised = raw * sc + sh
 __global__ void __launch_bounds__(256) k_gn_table(const double *__restrict__ stats, const float *__restrict__ gamma,
                                                   const float *__restrict__ beta, int C, long long HW,
@@ -831,9 +911,15 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     // 5. fine decoder: bilinear(s8) || s4 -> 3x3 conv 384->128 (+GELU, GN stats)
     {
         ProfScope ps(PR_ENC_MISC, s2);
-        dim3 ug((unsigned)((p.W4 * (256 / 8) + 255) / 256), (unsigned)p.H4, (unsigned)B);
-        k_upsample<<<ug, 256, 0, s2>>>(W<__nv_bfloat16>(ws, p.o_y3), p.H8, p.W8, 256, p.H4, p.W4,
-                                       gn3_fly ? gtab : nullptr, W<__nv_bfloat16>(ws, p.o_cat));
+        if (p.H4 == 2 * p.H8 && p.W4 == 2 * p.W8) {
+            dim3 ug((unsigned)((p.W8 * (256 / 8) + 255) / 256), (unsigned)p.H8, (unsigned)B);
+            k_upsample2x<<<ug, 256, 0, s2>>>(W<__nv_bfloat16>(ws, p.o_y3), p.H8, p.W8, 256, gn3_fly ? gtab : nullptr,
+                                             W<__nv_bfloat16>(ws, p.o_cat));
+        } else {
+            dim3 ug((unsigned)((p.W4 * (256 / 8) + 255) / 256), (unsigned)p.H4, (unsigned)B);
+            k_upsample<<<ug, 256, 0, s2>>>(W<__nv_bfloat16>(ws, p.o_y3), p.H8, p.W8, 256, p.H4, p.W4,
+                                           gn3_fly ? gtab : nullptr, W<__nv_bfloat16>(ws, p.o_cat));
+        }
     }
     memset(&cd, 0, sizeof(cd));
     cd.B = B; cd.H = p.H4; cd.W = p.W4; cd.Cin = 384; cd.Cout = 128; cd.kh = 3; cd.kw = 3; cd.stride = 1; cd.pad = 1;

@@ -967,6 +967,134 @@ __global__ void __launch_bounds__(128) k_composite(RenderGeom G, const float *__
     }
 }
 
+// One upsampled group's contribution at the four pixels x0..x0+3 of a row (x0 % 4 == 0) for an exact
+// 1/2^K column scale (W = Wg << K, K >= 1).  The pixels' column taps then fall in NC source columns, a fixed
+// pattern per K: K = 1 uses columns (2m-1 .. 2m+2) of x0 = 4m, taps at slots (0,1) (1,2) (1,2) (2,3);
+// K = 2 columns (m-1 .. m+1), slots (0,1) (0,1) (1,2) (1,2); K >= 3 the two taps of pixel x0 for all four.
+// Columns are loaded clamped to the plane, so at a border the slot holds the same column as its
+// neighbour while lin_index_s gives that pixel the weights (1, 0) or a tap pair with equal columns: every
+// pixel gets the value gather_sums computes (same taps, weights and operation order).
+template <int K>
+__device__ __forceinline__ void up_group4(const float *__restrict__ f, int plane, int Wg, float usx, int ra, int rb,
+                                          float h0, float h1, int x0, float (&S)[5][4]) {
+    constexpr int NC = K == 1 ? 4 : (K == 2 ? 3 : 2);
+    float w0[4], w1[4];
+    int first = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        int i0, i1;
+        lin_index_s(x0 + j, Wg, usx, i0, i1, w0[j], w1[j]);
+        if (j == 0) first = i0;
+    }
+    const int cl = K >= 3 ? first : (x0 >> K) - 1;
+    int col[NC];
+#pragma unroll
+    for (int s = 0; s < NC; s++) col[s] = min(max(cl + s, 0), Wg - 1);
+#pragma unroll
+    for (int c = 0; c < 5; c++) {
+        const float *fc = f + c * plane;
+        float top[NC], bot[NC];
+#pragma unroll
+        for (int s = 0; s < NC; s++) {
+            top[s] = __ldg(fc + ra + col[s]);
+            bot[s] = __ldg(fc + rb + col[s]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int s0 = K == 1 ? (j + 1) >> 1 : (K == 2 ? j >> 1 : 0);
+            S[c][j] += h0 * (w0[j] * top[s0] + w1[j] * top[s0 + 1]) + h1 * (w0[j] * bot[s0] + w1[j] * bot[s0 + 1]);
+        }
+    }
+}
+
+// k_composite with four neighbouring pixels of a row per thread (W % 4 == 0, output 16-byte aligned):
+// float4 loads of a native-resolution group's fields and float4 stores, exact power-of-two groups through
+// up_group4 (2-4 source columns per four pixels instead of 2 per pixel), others per pixel as gather_sums.
+// grid = (ceil(W / 256), band rows, B), 64 threads.
+__global__ void __launch_bounds__(64) k_composite4(RenderGeom G, const float *__restrict__ fields,
+                                                   const int *__restrict__ gsplats, const float *__restrict__ bg,
+                                                   float *__restrict__ out) {
+    const int b = blockIdx.z;
+    const int y = G.y0 + blockIdx.y;
+    const int x0 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (x0 >= G.W) return;
+    float S[5][4];
+#pragma unroll
+    for (int c = 0; c < 5; c++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) S[c][j] = 0.f;
+    const float *fimg = fields + (long long)b * G.fld_per_image;
+#pragma unroll 1
+    for (int k = 0; k < G.ngroups; k++) {
+        const int g = G.order[k];
+        if (gsplats[b * G.ngroups + g] == 0) continue;
+        const float *f = fimg + G.g[g].fld_off;
+        const int Hg = G.g[g].H, Wg = G.g[g].W;
+        const int plane = Hg * Wg;
+        if (Hg == G.H && Wg == G.W) {
+            const int p = y * Wg + x0;
+            if ((reinterpret_cast<uintptr_t>(f) & 15) == 0) {
+#pragma unroll
+                for (int c = 0; c < 5; c++) {
+                    const float4 v = __ldg(reinterpret_cast<const float4 *>(f + c * plane + p));
+                    S[c][0] += v.x;
+                    S[c][1] += v.y;
+                    S[c][2] += v.z;
+                    S[c][3] += v.w;
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 5; c++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++) S[c][j] += f[c * plane + p + j];
+            }
+            continue;
+        }
+        int y0, y1;
+        float h0, h1;
+        lin_index_s(y, Hg, G.g[g].up_sy, y0, y1, h0, h1);
+        const int ra = y0 * Wg, rb = y1 * Wg;
+        const float usx = G.g[g].up_sx;
+        if ((Wg << 1) == G.W) {
+            up_group4<1>(f, plane, Wg, usx, ra, rb, h0, h1, x0, S);
+        } else if ((Wg << 2) == G.W) {
+            up_group4<2>(f, plane, Wg, usx, ra, rb, h0, h1, x0, S);
+        } else if (Wg < G.W && (G.W % Wg) == 0 && __popc(G.W / Wg) == 1) {
+            up_group4<3>(f, plane, Wg, usx, ra, rb, h0, h1, x0, S);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                int xa, xb;
+                float w0, w1;
+                lin_index_s(x0 + j, Wg, usx, xa, xb, w0, w1);
+#pragma unroll
+                for (int c = 0; c < 5; c++) {
+                    const float *fc = f + c * plane;
+                    S[c][j] += h0 * (w0 * fc[ra + xa] + w1 * fc[ra + xb]) + h1 * (w0 * fc[rb + xa] + w1 * fc[rb + xb]);
+                }
+            }
+        }
+    }
+    float T[4], ra[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        ra[j] = 1.0f / fmaxf(S[1][j], 1e-8f);
+        T[j] = expf(S[0][j]);
+    }
+    const long long P = (long long)G.H * G.W;
+    float *ob = out + (long long)b * G.C * P + (long long)y * G.W + x0;
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+        if (c < G.C) {
+            const float bgc = bg[b * G.C + c];
+            float o[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) o[j] = (1.0f - T[j]) * (S[2 + c][j] * ra[j]) + T[j] * bgc;
+            *reinterpret_cast<float4 *>(ob + c * P) = make_float4(o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
 // fields of group g += the mapped prior group's fields (every group with prior_off >= 0, all images);
 // grid = (texel blocks, groups, images)
 __global__ void __launch_bounds__(256) k_add_prior(RenderGeom G, const float *__restrict__ prior,
@@ -2154,11 +2282,18 @@ int gs_render_fwd_prior(const gs_render_desc *d, const float *mu, const float *l
             GS_CHECK_LAUNCH("k_add_prior");
         }
     }
-    dim3 cg((unsigned)((d->W + 127) / 128), (unsigned)std::max(1, G.y1 - G.y0), (unsigned)d->B);
     if (G.y1 > G.y0) {
         ProfScope ps(PR_COMPOSITE, s);
-        k_composite<<<cg, 128, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,
-                                       out);
+        const unsigned rows = (unsigned)std::max(1, G.y1 - G.y0);
+        if (d->W % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+            dim3 cg((unsigned)((d->W / 4 + 63) / 64), rows, (unsigned)d->B);
+            k_composite4<<<cg, 64, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,
+                                           out);
+        } else {
+            dim3 cg((unsigned)((d->W + 127) / 128), rows, (unsigned)d->B);
+            k_composite<<<cg, 128, 0, s>>>(G, at<float>(workspace, pl.o_fields), at<int>(workspace, pl.o_gsplats), bg,
+                                           out);
+        }
         GS_CHECK_LAUNCH("k_composite");
     }
     return GS_OK;

@@ -7,8 +7,8 @@ into a CUDA graph and replay it: the same kernels, the same numerics, one launch
 
 * ``EncodeRender`` -- ``EfficientGaussianEncoder`` forward + ``render_alpha_octave`` of its splats
   (examples/encode_and_render.py:31-38 of the reference), inference.
-* ``EncodeRenderStream`` -- the same for a stream of images, several in flight at once on their own
-  streams, with the PCIe copies of neighbouring images overlapped with the kernels.
+* ``EncodeRenderStream`` -- the same for a stream of image batches, several in flight at once on their
+  own streams, with the PCIe copies of neighbouring batches overlapped with the kernels.
 * ``RenderFitStep`` -- ``render_alpha_octave`` forward + an L2 loss + the gradients of the six splat
   leaves (the fitting step of configs 1 and 4).
 
@@ -80,15 +80,17 @@ class EncodeRenderStream:
     """Throughput form of ``EncodeRender`` for a stream of host images (config 3's image batches).
 
     ``depth`` graph instances, each with its own input, workspace and output buffers and its own compute
-    stream, take images in turn: up to ``depth`` images are encoded and rendered at once (one image's
-    latency-bound kernel chains -- binning, the small convolutions -- leave most SMs idle, which the
-    neighbouring images fill), and the host-to-device copy of the next image and the device-to-host copy
-    of a finished reconstruction run on their own streams, so PCIe traffic hides behind the kernels.
-    ``submit(image, out)`` enqueues one image (pinned host or device [1,3,H,W]) and optionally its
-    destination (pinned host [1,3,H,W]); ``synchronize()`` waits for every submitted reconstruction."""
+    stream, take batches of ``batch`` images in turn: up to ``depth * batch`` images are encoded and
+    rendered at once (one image's latency-bound kernel chains -- binning, the small convolutions -- leave
+    most SMs idle; a batch gives every launch ``batch`` images' work and the neighbouring batches fill
+    what is left), and the host-to-device copy of the next batch and the device-to-host copy of a
+    finished reconstruction run on their own streams, so PCIe traffic hides behind the kernels.
+    ``submit(images, out)`` enqueues one batch (pinned host or device [batch,3,H,W]) and optionally its
+    destination (pinned host [batch,3,H,W]); ``synchronize()`` waits for every submitted reconstruction."""
 
-    def __init__(self, encoder, H: int, W: int, device=None, depth: int = 4):
-        self.slots = [EncodeRender(encoder, 1, H, W, device) for _ in range(depth)]
+    def __init__(self, encoder, H: int, W: int, device=None, depth: int = 4, batch: int = 1):
+        self.batch = batch
+        self.slots = [EncodeRender(encoder, batch, H, W, device) for _ in range(depth)]
         dev = self.slots[0].dev
         self.dev = dev
         self.h2d, self.d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
@@ -104,10 +106,10 @@ class EncodeRenderStream:
         return self
 
     def submit(self, image: torch.Tensor, out: torch.Tensor | None = None):
-        """Enqueue one image.  A host image (pinned) is copied in on the H2D stream; a device image is
-        copied into the slot's input buffer on the slot's own stream.  With `out` (pinned host) the
+        """Enqueue one batch of images.  A host batch (pinned) is copied in on the H2D stream; a device
+        batch is copied into the slot's input buffer on the slot's own stream.  With `out` (pinned host) the
         reconstruction is copied out on the D2H stream; without it, it stays in the slot's static buffer,
-        which is returned and stays valid until that slot's next image (``depth`` submits later)."""
+        which is returned and stays valid until that slot's next batch (``depth`` submits later)."""
         k = self.n % len(self.slots)
         slot = self.slots[k]
         if slot.graph is None:

@@ -82,6 +82,22 @@ def test_encode_render_stream_matches_single(lib):
     st.synchronize()
     for rec, r in zip(recs, refs):
         assert float((rec.cpu() - r).abs().max()) < REORDER_TOL
+    # batches of two images per graph replay (the bench's throughput form), host and device batches
+    sb = pipeline.EncodeRenderStream(enc, 256, 256, depth=2, batch=2).capture()
+    pairs = [torch.cat(imgs[i:i + 2]).pin_memory() for i in (0, 2)]
+    bouts = [torch.empty(2, 3, 256, 256).pin_memory() for _ in pairs]
+    sb.start_after()
+    for x, o in zip(pairs, bouts):
+        sb.submit(x, o)
+    sb.synchronize()
+    for j, o in enumerate(bouts):
+        for t in range(2):
+            assert float((o[t] - refs[2 * j + t][0]).abs().max()) < REORDER_TOL
+    sb.start_after()
+    rec = sb.submit(pairs[1].cuda())
+    sb.synchronize()
+    for t in range(2):
+        assert float((rec[t].cpu() - refs[2 + t][0]).abs().max()) < REORDER_TOL
 
 
 def test_render_fit_step_graph_matches_eager(lib):
