@@ -19,6 +19,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
 #include <stdio.h>
 
 #include <algorithm>
@@ -69,7 +71,7 @@ __device__ __forceinline__ float gelu_erf(float x) {
 //                 bias, GELU (gelu_erf), GroupNorm(8) partial sums, bf16 NHWC store
 // Every wait is bounded; a wait that gives up records its stage in *err and raises a CTA-wide abort
 // flag so the other roles stop issuing, then the CTA drains its copies and MMAs and frees TMEM.
-template <int BN, int KC, int STAGES, int MT, int CPG, int MINB, int CS>
+template <int BN, int KC, int STAGES, int MT, int CPG, int MINB, int CS, bool HALO>
 __global__ void __launch_bounds__(64 + 128 * MT * CS, MINB)
     k_conv_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
               const __grid_constant__ CUtensorMap tmB, ConvArgs a) {
@@ -87,10 +89,10 @@ __global__ void __launch_bounds__(64 + 128 * MT * CS, MINB)
     static_assert(CPG % 8 == 0 && (CPG >= 16 ? CPG % 16 == 0 : true), "GroupNorm channels per group");
     extern __shared__ uint8_t dsmem[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
-    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2], mdone;
+    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2], mdone, bfull;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;
-    __shared__ int issued, consumed;
+    __shared__ int issued, consumed, b_issued;
     __shared__ __align__(16) float sbias[256];
     __shared__ float sacc[NEPI][16];
 
@@ -114,9 +116,11 @@ __global__ void __launch_bounds__(64 + 128 * MT * CS, MINB)
             mbar_init(&tempty[j], NEPI);
         }
         mbar_init(&mdone, 1);
+        mbar_init(&bfull, 1);
         abort_flag = 0;
         issued = 0;
         consumed = 0;
+        b_issued = 0;
         fence_barrier_init();
         prefetch_tensormap(&tmA);
         if (a.nchunks1 < a.nchunks) prefetch_tensormap(&tmA2);
@@ -127,7 +131,81 @@ __global__ void __launch_bounds__(64 + 128 * MT * CS, MINB)
     tc_fence_after();
     const uint32_t tbase = tmem_base;
 
-    if (warp == 0) {
+    // halo form: [weights, hbreg bytes][STAGES windows of KC/8 slices]
+    uint8_t *const hwin = smem + a.hbreg;
+    const uint32_t hstage = (uint32_t)(KC / 8) * (uint32_t)a.hslice;
+    if (HALO && warp == 0) {
+        if (lane == 0) {
+            // every (tap, 8-channel slice) of the BN weight rows once: [tap][slice][BN rows][16 B]
+            mbar_arrive_expect_tx(&bfull, (uint32_t)a.hbreg);
+            const int ntap = a.KH * a.KW;
+            for (int t = 0; t < ntap; t++)
+#pragma unroll
+                for (int sl = 0; sl < KC / 8; sl++)
+                    tma_load_2d(smem + (t * (KC / 8) + sl) * BN * 16, &tmB, &bfull, t * KC + sl * 8, 0);
+            b_issued = 1;
+            int it = 0;
+            for (int item = blockIdx.x; item < n_items && !abort_flag; item += gridDim.x, it++) {
+                int t = item;
+                t /= nsplit;
+                const int tx = t % a.tiles_x;
+                t /= a.tiles_x;
+                const int ty = t % a.tiles_y;
+                const int b = t / a.tiles_y;
+                const int x0 = tx * a.TX, y0 = ty * MT;  // TX = 128, TY = 1
+                const int s = it % STAGES;
+                if (it >= STAGES && !mbar_wait_or_abort(&empty[s], ((it / STAGES) - 1) & 1, &abort_flag, a.err, 1))
+                    break;
+                if (abort_flag) break;
+                // (the boxes' bytes: the slices are padded to 128-byte multiples in shared memory only)
+                mbar_arrive_expect_tx(&full[s], (uint32_t)(KC / 8) * 16u * (uint32_t)(a.hcols * a.hrows));
+#pragma unroll
+                for (int sl = 0; sl < KC / 8; sl++)
+                    tma_load_4d(hwin + s * hstage + sl * a.hslice, &tmA, &full[s], sl * 8, x0 - a.padw, y0 - a.pad, b);
+                issued = it + 1;
+            }
+        }
+    } else if (HALO && warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16_f32(128, BN);
+            const uint32_t sbw = smem_u32(smem), sw0 = smem_u32(hwin);
+            const uint32_t rowb = (uint32_t)a.hcols * 16u;
+            bool ok = mbar_wait_or_abort(&bfull, 0, &abort_flag, a.err, 7);
+            int it = 0, tc = 0;
+            for (int item = blockIdx.x; ok && item < n_items && !abort_flag; item += gridDim.x, tc++, it++) {
+                const int buf = tc & 1;
+                if (tc >= 2 && !mbar_wait_or_abort(&tempty[buf], ((tc >> 1) - 1) & 1, &abort_flag, a.err, 2)) break;
+                tc_fence_after();
+                const uint32_t dcol = tbase + (uint32_t)buf * ACC;
+                const int s = it % STAGES;
+                if (!mbar_wait_or_abort(&full[s], (it / STAGES) & 1, &abort_flag, a.err, 3)) break;
+                tc_fence_after();
+                const uint32_t win = sw0 + (uint32_t)s * hstage;
+                // tap (kh, kw) of output row mt: the window from row mt + kh, column kw (a 16-byte offset per
+                // pixel in the unswizzled layout); K = 16 per instruction = two 8-channel slices (LBO apart)
+                for (int kh = 0; kh < a.KH; kh++)
+                    for (int kw = 0; kw < a.KW; kw++) {
+                        const uint32_t tap = (uint32_t)(kh * a.KW + kw);
+#pragma unroll
+                        for (int k = 0; k < KC / 16; k++) {
+                            const uint64_t bd = sdesc_ns(sbw + (tap * (KC / 8) + 2 * k) * BN * 16, BN * 16, 128);
+#pragma unroll
+                            for (int mt = 0; mt < MT; mt++) {
+                                const uint32_t aa = win + 2u * k * (uint32_t)a.hslice + (uint32_t)(mt + kh) * rowb +
+                                                    (uint32_t)kw * 16u;
+                                mma_bf16(dcol + (uint32_t)(mt * BN), sdesc_ns(aa, (uint32_t)a.hslice, 128), bd, idesc,
+                                         (tap | k) != 0 ? 1u : 0u);
+                            }
+                        }
+                    }
+                mma_commit(&empty[s]);
+                consumed = it + 1;
+                mma_commit(&tfull[buf]);
+            }
+            mma_commit(&mdone);
+            mbar_wait(&mdone, 0, a.err, 4);
+        }
+    } else if (warp == 0) {
         if (lane == 0) {
             int it = 0;
             for (int item = blockIdx.x; item < n_items && !abort_flag; item += gridDim.x) {
@@ -344,6 +422,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * CS, MINB)
     if (abort_flag && threadIdx.x == 0) {
         // copies that were issued but never consumed still land in shared memory: wait for them
         for (int j = consumed; j < issued; j++) mbar_wait(&full[j % STAGES], (j / STAGES) & 1, a.err, 6);
+        if (HALO && b_issued) mbar_wait(&bfull, 0, a.err, 8);
     }
     __syncthreads();
     tc_fence_after();
@@ -387,15 +466,16 @@ int sm_count() {
     return n[dev];
 }
 
-template <int BN, int KC, int STAGES, int MT, int CPG, int MINB, int CS>
+template <int BN, int KC, int STAGES, int MT, int CPG, int MINB, int CS, bool HALO = false>
 int launch(const CUtensorMap &tA, const CUtensorMap &tA2, const CUtensorMap &tB, const ConvArgs &a,
            cudaStream_t st) {
-    constexpr size_t SMEM = (size_t)STAGES * (MT * 128 * KC * 2 + BN * KC * 2) + 1024;
-    auto kern = k_conv_tc<BN, KC, STAGES, MT, CPG, MINB, CS>;
-    static bool configured = false;
-    if (!configured) {
+    const size_t SMEM = HALO ? (size_t)a.hbreg + (size_t)STAGES * (KC / 8) * a.hslice + 1024
+                             : (size_t)STAGES * (MT * 128 * KC * 2 + BN * KC * 2) + 1024;
+    auto kern = k_conv_tc<BN, KC, STAGES, MT, CPG, MINB, CS, HALO>;
+    static size_t configured = 0;
+    if (configured < SMEM) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
-        configured = true;
+        configured = SMEM;
     }
     const long long items = (long long)a.B * a.tiles_y * a.tiles_x * (a.Co / BN);
     const long long slots = (long long)sm_count() * MINB;
@@ -449,6 +529,7 @@ int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in
     const int MT = (KC == 64 && Co >= 128) ? 1 : 2;
     const int BN = Co == 256 ? 64 : Co;
     ConvArgs a;
+    memset(&a, 0, sizeof(a));
     a.B = B; a.Hi = Hi; a.Wi = Wi; a.Ci = Ci; a.Co = Co;
     a.KH = d->kh; a.KW = d->kw; a.stride = d->stride; a.pad = d->pad; a.padw = padw >= 0 ? padw : d->pad;
     a.Ho = d->Ho > 0 ? d->Ho : (Hi + 2 * d->pad - d->kh) / d->stride + 1;
@@ -496,6 +577,28 @@ int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in
         s = make_map(&tB, w, 2, dims, str, box, swz);
     }
     if (s != GS_OK) return s;
+    // halo form for the stride-1 layer on one 16-channel chunk (the first convolution): one window per item
+    // (MT + KH - 1 rows x 128 + KW - 1 pixels, two 8-channel slices, unswizzled) serves all KH x KW taps,
+    // and the layer's weights stay in shared memory for the CTA's whole life: 2 TMA copies per item
+    // instead of 3 per tap
+    const char *hv = getenv("GS_CONV_HALO");
+    if (KC == 16 && d->stride == 1 && Ci == KC && Ci2 == 0 && a.TX == 128 && a.TY == 1 && BN == Co && MT == 2 &&
+        d->kw <= 129 && MT + d->kh - 1 <= 256 && !(hv && hv[0] == '0')) {
+        a.hcols = 128 + d->kw - 1;
+        a.hrows = MT + d->kh - 1;
+        a.hslice = (16 * a.hcols * a.hrows + 127) & ~127;
+        a.hbreg = d->kh * d->kw * (KC / 8) * BN * 16;
+        CUtensorMap hA, hB;
+        uint64_t dims[4] = {(uint64_t)Ci, (uint64_t)Wi, (uint64_t)Hi, (uint64_t)B};
+        uint64_t str[3] = {(uint64_t)Ci * 2, (uint64_t)Wi * Ci * 2, (uint64_t)Hi * Wi * Ci * 2};
+        uint32_t box[4] = {8, (uint32_t)a.hcols, (uint32_t)a.hrows, 1};
+        if ((s = make_map(&hA, in, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)) != GS_OK) return s;
+        uint64_t wd[2] = {(uint64_t)K, (uint64_t)Co};
+        uint64_t ws[1] = {(uint64_t)K * 2};
+        uint32_t wb[2] = {8, (uint32_t)BN};
+        if ((s = make_map(&hB, w, 2, wd, ws, wb, CU_TENSOR_MAP_SWIZZLE_NONE)) != GS_OK) return s;
+        return launch<64, 16, 3, 2, 8, 2, 1, true>(hA, hA, hB, a, st);
+    }
     // one column slice per accumulator: doubling the epilogue warps (CS = 2) measured slower on B200
     if (KC == 16) return launch<64, 16, 8, 2, 8, 2, 1>(tA, tA2, tB, a, st);
     if (Co == 64) return launch<64, 64, 5, 2, 8, 1, 1>(tA, tA2, tB, a, st);

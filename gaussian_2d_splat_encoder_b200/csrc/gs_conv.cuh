@@ -18,6 +18,9 @@ struct ConvArgs {
     __nv_bfloat16 *out;
     double *stats;  // [B][8][2] GroupNorm partial sums (sum, sum of squares), accumulated
     int *err;       // set to a non-zero stage code when a bounded wait gives up
+    // halo form (stride 1, one input-channel chunk): per item one window of hrows x hcols pixels per 8-channel
+    // slice (hslice bytes apart), every tap an offset view of it; hbreg bytes of weights loaded once per CTA
+    int hrows, hcols, hslice, hbreg;
 };
 
 void gs_conv_pick_tile(int Ho, int Wo, int MT, int *TX, int *TY);

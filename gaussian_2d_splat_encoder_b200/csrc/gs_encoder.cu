@@ -54,31 +54,44 @@ __device__ __forceinline__ float lin_center(int i, int n) {
     return i < n / 2 ? start + step * (float)i : end - step * (float)(n - 1 - i);
 }
 
-__device__ __forceinline__ float gray_at(const float *img, int H, int W, int y, int x) {
-    if (y < 0 || y >= H || x < 0 || x >= W) return 0.0f;
-    long long P = (long long)H * W, p = (long long)y * W + x;
-    return (img[p] + img[P + p] + img[2 * P + p]) / 3.0f;
-}
-
 // grad [B][H][W] fp32 and the space-to-depth bf16 input Z[B][H/2][W/2][16],
 // Z[p][q][(dy*2+dx)*4 + c] = X[2p+dy][2q+dx][c], X = (R, G, B, grad).
+// A block = 32 x 8 Z cells (64 x 16 pixels) of one image (grid = (ceil(W/64), ceil(H/16), B)): the grey
+// values of the tile and its one-pixel halo (zero outside the image, the convolution's padding) are
+// computed once into shared memory, then each thread takes the 4x4 grey neighbourhood of its 2x2 pixels.
+#define PREP_TX 32
+#define PREP_TY 8
 __global__ void __launch_bounds__(256) k_prep(const float *__restrict__ image, int B, int H, int W,
                                               float *__restrict__ grad, __nv_bfloat16 *__restrict__ Z) {
+    constexpr int GW = 2 * PREP_TX + 2, GH = 2 * PREP_TY + 2;
+    __shared__ float gs[GH][GW + 1];
+    const int b = blockIdx.z;
     const int Hz = H / 2, Wz = W / 2;
-    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long long)B * Hz * Wz) return;
-    int b = (int)(i / ((long long)Hz * Wz));
-    int r = (int)(i - (long long)b * Hz * Wz);
-    int p = r / Wz, q = r - p * Wz;
     const float *img = image + (long long)b * 3 * H * W;
     const long long P = (long long)H * W;
-    // 4x4 grey neighbourhood of the 2x2 block
+    const int y0 = 2 * PREP_TY * blockIdx.y - 1, x0 = 2 * PREP_TX * blockIdx.x - 1;
+    for (int k = threadIdx.x; k < GH * GW; k += blockDim.x) {
+        const int a = k / GW, c = k - a * GW;
+        const int y = y0 + a, x = x0 + c;
+        float v = 0.0f;
+        if (y >= 0 && y < H && x >= 0 && x < W) {
+            const long long pp = (long long)y * W + x;
+            v = (img[pp] + img[P + pp] + img[2 * P + pp]) / 3.0f;
+        }
+        gs[a][c] = v;
+    }
+    __syncthreads();
+    const int tx = threadIdx.x % PREP_TX, ty = threadIdx.x / PREP_TX;
+    const int q = blockIdx.x * PREP_TX + tx, p = blockIdx.y * PREP_TY + ty;
+    if (p >= Hz || q >= Wz) return;
+    // 4x4 grey neighbourhood of the 2x2 block: rows 2p-1 .. 2p+2, columns 2q-1 .. 2q+2
     float g[4][4];
 #pragma unroll
     for (int a = 0; a < 4; a++)
 #pragma unroll
-        for (int c = 0; c < 4; c++) g[a][c] = gray_at(img, H, W, 2 * p - 1 + a, 2 * q - 1 + c);
+        for (int c = 0; c < 4; c++) g[a][c] = gs[2 * ty + a][2 * tx + c];
     __align__(16) __nv_bfloat16 z[16];
+    float gmv[2][2];
 #pragma unroll
     for (int dy = 0; dy < 2; dy++)
 #pragma unroll
@@ -94,17 +107,20 @@ __global__ void __launch_bounds__(256) k_prep(const float *__restrict__ image, i
                     gx += (k[u][v] / 4.0f) * gv;
                     gy += (k[v][u] / 4.0f) * gv;
                 }
-            float gm = sqrtf(gx * gx + gy * gy + 1e-6f);
-            int y = 2 * p + dy, x = 2 * q + dx;
-            grad[(long long)b * P + (long long)y * W + x] = gm;
-            int base = (dy * 2 + dx) * 4;
-            long long pp = (long long)y * W + x;
+            const float gm = sqrtf(gx * gx + gy * gy + 1e-6f);
+            gmv[dy][dx] = gm;
+            const long long pp = (long long)(2 * p + dy) * W + 2 * q + dx;
+            const int base = (dy * 2 + dx) * 4;
             z[base + 0] = __float2bfloat16_rn(img[pp]);
             z[base + 1] = __float2bfloat16_rn(img[P + pp]);
             z[base + 2] = __float2bfloat16_rn(img[2 * P + pp]);
             z[base + 3] = __float2bfloat16_rn(gm);
         }
-    uint4 *dst = reinterpret_cast<uint4 *>(Z + i * 16);
+#pragma unroll
+    for (int dy = 0; dy < 2; dy++)
+        *reinterpret_cast<float2 *>(grad + (long long)b * P + (long long)(2 * p + dy) * W + 2 * q) =
+            make_float2(gmv[dy][0], gmv[dy][1]);
+    uint4 *dst = reinterpret_cast<uint4 *>(Z + (((long long)b * Hz + p) * Wz + q) * 16);
     dst[0] = reinterpret_cast<uint4 *>(z)[0];
     dst[1] = reinterpret_cast<uint4 *>(z)[1];
 }
@@ -286,6 +302,9 @@ __global__ void __launch_bounds__(1024) k_bg(const float *__restrict__ chsum, in
 
 #define GN_BG_BLOCKS 128  // blocks of the GroupNorm launch that also sums channels for the background head
 
+#define HEAD_NP 20     // head outputs (9 per splat, 2 splats per cell) padded to a multiple of 4
+#define HEAD_CELLS 32  // cells per warp of k_head
+
 struct HeadArgs {
     int B, fH, fW, M;          // grid and splats per cell
     int Cfeat;                 // feature channels read from `feat` (NHWC bf16)
@@ -303,7 +322,86 @@ struct HeadArgs {
     int Ntot, n0;
     float *mu, *ls, *col, *op, *th;
     float *cmu, *cls, *ccol, *cop, *cth;  // contiguous [B][fH*fW*M] copies (coarse render input)
+    // k_head_tc operands (k_head_prep): B fragments and bias' per image, the extra channels' weights
+    const uint4 *frag;
+    const float *fbias, *wext;
 };
+
+// acc += the extra input channels of a head: the pooled gradient (channel Cfeat) and, for the fine
+// head, the bilinear-sampled cond map (Cfeat+1..+4); wext = their weights, [Cin - Cfeat][HEAD_NP]
+__device__ __forceinline__ void head_extra(const HeadArgs &a, const float *wext, long long cell, int b, int y, int x,
+                                           float (&acc)[HEAD_NP]) {
+    auto fma_row = [&](int e, float v) {
+        const float4 *wc = reinterpret_cast<const float4 *>(wext + e * HEAD_NP);
+#pragma unroll
+        for (int q = 0; q < HEAD_NP / 4; q++) {
+            const float4 w4 = wc[q];
+            acc[4 * q + 0] = fmaf(w4.x, v, acc[4 * q + 0]);
+            acc[4 * q + 1] = fmaf(w4.y, v, acc[4 * q + 1]);
+            acc[4 * q + 2] = fmaf(w4.z, v, acc[4 * q + 2]);
+            acc[4 * q + 3] = fmaf(w4.w, v, acc[4 * q + 3]);
+        }
+    };
+    fma_row(0, a.gpool[cell]);
+    if (a.cond) {
+        int y0, y1, x0, x1;
+        float h0, h1, w0, w1;
+        lin_idx(y, a.rg, a.fH, y0, y1, h0, h1);
+        lin_idx(x, a.rg, a.fW, x0, x1, w0, w1);
+        const float *cb = a.cond + (long long)b * a.rg * a.rg * 4;
+        const float4 c00 = *reinterpret_cast<const float4 *>(cb + ((long long)y0 * a.rg + x0) * 4);
+        const float4 c01 = *reinterpret_cast<const float4 *>(cb + ((long long)y0 * a.rg + x1) * 4);
+        const float4 c10 = *reinterpret_cast<const float4 *>(cb + ((long long)y1 * a.rg + x0) * 4);
+        const float4 c11 = *reinterpret_cast<const float4 *>(cb + ((long long)y1 * a.rg + x1) * 4);
+        fma_row(1, h0 * (w0 * c00.x + w1 * c01.x) + h1 * (w0 * c10.x + w1 * c11.x));
+        fma_row(2, h0 * (w0 * c00.y + w1 * c01.y) + h1 * (w0 * c10.y + w1 * c11.y));
+        fma_row(3, h0 * (w0 * c00.z + w1 * c01.z) + h1 * (w0 * c10.z + w1 * c11.z));
+        fma_row(4, h0 * (w0 * c00.w + w1 * c01.w) + h1 * (w0 * c10.w + w1 * c11.w));
+    }
+}
+
+// activations and stores of cell (b, r = y * fW + x) of a head (efficient_encoder.py:170-197): the splat
+// slots m with m % NFIN == part.  Channel layout of acc: (m, component) per parameter block.
+// M (splats per cell) is a template parameter so every acc[] index is static and acc stays in registers.
+template <int M, int NFIN>
+__device__ __forceinline__ void head_activate(const HeadArgs &a, int part, int b, int r, int y, int x,
+                                              const float (&acc)[HEAD_NP]) {
+    const float by = lin_center(y, a.fH), bx = lin_center(x, a.fW);
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+        if (m % NFIN != part) continue;
+        const long long nl = (long long)r * M + m;  // splat index inside the group (cell-major, then slot)
+        const long long n = (long long)b * a.Ntot + a.n0 + nl;
+        float muy = by + tanhf(acc[m * 2 + 0]) * a.off_scale;
+        float mux = bx + tanhf(acc[m * 2 + 1]) * a.off_scale;
+        muy = fminf(fmaxf(muy, 0.005f), 0.995f);
+        mux = fminf(fmaxf(mux, 0.005f), 0.995f);
+        float ly = acc[2 * M + m * 2 + 0], lx = acc[2 * M + m * 2 + 1];
+        ly = fmaxf(ly, a.ls_floor);
+        lx = fmaxf(lx, a.ls_floor);
+        float cc[3];
+#pragma unroll
+        for (int c = 0; c < 3; c++) cc[c] = 1.0f / (1.0f + expf(-acc[4 * M + m * 3 + c]));
+        float o = 1.0f / (1.0f + expf(-acc[7 * M + m]));
+        if (a.min_op > 0.f) o = a.min_op + (1.0f - a.min_op) * o;
+        float t = a.use_rot ? tanhf(acc[8 * M + m]) * 1.5707963267948966f : 0.f;
+        a.mu[n * 2] = muy; a.mu[n * 2 + 1] = mux;
+        a.ls[n * 2] = ly; a.ls[n * 2 + 1] = lx;
+#pragma unroll
+        for (int c = 0; c < 3; c++) a.col[n * 3 + c] = cc[c];
+        a.op[n] = o;
+        if (a.use_rot && a.th) a.th[n] = t;
+        if (a.cmu) {
+            const long long q = (long long)b * a.fH * a.fW * M + nl;
+            a.cmu[q * 2] = muy; a.cmu[q * 2 + 1] = mux;
+            a.cls[q * 2] = ly; a.cls[q * 2 + 1] = lx;
+#pragma unroll
+            for (int c = 0; c < 3; c++) a.ccol[q * 3 + c] = cc[c];
+            a.cop[q] = o;
+            if (a.cth) a.cth[q] = t;
+        }
+    }
+}
 
 // 1x1 convolution of the head + activations (efficient_encoder.py:170-197).  A block takes HEAD_CELLS
 // feature cells (lane = cell) and PARTS warps, each warp accumulating its slice of the feature channels;
@@ -313,8 +411,6 @@ struct HeadArgs {
 // one staging of the weights and GroupNorm table) suits many cells; a channel split (PARTS = 4) gives
 // small grids enough warps.  Weights sit transposed in shared memory, [Cin][20] (18 outputs padded to
 // 20), so one input channel is 5 broadcast 16-byte loads for 18 FMAs.
-#define HEAD_NP 20
-#define HEAD_CELLS 32
 template <int M, int PARTS, int WPB = 1>
 __global__ void __launch_bounds__(32 * PARTS * WPB) k_head(HeadArgs a) {
     static_assert(PARTS == 1 || WPB == 1, "a channel split works on one group of 32 cells");
@@ -427,68 +523,177 @@ __global__ void __launch_bounds__(32 * PARTS * WPB) k_head(HeadArgs a) {
     const int b = (int)(cell / ((long long)a.fH * a.fW));
     const int r = (int)(cell - (long long)b * a.fH * a.fW);
     const int y = r / a.fW, x = r - y * a.fW;
-    fma_channel(a.Cfeat, a.gpool[cell]);
-    if (a.cond) {
-        int y0, y1, x0, x1;
-        float h0, h1, w0, w1;
-        lin_idx(y, a.rg, a.fH, y0, y1, h0, h1);
-        lin_idx(x, a.rg, a.fW, x0, x1, w0, w1);
-        const float *cb = a.cond + (long long)b * a.rg * a.rg * 4;
-        const float4 c00 = *reinterpret_cast<const float4 *>(cb + ((long long)y0 * a.rg + x0) * 4);
-        const float4 c01 = *reinterpret_cast<const float4 *>(cb + ((long long)y0 * a.rg + x1) * 4);
-        const float4 c10 = *reinterpret_cast<const float4 *>(cb + ((long long)y1 * a.rg + x0) * 4);
-        const float4 c11 = *reinterpret_cast<const float4 *>(cb + ((long long)y1 * a.rg + x1) * 4);
-        fma_channel(a.Cfeat + 1, h0 * (w0 * c00.x + w1 * c01.x) + h1 * (w0 * c10.x + w1 * c11.x));
-        fma_channel(a.Cfeat + 2, h0 * (w0 * c00.y + w1 * c01.y) + h1 * (w0 * c10.y + w1 * c11.y));
-        fma_channel(a.Cfeat + 3, h0 * (w0 * c00.z + w1 * c01.z) + h1 * (w0 * c10.z + w1 * c11.z));
-        fma_channel(a.Cfeat + 4, h0 * (w0 * c00.w + w1 * c01.w) + h1 * (w0 * c10.w + w1 * c11.w));
+    head_extra(a, wT + a.Cfeat * HEAD_NP, cell, b, y, x, acc);
+    head_activate<M, NFIN>(a, part, b, r, y, x, acc);
+}
+
+// ---- the heads on the tensor cores ----
+// The head is a [cells x Cfeat] x [Cfeat x 18] contraction: far too narrow (N = 18) for a tcgen05 tile, and
+// bound by reading its bf16 features, so it runs on the warp-level mma.sync (m16n8k16, bf16 in, fp32
+// accumulate).  The features are exact bf16 operands; GroupNorm folds into the weights of the block's
+// image, w'[o][c] = w[o][c] * sc[c] and bias'[o] = b[o] + sum_c w[o][c] * sh[c], and w' enters as three bf16
+// terms (hi + mid + lo, together exact to ~2^-24 of |w'|), so the products match fp32 arithmetic.
+__device__ __forceinline__ void mma_16816_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void split3_bf16(float w, __nv_bfloat16 &h, __nv_bfloat16 &m, __nv_bfloat16 &l) {
+    h = __float2bfloat16_rn(w);
+    float r = w - __bfloat162float(h);  // exact
+    m = __float2bfloat16_rn(r);
+    r -= __bfloat162float(m);           // exact
+    l = __float2bfloat16_rn(r);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(__nv_bfloat16 lo, __nv_bfloat16 hi) {
+    return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
+
+// Per-image operands of k_head_tc, written by k_head_prep: the B fragments
+// frag[b][Cfeat/32 chunks][3 terms][3 n-tiles][32 lanes] (16 bytes: lane (g, t) holds outputs 8j + g at
+// channels 32 chunk + 8t .. +8 of one term) and bias'[b][24].
+size_t head_frag_bytes(int Cfeat) { return (size_t)(Cfeat / 32) * 9 * 32 * 16; }
+
+// grid = (ceil(Cfeat/32 * 96 / 128), B): one (chunk, n-tile, lane) item per thread; block x = 0 also sums
+// bias' (one warp per output: lane-strided sums, then a fixed xor tree).  The GroupNorm scale/shift are the
+// ones k_head applies on the fly (same float/double arithmetic).
+__global__ void __launch_bounds__(128) k_head_prep(HeadArgs a, uint4 *__restrict__ frag, float *__restrict__ fbias,
+                                                   float *__restrict__ wext) {
+    __shared__ double gmean[8];
+    __shared__ float grstd[8];
+    const int b = blockIdx.y;
+    const int nch = a.Cfeat / 32, cpg = a.Cfeat / 8;
+    if (threadIdx.x < 8 && a.gn_stats) {
+        const double n = (double)a.fH * a.fW * cpg;
+        const double mean = a.gn_stats[(b * 8 + threadIdx.x) * 2] / n;
+        double var = a.gn_stats[(b * 8 + threadIdx.x) * 2 + 1] / n - mean * mean;
+        if (var < 0) var = 0;
+        gmean[threadIdx.x] = mean;
+        grstd[threadIdx.x] = (float)(1.0 / sqrt(var + 1e-5));
     }
-    // activations; channel layout of each head: (m, component)
-    // M (splats per cell) is a template parameter so every acc[] index is static and acc stays in registers
-    const float by = lin_center(y, a.fH), bx = lin_center(x, a.fW);
+    __syncthreads();
+    auto scale = [&](int c) { return a.gn_stats ? a.gn_gamma[c] * grstd[c / cpg] : 1.f; };
+    auto shift = [&](int c) {
+        return a.gn_stats ? a.gn_beta[c] - (float)gmean[c / cpg] * a.gn_gamma[c] * grstd[c / cpg] : 0.f;
+    };
+    const int it = blockIdx.x * blockDim.x + threadIdx.x;
+    if (it < nch * 96) {
+        const int ln = it & 31, j = (it >> 5) % 3, ch = it / 96;
+        const int o = 8 * j + (ln >> 2), c0 = ch * 32 + 8 * (ln & 3);
+        uint32_t hv[4], mv[4], lv[4];
 #pragma unroll
-    for (int m = 0; m < M; m++) {
-        if (m % NFIN != part) continue;
-        const long long nl = (long long)r * M + m;  // splat index inside the group (cell-major, then slot)
-        const long long n = (long long)b * a.Ntot + a.n0 + nl;
-        float muy = by + tanhf(acc[m * 2 + 0]) * a.off_scale;
-        float mux = bx + tanhf(acc[m * 2 + 1]) * a.off_scale;
-        muy = fminf(fmaxf(muy, 0.005f), 0.995f);
-        mux = fminf(fmaxf(mux, 0.005f), 0.995f);
-        float ly = acc[2 * M + m * 2 + 0], lx = acc[2 * M + m * 2 + 1];
-        ly = fmaxf(ly, a.ls_floor);
-        lx = fmaxf(lx, a.ls_floor);
-        float cc[3];
+        for (int e = 0; e < 8; e += 2) {
+            float w0 = 0.f, w1 = 0.f;
+            if (o < a.nout) {
+                w0 = __ldg(a.w + o * a.Cin + c0 + e) * scale(c0 + e);
+                w1 = __ldg(a.w + o * a.Cin + c0 + e + 1) * scale(c0 + e + 1);
+            }
+            __nv_bfloat16 h0, m0, l0, h1, m1, l1;
+            split3_bf16(w0, h0, m0, l0);
+            split3_bf16(w1, h1, m1, l1);
+            hv[e >> 1] = pack_bf16(h0, h1);
+            mv[e >> 1] = pack_bf16(m0, m1);
+            lv[e >> 1] = pack_bf16(l0, l1);
+        }
+        uint4 *fr = frag + (size_t)b * nch * 9 * 32;
+        fr[(ch * 9 + 0 + j) * 32 + ln] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        fr[(ch * 9 + 3 + j) * 32 + ln] = make_uint4(mv[0], mv[1], mv[2], mv[3]);
+        fr[(ch * 9 + 6 + j) * 32 + ln] = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    }
+    if (blockIdx.x == 0) {
+        if (b == 0)  // the extra channels' weights, [Cin - Cfeat][HEAD_NP]
+            for (int i = threadIdx.x; i < (a.Cin - a.Cfeat) * HEAD_NP; i += blockDim.x) {
+                const int e = i / HEAD_NP, o = i - e * HEAD_NP;
+                wext[i] = o < a.nout ? __ldg(a.w + o * a.Cin + a.Cfeat + e) : 0.f;
+            }
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int o = warp; o < 24; o += 4) {
+            float sum = 0.f;
+            if (o < a.nout)
+                for (int c = lane; c < a.Cfeat; c += 32) sum = fmaf(__ldg(a.w + o * a.Cin + c), shift(c), sum);
 #pragma unroll
-        for (int c = 0; c < 3; c++) cc[c] = 1.0f / (1.0f + expf(-acc[4 * M + m * 3 + c]));
-        float o = 1.0f / (1.0f + expf(-acc[7 * M + m]));
-        if (a.min_op > 0.f) o = a.min_op + (1.0f - a.min_op) * o;
-        float t = a.use_rot ? tanhf(acc[8 * M + m]) * 1.5707963267948966f : 0.f;
-        a.mu[n * 2] = muy; a.mu[n * 2 + 1] = mux;
-        a.ls[n * 2] = ly; a.ls[n * 2 + 1] = lx;
-#pragma unroll
-        for (int c = 0; c < 3; c++) a.col[n * 3 + c] = cc[c];
-        a.op[n] = o;
-        if (a.use_rot && a.th) a.th[n] = t;
-        if (a.cmu) {
-            const long long q = (long long)b * a.fH * a.fW * M + nl;
-            a.cmu[q * 2] = muy; a.cmu[q * 2 + 1] = mux;
-            a.cls[q * 2] = ly; a.cls[q * 2 + 1] = lx;
-#pragma unroll
-            for (int c = 0; c < 3; c++) a.ccol[q * 3 + c] = cc[c];
-            a.cop[q] = o;
-            if (a.cth) a.cth[q] = t;
+            for (int k = 16; k > 0; k >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, k);
+            if (lane == 0) fbias[b * 24 + o] = o < a.nout ? a.b[o] + sum : 0.f;
         }
     }
 }
 
+// One block = 4 warps over 64 consecutive cells of one image (grid = (fH*fW / 64, B)); each warp takes one
+// m-tile of 16 cells.  Lane (g, t) = (lane / 4, lane % 4) loads channels [32 ch + 8t, +8) of its rows g and
+// g + 8 with one 16-byte load each and feeds them as the k-slots (2t, 2t+1 | 2t+8, 2t+9) of the chunk's two
+// k-steps; k_head_prep laid the B fragments out with the same channel permutation, so the sum over k is the
+// sum over channels.  All NCH = Cfeat/32 chunks of the warp's features are loaded up front (2-4 KB per warp
+// in flight: the head is bound by reading its features), the B fragments (9 x 512 bytes per chunk, shared by
+// every warp of the image) come through L1.
+// Epilogue: the accumulators go through shared memory so that lane l < 16 owns cell l of its warp, which
+// adds bias', the extra channels in fp32 (head_extra) and applies the activations (head_activate).
+template <int M, int NCH>
+__global__ void __launch_bounds__(128) k_head_tc(HeadArgs a) {
+    __shared__ float stage[4][16][25];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.y;
+    const int HW = a.fH * a.fW;
+    const int cw = blockIdx.x * 64 + warp * 16;  // the warp's first cell inside image b
+    const int g = lane >> 2, t = lane & 3;
+    const __nv_bfloat16 *fb = a.feat + ((long long)b * HW + cw + g) * (NCH * 32) + 8 * t;
+    uint4 ar[NCH][2];
+#pragma unroll
+    for (int ch = 0; ch < NCH; ch++)
+#pragma unroll
+        for (int q = 0; q < 2; q++)
+            ar[ch][q] = __ldg(reinterpret_cast<const uint4 *>(fb + q * 8 * (NCH * 32) + ch * 32));
+    const uint4 *fr = a.frag + (size_t)b * NCH * 9 * 32 + lane;
+    float acc[3][4];
+#pragma unroll
+    for (int j = 0; j < 3; j++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[j][e] = 0.f;
+#pragma unroll
+    for (int ch = 0; ch < NCH; ch++) {
+        const uint4 &r0 = ar[ch][0], &r1 = ar[ch][1];  // rows g, g + 8
+#pragma unroll
+        for (int k = 0; k < 9; k++) {
+            const uint4 bv = __ldg(fr + (ch * 9 + k) * 32);
+            const int j = k % 3;
+            mma_16816_bf16(acc[j], r0.x, r1.x, r0.y, r1.y, bv.x, bv.y);
+            mma_16816_bf16(acc[j], r0.z, r1.z, r0.w, r1.w, bv.z, bv.w);
+        }
+    }
+    // epilogue: C fragment (row g | g + 8, outputs 8j + 2t, +1) -> stage[cell][output] -> lane = cell
+    float(*sw)[25] = stage[warp];
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        const int o = 8 * j + 2 * t;
+        sw[g][o] = acc[j][0];
+        sw[g][o + 1] = acc[j][1];
+        sw[g + 8][o] = acc[j][2];
+        sw[g + 8][o + 1] = acc[j][3];
+    }
+    __syncwarp();
+    if (lane >= 16) return;
+    float v[HEAD_NP];
+    const float *fbias = a.fbias + b * 24;
+#pragma unroll
+    for (int k = 0; k < HEAD_NP; k++) v[k] = sw[lane][k] + __ldg(fbias + k);
+    const int r = cw + lane;
+    const int y = r / a.fW, x = r - y * a.fW;
+    const long long cell = (long long)b * HW + r;
+    head_extra(a, a.wext, cell, b, y, x, v);
+    head_activate<M, 1>(a, 0, b, r, y, x, v);
+}
+
 // cond[B][rg][rg][4] = (|bilinear(image) - render|, mean_c(render)) (efficient_encoder.py:349-351)
+// grid = (ceil(rg^2 / 256), B)
 __global__ void k_cond(const float *__restrict__ image, int B, int H, int W, const float *__restrict__ render, int rg,
                        float *__restrict__ cond) {
-    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long long)B * rg * rg) return;
-    int b = (int)(i / ((long long)rg * rg));
-    int r = (int)(i - (long long)b * rg * rg);
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rg * rg) return;
+    const int b = blockIdx.y;
+    const long long i = (long long)b * rg * rg + r;
     int y = r / rg, x = r - y * rg;
     int y0, y1, x0, x1;
     float h0, h1, w0, w1;
@@ -656,13 +861,16 @@ __global__ void __launch_bounds__(256) k_gn_table(const double *__restrict__ sta
 // GroupNorm(8) applied to NHWC bf16 [B][HW][C] written as NHWC fp32, 8 channels per thread, from a
 // scale/shift table (the fine decoder's normalised features for return_latents; the backbone features
 // when s8 stays raw)
+// grid = (ceil(HW * C / 8 / 256), B): 32-bit index arithmetic inside one image
 __global__ void __launch_bounds__(256) k_gn_to_f32(const __nv_bfloat16 *__restrict__ x, int B, long long HW, int C,
                                                    const float2 *__restrict__ table, float *__restrict__ out) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // vector of 8 channels
-    if (i * 8 >= (long long)B * HW * C) return;
     const int nv = C / 8;
-    const int c0 = (int)(i % nv) * 8;
-    const int b = (int)(i / (HW * nv));
+    const int nvi = (int)HW * nv;  // vectors of 8 channels per image
+    const int iv = blockIdx.x * blockDim.x + threadIdx.x;
+    if (iv >= nvi) return;
+    const int b = blockIdx.y;
+    const int c0 = (iv % nv) * 8;
+    const long long i = (long long)b * nvi + iv;
     const float4 *t = reinterpret_cast<const float4 *>(table + (long long)b * C + c0);
     const float4 t0 = t[0], t1 = t[1], t2 = t[2], t3 = t[3];
     const uint4 u = reinterpret_cast<const uint4 *>(x)[i];
@@ -693,7 +901,43 @@ size_t head_smem(const HeadArgs &h, long long ncell) {
     return ((size_t)h.Cin * HEAD_NP + HEAD_NP + 2 * h.Cfeat + (parts > 1 ? parts * HEAD_CELLS * HEAD_NP : 0)) * 4;
 }
 
+template <int M, int NCH>
+void launch_head_tc(const HeadArgs &h, cudaStream_t s) {
+    dim3 grid((unsigned)(h.fH * h.fW / 64), (unsigned)h.B);
+    k_head_tc<M, NCH><<<grid, 128, 0, s>>>(h);
+}
+
+// k_head_tc takes heads whose image block is a multiple of 64 cells with 128 or 256 feature channels, up
+// to 5 extra channels and at most 2 splats per cell
+bool head_tc_ok(const HeadArgs &h) {
+    return ((long long)h.fH * h.fW) % 64 == 0 && (h.Cfeat == 128 || h.Cfeat == 256) && h.Cin > h.Cfeat &&
+           h.Cin - h.Cfeat <= 5 && h.nout <= HEAD_NP && (h.M == 1 || h.M == 2);
+}
+
+// workspace of the tensor-core head's per-image operands
+size_t head_tc_ws(int B, int Cfeat) { return (size_t)B * head_frag_bytes(Cfeat) + (size_t)B * 24 * 4 + 5 * HEAD_NP * 4; }
+
+// k_head_prep for head h into ws (head_tc_ws bytes, 16-byte aligned); sets h's operand pointers.  Returns the
+// number of launches (0 when the head takes the SIMT kernel).
+int launch_head_prep(HeadArgs &h, void *ws, cudaStream_t s) {
+    if (!head_tc_ok(h)) return 0;
+    uint4 *frag = reinterpret_cast<uint4 *>(ws);
+    float *fbias = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + (size_t)h.B * head_frag_bytes(h.Cfeat));
+    float *wext = fbias + h.B * 24;
+    dim3 grid((unsigned)((h.Cfeat / 32 * 96 + 127) / 128), (unsigned)h.B);
+    k_head_prep<<<grid, 128, 0, s>>>(h, frag, fbias, wext);
+    h.frag = frag;
+    h.fbias = fbias;
+    h.wext = wext;
+    return 1;
+}
+
 void launch_head(const HeadArgs &h, long long ncell, cudaStream_t s) {
+    if (h.frag) {
+        if (h.Cfeat == 128) h.M == 1 ? launch_head_tc<1, 4>(h, s) : launch_head_tc<2, 4>(h, s);
+        else h.M == 1 ? launch_head_tc<1, 8>(h, s) : launch_head_tc<2, 8>(h, s);
+        return;
+    }
     const size_t smem = head_smem(h, ncell);
     if (head_parts(ncell) == 4) {
         const unsigned grid = (unsigned)((ncell + HEAD_CELLS - 1) / HEAD_CELLS);
@@ -715,8 +959,8 @@ size_t al(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct EncPlan {
     int B, H, W, H2, W2, H4, W4, H8, W8, d, Nc, Nf, N, rg;
-    size_t o_Z, o_y1, o_y2, o_y3, o_cat, o_y4, o_grad, o_g4, o_g8, o_stats, o_chsum, o_gtab, o_err, o_c[5], o_render,
-        o_cond, o_rws, total;
+    size_t o_Z, o_y1, o_y2, o_y3, o_cat, o_y4, o_grad, o_g4, o_g8, o_stats, o_chsum, o_gtab, o_err, o_ht3, o_ht4,
+        o_c[5], o_render, o_cond, o_rws, total;
     gs_render_desc rd;
     size_t rws;
 };
@@ -749,6 +993,8 @@ int enc_plan(const gs_encoder_desc *e, EncPlan &p) {
     p.o_chsum = take(B * GN_BG_BLOCKS * 256 * 4);  // per-block channel sums of the normalised s8
     p.o_gtab = take(B * (256 + 128) * 8);            // GroupNorm scale/shift tables: s8, decoder output
     p.o_err = take(64);
+    p.o_ht3 = take(head_tc_ws(p.B, 256));  // tensor-core head operands: coarse head, fine head
+    p.o_ht4 = take(head_tc_ws(p.B, 128));
     const size_t nc = B * p.Nc;
     p.o_c[0] = take(nc * 2 * 4);
     p.o_c[1] = take(nc * 2 * 4);
@@ -852,8 +1098,8 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     // 1. input preparation
     {
         ProfScope ps(PR_ENC_PREP, s);
-        long long n = (long long)B * p.H2 * p.W2;
-        k_prep<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(image, B, p.H, p.W, grad, W<__nv_bfloat16>(ws, p.o_Z));
+        dim3 pg((unsigned)((p.W2 + PREP_TX - 1) / PREP_TX), (unsigned)((p.H2 + PREP_TY - 1) / PREP_TY), (unsigned)B);
+        k_prep<<<pg, PREP_TX * PREP_TY, 0, s>>>(image, B, p.H, p.W, grad, W<__nv_bfloat16>(ws, p.o_Z));
         long long n8 = (long long)B * p.H8 * p.W8 * 8;
         k_pool48<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(grad, B, p.H, p.W, W<float>(ws, p.o_g4),
                                                              W<float>(ws, p.o_g8));
@@ -930,6 +1176,18 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
                                W<void>(ws, p.o_y4), stats + 3 * B * 16, err, s2)))
             return st;
     }
+    // the fine head's arguments; its tensor-core operands (GroupNorm folded into the weights) are prepared
+    // on the side stream as soon as the decoder's statistics exist
+    HeadArgs hf;
+    memset(&hf, 0, sizeof(hf));
+    hf.B = B; hf.fH = p.H4; hf.fW = p.W4; hf.M = e->Mf; hf.Cfeat = 128; hf.feat = W<__nv_bfloat16>(ws, p.o_y4);
+    hf.gn_stats = stats + 3 * B * 16; hf.gn_gamma = w->gn4_w; hf.gn_beta = w->gn4_b;
+    hf.gpool = W<float>(ws, p.o_g4); hf.cond = W<float>(ws, p.o_cond); hf.rg = p.rg;
+    hf.w = w->hf_w; hf.b = w->hf_b; hf.Cin = 133; hf.nout = (e->use_rotation ? 9 : 8) * e->Mf;
+    hf.off_scale = e->fine_offset / (float)std::max(p.H4, p.W4);
+    hf.ls_floor = -INFINITY; hf.min_op = 0.f; hf.use_rot = e->use_rotation;
+    hf.Ntot = p.N; hf.n0 = p.Nc; hf.mu = mu; hf.ls = log_scale; hf.col = color; hf.op = opacity; hf.th = theta;
+    int nprep = launch_head_prep(hf, W<void>(ws, p.o_ht4), s2);
     // 3. coarse head (writes the API tensors and a contiguous copy for the coarse render)
     HeadArgs h;
     memset(&h, 0, sizeof(h));
@@ -946,6 +1204,7 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
     {
         ProfScope ps(PR_HEADS, s);
         long long ncell = (long long)B * p.H8 * p.W8;
+        nprep += launch_head_prep(h, W<void>(ws, p.o_ht3), s);
         launch_head(h, ncell, s);
     }
     // 4. coarse render at residual_grid^2 (odds) -> cond map
@@ -957,44 +1216,34 @@ extern "C" int gs_encoder_fwd(const gs_encoder_desc *e, const gs_encoder_weights
                            W<void>(ws, p.o_rws), p.rws, stream);
         gs_prof_set_internal(0);
         if (st != GS_OK) return st;
-        long long n = (long long)B * p.rg * p.rg;
-        k_cond<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(image, B, p.H, p.W, W<float>(ws, p.o_render), p.rg,
-                                                          W<float>(ws, p.o_cond));
+        k_cond<<<dim3((unsigned)((p.rg * p.rg + 255) / 256), (unsigned)B), 256, 0, s>>>(
+            image, B, p.H, p.W, W<float>(ws, p.o_render), p.rg, W<float>(ws, p.o_cond));
     }
     // join: the fine head needs the decoder's output and statistics and the coarse render's cond map
     fork.join();
-    // 6. fine head: GN on the fly, + pooled gradient + bilinear(cond)
-    memset(&h, 0, sizeof(h));
-    h.B = B; h.fH = p.H4; h.fW = p.W4; h.M = e->Mf; h.Cfeat = 128; h.feat = W<__nv_bfloat16>(ws, p.o_y4);
-    h.gn_stats = stats + 3 * B * 16; h.gn_gamma = w->gn4_w; h.gn_beta = w->gn4_b;
-    h.gpool = W<float>(ws, p.o_g4); h.cond = W<float>(ws, p.o_cond); h.rg = p.rg;
-    h.w = w->hf_w; h.b = w->hf_b; h.Cin = 133; h.nout = (e->use_rotation ? 9 : 8) * e->Mf;
-    h.off_scale = e->fine_offset / (float)std::max(p.H4, p.W4);
-    h.ls_floor = -INFINITY; h.min_op = 0.f; h.use_rot = e->use_rotation;
-    h.Ntot = p.N; h.n0 = p.Nc; h.mu = mu; h.ls = log_scale; h.col = color; h.op = opacity; h.th = theta;
+    // 6. fine head: GN on the fly (or folded into its tensor-core operands), + pooled gradient + bilinear(cond)
     {
         ProfScope ps(PR_HEADS, s);
         long long ncell = (long long)B * p.H4 * p.W4;
-        launch_head(h, ncell, s);
+        launch_head(hf, ncell, s);
     }
     if (latents) {
-        long long n = (long long)B * p.H4 * p.W4 * 128;
         float2 *gtab4 = W<float2>(ws, p.o_gtab) + B * 256;
         k_gn_table<<<B, 128, 0, s>>>(stats + 3 * B * 16, w->gn4_w, w->gn4_b, 128, (long long)p.H4 * p.W4, gtab4);
-        k_gn_to_f32<<<(unsigned)((n / 8 + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y4), B,
-                                                                (long long)p.H4 * p.W4, 128, gtab4, latents);
+        dim3 tg((unsigned)(((long long)p.H4 * p.W4 * 16 + 255) / 256), (unsigned)B);
+        k_gn_to_f32<<<tg, 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y4), B, (long long)p.H4 * p.W4, 128, gtab4, latents);
         gs_count_launch(2);
     }
     if (features) {
         long long n = (long long)B * p.H8 * p.W8 * 256;
         if (gn3_fly)
-            k_gn_to_f32<<<(unsigned)((n / 8 + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), B,
-                                                                        (long long)p.H8 * p.W8, 256, gtab, features);
+            k_gn_to_f32<<<dim3((unsigned)(((long long)p.H8 * p.W8 * 32 + 255) / 256), (unsigned)B), 256, 0, s>>>(
+                W<__nv_bfloat16>(ws, p.o_y3), B, (long long)p.H8 * p.W8, 256, gtab, features);
         else
             k_bf16_to_f32<<<(unsigned)((n / 8 + 255) / 256), 256, 0, s>>>(W<__nv_bfloat16>(ws, p.o_y3), features, n);
     }
     // memset, prep, pool, 4 convs, 3 GN applies, bg, 2 heads, cond, upsample, optional feature copy
-    gs_count_launch(16 + (features ? 1 : 0));
+    gs_count_launch(16 + (features ? 1 : 0) + nprep);
     cudaError_t ce = cudaGetLastError();
     if (ce != cudaSuccess) {
         fprintf(stderr, "gs_encoder_fwd: %s\n", cudaGetErrorString(ce));

@@ -114,6 +114,16 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t sbo_bytes, ui
     d |= (uint64_t)(layout & 7u) << 61;
     return d;
 }
+// Shared-memory matrix descriptor, K-major, no swizzle: core matrices of 8 rows x 16 bytes stored as 128
+// contiguous bytes; LBO = byte distance between core matrices adjacent in K, SBO = between 8-row groups.
+__device__ __forceinline__ uint64_t sdesc_ns(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;
+    return d;
+}
 // Instruction descriptor kind::f16: D f32, A/B bf16, both K-major, M = 128, N = n.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);

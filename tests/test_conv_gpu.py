@@ -50,7 +50,7 @@ def _rand(*shape, scale=1.0, seed=0):
     return (torch.randn(*shape, generator=g, device="cuda") * scale)
 
 
-@pytest.mark.parametrize("shape", [(2, 64, 64), (1, 48, 80), (1, 768, 768)])
+@pytest.mark.parametrize("shape", [(2, 64, 64), (1, 48, 80), (1, 768, 768), (2, 256, 512), (1, 202, 256)])
 def test_first_layer(lib, shape):
     from gaussian_2d_splat_encoder_b200.efficient_encoder import pack_first_layer, space_to_depth_input
 
@@ -63,6 +63,27 @@ def test_first_layer(lib, shape):
     out, st = run_conv(lib, z, wp, b, 64, 4, 4, 1, 2, Ho=H // 2, Wo=W // 2, kind=1)
     ref = F.gelu(F.conv2d(x.float(), w.float(), b, stride=2, padding=3))
     check(out, ref, st)
+
+
+@pytest.mark.parametrize("shape", [(1, 768, 768), (2, 256, 512)])
+def test_first_layer_halo_matches_per_tap_loads(lib, shape, monkeypatch):
+    """The halo form of the first layer (one window per item, taps as offset views, unswizzled) issues the
+    same MMAs on the same operands as the per-tap TMA form (GS_CONV_HALO=0): identical outputs."""
+    from gaussian_2d_splat_encoder_b200.efficient_encoder import pack_first_layer, space_to_depth_input
+
+    B, H, W = shape
+    x = _rand(B, 4, H, W, seed=5).bfloat16()
+    w = _rand(64, 4, 7, 7, scale=0.1, seed=6).bfloat16()
+    b = _rand(64, scale=0.1, seed=7)
+    z = space_to_depth_input(x)
+    wp = pack_first_layer(w.float()).bfloat16().contiguous()
+    outs = []
+    for flag in ("1", "0"):
+        monkeypatch.setenv("GS_CONV_HALO", flag)
+        out, _ = run_conv(lib, z, wp, b, 64, 4, 4, 1, 2, Ho=H // 2, Wo=W // 2, kind=1)
+        outs.append(out.clone())
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]), (outs[0].float() - outs[1].float()).abs().max()
 
 
 @pytest.mark.parametrize("Ci,Co,H,W,stride", [(64, 128, 32, 48, 2), (128, 256, 16, 24, 2), (384, 128, 16, 24, 1),
