@@ -535,6 +535,7 @@ int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in
     a.Ho = d->Ho > 0 ? d->Ho : (Hi + 2 * d->pad - d->kh) / d->stride + 1;
     a.Wo = d->Wo > 0 ? d->Wo : (Wi + 2 * a.padw - d->kw) / d->stride + 1;
     if (a.Ho <= 0 || a.Wo <= 0) return GS_ERR_BAD_ARGUMENT;
+
     gs_conv_pick_tile(a.Ho, a.Wo, MT, &a.TX, &a.TY);
     a.tiles_x = (a.Wo + a.TX - 1) / a.TX;
     a.tiles_y = (a.Ho + a.TY * MT - 1) / (a.TY * MT);
@@ -602,6 +603,7 @@ int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in
     // one column slice per accumulator: doubling the epilogue warps (CS = 2) measured slower on B200
     if (KC == 16) return launch<64, 16, 8, 2, 8, 2, 1>(tA, tA2, tB, a, st);
     if (Co == 64) return launch<64, 64, 5, 2, 8, 1, 1>(tA, tA2, tB, a, st);
+    // (Cout 128 in two-M-tile items at 4 stages, one CTA per SM, measured no faster at four images per launch)
     if (Co == 128) return launch<128, 64, 3, 1, 16, 2, 1>(tA, tA2, tB, a, st);
     return launch<64, 64, 3, 1, 32, 3, 1>(tA, tA2, tB, a, st);
 }

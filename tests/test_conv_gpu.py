@@ -86,13 +86,16 @@ def test_first_layer_halo_matches_per_tap_loads(lib, shape, monkeypatch):
     assert torch.equal(outs[0], outs[1]), (outs[0].float() - outs[1].float()).abs().max()
 
 
-@pytest.mark.parametrize("Ci,Co,H,W,stride", [(64, 128, 32, 48, 2), (128, 256, 16, 24, 2), (384, 128, 16, 24, 1),
-                                              (64, 128, 384, 384, 2), (128, 256, 192, 192, 2),
-                                              (384, 128, 192, 192, 1), (64, 64, 20, 36, 1)])
-def test_conv3x3(lib, Ci, Co, H, W, stride):
+@pytest.mark.parametrize("Ci,Co,H,W,stride,nb", [(64, 128, 32, 48, 2, 2), (128, 256, 16, 24, 2, 2),
+                                                 (384, 128, 16, 24, 1, 2), (64, 128, 384, 384, 2, 2),
+                                                 (128, 256, 192, 192, 2, 2), (384, 128, 192, 192, 1, 2),
+                                                 (64, 64, 20, 36, 1, 2), (64, 128, 384, 384, 2, 4),
+                                                 (384, 128, 192, 192, 1, 4)])
+def test_conv3x3(lib, Ci, Co, H, W, stride, nb):
+    """nb = 4: the shapes of the batched throughput form."""
     from gaussian_2d_splat_encoder_b200.efficient_encoder import pack_conv
 
-    x = _rand(2, Ci, H, W, seed=3).bfloat16()
+    x = _rand(nb, Ci, H, W, seed=3).bfloat16()
     w = _rand(Co, Ci, 3, 3, scale=(1.0 / (9 * Ci)) ** 0.5, seed=4).bfloat16()
     b = _rand(Co, scale=0.1, seed=5)
     xn = x.permute(0, 2, 3, 1).contiguous()
