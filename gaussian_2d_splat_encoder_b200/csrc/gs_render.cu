@@ -562,9 +562,13 @@ __device__ __forceinline__ SplatRec null_rec() {
 
 // Composite the staged records into the lane's PPL pixels, all in one column (x terms once per splat), the
 // two half-warps on alternate records: half h takes sr[h], sr[h + 2], ... (nb16 a multiple of 16, so each
-// half renormalises after every 8 of its splats).  alpha = min(2^(log2 op - u^2 - v^2), 1 - 1e-4), the
-// running product of (1 - alpha) renormalised every 8 splats, and the weight sums (w = alpha / (1 - alpha)
-// for odds).
+// half renormalises after every 8 of its splats).  alpha = min(2^(log2 op - u^2 - v^2), 1 - 1e-4) and the
+// weight sums (w = alpha / (1 - alpha) for odds).  Alpha mode keeps the running product P of (1 - alpha);
+// odds mode forms the weight without alpha itself: r = 2^(u^2 + v^2 - log2 op) = 1 / alpha, w = 1 / (r - 1)
+// with r - 1 clamped below at (1 - AMAX) / AMAX (exactly the clamped alpha's odds), and keeps
+// P = prod (1 + w) = 1 / prod (1 - alpha) instead -- one multiply per pixel-pair less.  Both products are
+// renormalised every 8 splats (P stays within 2^+-128: at most 1e4^8 growth or 1e-32 decay in between).
+#define GS_ODDS_TMIN ((1.0f - GS_ALPHA_MAX) / GS_ALPHA_MAX)
 template <int PPL, bool ODDS>
 __device__ __forceinline__ void fields_sweep16h(const SplatRec *__restrict__ sr, int nb16, int h, const float (&py)[PPL],
                                                 float pxl, float (&P)[PPL], int (&E)[PPL], float (&Sw)[PPL],
@@ -581,11 +585,16 @@ __device__ __forceinline__ void fields_sweep16h(const SplatRec *__restrict__ sr,
                 const float dy = py[j] - A.x;
                 const float u = fmaf(A.z, dy, ux);
                 const float v = fmaf(Bv.x, dy, vx);
-                const float arg = fmaf(-u, u, fmaf(-v, v, Bv.w));
-                const float a = fminf(gs_ex2(arg), GS_ALPHA_MAX);
-                const float om = 1.0f - a;
-                P[j] *= om;
-                const float w = ODDS ? a * gs_rcp(om) : a;
+                float w;
+                if (ODDS) {
+                    const float narg = fmaf(u, u, fmaf(v, v, -Bv.w));
+                    w = gs_rcp(fmaxf(gs_ex2(narg) - 1.0f, GS_ODDS_TMIN));
+                    P[j] = fmaf(P[j], w, P[j]);
+                } else {
+                    const float arg = fmaf(-u, u, fmaf(-v, v, Bv.w));
+                    w = fminf(gs_ex2(arg), GS_ALPHA_MAX);
+                    P[j] *= 1.0f - w;
+                }
                 Sw[j] += w;
                 S0[j] = fmaf(w, Cv.x, S0[j]);
                 S1[j] = fmaf(w, Cv.y, S1[j]);
@@ -655,6 +664,7 @@ __global__ void __launch_bounds__(128) k_fields_w8(RenderGeom G, const SplatRec 
     for (int j = 0; j < 4; j++) {
         renorm(P[j], E[j]);
         float sl = __logf(P[j]) + (float)E[j] * GS_LN2;
+        if (ODDS) sl = -sl;  // P = 1 / transmittance
         sl += __shfl_xor_sync(0xffffffffu, sl, 16);
         const float sw = Sw[j] + __shfl_xor_sync(0xffffffffu, Sw[j], 16);
         const float s0 = S0[j] + __shfl_xor_sync(0xffffffffu, S0[j], 16);
@@ -721,6 +731,7 @@ __global__ void __launch_bounds__(FW_DEEP_NW * 32) k_fields_deep8(RenderGeom G, 
         for (int j = 0; j < 4; j++) {
             renorm(P[j], E[j]);
             float sl = __logf(P[j]) + (float)E[j] * GS_LN2;
+            if (ODDS) sl = -sl;  // P = 1 / transmittance
             sl += __shfl_xor_sync(0xffffffffu, sl, 16);
             const float sw = Sw[j] + __shfl_xor_sync(0xffffffffu, Sw[j], 16);
             const float s0 = S0[j] + __shfl_xor_sync(0xffffffffu, S0[j], 16);
