@@ -433,11 +433,12 @@ __global__ void __launch_bounds__(TS_THREADS) k_tile_scan(const int *__restrict_
 
 // Every pair of the call placed at its tile's cursor.  Splat block j (256 splats, the preprocessing block)
 // is shared by `parts` scatter blocks, part p taking pairs [min(p*c, tot_j), min((p+1)*c, tot_j)) of the
-// block's pairs in splat order, c = ceil(tot_j / parts).  A block works in chunks of SC_CHUNK pairs: it
-// counts the chunk's pairs per tile in a shared-memory hash table (the rank of each pair inside its
-// tile's group), reserves each tile's group with ONE global atomic, then writes the pairs.  Deep tiles (a
-// coarse octave tile under a thousand splats of neighbouring encoder cells) otherwise serialise on their
-// cursor.
+// block's pairs in splat order, c = ceil(tot_j / parts).  A block works in chunks of SC_CHUNK pairs: each
+// thread lists its own splat's pairs of the chunk (tile ids stepped along the rectangle's rows, one
+// division per splat and chunk), then every pair is counted per tile in a shared-memory hash table (the
+// rank of each pair inside its tile's group), each tile's group is reserved with ONE global atomic, and
+// the pairs are written.  Deep tiles (a coarse octave tile under a thousand splats of neighbouring encoder
+// cells) otherwise serialise on their cursor.
 #define SC_CHUNK 2048
 #define SC_HASH 4096  // >= 2 * SC_CHUNK: a probe sequence always ends
 __global__ void __launch_bounds__(256) k_scatter(RenderGeom G, const int4 *__restrict__ meta,
@@ -449,8 +450,7 @@ __global__ void __launch_bounds__(256) k_scatter(RenderGeom G, const int4 *__res
     __shared__ int4 smeta[256];
     __shared__ int hkey[SC_HASH];
     __shared__ int hval[SC_HASH];               // per tile: pairs in the chunk, then their global start
-    __shared__ unsigned short pslot[SC_CHUNK];  // per pair: hash slot of its tile
-    __shared__ unsigned short prank[SC_CHUNK];  // per pair: rank among the chunk's pairs of that tile
+    __shared__ int ptile[SC_CHUNK];             // per pair: its tile, then (hash slot | rank << 16)
     __shared__ unsigned char psplat[SC_CHUNK];  // per pair: splat of the block
     // after a capacity overflow (k_tile_scan) nothing is scattered
     if (*reinterpret_cast<const int *>(misc + MISC_STATUS) != 0) return;
@@ -482,28 +482,35 @@ __global__ void __launch_bounds__(256) k_scatter(RenderGeom G, const int4 *__res
             hkey[i] = -1;
             hval[i] = 0;
         }
+        {
+            // this thread's splat: its pairs [e0, e1) of the chunk, row by row of its tile rectangle
+            const int e0 = max(soff[tid], c0), e1 = min(soff[tid + 1], c0 + n);
+            if (e0 < e1) {
+                const int4 m = smeta[tid];
+                const int w = m.y & 0xffffff;
+                const int r = e0 - soff[tid];
+                const int q = r / w;
+                int col = r - q * w, rowbase = m.x + q * m.z;
+                for (int e = e0; e < e1; e++) {
+                    ptile[e - c0] = rowbase + col;
+                    psplat[e - c0] = (unsigned char)tid;
+                    if (++col == w) {
+                        col = 0;
+                        rowbase += m.z;
+                    }
+                }
+            }
+        }
         __syncthreads();
         for (int jj = tid; jj < n; jj += 256) {
-            const int e = c0 + jj;
-            int lo = 0, hi = 255;  // splat k of this block with soff[k] <= e < soff[k+1]
-            while (lo < hi) {
-                const int mid = (lo + hi + 1) >> 1;
-                if (soff[mid] <= e) lo = mid; else hi = mid - 1;
-            }
-            const int4 m = smeta[lo];
-            const int r = e - soff[lo];
-            const int w = m.y & 0xffffff;
-            const int q = r / w;
-            const int tile = m.x + q * m.z + (r - q * w);
+            const int tile = ptile[jj];
             unsigned h = ((unsigned)tile * 2654435761u) >> (32 - hbits);
             for (int probe = 0; probe < hsize; probe++) {
                 const int k = atomicCAS(&hkey[h], -1, tile);
                 if (k == -1 || k == tile) break;
                 h = (h + 1) & (unsigned)(hsize - 1);
             }
-            pslot[jj] = (unsigned short)h;
-            prank[jj] = (unsigned short)atomicAdd(&hval[h], 1);
-            psplat[jj] = (unsigned char)lo;
+            ptile[jj] = (int)h | (atomicAdd(&hval[h], 1) << 16);
         }
         __syncthreads();
         {
@@ -527,7 +534,8 @@ __global__ void __launch_bounds__(256) k_scatter(RenderGeom G, const int4 *__res
         }
         __syncthreads();
         for (int jj = tid; jj < n; jj += 256) {
-            const int pos = hval[pslot[jj]] + prank[jj];
+            const int sr = ptile[jj];
+            const int pos = hval[sr & 0xffff] + (sr >> 16);
             if (pos >= 0 && pos < cap) vals[pos] = (int)(s0 + psplat[jj]);  // (always: the counts bound the cursors)
         }
         __syncthreads();
