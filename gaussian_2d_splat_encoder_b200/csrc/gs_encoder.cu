@@ -817,33 +817,41 @@ __global__ void __launch_bounds__(256) k_upsample2x(const __nv_bfloat16 *__restr
             sh[2 * k + 1] = g.w;
         }
     }
-    uint4 res[2][2];
+    // channel pairs: one bf16x2 -> float2 unpack per source word, one packed rounding per output pair
+    uint32_t res[2][2][4];
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        float f[3][3];
+    for (int k2 = 0; k2 < 4; k2++) {
+        float2 f[3][3];
 #pragma unroll
         for (int r = 0; r < 3; r++)
 #pragma unroll
-            for (int c = 0; c < 3; c++) f[r][c] = __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(&v[r][c])[k]);
+            for (int c = 0; c < 3; c++) f[r][c] = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162 *>(&v[r][c])[k2]);
         // horizontal blends of the three source rows at the two output columns
-        float hb[3][2];
+        float2 hb[3][2];
 #pragma unroll
         for (int r = 0; r < 3; r++)
 #pragma unroll
-            for (int t = 0; t < 2; t++) hb[r][t] = wx[t][0] * f[r][t] + wx[t][1] * f[r][t + 1];
+            for (int t = 0; t < 2; t++) {
+                hb[r][t].x = wx[t][0] * f[r][t].x + wx[t][1] * f[r][t + 1].x;
+                hb[r][t].y = wx[t][0] * f[r][t].y + wx[t][1] * f[r][t + 1].y;
+            }
 #pragma unroll
         for (int ty = 0; ty < 2; ty++)
 #pragma unroll
             for (int tx = 0; tx < 2; tx++) {
-                const float o = hy[ty][0] * hb[ty][tx] + hy[ty][1] * hb[ty + 1][tx];
-                reinterpret_cast<__nv_bfloat16 *>(&res[ty][tx])[k] = __float2bfloat16_rn(fmaf(o, sc[k], sh[k]));
+                const float ox = hy[ty][0] * hb[ty][tx].x + hy[ty][1] * hb[ty + 1][tx].x;
+                const float oy = hy[ty][0] * hb[ty][tx].y + hy[ty][1] * hb[ty + 1][tx].y;
+                const __nv_bfloat162 pk =
+                    __floats2bfloat162_rn(fmaf(ox, sc[2 * k2], sh[2 * k2]), fmaf(oy, sc[2 * k2 + 1], sh[2 * k2 + 1]));
+                res[ty][tx][k2] = *reinterpret_cast<const uint32_t *>(&pk);
             }
     }
 #pragma unroll
     for (int ty = 0; ty < 2; ty++)
 #pragma unroll
         for (int tx = 0; tx < 2; tx++)
-            *reinterpret_cast<uint4 *>(up + (((long long)b * H4 + 2 * p + ty) * W4 + 2 * q + tx) * Cu + c0) = res[ty][tx];
+            *reinterpret_cast<uint4 *>(up + (((long long)b * H4 + 2 * p + ty) * W4 + 2 * q + tx) * Cu + c0) =
+                make_uint4(res[ty][tx][0], res[ty][tx][1], res[ty][tx][2], res[ty][tx][3]);
 }
 
 // per-channel GroupNorm(8) scale and shift, table[b][c] = (sc, sh) with normalised = raw * sc + sh

@@ -997,13 +997,17 @@ template <int K>
 __device__ __forceinline__ void up_group4(const float *__restrict__ f, int plane, int Wg, float usx, int ra, int rb,
                                           float h0, float h1, int x0, float (&S)[5][4]) {
     constexpr int NC = K == 1 ? 4 : (K == 2 ? 3 : 2);
+    // lin_index_s's weights without its index clamps: with usx = 2^-K the source coordinate
+    // (x + 0.5) usx - 0.5 is exact, stays below Wg - 1/2 (so its floor is a valid column) and is clamped at 0
     float w0[4], w1[4];
     int first = 0;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-        int i0, i1;
-        lin_index_s(x0 + j, Wg, usx, i0, i1, w0[j], w1[j]);
-        if (j == 0) first = i0;
+        const float src = fmaxf(__fsub_rn(__fmul_rn(usx, __fadd_rn((float)(x0 + j), 0.5f)), 0.5f), 0.0f);
+        const float fl = floorf(src);
+        w1[j] = src - fl;
+        w0[j] = 1.0f - w1[j];
+        if (j == 0) first = (int)fl;
     }
     const int cl = K >= 3 ? first : (x0 >> K) - 1;
     int col[NC];
