@@ -559,7 +559,7 @@ __device__ __forceinline__ uint32_t pack_bf16(__nv_bfloat16 lo, __nv_bfloat16 hi
 size_t head_frag_bytes(int Cfeat) { return (size_t)(Cfeat / 32) * 9 * 32 * 16; }
 
 // grid = (ceil(Cfeat/32 * 96 / 128), B): one (chunk, n-tile, lane) item per thread; block x = 0 also sums
-// bias' (one warp per output: lane-strided sums, then a fixed xor tree).  The GroupNorm scale/shift are the
+// bias' (each warp six outputs at once: lane-strided sums, then a fixed xor tree).  The GroupNorm scale/shift are the
 // ones k_head applies on the fly (same float/double arithmetic).
 __global__ void __launch_bounds__(128) k_head_prep(HeadArgs a, uint4 *__restrict__ frag, float *__restrict__ fbias,
                                                    float *__restrict__ wext) {
@@ -610,14 +610,24 @@ __global__ void __launch_bounds__(128) k_head_prep(HeadArgs a, uint4 *__restrict
                 const int e = i / HEAD_NP, o = i - e * HEAD_NP;
                 wext[i] = o < a.nout ? __ldg(a.w + o * a.Cin + a.Cfeat + e) : 0.f;
             }
+        // warp w sums outputs w, w + 4, ..., w + 20 at once: lane-strided channel sums (all six outputs'
+        // loads of a channel in flight together), then a fixed xor tree per output
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        for (int o = warp; o < 24; o += 4) {
-            float sum = 0.f;
-            if (o < a.nout)
-                for (int c = lane; c < a.Cfeat; c += 32) sum = fmaf(__ldg(a.w + o * a.Cin + c), shift(c), sum);
+        float sum[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int c = lane; c < a.Cfeat; c += 32) {
+            const float shc = shift(c);
 #pragma unroll
-            for (int k = 16; k > 0; k >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, k);
-            if (lane == 0) fbias[b * 24 + o] = o < a.nout ? a.b[o] + sum : 0.f;
+            for (int k = 0; k < 6; k++) {
+                const int o = warp + 4 * k;
+                if (o < a.nout) sum[k] = fmaf(__ldg(a.w + o * a.Cin + c), shc, sum[k]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 6; k++) {
+#pragma unroll
+            for (int m = 16; m > 0; m >>= 1) sum[k] += __shfl_xor_sync(0xffffffffu, sum[k], m);
+            const int o = warp + 4 * k;
+            if (lane == 0) fbias[b * 24 + o] = o < a.nout ? a.b[o] + sum[k] : 0.f;
         }
     }
 }
