@@ -305,32 +305,30 @@ __global__ void __launch_bounds__(64 + 128 * MT * CS, MINB)
         const int m = q * 32 + lane;
         float *acc = sacc[e];
         int cur_b = -1, tc = 0;
-        // CPG = 8: per-lane GroupNorm sums of the warp's BNS / 8 groups for the current (image, slice)
-        float ls[CPG == 8 ? BNS / 8 : 1], lq[CPG == 8 ? BNS / 8 : 1];
+        // per-lane GroupNorm sums of the warp's NG = BNS / CPG groups for the current (image, slice)
+        constexpr int NG = BNS / CPG;
+        float ls[NG], lq[NG];
 #pragma unroll
-        for (int k = 0; k < (CPG == 8 ? BNS / 8 : 1); k++) ls[k] = lq[k] = 0.f;
+        for (int k = 0; k < NG; k++) ls[k] = lq[k] = 0.f;
         int lane_b = -1, lane_nb = 0;
         // the lanes' sums of (lane_b, lane_nb) into the warp's accumulators, in a fixed xor-tree order
         auto fold_lanes = [&]() {
-            if constexpr (CPG == 8) {
-                if (lane_b >= 0) {
+            if (lane_b < 0) return;
 #pragma unroll
-                    for (int k = 0; k < BNS / 8; k++) {
+            for (int k = 0; k < NG; k++) {
 #pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) {
-                            ls[k] += __shfl_xor_sync(0xffffffffu, ls[k], o);
-                            lq[k] += __shfl_xor_sync(0xffffffffu, lq[k], o);
-                        }
-                        if (lane == 0) {
-                            const int g = (lane_nb * BN + clo) / 8 + k;
-                            acc[2 * g] += ls[k];
-                            acc[2 * g + 1] += lq[k];
-                        }
-                        ls[k] = lq[k] = 0.f;
-                    }
-                    __syncwarp();
+                for (int o = 16; o > 0; o >>= 1) {
+                    ls[k] += __shfl_xor_sync(0xffffffffu, ls[k], o);
+                    lq[k] += __shfl_xor_sync(0xffffffffu, lq[k], o);
                 }
+                if (lane == 0) {
+                    const int g = (lane_nb * BN + clo) / CPG + k;
+                    acc[2 * g] += ls[k];
+                    acc[2 * g + 1] += lq[k];
+                }
+                ls[k] = lq[k] = 0.f;
             }
+            __syncwarp();
         };
         for (int item = blockIdx.x; item < n_items; item += gridDim.x, tc++) {
             int t = item;
@@ -345,13 +343,11 @@ __global__ void __launch_bounds__(64 + 128 * MT * CS, MINB)
             const int buf = tc & 1;
             if (!mbar_wait_or_abort(&tfull[buf], (tc >> 1) & 1, &abort_flag, a.err, 5)) break;
             tc_fence_after();
-            if constexpr (CPG == 8) {
-                // the lanes' sums of the previous (image, slice) reach the warp's accumulators first
-                if (a.stats && (b != lane_b || nb != lane_nb)) {
-                    fold_lanes();
-                    lane_b = b;
-                    lane_nb = nb;
-                }
+            // the lanes' sums of the previous (image, slice) reach the warp's accumulators first
+            if (a.stats && (b != lane_b || nb != lane_nb)) {
+                fold_lanes();
+                lane_b = b;
+                lane_nb = nb;
             }
             if (a.stats && b != cur_b) {
                 if (cur_b >= 0 && lane < 16) {
@@ -412,51 +408,28 @@ __global__ void __launch_bounds__(64 + 128 * MT * CS, MINB)
                     reinterpret_cast<uint4 *>(dst + c0)[1] = p1;
                 }
             };
-            if constexpr (CPG == 8) {
-                // GroupNorm sums stay in the lane's registers across chunks and items (ls/lq, folded into the
-                // warp's shared accumulators when the image or channel slice changes, above): no warp
-                // reduction per chunk
+            // GroupNorm sums stay in the lane's registers across chunks and items (ls/lq, folded into the
+            // warp's shared accumulators when the image or channel slice changes, above): no warp
+            // reduction per chunk
 #pragma unroll
-                for (int ci = 0; ci < BNS / 16; ci++) {
-                    float s0, q0, s1, q1;
-                    process(clo + 16 * ci, s0, q0, s1, q1);
-                    if (a.stats && valid) {
+            for (int ci = 0; ci < BNS / 16; ci++) {
+                float s0, q0, s1, q1;
+                process(clo + 16 * ci, s0, q0, s1, q1);
+                if (a.stats && valid) {
+                    if (CPG == 8) {
                         ls[2 * ci] += s0;
                         lq[2 * ci] += q0;
                         ls[2 * ci + 1] += s1;
                         lq[2 * ci + 1] += q1;
-                    }
-                }
-            } else {
-                float rs = 0.f, rq = 0.f;
-#pragma unroll 1
-                for (int c0 = clo; c0 < chi; c0 += 16) {
-                    float s0, q0, s1, q1;
-                    process(c0, s0, q0, s1, q1);
-                    if (a.stats) {
-                        if (!valid) s0 = q0 = 0.f;
-                        rs += s0;
-                        rq += q0;
-                        if ((c0 + 16) % CPG == 0) {
-#pragma unroll
-                            for (int o = 16; o > 0; o >>= 1) {
-                                rs += __shfl_xor_sync(0xffffffffu, rs, o);
-                                rq += __shfl_xor_sync(0xffffffffu, rq, o);
-                            }
-                            if (lane == 0) {
-                                const int g = (n0 + c0) / CPG;
-                                acc[2 * g] += rs;
-                                acc[2 * g + 1] += rq;
-                            }
-                            rs = rq = 0.f;
-                        }
+                    } else {
+                        ls[ci * 16 / CPG] += s0;
+                        lq[ci * 16 / CPG] += q0;
                     }
                 }
             }
         }
-        if constexpr (CPG == 8) {
-            if (a.stats) fold_lanes();
-        }
+        __syncwarp();
+        if (a.stats) fold_lanes();
         __syncwarp();
         if (a.stats && cur_b >= 0 && lane < 16) atomicAdd(&a.stats[cur_b * 16 + lane], (double)acc[lane]);
     }
