@@ -1118,6 +1118,25 @@ __global__ void __launch_bounds__(64) k_composite4(RenderGeom G, const float *__
     }
 }
 
+// fields[b][lo + i] += prior[b][plo + i] for i < n (n % 4 == 0, both offsets multiples of 4): the mapped
+// groups when they are consecutive here and in the prior (the octaves k >= 2 of the encoder's final render
+// map to the prior's k - 1), one flat float4 pass; grid = (ceil(n / 1024), B)
+__global__ void __launch_bounds__(256) k_add_prior_flat(const float *__restrict__ prior, long long prior_per_image,
+                                                        long long plo, float *__restrict__ fields,
+                                                        long long fld_per_image, long long lo, int n4) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n4) return;
+    const int b = blockIdx.y;
+    const float4 p = reinterpret_cast<const float4 *>(prior + b * prior_per_image + plo)[i];
+    float4 *f = reinterpret_cast<float4 *>(fields + b * fld_per_image + lo) + i;
+    float4 v = *f;
+    v.x += p.x;
+    v.y += p.y;
+    v.z += p.z;
+    v.w += p.w;
+    *f = v;
+}
+
 // fields of group g += the mapped prior group's fields (every group with prior_off >= 0, all images);
 // grid = (texel blocks, groups, images)
 __global__ void __launch_bounds__(256) k_add_prior(RenderGeom G, const float *__restrict__ prior,
@@ -2300,8 +2319,29 @@ int gs_render_fwd_prior(const gs_render_desc *d, const float *mu, const float *l
             long long big = 0;
             for (int k = 0; k < G.ngroups; k++)
                 if (G.g[k].prior_off >= 0) big = std::max(big, 5LL * G.g[k].H * G.g[k].W);
-            dim3 pg((unsigned)((big + 255) / 256), (unsigned)G.ngroups, (unsigned)d->B);
-            k_add_prior<<<pg, 256, 0, s>>>(G, prior->fields, prior->fld_per_image, at<float>(workspace, pl.o_fields));
+            // the mapped groups as one range when they are consecutive in both layouts
+            int k0 = -1, k1 = -1;
+            bool flat = true;
+            for (int k = 0; k < G.ngroups; k++) {
+                if (G.g[k].prior_off < 0) continue;
+                if (k0 < 0) k0 = k;
+                else if (k != k1 + 1 || G.g[k].prior_off - G.g[k1].prior_off != (long long)G.g[k].fld_off - G.g[k1].fld_off)
+                    flat = false;
+                k1 = k;
+            }
+            const long long lo = k0 >= 0 ? G.g[k0].fld_off : 0, plo = k0 >= 0 ? G.g[k0].prior_off : 0;
+            const long long n = k0 >= 0 ? (long long)G.g[k1].fld_off + 5LL * G.g[k1].H * G.g[k1].W - lo : 0;
+            float *fl = at<float>(workspace, pl.o_fields);
+            if (flat && n > 0 && n % 4 == 0 && lo % 4 == 0 && plo % 4 == 0 && G.fld_per_image % 4 == 0 &&
+                prior->fld_per_image % 4 == 0 && (reinterpret_cast<uintptr_t>(prior->fields) & 15) == 0 &&
+                (reinterpret_cast<uintptr_t>(fl) & 15) == 0 && n / 4 < (1LL << 31)) {
+                dim3 pg((unsigned)((n / 4 + 255) / 256), (unsigned)d->B);
+                k_add_prior_flat<<<pg, 256, 0, s>>>(prior->fields, prior->fld_per_image, plo, fl, G.fld_per_image, lo,
+                                                    (int)(n / 4));
+            } else {
+                dim3 pg((unsigned)((big + 255) / 256), (unsigned)G.ngroups, (unsigned)d->B);
+                k_add_prior<<<pg, 256, 0, s>>>(G, prior->fields, prior->fld_per_image, fl);
+            }
             GS_CHECK_LAUNCH("k_add_prior");
         }
     }
