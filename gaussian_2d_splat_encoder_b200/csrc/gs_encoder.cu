@@ -210,7 +210,21 @@ __global__ void __launch_bounds__(256) k_gn_apply(__nv_bfloat16 *__restrict__ x,
             cs[k] += __bfloat162float(e[k]);
         }
     };
-    for (; v + stride < nvec; v += 2 * stride) {
+    // four vectors in flight per thread, then two, then one (the sums keep the order of the vectors)
+    for (; v + 3 * stride < nvec; v += 4 * stride) {
+        uint4 u0 = xb[v], u1 = xb[v + stride], u2 = xb[v + 2 * stride], u3 = xb[v + 3 * stride];
+        norm(u0);
+        norm(u1);
+        norm(u2);
+        norm(u3);
+        if (apply) {
+            xb[v] = u0;
+            xb[v + stride] = u1;
+            xb[v + 2 * stride] = u2;
+            xb[v + 3 * stride] = u3;
+        }
+    }
+    if (v + stride < nvec) {
         uint4 u0 = xb[v], u1 = xb[v + stride];
         norm(u0);
         norm(u1);
@@ -218,6 +232,7 @@ __global__ void __launch_bounds__(256) k_gn_apply(__nv_bfloat16 *__restrict__ x,
             xb[v] = u0;
             xb[v + stride] = u1;
         }
+        v += 2 * stride;
     }
     if (v < nvec) {
         uint4 u0 = xb[v];
