@@ -654,8 +654,9 @@ __global__ void __launch_bounds__(128) k_head_prep(HeadArgs a, uint4 *__restrict
 // sum over channels.  All NCH = Cfeat/32 chunks of the warp's features are loaded up front (2-4 KB per warp
 // in flight: the head is bound by reading its features), the B fragments (9 x 512 bytes per chunk, shared by
 // every warp of the image) come through L1.
-// Epilogue: the accumulators go through shared memory so that lane l < 16 owns cell l of its warp, which
-// adds bias', the extra channels in fp32 (head_extra) and applies the activations (head_activate).
+// Epilogue: the accumulators go through shared memory so that lanes l and l + 16 own cell l of the warp:
+// both add bias' and the extra channels in fp32 (head_extra), each applies the activations of half of the
+// cell's splat slots (head_activate).
 template <int M, int NCH>
 __global__ void __launch_bounds__(128) k_head_tc(HeadArgs a) {
     __shared__ float stage[4][16][25];
@@ -699,16 +700,19 @@ __global__ void __launch_bounds__(128) k_head_tc(HeadArgs a) {
         sw[g + 8][o + 1] = acc[j][3];
     }
     __syncwarp();
-    if (lane >= 16) return;
+    // lane = (splat slot half, cell): both half-warps finish the 16 cells, half h the slots m with m % 2 == h
+    constexpr int NFIN = M < 2 ? M : 2;
+    const int lc = lane & 15, part = lane >> 4;
+    if (part >= NFIN) return;
     float v[HEAD_NP];
     const float *fbias = a.fbias + b * 24;
 #pragma unroll
-    for (int k = 0; k < HEAD_NP; k++) v[k] = sw[lane][k] + __ldg(fbias + k);
-    const int r = cw + lane;
+    for (int k = 0; k < HEAD_NP; k++) v[k] = sw[lc][k] + __ldg(fbias + k);
+    const int r = cw + lc;
     const int y = r / a.fW, x = r - y * a.fW;
     const long long cell = (long long)b * HW + r;
     head_extra(a, a.wext, cell, b, y, x, v);
-    head_activate<M, 1>(a, 0, b, r, y, x, v);
+    head_activate<M, NFIN>(a, part, b, r, y, x, v);
 }
 
 // cond[B][rg][rg][4] = (|bilinear(image) - render|, mean_c(render)) (efficient_encoder.py:349-351)
