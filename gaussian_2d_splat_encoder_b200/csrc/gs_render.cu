@@ -569,8 +569,8 @@ __device__ __forceinline__ SplatRec null_rec() {
 }
 
 // Composite the staged records into the lane's PPL pixels, all in one column (x terms once per splat), the
-// two half-warps on alternate records: half h takes sr[h], sr[h + 2], ... (nb16 a multiple of 16, so each
-// half renormalises after every 8 of its splats).  alpha = min(2^(log2 op - u^2 - v^2), 1 - 1e-4) and the
+// two half-warps on alternate records: half h takes sr[h], sr[h + 2], ... (nb even: blocks of 16 records
+// unrolled, each half renormalising after its 8, then the batch's tail of fewer than 8 per half).  alpha = min(2^(log2 op - u^2 - v^2), 1 - 1e-4) and the
 // weight sums (w = alpha / (1 - alpha) for odds).  Alpha mode keeps the running product P of (1 - alpha);
 // odds mode forms the weight without alpha itself: r = 2^(u^2 + v^2 - log2 op) = 1 / alpha, w = 1 / (r - 1)
 // with r - 1 clamped below at (1 - AMAX) / AMAX (exactly the clamped alpha's odds), and keeps
@@ -578,37 +578,46 @@ __device__ __forceinline__ SplatRec null_rec() {
 // renormalised every 8 splats (P stays within 2^+-128: at most 1e4^8 growth or 1e-32 decay in between).
 #define GS_ODDS_TMIN ((1.0f - GS_ALPHA_MAX) / GS_ALPHA_MAX)
 template <int PPL, bool ODDS>
-__device__ __forceinline__ void fields_sweep16h(const SplatRec *__restrict__ sr, int nb16, int h, const float (&py)[PPL],
+__device__ __forceinline__ void fields_sweep16h(const SplatRec *__restrict__ sr, int nb, int h, const float (&py)[PPL],
                                                 float pxl, float (&P)[PPL], int (&E)[PPL], float (&Sw)[PPL],
                                                 float (&S0)[PPL], float (&S1)[PPL], float (&S2)[PPL]) {
-    for (int i = 0; i < nb16; i += 16) {
+    auto one = [&](int k) {
+        const SplatRec &r = sr[k];
+        const float4 A = r.a, Bv = r.b, Cv = r.c;
+        const float dx = pxl - A.y;
+        const float ux = A.w * dx, vx = Bv.y * dx;
 #pragma unroll
-        for (int ii = 0; ii < 8; ii++) {
-            const SplatRec &r = sr[i + 2 * ii + h];
-            const float4 A = r.a, Bv = r.b, Cv = r.c;
-            const float dx = pxl - A.y;
-            const float ux = A.w * dx, vx = Bv.y * dx;
-#pragma unroll
-            for (int j = 0; j < PPL; j++) {
-                const float dy = py[j] - A.x;
-                const float u = fmaf(A.z, dy, ux);
-                const float v = fmaf(Bv.x, dy, vx);
-                float w;
-                if (ODDS) {
-                    const float narg = fmaf(u, u, fmaf(v, v, -Bv.w));
-                    w = gs_rcp(fmaxf(gs_ex2(narg) - 1.0f, GS_ODDS_TMIN));
-                    P[j] = fmaf(P[j], w, P[j]);
-                } else {
-                    const float arg = fmaf(-u, u, fmaf(-v, v, Bv.w));
-                    w = fminf(gs_ex2(arg), GS_ALPHA_MAX);
-                    P[j] *= 1.0f - w;
-                }
-                Sw[j] += w;
-                S0[j] = fmaf(w, Cv.x, S0[j]);
-                S1[j] = fmaf(w, Cv.y, S1[j]);
-                S2[j] = fmaf(w, Cv.z, S2[j]);
+        for (int j = 0; j < PPL; j++) {
+            const float dy = py[j] - A.x;
+            const float u = fmaf(A.z, dy, ux);
+            const float v = fmaf(Bv.x, dy, vx);
+            float w;
+            if (ODDS) {
+                const float narg = fmaf(u, u, fmaf(v, v, -Bv.w));
+                w = gs_rcp(fmaxf(gs_ex2(narg) - 1.0f, GS_ODDS_TMIN));
+                P[j] = fmaf(P[j], w, P[j]);
+            } else {
+                const float arg = fmaf(-u, u, fmaf(-v, v, Bv.w));
+                w = fminf(gs_ex2(arg), GS_ALPHA_MAX);
+                P[j] *= 1.0f - w;
             }
+            Sw[j] += w;
+            S0[j] = fmaf(w, Cv.x, S0[j]);
+            S1[j] = fmaf(w, Cv.y, S1[j]);
+            S2[j] = fmaf(w, Cv.z, S2[j]);
         }
+    };
+    int i = 0;
+    for (; i + 16 <= nb; i += 16) {
+#pragma unroll
+        for (int ii = 0; ii < 8; ii++) one(i + 2 * ii + h);
+#pragma unroll
+        for (int j = 0; j < PPL; j++) renorm(P[j], E[j]);
+    }
+    if (i < nb) {
+        // the batch's last (nb - i) / 2 < 8 records of each half (nb even)
+#pragma unroll 1
+        for (int k = i + h; k < nb; k += 2) one(k);
 #pragma unroll
         for (int j = 0; j < PPL; j++) renorm(P[j], E[j]);
     }
@@ -661,8 +670,8 @@ __global__ void __launch_bounds__(128) k_fields_w8(RenderGeom G, const SplatRec 
     SplatRec nxt;
     if (lane < n) nxt = rec[ids[lane]];
     for (int base = 0; base < n; base += 32) {
-        const int nb16 = stage_batch<16>(srec[warp], nxt, rec, ids, base, n, lane);
-        fields_sweep16h<4, ODDS>(srec[warp], nb16, h, py, pxl, P, E, Sw, S0, S1, S2);
+        const int nb2 = stage_batch<2>(srec[warp], nxt, rec, ids, base, n, lane);
+        fields_sweep16h<4, ODDS>(srec[warp], nb2, h, py, pxl, P, E, Sw, S0, S1, S2);
         __syncwarp();
     }
     // lanes l and l + 16 hold the same pixels: the halves' sums combine (log form for the transmittance)
@@ -731,8 +740,8 @@ __global__ void __launch_bounds__(FW_DEEP_NW * 32) k_fields_deep8(RenderGeom G, 
         SplatRec nxt;
         if (lane < m) nxt = rec[ids[lane]];
         for (int base = 0; base < m; base += 32) {
-            const int nb16 = stage_batch<16>(srec[warp], nxt, rec, ids, base, m, lane);
-            fields_sweep16h<4, ODDS>(srec[warp], nb16, h, py, pxl, P, E, Sw, S0, S1, S2);
+            const int nb2 = stage_batch<2>(srec[warp], nxt, rec, ids, base, m, lane);
+            fields_sweep16h<4, ODDS>(srec[warp], nb2, h, py, pxl, P, E, Sw, S0, S1, S2);
             __syncwarp();
         }
 #pragma unroll
