@@ -1001,7 +1001,8 @@ __global__ void __launch_bounds__(128) k_composite(RenderGeom G, const float *__
 // K = 2 columns (m-1 .. m+1), slots (0,1) (0,1) (1,2) (1,2); K >= 3 the two taps of pixel x0 for all four.
 // Columns are loaded clamped to the plane, so at a border the slot holds the same column as its
 // neighbour while lin_index_s gives that pixel the weights (1, 0) or a tap pair with equal columns: every
-// pixel gets the value gather_sums computes (same taps, weights and operation order).
+// pixel gets gather_sums' value with the same taps and weights (the row blend of each source column is
+// formed first, so the rounding differs from gather_sums' column-then-row order by an ulp or so).
 template <int K>
 __device__ __forceinline__ void up_group4(const float *__restrict__ f, int plane, int Wg, float usx, int ra, int rb,
                                           float h0, float h1, int x0, float (&S)[5][4]) {
@@ -1022,19 +1023,18 @@ __device__ __forceinline__ void up_group4(const float *__restrict__ f, int plane
     int col[NC];
 #pragma unroll
     for (int s = 0; s < NC; s++) col[s] = min(max(cl + s, 0), Wg - 1);
+    // separable: the row blend of each source column once, then two FMAs per pixel (the same bilinear
+    // value as gather_sums' row-then-column order up to float rounding)
 #pragma unroll
     for (int c = 0; c < 5; c++) {
         const float *fc = f + c * plane;
-        float top[NC], bot[NC];
+        float vc[NC];
 #pragma unroll
-        for (int s = 0; s < NC; s++) {
-            top[s] = __ldg(fc + ra + col[s]);
-            bot[s] = __ldg(fc + rb + col[s]);
-        }
+        for (int s = 0; s < NC; s++) vc[s] = fmaf(h1, __ldg(fc + rb + col[s]), h0 * __ldg(fc + ra + col[s]));
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int s0 = K == 1 ? (j + 1) >> 1 : (K == 2 ? j >> 1 : 0);
-            S[c][j] += h0 * (w0[j] * top[s0] + w1[j] * top[s0 + 1]) + h1 * (w0[j] * bot[s0] + w1[j] * bot[s0 + 1]);
+            S[c][j] = fmaf(w1[j], vc[s0 + 1], fmaf(w0[j], vc[s0], S[c][j]));
         }
     }
 }
