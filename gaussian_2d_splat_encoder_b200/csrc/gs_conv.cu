@@ -544,7 +544,7 @@ int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in
     // two or three CTAs share an SM: a layer at 768^2 has only ~150 items of MT = 2, one per SM, whose TMA +
     // MMA latency chain and epilogue then ran back to back with nothing to overlap them
     const int MT = (KC == 64 && Co >= 128) ? 1 : 2;
-    const int BN = Co == 256 ? 64 : Co;
+    int BN = Co == 256 ? 64 : Co;
     ConvArgs a;
     memset(&a, 0, sizeof(a));
     a.B = B; a.Hi = Hi; a.Wi = Wi; a.Ci = Ci; a.Co = Co;
@@ -552,6 +552,9 @@ int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in
     a.Ho = d->Ho > 0 ? d->Ho : (Hi + 2 * d->pad - d->kh) / d->stride + 1;
     a.Wo = d->Wo > 0 ? d->Wo : (Wi + 2 * a.padw - d->kw) / d->stride + 1;
     if (a.Ho <= 0 || a.Wo <= 0) return GS_ERR_BAD_ARGUMENT;
+    // Cout 256: 128-channel slices (each A tile read twice instead of four times) once the layer has items
+    // enough for two CTAs per SM
+    if (Co == 256 && KC == 64 && (long long)B * a.Ho * a.Wo / 128 * 2 >= 2LL * sm_count()) BN = 128;
 
     gs_conv_pick_tile(a.Ho, a.Wo, MT, &a.TX, &a.TY);
     a.tiles_x = (a.Wo + a.TX - 1) / a.TX;
@@ -622,7 +625,8 @@ int gs_conv_run2(const gs_conv_desc *d, const void *in, int Cin1, const void *in
     if (Co == 64) return launch<64, 64, 5, 2, 8, 1, 1>(tA, tA2, tB, a, st);
     // (Cout 128 in two-M-tile items at 4 stages, one CTA per SM, measured no faster at four images per launch)
     if (Co == 128) return launch<128, 64, 3, 1, 16, 2, 1>(tA, tA2, tB, a, st);
-    return launch<64, 64, 3, 1, 32, 3, 1>(tA, tA2, tB, a, st);
+    return BN == 128 ? launch<128, 64, 3, 1, 32, 2, 1>(tA, tA2, tB, a, st)
+                     : launch<64, 64, 3, 1, 32, 3, 1>(tA, tA2, tB, a, st);
 }
 
 extern "C" int gs_conv2d(const gs_conv_desc *d, const void *in_bf16, const void *w_bf16, const float *bias,

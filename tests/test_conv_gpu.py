@@ -90,7 +90,7 @@ def test_first_layer_halo_matches_per_tap_loads(lib, shape, monkeypatch):
                                                  (384, 128, 16, 24, 1, 2), (64, 128, 384, 384, 2, 2),
                                                  (128, 256, 192, 192, 2, 2), (384, 128, 192, 192, 1, 2),
                                                  (64, 64, 20, 36, 1, 2), (64, 128, 384, 384, 2, 4),
-                                                 (384, 128, 192, 192, 1, 4)])
+                                                 (384, 128, 192, 192, 1, 4), (128, 256, 192, 192, 2, 4)])
 def test_conv3x3(lib, Ci, Co, H, W, stride, nb):
     """nb = 4: the shapes of the batched throughput form."""
     from gaussian_2d_splat_encoder_b200.efficient_encoder import pack_conv
