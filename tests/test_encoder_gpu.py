@@ -45,6 +45,24 @@ def test_encoder_cfg0_random_init(lib):
     _compare(o, {k: d[k] for k in d.files}, "cfg0")
 
 
+def test_encoder_one_splat_per_cell(lib):
+    """gaussians_per_cell = fine_per_cell = 1 (the heads' M = 1 instantiations) against the oracle encoder."""
+    from gaussian_2d_splat_encoder_b200 import synth
+    from gaussian_2d_splat_encoder_b200.efficient_encoder import EfficientGaussianEncoder
+    from oracle import encoder_oracle as E
+
+    cfg = {**GOLDEN_CFG, "gaussians_per_cell": 1, "fine_per_cell": 1, "residual_grid": 64}
+    torch.manual_seed(3)
+    m = EfficientGaussianEncoder(**cfg).eval()
+    x = synth.synth_card(128, 128, 40, 12, 5)
+    ref = E.encode(m.state_dict(), cfg, x)
+    with torch.no_grad():
+        o = m.cuda()(x.cuda())
+    torch.cuda.synchronize()
+    assert o["mu"].shape[1] == (16 * 16 + 32 * 32)
+    _compare(o, {k: (v.numpy() if torch.is_tensor(v) else v) for k, v in ref.items()}, "m1")
+
+
 def test_encoder_golden64(lib):
     from gaussian_2d_splat_encoder_b200.efficient_encoder import EfficientGaussianEncoder
 
