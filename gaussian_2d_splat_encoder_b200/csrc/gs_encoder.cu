@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(256) k_prep(const float *__restrict__ image, i
                                               float *__restrict__ grad, __nv_bfloat16 *__restrict__ Z) {
     constexpr int GW = 2 * PREP_TX + 2, GH = 2 * PREP_TY + 2;
     __shared__ float gs[GH][GW + 1];
+    __shared__ uint2 rgb[GH - 2][GW - 2];  // the tile's own pixels as bf16 (R, G, B, 0) for Z
     const int b = blockIdx.z;
     const int Hz = H / 2, Wz = W / 2;
     const float *img = image + (long long)b * 3 * H * W;
@@ -73,12 +74,19 @@ __global__ void __launch_bounds__(256) k_prep(const float *__restrict__ image, i
     for (int k = threadIdx.x; k < GH * GW; k += blockDim.x) {
         const int a = k / GW, c = k - a * GW;
         const int y = y0 + a, x = x0 + c;
-        float v = 0.0f;
+        float v = 0.0f, r = 0.f, g = 0.f, bl = 0.f;
         if (y >= 0 && y < H && x >= 0 && x < W) {
             const long long pp = (long long)y * W + x;
-            v = (img[pp] + img[P + pp] + img[2 * P + pp]) / 3.0f;
+            r = img[pp];
+            g = img[P + pp];
+            bl = img[2 * P + pp];
+            v = (r + g + bl) / 3.0f;
         }
         gs[a][c] = v;
+        if (a >= 1 && a <= GH - 2 && c >= 1 && c <= GW - 2) {
+            const __nv_bfloat162 rg = __floats2bfloat162_rn(r, g), b0 = __floats2bfloat162_rn(bl, 0.f);
+            rgb[a - 1][c - 1] = make_uint2(*reinterpret_cast<const uint32_t *>(&rg), *reinterpret_cast<const uint32_t *>(&b0));
+        }
     }
     __syncthreads();
     const int tx = threadIdx.x % PREP_TX, ty = threadIdx.x / PREP_TX;
@@ -109,11 +117,12 @@ __global__ void __launch_bounds__(256) k_prep(const float *__restrict__ image, i
                 }
             const float gm = sqrtf(gx * gx + gy * gy + 1e-6f);
             gmv[dy][dx] = gm;
-            const long long pp = (long long)(2 * p + dy) * W + 2 * q + dx;
             const int base = (dy * 2 + dx) * 4;
-            z[base + 0] = __float2bfloat16_rn(img[pp]);
-            z[base + 1] = __float2bfloat16_rn(img[P + pp]);
-            z[base + 2] = __float2bfloat16_rn(img[2 * P + pp]);
+            const uint2 c3 = rgb[2 * ty + dy][2 * tx + dx];
+            const __nv_bfloat16 *e3 = reinterpret_cast<const __nv_bfloat16 *>(&c3);
+            z[base + 0] = e3[0];
+            z[base + 1] = e3[1];
+            z[base + 2] = e3[2];
             z[base + 3] = __float2bfloat16_rn(gm);
         }
 #pragma unroll
