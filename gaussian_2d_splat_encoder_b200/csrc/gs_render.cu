@@ -637,17 +637,19 @@ __device__ __forceinline__ int stage_batch(SplatRec *__restrict__ sr, SplatRec &
     return nb8;
 }
 
-// TILE 8, binned modes: one WARP per tile (four tiles per CTA), 2 pixels per lane in one column, so there
+// (1, 2 and 4 tiles per CTA measured within 1% of each other at four images per launch)
+#define FW_W8_WPB 4
+// TILE 8, binned modes: one WARP per tile (FW_W8_WPB tiles per CTA), 2 pixels per lane in one column, so there
 // is no cross-warp reduction and one set-up per tile and lane; each lane writes its pixels' five sums.
 // Tiles with more than FW_DEEP pairs are left to k_fields_deep8.
-template <bool ODDS>
-__global__ void __launch_bounds__(128) k_fields_w8(RenderGeom G, const SplatRec *__restrict__ rec,
-                                                   const int2 *__restrict__ ranges, const int *__restrict__ vals,
-                                                   float *__restrict__ fields, int nt) {
-    __shared__ SplatRec srec[4][32];
+template <bool ODDS, int WPB>
+__global__ void __launch_bounds__(WPB * 32) k_fields_w8(RenderGeom G, const SplatRec *__restrict__ rec,
+                                                        const int2 *__restrict__ ranges, const int *__restrict__ vals,
+                                                        float *__restrict__ fields, int nt) {
+    __shared__ SplatRec srec[WPB][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int h = lane >> 4, hl = lane & 15;  // half-warp; pixels (column hl & 7, rows (hl >> 3) + 2j)
-    const int gt = blockIdx.x * 4 + warp;
+    const int gt = blockIdx.x * WPB + warp;
     if (gt >= nt) return;  // (warp-uniform; the kernel synchronises warps only)
     const int2 rg = ranges[gt];  // empty tile: begin == end
     const int p0 = rg.y > rg.x ? rg.x : 0;
@@ -2053,13 +2055,14 @@ int launch_fields_fwd(const Plan &pl, void *ws, cudaStream_t st) {
         const unsigned char *misc = at<unsigned char>(ws, pl.o_misc);
         const unsigned dgrid = (unsigned)std::max(1, std::min(pl.dcap, 148 * 3));
         const int nt = (int)((long long)G.B * G.tiles_per_image);
-        const unsigned wgrid = (unsigned)((nt + 3) / 4);
+        constexpr int WPB = FW_W8_WPB;
+        const unsigned wgrid = (unsigned)((nt + WPB - 1) / WPB);
         if (G.odds) {
             k_fields_deep8<true><<<dgrid, FW_DEEP_NW * 32, 0, st>>>(G, rec, rng, vals, dl, misc, fld);
-            k_fields_w8<true><<<wgrid, 128, 0, st>>>(G, rec, rng, vals, fld, nt);
+            k_fields_w8<true, WPB><<<wgrid, WPB * 32, 0, st>>>(G, rec, rng, vals, fld, nt);
         } else {
             k_fields_deep8<false><<<dgrid, FW_DEEP_NW * 32, 0, st>>>(G, rec, rng, vals, dl, misc, fld);
-            k_fields_w8<false><<<wgrid, 128, 0, st>>>(G, rec, rng, vals, fld, nt);
+            k_fields_w8<false, WPB><<<wgrid, WPB * 32, 0, st>>>(G, rec, rng, vals, fld, nt);
         }
         GS_COUNT(1);
         GS_CHECK_LAUNCH("k_fields_w8");
